@@ -1,0 +1,77 @@
+/*
+ * qwen_asr_ext.h — extensions of libqwen_asr beyond the reference's C-FFI.
+ *
+ * Each entry names the reference item it exposes. None changes the behaviour of the
+ * functions in qwen_asr.h.
+ */
+#ifndef QWEN_ASR_EXT_H
+#define QWEN_ASR_EXT_H
+
+#include "qwen_asr.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Load onto an explicit CUDA device (-1 = $QASR_DEVICE or the current device). */
+QwenAsrEngine* qwen_asr_load_model_on_device(const char* model_dir, int32_t device, int32_t verbosity);
+/* Message of the last failure on this thread ("" if none). */
+const char* qwen_asr_last_error(void);
+/* QwenCtx::set_prompt (context.rs:167-175); 0 ok. */
+int32_t qwen_asr_set_prompt(QwenAsrEngine* engine, const char* prompt);
+/* QwenCtx.past_text_conditioning (context.rs:56; CLI --past-text). */
+void qwen_asr_set_past_text(QwenAsrEngine* engine, int32_t on);
+/* QwenCtx.skip_silence (context.rs:57; compact_silence, audio.rs:375-479). */
+void qwen_asr_set_skip_silence(QwenAsrEngine* engine, int32_t on);
+/* Decode weights: 0 = int8 per-row (the reference's decode, decoder.rs:106-118, default),
+ * 1 = bf16 (the reference's bf16 matvec family, kernels/mod.rs:630-835). */
+int32_t qwen_asr_set_decode_mode(QwenAsrEngine* engine, int32_t mode);
+/* Benchmark mode: run exactly n decode steps per segment, ignoring EOS (0 = off). */
+void qwen_asr_set_force_n_tokens(QwenAsrEngine* engine, int32_t n);
+/* 1 (default): decode steps replay a CUDA graph; 0: plain launches. */
+void qwen_asr_set_use_graph(QwenAsrEngine* engine, int32_t on);
+/* Generated ids of segment/chunk `segment` of the last call (including the stop token);
+ * returns the count (copies at most cap), -1 if out of range. */
+int32_t qwen_asr_last_tokens(QwenAsrEngine* engine, int32_t segment, int32_t* out, int32_t cap);
+int32_t qwen_asr_last_segments(QwenAsrEngine* engine);
+/* Perf counters of the last call (context.rs:67-73 + per-stage GPU times):
+ * total_ms, audio_ms, encode_ms, decode_ms, text_tokens, mel_ms, enc_ms, prefill_ms,
+ * decode_ms(gpu), decode_steps. Returns the number of values. */
+int32_t qwen_asr_get_perf(QwenAsrEngine* engine, double* out, int32_t cap);
+/* enc_d, enc_layers, enc_heads, enc_ffn, dec_hidden, dec_layers, dec_heads, dec_kv_heads,
+ * dec_inter, vocab, device. */
+int32_t qwen_asr_model_info(QwenAsrEngine* engine, int32_t* out, int32_t cap);
+
+/* ---- parity hooks (tests) ---- */
+/* mel_spectrogram (audio.rs:273-372): out [n_frames][128] (frame-major). Returns n_frames. */
+int32_t qwen_asr_debug_mel(QwenAsrEngine* engine, const float* samples, int32_t n, float* out, int64_t cap);
+/* Encoder::forward (encoder.rs:186-358) of mel [n_frames][128]: out [T][dec_hidden]; returns T. */
+int32_t qwen_asr_debug_encode(QwenAsrEngine* engine, const float* mel, int32_t n_frames, float* out, int64_t cap);
+/* decoder_prefill over rows[0..n_rows-1) then n_steps decoder_forward steps starting from
+ * row n_rows-1 (transcribe.rs:171-226). With `forced`, step i+1's input is forced[i]
+ * (teacher forcing). out_ids [n_steps]; out_logits [n_steps][vocab] (optional);
+ * out_hidden [n_rows][hidden] final prefill hidden states (optional). Returns n_steps. */
+int32_t qwen_asr_debug_decode(QwenAsrEngine* engine, const float* rows, int32_t n_rows, const int32_t* forced,
+                              int32_t n_steps, int32_t* out_ids, float* out_logits, float* out_hidden);
+
+/* ---- host-only hooks (no GPU needed) ---- */
+/* QwenTokenizer::encode (tokenizer.rs:227-279): returns the id count, -2 if unencodable. */
+int32_t qwen_asr_debug_tokenize(const char* model_dir, const char* text, int32_t* out, int32_t cap);
+/* Concatenated decode_bytes (tokenizer.rs:217-225) of ids; returns the byte count. */
+int32_t qwen_asr_debug_detokenize(const char* model_dir, const int32_t* ids, int32_t n, char* out, int32_t cap);
+/* parse_wav_buffer (audio.rs:22-91) incl. resample (audio.rs:133-196); returns sample count. */
+int64_t qwen_asr_debug_parse_wav(const uint8_t* data, int64_t len, float* out, int64_t cap);
+/* Segment start offsets of transcribe_audio (transcribe.rs:253-346); returns the count. */
+int32_t qwen_asr_debug_split_points(const float* samples, int64_t n, float segment_sec, float search_sec,
+                                    int64_t* out, int32_t cap);
+/* compact_silence (audio.rs:375-479); returns the kept sample count. */
+int64_t qwen_asr_debug_compact_silence(const float* samples, int64_t n, float* out, int64_t cap);
+/* String::from_utf8_lossy + str::trim as used on transcripts (transcribe.rs:237-238). */
+int32_t qwen_asr_debug_lossy_trim(const char* bytes, int32_t n, char* out, int32_t cap);
+/* normalize_language (config.rs:167-182); "" when unsupported. */
+int32_t qwen_asr_debug_normalize_language(const char* lang, char* out, int32_t cap);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QWEN_ASR_EXT_H */

@@ -1,0 +1,254 @@
+"""Python binding of libqwen_asr (the B200 Qwen3-ASR engine) over its C ABI.
+
+Mirrors the reference's public surface (crates/qwen-asr/src/c_api.rs and the Rust API
+QwenCtx::load / transcribe / transcribe_audio / StreamState / stream_push_audio): an
+`Engine` owns one loaded model on one GPU; `Stream` is an incremental streaming state.
+Every call goes through ctypes into the CUDA library; there is no CPU fallback — if the
+library is missing, importing `lib()` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libqwen_asr.so")
+_lib = None
+
+_F32P = C.POINTER(C.c_float)
+_I32P = C.POINTER(C.c_int32)
+_I64P = C.POINTER(C.c_int64)
+_U8P = C.POINTER(C.c_uint8)
+_VP = C.c_void_p
+
+# name: (restype, argtypes)
+SIGNATURES = {
+    "qwen_asr_load_model": (_VP, [C.c_char_p, C.c_int32, C.c_int32]),
+    "qwen_asr_transcribe_file": (_VP, [_VP, C.c_char_p]),
+    "qwen_asr_transcribe_pcm": (_VP, [_VP, _F32P, C.c_int32]),
+    "qwen_asr_transcribe_wav_buffer": (_VP, [_VP, _U8P, C.c_int32]),
+    "qwen_asr_set_segment_sec": (None, [_VP, C.c_float]),
+    "qwen_asr_set_language": (C.c_int32, [_VP, C.c_char_p]),
+    "qwen_asr_free_string": (None, [_VP]),
+    "qwen_asr_free": (None, [_VP]),
+    "qwen_asr_stream_new": (_VP, []),
+    "qwen_asr_stream_free": (None, [_VP]),
+    "qwen_asr_stream_reset": (None, [_VP]),
+    "qwen_asr_stream_push": (_VP, [_VP, _VP, _F32P, C.c_int32, C.c_int32]),
+    "qwen_asr_stream_get_result": (_VP, [_VP]),
+    "qwen_asr_stream_set_chunk_sec": (None, [_VP, C.c_float]),
+    "qwen_asr_stream_set_rollback": (None, [_VP, C.c_int32]),
+    "qwen_asr_stream_set_unfixed_chunks": (None, [_VP, C.c_int32]),
+    "qwen_asr_stream_set_max_new_tokens": (None, [_VP, C.c_int32]),
+    # extensions
+    "qwen_asr_load_model_on_device": (_VP, [C.c_char_p, C.c_int32, C.c_int32]),
+    "qwen_asr_last_error": (C.c_char_p, []),
+    "qwen_asr_set_prompt": (C.c_int32, [_VP, C.c_char_p]),
+    "qwen_asr_set_past_text": (None, [_VP, C.c_int32]),
+    "qwen_asr_set_skip_silence": (None, [_VP, C.c_int32]),
+    "qwen_asr_set_decode_mode": (C.c_int32, [_VP, C.c_int32]),
+    "qwen_asr_set_force_n_tokens": (None, [_VP, C.c_int32]),
+    "qwen_asr_set_use_graph": (None, [_VP, C.c_int32]),
+    "qwen_asr_last_tokens": (C.c_int32, [_VP, C.c_int32, _I32P, C.c_int32]),
+    "qwen_asr_last_segments": (C.c_int32, [_VP]),
+    "qwen_asr_get_perf": (C.c_int32, [_VP, C.POINTER(C.c_double), C.c_int32]),
+    "qwen_asr_model_info": (C.c_int32, [_VP, _I32P, C.c_int32]),
+    "qwen_asr_debug_mel": (C.c_int32, [_VP, _F32P, C.c_int32, _F32P, C.c_int64]),
+    "qwen_asr_debug_encode": (C.c_int32, [_VP, _F32P, C.c_int32, _F32P, C.c_int64]),
+    "qwen_asr_debug_decode": (C.c_int32, [_VP, _F32P, C.c_int32, _I32P, C.c_int32, _I32P, _F32P, _F32P]),
+    "qwen_asr_debug_tokenize": (C.c_int32, [C.c_char_p, C.c_char_p, _I32P, C.c_int32]),
+    "qwen_asr_debug_detokenize": (C.c_int32, [C.c_char_p, _I32P, C.c_int32, C.c_char_p, C.c_int32]),
+    "qwen_asr_debug_parse_wav": (C.c_int64, [_U8P, C.c_int64, _F32P, C.c_int64]),
+    "qwen_asr_debug_split_points": (C.c_int32, [_F32P, C.c_int64, C.c_float, C.c_float, _I64P, C.c_int32]),
+    "qwen_asr_debug_compact_silence": (C.c_int64, [_F32P, C.c_int64, _F32P, C.c_int64]),
+    "qwen_asr_debug_lossy_trim": (C.c_int32, [C.c_char_p, C.c_int32, C.c_char_p, C.c_int32]),
+    "qwen_asr_debug_normalize_language": (C.c_int32, [C.c_char_p, C.c_char_p, C.c_int32]),
+}
+
+
+def lib():
+    """Loads libqwen_asr.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m qwen_asr_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _f32(a):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    return a, a.ctypes.data_as(_F32P)
+
+
+def _take_string(ptr):
+    if not ptr:
+        return None
+    s = C.string_at(ptr).decode("utf-8")
+    lib().qwen_asr_free_string(ptr)
+    return s
+
+
+def last_error() -> str:
+    return (lib().qwen_asr_last_error() or b"").decode("utf-8", "replace")
+
+
+class Engine:
+    """QwenCtx equivalent on one GPU (context.rs:86-163 via c_api.rs:20-46)."""
+
+    def __init__(self, model_dir: str, device: int = -1, verbosity: int = 0):
+        self._h = lib().qwen_asr_load_model_on_device(model_dir.encode(), device, verbosity)
+        if not self._h:
+            raise RuntimeError(f"qwen_asr_load_model failed: {last_error()}")
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().qwen_asr_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    # --- reference C-FFI surface ---
+    def transcribe_pcm(self, samples) -> str | None:
+        a, p = _f32(samples)
+        return _take_string(lib().qwen_asr_transcribe_pcm(self._h, p, len(a)))
+
+    def transcribe_file(self, path: str) -> str | None:
+        return _take_string(lib().qwen_asr_transcribe_file(self._h, path.encode()))
+
+    def transcribe_wav_buffer(self, data: bytes) -> str | None:
+        buf = (C.c_uint8 * len(data)).from_buffer_copy(data)
+        return _take_string(lib().qwen_asr_transcribe_wav_buffer(self._h, buf, len(data)))
+
+    def set_segment_sec(self, sec: float):
+        lib().qwen_asr_set_segment_sec(self._h, sec)
+
+    def set_language(self, lang: str) -> int:
+        return lib().qwen_asr_set_language(self._h, lang.encode())
+
+    def stream_set_chunk_sec(self, sec):
+        lib().qwen_asr_stream_set_chunk_sec(self._h, sec)
+
+    def stream_set_rollback(self, n):
+        lib().qwen_asr_stream_set_rollback(self._h, n)
+
+    def stream_set_unfixed_chunks(self, n):
+        lib().qwen_asr_stream_set_unfixed_chunks(self._h, n)
+
+    def stream_set_max_new_tokens(self, n):
+        lib().qwen_asr_stream_set_max_new_tokens(self._h, n)
+
+    # --- extensions ---
+    def set_prompt(self, prompt: str) -> int:
+        return lib().qwen_asr_set_prompt(self._h, prompt.encode())
+
+    def set_past_text(self, on: bool):
+        lib().qwen_asr_set_past_text(self._h, int(on))
+
+    def set_skip_silence(self, on: bool):
+        lib().qwen_asr_set_skip_silence(self._h, int(on))
+
+    def set_decode_mode(self, mode: str):
+        if lib().qwen_asr_set_decode_mode(self._h, {"int8": 0, "bf16": 1}[mode]) != 0:
+            raise ValueError(mode)
+
+    def set_force_n_tokens(self, n: int):
+        lib().qwen_asr_set_force_n_tokens(self._h, n)
+
+    def set_use_graph(self, on: bool):
+        lib().qwen_asr_set_use_graph(self._h, int(on))
+
+    def last_tokens(self):
+        L = lib()
+        out = []
+        for s in range(L.qwen_asr_last_segments(self._h)):
+            n = L.qwen_asr_last_tokens(self._h, s, None, 0)
+            buf = (C.c_int32 * max(n, 1))()
+            L.qwen_asr_last_tokens(self._h, s, buf, n)
+            out.append(list(buf[:n]))
+        return out
+
+    def perf(self) -> dict:
+        v = (C.c_double * 16)()
+        n = lib().qwen_asr_get_perf(self._h, v, 16)
+        keys = ["total_ms", "audio_ms", "encode_ms", "decode_ms", "text_tokens", "gpu_mel_ms", "gpu_enc_ms",
+                "gpu_prefill_ms", "gpu_decode_ms", "decode_steps"]
+        return {k: v[i] for i, k in enumerate(keys[:n])}
+
+    def model_info(self) -> dict:
+        v = (C.c_int32 * 16)()
+        n = lib().qwen_asr_model_info(self._h, v, 16)
+        keys = ["enc_d_model", "enc_layers", "enc_heads", "enc_ffn_dim", "dec_hidden", "dec_layers", "dec_heads",
+                "dec_kv_heads", "dec_intermediate", "vocab_size", "device"]
+        return {k: v[i] for i, k in enumerate(keys[:n])}
+
+    # --- parity hooks ---
+    def debug_mel(self, samples) -> np.ndarray:
+        a, p = _f32(samples)
+        F = lib().qwen_asr_debug_mel(self._h, p, len(a), None, 0)
+        if F <= 0:
+            raise RuntimeError(last_error())
+        out = np.empty((F, 128), dtype=np.float32)
+        lib().qwen_asr_debug_mel(self._h, p, len(a), out.ctypes.data_as(_F32P), out.size)
+        return out
+
+    def debug_encode(self, mel_fm: np.ndarray) -> np.ndarray:
+        m, p = _f32(mel_fm)
+        hid = self.model_info()["dec_hidden"]
+        F = m.shape[0]
+        cap = (F // 8 + 16) * hid
+        out = np.empty(cap, dtype=np.float32)
+        T = lib().qwen_asr_debug_encode(self._h, p, F, out.ctypes.data_as(_F32P), cap)
+        if T <= 0:
+            raise RuntimeError(last_error())
+        return out[:T * hid].reshape(T, hid).copy()
+
+    def debug_decode(self, rows: np.ndarray, n_steps: int, forced=None, want_logits=False, want_hidden=False):
+        r, p = _f32(rows)
+        info = self.model_info()
+        ids = np.zeros(max(n_steps, 1), dtype=np.int32)
+        fz = None
+        if forced is not None:
+            fz = np.ascontiguousarray(forced, dtype=np.int32)
+        lg = np.zeros((n_steps, info["vocab_size"]), dtype=np.float32) if want_logits else None
+        hd = np.zeros((r.shape[0], info["dec_hidden"]), dtype=np.float32) if want_hidden else None
+        n = lib().qwen_asr_debug_decode(
+            self._h, p, r.shape[0], fz.ctypes.data_as(_I32P) if fz is not None else None, n_steps,
+            ids.ctypes.data_as(_I32P), lg.ctypes.data_as(_F32P) if lg is not None else None,
+            hd.ctypes.data_as(_F32P) if hd is not None else None)
+        if n < 0:
+            raise RuntimeError(last_error())
+        return ids[:n_steps], lg, hd
+
+
+class Stream:
+    """Incremental streaming state (transcribe.rs:801-893 via c_api.rs:179-265)."""
+
+    def __init__(self):
+        self._h = lib().qwen_asr_stream_new()
+
+    def push(self, engine: Engine, samples, finalize: bool = False) -> str | None:
+        a, p = _f32(samples)
+        return _take_string(lib().qwen_asr_stream_push(engine._h, self._h, p, len(a), int(finalize)))
+
+    def result(self) -> str | None:
+        return _take_string(lib().qwen_asr_stream_get_result(self._h))
+
+    def reset(self):
+        lib().qwen_asr_stream_reset(self._h)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().qwen_asr_stream_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()

@@ -1,0 +1,338 @@
+// C ABI of libqwen_asr: the 17 exports of crates/qwen-asr/src/c_api.rs with the same
+// names, argument meaning and error convention (NULL / -1, never an exception), plus
+// the clearly separated extensions declared in include/qwen_asr_ext.h.
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <mutex>
+#include <new>
+#include <sstream>
+
+#include "../../include/qwen_asr.h"
+#include "../../include/qwen_asr_ext.h"
+#include "transcribe.h"
+
+struct QwenAsrEngine {
+  qasr::Ctx ctx;
+};
+
+struct QwenAsrStreamState {
+  qasr::StreamState state;
+  std::vector<float> audio_buf;  // the reference passes the full accumulated buffer (c_api.rs:171-175)
+};
+
+namespace {
+// Returns a malloc'ed copy, or NULL when the text holds an interior NUL (CString::new).
+char* to_c_string(const std::string& s) {
+  if (memchr(s.data(), 0, s.size())) return nullptr;
+  char* out = (char*)malloc(s.size() + 1);
+  if (!out) return nullptr;
+  memcpy(out, s.data(), s.size() + 1);
+  return out;
+}
+
+int pick_device() {
+  if (const char* d = getenv("QASR_DEVICE")) return atoi(d);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+char* run_transcribe(QwenAsrEngine* e, const std::vector<float>& samples) {
+  std::string out;
+  try {
+    if (!e->ctx.transcribe_audio(samples, out)) return nullptr;
+  } catch (const std::exception& ex) {
+    qasr::set_error(std::string("transcribe: ") + ex.what());
+    return nullptr;
+  }
+  return to_c_string(out);
+}
+}  // namespace
+
+extern "C" {
+
+QwenAsrEngine* qwen_asr_load_model(const char* model_dir, int32_t n_threads, int32_t verbosity) {
+  (void)n_threads;  // the CPU thread count has no meaning here: all math runs on the GPU
+  return qwen_asr_load_model_on_device(model_dir, -1, verbosity);
+}
+
+QwenAsrEngine* qwen_asr_load_model_on_device(const char* model_dir, int32_t device, int32_t verbosity) {
+  if (!model_dir) return nullptr;
+  qasr::g_verbose = verbosity;
+  QwenAsrEngine* e = new (std::nothrow) QwenAsrEngine();
+  if (!e) return nullptr;
+  try {
+    if (!e->ctx.load(model_dir, device >= 0 ? device : pick_device())) {
+      delete e;
+      return nullptr;
+    }
+  } catch (const std::exception& ex) {
+    qasr::set_error(std::string("load: ") + ex.what());
+    delete e;
+    return nullptr;
+  }
+  return e;
+}
+
+char* qwen_asr_transcribe_file(QwenAsrEngine* e, const char* wav_path) {
+  if (!e || !wav_path) return nullptr;
+  std::ifstream f(wav_path, std::ios::binary);
+  if (!f) {
+    qasr::set_error(std::string("cannot read ") + wav_path);
+    return nullptr;
+  }
+  std::stringstream ss;
+  ss << f.rdbuf();
+  std::string data = ss.str();
+  std::vector<float> samples;
+  if (!qasr::parse_wav_buffer((const uint8_t*)data.data(), data.size(), samples)) return nullptr;
+  return run_transcribe(e, samples);
+}
+
+char* qwen_asr_transcribe_pcm(QwenAsrEngine* e, const float* samples, int32_t n_samples) {
+  if (!e || !samples || n_samples <= 0) return nullptr;
+  return run_transcribe(e, std::vector<float>(samples, samples + n_samples));
+}
+
+char* qwen_asr_transcribe_wav_buffer(QwenAsrEngine* e, const uint8_t* wav_data, int32_t wav_len) {
+  if (!e || !wav_data || wav_len <= 0) return nullptr;
+  std::vector<float> samples;
+  if (!qasr::parse_wav_buffer(wav_data, (size_t)wav_len, samples)) return nullptr;
+  return run_transcribe(e, samples);
+}
+
+void qwen_asr_set_segment_sec(QwenAsrEngine* e, float sec) {
+  if (e) e->ctx.segment_sec = sec;
+}
+
+int32_t qwen_asr_set_language(QwenAsrEngine* e, const char* language) {
+  if (!e || !language) return -1;
+  return e->ctx.set_force_language(language) ? 0 : -1;
+}
+
+void qwen_asr_free_string(char* s) { free(s); }
+
+void qwen_asr_free(QwenAsrEngine* e) { delete e; }
+
+QwenAsrStreamState* qwen_asr_stream_new(void) { return new (std::nothrow) QwenAsrStreamState(); }
+
+void qwen_asr_stream_free(QwenAsrStreamState* s) { delete s; }
+
+void qwen_asr_stream_reset(QwenAsrStreamState* s) {
+  if (!s) return;
+  s->state.reset();
+  s->audio_buf.clear();
+}
+
+char* qwen_asr_stream_push(QwenAsrEngine* e, QwenAsrStreamState* s, const float* samples, int32_t n_samples,
+                           int32_t finalize) {
+  if (!e || !s) return nullptr;
+  if (samples && n_samples > 0) s->audio_buf.insert(s->audio_buf.end(), samples, samples + n_samples);
+  std::string delta;
+  try {
+    if (!e->ctx.stream_push_audio(s->audio_buf, s->state, finalize != 0, delta)) return nullptr;
+  } catch (const std::exception& ex) {
+    qasr::set_error(std::string("stream: ") + ex.what());
+    return nullptr;
+  }
+  std::string txt = qasr::utf8_lossy(delta);
+  if (txt.empty()) return nullptr;
+  return to_c_string(txt);
+}
+
+char* qwen_asr_stream_get_result(QwenAsrStreamState* s) {
+  if (!s) return nullptr;
+  std::string txt = qasr::utf8_lossy(s->state.result_bytes);
+  if (txt.empty()) return nullptr;
+  return to_c_string(txt);
+}
+
+void qwen_asr_stream_set_chunk_sec(QwenAsrEngine* e, float sec) {
+  if (e && sec > 0.0f) e->ctx.stream_chunk_sec = sec;
+}
+void qwen_asr_stream_set_rollback(QwenAsrEngine* e, int32_t tokens) {
+  if (e && tokens >= 0) e->ctx.stream_rollback = tokens;
+}
+void qwen_asr_stream_set_unfixed_chunks(QwenAsrEngine* e, int32_t chunks) {
+  if (e && chunks >= 0) e->ctx.stream_unfixed_chunks = chunks;
+}
+void qwen_asr_stream_set_max_new_tokens(QwenAsrEngine* e, int32_t tokens) {
+  if (e && tokens > 0) e->ctx.stream_max_new_tokens = tokens;
+}
+
+// ------------------------------------------------------------------ extensions
+const char* qwen_asr_last_error(void) {
+  static thread_local std::string s;
+  s = qasr::last_error();
+  return s.c_str();
+}
+
+int32_t qwen_asr_set_prompt(QwenAsrEngine* e, const char* prompt) {
+  if (!e || !prompt) return -1;
+  e->ctx.set_prompt(prompt);
+  return 0;
+}
+void qwen_asr_set_past_text(QwenAsrEngine* e, int32_t on) {
+  if (e) e->ctx.past_text_conditioning = on != 0;
+}
+void qwen_asr_set_skip_silence(QwenAsrEngine* e, int32_t on) {
+  if (e) e->ctx.skip_silence = on != 0;
+}
+int32_t qwen_asr_set_decode_mode(QwenAsrEngine* e, int32_t mode) {
+  if (!e || (mode != 0 && mode != 1)) return -1;
+  e->ctx.eng.set_decode_mode(mode == 0 ? qasr::DECODE_INT8 : qasr::DECODE_BF16);
+  return 0;
+}
+void qwen_asr_set_force_n_tokens(QwenAsrEngine* e, int32_t n) {
+  if (e) e->ctx.force_n_tokens = n > 0 ? n : 0;
+}
+void qwen_asr_set_use_graph(QwenAsrEngine* e, int32_t on) {
+  if (e) e->ctx.eng.use_graph = on != 0;
+}
+
+int32_t qwen_asr_last_tokens(QwenAsrEngine* e, int32_t segment, int32_t* out, int32_t cap) {
+  if (!e || segment < 0 || segment >= (int)e->ctx.last_tokens.size()) return -1;
+  const auto& v = e->ctx.last_tokens[segment];
+  if (out)
+    for (int i = 0; i < (int)v.size() && i < cap; ++i) out[i] = v[i];
+  return (int32_t)v.size();
+}
+int32_t qwen_asr_last_segments(QwenAsrEngine* e) { return e ? (int32_t)e->ctx.last_tokens.size() : -1; }
+
+int32_t qwen_asr_get_perf(QwenAsrEngine* e, double* out, int32_t cap) {
+  if (!e || !out) return -1;
+  const auto& c = e->ctx;
+  double v[] = {c.perf_total_ms, c.perf_audio_ms, c.perf_encode_ms, c.perf_decode_ms, (double)c.perf_text_tokens,
+                c.eng.perf.mel_ms, c.eng.perf.enc_ms, c.eng.perf.prefill_ms, c.eng.perf.decode_ms,
+                (double)c.eng.perf.decode_steps};
+  int n = (int)(sizeof(v) / sizeof(v[0]));
+  for (int i = 0; i < n && i < cap; ++i) out[i] = v[i];
+  return n;
+}
+
+int32_t qwen_asr_model_info(QwenAsrEngine* e, int32_t* out, int32_t cap) {
+  if (!e || !out) return -1;
+  const auto& c = e->ctx.eng.cfg();
+  int v[] = {c.enc_d_model, c.enc_layers, c.enc_heads, c.enc_ffn_dim, c.dec_hidden, c.dec_layers, c.dec_heads,
+             c.dec_kv_heads, c.dec_intermediate, c.vocab_size, e->ctx.eng.device()};
+  int n = (int)(sizeof(v) / sizeof(v[0]));
+  for (int i = 0; i < n && i < cap; ++i) out[i] = v[i];
+  return n;
+}
+
+int32_t qwen_asr_debug_mel(QwenAsrEngine* e, const float* samples, int32_t n, float* out, int64_t cap) {
+  if (!e || !samples || n <= 0) return -1;
+  int F = e->ctx.eng.mel(samples, n, false);
+  if (F <= 0) return -1;
+  if (out) {
+    if ((int64_t)F * 128 > cap) return -1;
+    if (cudaMemcpy(out, e->ctx.eng.mel_buf(), (size_t)F * 128 * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  }
+  return F;
+}
+
+int32_t qwen_asr_debug_encode(QwenAsrEngine* e, const float* mel, int32_t n_frames, float* out, int64_t cap) {
+  if (!e || !mel || n_frames <= 0) return -1;
+  qasr::DevBuf<float> d;
+  if (!d.alloc((size_t)n_frames * 128)) return -1;
+  if (cudaMemcpy(d.p, mel, (size_t)n_frames * 128 * 4, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
+  int T = e->ctx.eng.encode(d.p, n_frames);
+  if (T <= 0) return -1;
+  size_t n = (size_t)T * e->ctx.eng.cfg().dec_hidden;
+  if (out) {
+    if ((int64_t)n > cap) return -1;
+    if (cudaMemcpy(out, e->ctx.eng.enc_out(), n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  }
+  return T;
+}
+
+int32_t qwen_asr_debug_decode(QwenAsrEngine* e, const float* rows, int32_t n_rows, const int32_t* forced,
+                              int32_t n_steps, int32_t* out_ids, float* out_logits, float* out_hidden) {
+  if (!e || !rows || n_rows <= 0 || n_steps < 0) return -1;
+  auto& eng = e->ctx.eng;
+  if (!eng.prefill_rows(rows, n_rows, 0)) return -1;
+  if (out_hidden) {
+    std::vector<float> h;
+    if (!eng.copy_prefill_hidden(h, n_rows)) return -1;
+    memcpy(out_hidden, h.data(), h.size() * 4);
+  }
+  std::vector<int> f, ids;
+  std::vector<float> lg;
+  if (forced) f.assign(forced, forced + n_steps);
+  if (!eng.decode(n_steps, false, ids, forced ? &f : nullptr, out_logits ? &lg : nullptr)) return -1;
+  if (out_ids)
+    for (int i = 0; i < (int)ids.size(); ++i) out_ids[i] = ids[i];
+  if (out_logits) memcpy(out_logits, lg.data(), lg.size() * 4);
+  return (int32_t)ids.size();
+}
+
+// ---- host-only hooks (no GPU needed): tokenizer, WAV, segmentation, text handling ----
+int32_t qwen_asr_debug_tokenize(const char* model_dir, const char* text, int32_t* out, int32_t cap) {
+  if (!model_dir || !text) return -1;
+  qasr::Tokenizer t;
+  if (!t.load(model_dir)) return -1;
+  std::vector<int> ids;
+  if (!t.encode(text, ids)) return -2;
+  for (int i = 0; i < (int)ids.size() && i < cap; ++i) out[i] = ids[i];
+  return (int32_t)ids.size();
+}
+
+int32_t qwen_asr_debug_detokenize(const char* model_dir, const int32_t* ids, int32_t n, char* out, int32_t cap) {
+  if (!model_dir || !ids || n < 0) return -1;
+  qasr::Tokenizer t;
+  if (!t.load(model_dir)) return -1;
+  std::string b;
+  for (int i = 0; i < n; ++i) b += t.decode_bytes(ids[i]);
+  if ((int)b.size() > cap) return -1;
+  memcpy(out, b.data(), b.size());
+  return (int32_t)b.size();
+}
+
+int64_t qwen_asr_debug_parse_wav(const uint8_t* data, int64_t len, float* out, int64_t cap) {
+  if (!data || len <= 0) return -1;
+  std::vector<float> s;
+  if (!qasr::parse_wav_buffer(data, (size_t)len, s)) return -1;
+  if (out) {
+    if ((int64_t)s.size() > cap) return -1;
+    memcpy(out, s.data(), s.size() * 4);
+  }
+  return (int64_t)s.size();
+}
+
+int32_t qwen_asr_debug_split_points(const float* samples, int64_t n, float segment_sec, float search_sec,
+                                    int64_t* out, int32_t cap) {
+  if (!samples || n < 0) return -1;
+  std::vector<float> x(samples, samples + n);
+  auto sp = qasr::split_points(x, segment_sec, search_sec);
+  for (int i = 0; i < (int)sp.size() && i < cap; ++i) out[i] = (int64_t)sp[i];
+  return (int32_t)sp.size();
+}
+
+int64_t qwen_asr_debug_compact_silence(const float* samples, int64_t n, float* out, int64_t cap) {
+  if (!samples || n < 0) return -1;
+  auto r = qasr::compact_silence(std::vector<float>(samples, samples + n));
+  if (out) {
+    if ((int64_t)r.size() > cap) return -1;
+    memcpy(out, r.data(), r.size() * 4);
+  }
+  return (int64_t)r.size();
+}
+
+int32_t qwen_asr_debug_lossy_trim(const char* bytes, int32_t n, char* out, int32_t cap) {
+  if (!bytes || n < 0) return -1;
+  std::string r = qasr::rust_trim(qasr::utf8_lossy(std::string(bytes, bytes + n)));
+  if ((int)r.size() > cap) return -1;
+  memcpy(out, r.data(), r.size());
+  return (int32_t)r.size();
+}
+
+int32_t qwen_asr_debug_normalize_language(const char* lang, char* out, int32_t cap) {
+  if (!lang) return -1;
+  std::string r = qasr::normalize_language(lang);
+  if ((int)r.size() + 1 > cap) return -1;
+  memcpy(out, r.c_str(), r.size() + 1);
+  return (int32_t)r.size();
+}
+
+}  // extern "C"

@@ -1,0 +1,701 @@
+// Engine: weight upload, mel / encoder / prefill / decode stages on one GPU.
+#include "engine.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+namespace qasr {
+
+Engine::~Engine() {
+  if (device_ >= 0) cudaSetDevice(device_);
+  if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
+  for (void* p : allocs_) cudaFree(p);
+  if (hstate_) cudaFreeHost(hstate_);
+  if (htokens_) cudaFreeHost(htokens_);
+  if (ev0_) cudaEventDestroy(ev0_);
+  if (ev1_) cudaEventDestroy(ev1_);
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+void* Engine::dalloc(size_t bytes) {
+  void* p = nullptr;
+  if (cudaMalloc(&p, std::max<size_t>(bytes, 16)) != cudaSuccess) {
+    set_error("cudaMalloc failed (" + std::to_string(bytes) + " bytes)");
+    return nullptr;
+  }
+  allocs_.push_back(p);
+  return p;
+}
+
+namespace {
+// Host conversion of any float tensor (F32 or BF16) to f32.
+bool tensor_f32(const SafeTensors& st, const std::string& name, std::vector<float>& out) {
+  const TensorInfo* t = st.find(name);
+  if (!t) {
+    set_error("weight not found: " + name);
+    return false;
+  }
+  size_t n = t->numel();
+  out.resize(n);
+  if (t->dtype == "F32") {
+    memcpy(out.data(), t->data, n * 4);
+  } else if (t->dtype == "BF16") {
+    const uint16_t* s = (const uint16_t*)t->data;
+    for (size_t i = 0; i < n; ++i) {
+      uint32_t b = (uint32_t)s[i] << 16;
+      memcpy(&out[i], &b, 4);
+    }
+  } else {
+    set_error("unsupported dtype for " + name + ": " + t->dtype);
+    return false;
+  }
+  return true;
+}
+
+const uint16_t* tensor_bf16(const SafeTensors& st, const std::string& name, size_t expect) {
+  const TensorInfo* t = st.find(name);
+  if (!t) {
+    set_error("weight not found: " + name);
+    return nullptr;
+  }
+  if (t->dtype != "BF16") {
+    set_error(name + ": expected BF16, got " + t->dtype);
+    return nullptr;
+  }
+  if (expect && t->numel() != expect) {
+    set_error(name + ": unexpected shape");
+    return nullptr;
+  }
+  return (const uint16_t*)t->data;
+}
+}  // namespace
+
+bool Engine::load(const std::string& dir, int device, bool trunc_quant) {
+  device_ = device;
+  // Validate the model files before touching the GPU.
+  SafeTensors st;
+  if (!st.open(dir)) return false;
+  if (!detect_config(st, cfg_)) return false;
+  CUDA_OK(cudaSetDevice(device), false);
+  CUDA_OK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), false);
+  CUDA_OK(cudaEventCreate(&ev0_), false);
+  CUDA_OK(cudaEventCreate(&ev1_), false);
+  const Config& c = cfg_;
+  if (c.dec_head_dim != 128 || c.enc_head_dim != 64 || c.dec_heads % c.dec_kv_heads != 0 ||
+      c.dec_heads / c.dec_kv_heads > 4) {
+    set_error("unsupported model geometry");
+    return false;
+  }
+  QASR_LOG(1, "Detected: Qwen3-ASR (enc %dd %dL, dec %dd %dL, inter %d)\n", c.enc_d_model, c.enc_layers,
+           c.dec_hidden, c.dec_layers, c.dec_intermediate);
+
+  std::vector<float> f;
+  auto up_f32 = [&](const std::string& name, float*& dst) -> bool {
+    if (!tensor_f32(st, name, f)) return false;
+    dst = dalloc_t<float>(f.size());
+    return dst && cudaMemcpy(dst, f.data(), f.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+  };
+  auto up_bf16 = [&](const std::string& name, __nv_bfloat16*& dst, size_t n) -> bool {
+    const uint16_t* p = tensor_bf16(st, name, n);
+    if (!p) return false;
+    dst = dalloc_t<__nv_bfloat16>(n);
+    return dst && cudaMemcpy(dst, p, n * 2, cudaMemcpyHostToDevice) == cudaSuccess;
+  };
+  // Concatenates bf16 tensors row-wise into one device matrix.
+  auto up_cat = [&](const std::vector<std::string>& names, size_t per_row, __nv_bfloat16*& dst) -> bool {
+    size_t total = 0;
+    std::vector<const TensorInfo*> ts;
+    for (auto& n : names) {
+      const TensorInfo* t = st.find(n);
+      if (!t || t->dtype != "BF16") {
+        set_error("missing/non-bf16 weight: " + n);
+        return false;
+      }
+      if (t->numel() % per_row) {
+        set_error("bad shape: " + n);
+        return false;
+      }
+      ts.push_back(t);
+      total += t->numel();
+    }
+    dst = dalloc_t<__nv_bfloat16>(total);
+    if (!dst) return false;
+    size_t off = 0;
+    for (auto t : ts) {
+      if (cudaMemcpy(dst + off, t->data, t->nbytes, cudaMemcpyHostToDevice) != cudaSuccess) return false;
+      off += t->numel();
+    }
+    return true;
+  };
+  auto cat_f32 = [&](const std::vector<std::string>& names, float*& dst) -> bool {
+    std::vector<float> all;
+    for (auto& n : names) {
+      if (!tensor_f32(st, n, f)) return false;
+      all.insert(all.end(), f.begin(), f.end());
+    }
+    dst = dalloc_t<float>(all.size());
+    return dst && cudaMemcpy(dst, all.data(), all.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+  };
+
+  const std::string p = "thinker.audio_tower.";
+  const int d = c.enc_d_model, H = kConvHidden;
+  // conv2d1 [480][1][3][3] -> f32 [480][9]
+  if (!up_f32(p + "conv2d1.weight", conv1_w) || !up_f32(p + "conv2d1.bias", conv1_b)) return false;
+  // conv2d2/3 [oc][ic][3][3] -> bf16 [oc][(ki*3+kj)*480 + ic] (im2col column order)
+  for (int li = 2; li <= 3; ++li) {
+    const uint16_t* w = tensor_bf16(st, p + "conv2d" + std::to_string(li) + ".weight", (size_t)H * H * 9);
+    if (!w) return false;
+    std::vector<uint16_t> perm((size_t)H * H * 9);
+    for (int oc = 0; oc < H; ++oc)
+      for (int ic = 0; ic < H; ++ic)
+        for (int kk = 0; kk < 9; ++kk) perm[(size_t)oc * H * 9 + kk * H + ic] = w[((size_t)oc * H + ic) * 9 + kk];
+    __nv_bfloat16*& dst = li == 2 ? conv2_w : conv3_w;
+    dst = dalloc_t<__nv_bfloat16>(perm.size());
+    if (!dst) return false;
+    CUDA_OK(cudaMemcpy(dst, perm.data(), perm.size() * 2, cudaMemcpyHostToDevice), false);
+    if (!up_f32(p + "conv2d" + std::to_string(li) + ".bias", li == 2 ? conv2_b : conv3_b)) return false;
+  }
+  {  // conv_out [d][ch*16 + f] -> [d][f*480 + ch] (matches the channels-last conv3 output)
+    const uint16_t* w = tensor_bf16(st, p + "conv_out.weight", (size_t)d * H * 16);
+    if (!w) return false;
+    std::vector<uint16_t> perm((size_t)d * H * 16);
+    for (int o = 0; o < d; ++o)
+      for (int ch = 0; ch < H; ++ch)
+        for (int fr = 0; fr < 16; ++fr) perm[(size_t)o * H * 16 + fr * H + ch] = w[(size_t)o * H * 16 + ch * 16 + fr];
+    conv_out_w = dalloc_t<__nv_bfloat16>(perm.size());
+    if (!conv_out_w) return false;
+    CUDA_OK(cudaMemcpy(conv_out_w, perm.data(), perm.size() * 2, cudaMemcpyHostToDevice), false);
+  }
+  enc_layers_.resize(c.enc_layers);
+  for (int i = 0; i < c.enc_layers; ++i) {
+    std::string lp = p + "layers." + std::to_string(i) + ".";
+    EncLayerW& L = enc_layers_[i];
+    if (!up_cat({lp + "self_attn.q_proj.weight", lp + "self_attn.k_proj.weight", lp + "self_attn.v_proj.weight"}, d,
+                L.wqkv) ||
+        !cat_f32({lp + "self_attn.q_proj.bias", lp + "self_attn.k_proj.bias", lp + "self_attn.v_proj.bias"}, L.bqkv) ||
+        !up_bf16(lp + "self_attn.out_proj.weight", L.wo, (size_t)d * d) ||
+        !up_f32(lp + "self_attn.out_proj.bias", L.bo) || !up_f32(lp + "self_attn_layer_norm.weight", L.ln1w) ||
+        !up_f32(lp + "self_attn_layer_norm.bias", L.ln1b) ||
+        !up_bf16(lp + "fc1.weight", L.w1, (size_t)c.enc_ffn_dim * d) || !up_f32(lp + "fc1.bias", L.b1) ||
+        !up_bf16(lp + "fc2.weight", L.w2, (size_t)c.enc_ffn_dim * d) || !up_f32(lp + "fc2.bias", L.b2) ||
+        !up_f32(lp + "final_layer_norm.weight", L.ln2w) || !up_f32(lp + "final_layer_norm.bias", L.ln2b))
+      return false;
+  }
+  if (!up_f32(p + "ln_post.weight", ln_post_w) || !up_f32(p + "ln_post.bias", ln_post_b) ||
+      !up_bf16(p + "proj1.weight", proj1_w, (size_t)d * d) || !up_f32(p + "proj1.bias", proj1_b) ||
+      !up_bf16(p + "proj2.weight", proj2_w, (size_t)c.enc_output_dim * d) || !up_f32(p + "proj2.bias", proj2_b))
+    return false;
+
+  // ---- decoder
+  const std::string m = "thinker.model.";
+  const int h = c.dec_hidden, qd = c.dec_heads * 128, kvd = c.dec_kv_heads * 128, inter = c.dec_intermediate;
+  if (!up_bf16(m + "embed_tokens.weight", embed_, (size_t)c.vocab_size * h)) return false;
+  dec_layers_.resize(c.dec_layers);
+  std::vector<uint16_t> gu((size_t)2 * inter * h);
+  for (int i = 0; i < c.dec_layers; ++i) {
+    std::string lp = m + "layers." + std::to_string(i) + ".";
+    DecLayerW& L = dec_layers_[i];
+    if (!up_cat({lp + "self_attn.q_proj.weight", lp + "self_attn.k_proj.weight", lp + "self_attn.v_proj.weight"}, h,
+                L.wqkv) ||
+        !up_bf16(lp + "self_attn.o_proj.weight", L.wo, (size_t)h * qd) ||
+        !up_bf16(lp + "mlp.down_proj.weight", L.wdown, (size_t)h * inter) ||
+        !up_f32(lp + "self_attn.q_norm.weight", L.qn) || !up_f32(lp + "self_attn.k_norm.weight", L.kn) ||
+        !up_f32(lp + "input_layernorm.weight", L.n1) || !up_f32(lp + "post_attention_layernorm.weight", L.n2))
+      return false;
+    const uint16_t* g = tensor_bf16(st, lp + "mlp.gate_proj.weight", (size_t)inter * h);
+    const uint16_t* u = tensor_bf16(st, lp + "mlp.up_proj.weight", (size_t)inter * h);
+    if (!g || !u) return false;
+    for (int r = 0; r < inter; ++r) {
+      memcpy(&gu[(size_t)(2 * r) * h], g + (size_t)r * h, h * 2);
+      memcpy(&gu[(size_t)(2 * r + 1) * h], u + (size_t)r * h, h * 2);
+    }
+    L.wgu = dalloc_t<__nv_bfloat16>(gu.size());
+    if (!L.wgu) return false;
+    CUDA_OK(cudaMemcpy(L.wgu, gu.data(), gu.size() * 2, cudaMemcpyHostToDevice), false);
+    // int8 decode weights, quantised on the device from the bf16 copies (decoder.rs:106-118)
+    struct Q {
+      const __nv_bfloat16* w;
+      int rows, cols;
+      int8_t** q;
+      float** s;
+    } qs[] = {{L.wqkv, qd + 2 * kvd, h, &L.qqkv, &L.sqkv},
+              {L.wo, h, qd, &L.qo, &L.so},
+              {L.wgu, 2 * inter, h, &L.qgu, &L.sgu},
+              {L.wdown, h, inter, &L.qdown, &L.sdown}};
+    for (auto& e : qs) {
+      *e.q = dalloc_t<int8_t>((size_t)e.rows * e.cols);
+      *e.s = dalloc_t<float>(e.rows);
+      if (!*e.q || !*e.s) return false;
+      quantize_rows_int8(e.w, e.rows, e.cols, trunc_quant, *e.q, *e.s, stream_);
+    }
+  }
+  if (!up_f32(m + "norm.weight", final_norm_)) return false;
+  // Tied lm_head unless thinker.lm_head.weight exists (decoder.rs:145-151).
+  if (st.has("thinker.lm_head.weight")) {
+    __nv_bfloat16* lm = nullptr;
+    int rows = c.classify_num > 0 ? c.classify_num : c.vocab_size;
+    if (!up_bf16("thinker.lm_head.weight", lm, (size_t)rows * h)) return false;
+    lm_bf16_ = lm;
+  } else {
+    lm_bf16_ = embed_;
+  }
+  {
+    int rows = c.classify_num > 0 ? c.classify_num : c.vocab_size;
+    lm_q_ = dalloc_t<int8_t>((size_t)rows * h);
+    lm_s_ = dalloc_t<float>(rows);
+    if (!lm_q_ || !lm_s_) return false;
+    quantize_rows_int8(lm_bf16_, rows, h, trunc_quant, lm_q_, lm_s_, stream_);
+  }
+
+  // ---- tables
+  std::vector<float> t1, t2;
+  build_hann(t1);
+  hann_ = dalloc_t<float>(t1.size());
+  CUDA_OK(cudaMemcpy(hann_, t1.data(), t1.size() * 4, cudaMemcpyHostToDevice), false);
+  build_dft_tables(t1, t2);  // B matrix [408][400]: rows 0..200 cos, 201..401 sin, rest 0
+  {
+    std::vector<float> B((size_t)408 * kNfft, 0.f);
+    memcpy(B.data(), t1.data(), t1.size() * 4);
+    memcpy(B.data() + (size_t)kNfreq * kNfft, t2.data(), t2.size() * 4);
+    dft_ = dalloc_t<float>(B.size());
+    CUDA_OK(cudaMemcpy(dft_, B.data(), B.size() * 4, cudaMemcpyHostToDevice), false);
+  }
+  build_mel_filters(t1);  // [128][201] -> padded [128][208]
+  {
+    std::vector<float> B((size_t)kMelBins * 208, 0.f);
+    for (int r = 0; r < kMelBins; ++r) memcpy(&B[(size_t)r * 208], &t1[(size_t)r * kNfreq], kNfreq * 4);
+    mel_filt_ = dalloc_t<float>(B.size());
+    CUDA_OK(cudaMemcpy(mel_filt_, B.data(), B.size() * 4, cudaMemcpyHostToDevice), false);
+  }
+  // Per-chunk sinusoidal PE (positions restart at 0 in every 100-frame chunk).
+  build_sinusoidal_pe(64, d, t1);
+  pe_ = dalloc_t<float>(t1.size());
+  CUDA_OK(cudaMemcpy(pe_, t1.data(), t1.size() * 4, cudaMemcpyHostToDevice), false);
+
+  // ---- decode state
+  if (!ensure_kv(4096)) return false;
+  CUDA_OK(cudaMallocHost(&hstate_, sizeof(StepState)), false);
+  if (!dx_.alloc(h) || !dqkv_.alloc(qd + 2 * kvd) || !dattn_.alloc(qd) || !dffn_.alloc(inter) ||
+      !dpart_.alloc((size_t)c.dec_heads * 16 * 130) || !dticket_.alloc(c.dec_kv_heads) || !dam_ticket_.alloc(1) ||
+      !dam_part_.alloc(4096) || !dstate_.alloc(1) || !dlogits_.alloc(c.vocab_size))
+    return false;
+  CUDA_OK(cudaMemset(dticket_.p, 0, c.dec_kv_heads * sizeof(int)), false);
+  CUDA_OK(cudaMemset(dam_ticket_.p, 0, sizeof(int)), false);
+  for (auto& L : dec_layers_) {
+    pn1_.push_back(L.n1);
+    pn2_.push_back(L.n2);
+    pqn_.push_back(L.qn);
+    pkn_.push_back(L.kn);
+  }
+  CUDA_OK(cudaStreamSynchronize(stream_), false);
+  CUDA_OK(cudaGetLastError(), false);
+  return true;
+}
+
+bool Engine::ensure_kv(int needed) {
+  const Config& c = cfg_;
+  if (needed <= max_seq_ && rope_cap_ >= max_seq_) return true;
+  int nm = max_seq_ > 0 ? max_seq_ : 2048;
+  while (nm < needed) nm *= 2;
+  size_t per = (size_t)c.dec_layers * c.dec_kv_heads * nm * 128;
+  float *nk = nullptr, *nv = nullptr;
+  CUDA_OK(cudaMalloc(&nk, per * 4), false);
+  CUDA_OK(cudaMalloc(&nv, per * 4), false);
+  if (kc_.p && kv_len_ > 0) {
+    // copy [layer][head][0..len) rows into the wider layout (decoder.rs:199-231)
+    size_t rows = (size_t)c.dec_layers * c.dec_kv_heads;
+    CUDA_OK(cudaMemcpy2DAsync(nk, (size_t)nm * 128 * 4, kc_.p, (size_t)max_seq_ * 128 * 4, (size_t)kv_len_ * 128 * 4,
+                              rows, cudaMemcpyDeviceToDevice, stream_),
+            false);
+    CUDA_OK(cudaMemcpy2DAsync(nv, (size_t)nm * 128 * 4, vc_.p, (size_t)max_seq_ * 128 * 4, (size_t)kv_len_ * 128 * 4,
+                              rows, cudaMemcpyDeviceToDevice, stream_),
+            false);
+    CUDA_OK(cudaStreamSynchronize(stream_), false);
+  }
+  kc_.release();
+  vc_.release();
+  kc_.p = nk;
+  kc_.n = per;
+  vc_.p = nv;
+  vc_.n = per;
+  max_seq_ = nm;
+  std::vector<float> rc, rs;
+  build_rope_tables(nm, 128, c.dec_rope_theta, rc, rs);
+  if (rope_cos_) {
+    cudaFree(rope_cos_);
+    cudaFree(rope_sin_);
+    allocs_.erase(std::remove(allocs_.begin(), allocs_.end(), (void*)rope_cos_), allocs_.end());
+    allocs_.erase(std::remove(allocs_.begin(), allocs_.end(), (void*)rope_sin_), allocs_.end());
+  }
+  rope_cos_ = dalloc_t<float>(rc.size());
+  rope_sin_ = dalloc_t<float>(rs.size());
+  if (!rope_cos_ || !rope_sin_) return false;
+  CUDA_OK(cudaMemcpy(rope_cos_, rc.data(), rc.size() * 4, cudaMemcpyHostToDevice), false);
+  CUDA_OK(cudaMemcpy(rope_sin_, rs.data(), rs.size() * 4, cudaMemcpyHostToDevice), false);
+  rope_cap_ = nm;
+  graph_ok_ = false;
+  return true;
+}
+
+// ---------------------------------------------------------------------------- mel
+int Engine::mel(const float* samples, int n, bool on_device) {
+  cudaSetDevice(device_);
+  int n_frames = n / kHop;  // (n + 400 - 400) / 160 + 1 - 1  (audio.rs:293-294)
+  if (n <= 0 || n_frames <= 0) {
+    set_error("mel_spectrogram: audio too short (" + std::to_string(n) + " samples)");
+    return 0;
+  }
+  const float* dsamp = samples;
+  if (!on_device) {
+    if (!samples_.alloc(n)) return 0;
+    CUDA_OK(cudaMemcpyAsync(samples_.p, samples, (size_t)n * 4, cudaMemcpyHostToDevice, stream_), 0);
+    dsamp = samples_.p;
+  }
+  if (!frames_.alloc((size_t)n_frames * kNfft) || !spec_.alloc((size_t)n_frames * 408) ||
+      !power_.alloc((size_t)n_frames * 208) || !mel_.alloc((size_t)n_frames * kMelBins) || !gmax_.alloc(1))
+    return 0;
+  cudaEventRecord(ev0_, stream_);
+  mel_frames(dsamp, n, n_frames, hann_, frames_.p, stream_);
+  GemmArgs g;
+  g.M = n_frames; g.N = 408; g.K = kNfft;
+  g.A = frames_.p; g.lda = kNfft; g.B = dft_; g.b_is_f32 = true; g.ldb = kNfft;
+  g.C = spec_.p; g.ldc = 408;
+  gemm_simt(g, stream_);
+  mel_power(spec_.p, 408, n_frames, power_.p, 208, stream_);
+  mel_reset_max(gmax_.p, stream_);
+  GemmArgs g2;
+  g2.M = n_frames; g2.N = kMelBins; g2.K = 208;
+  g2.A = power_.p; g2.lda = 208; g2.B = mel_filt_; g2.b_is_f32 = true; g2.ldb = 208;
+  g2.C = mel_.p; g2.ldc = kMelBins; g2.epi = EPI_LOG10_MAX; g2.gmax = gmax_.p;
+  gemm_simt(g2, stream_);
+  mel_normalize(mel_.p, n_frames, gmax_.p, stream_);
+  cudaEventRecord(ev1_, stream_);
+  CUDA_OK(cudaEventSynchronize(ev1_), 0);
+  float ms = 0;
+  cudaEventElapsedTime(&ms, ev0_, ev1_);
+  perf.mel_ms += ms;
+  CUDA_OK(cudaGetLastError(), 0);
+  return n_frames;
+}
+
+// ---------------------------------------------------------------------------- encoder
+int Engine::encode(const float* d_mel, int F) {
+  cudaSetDevice(device_);
+  const Config& c = cfg_;
+  const int d = c.enc_d_model, cs = c.enc_chunk_size, H = kConvHidden;
+  auto cw = [](int w) { return (w + 2 - 3) / 2 + 1; };
+  const int n_chunks = (F + cs - 1) / cs, full = F / cs;
+  struct Grp { int c0, nc, w; };
+  std::vector<Grp> groups;
+  if (full > 0) groups.push_back({0, full, cs});
+  if (full < n_chunks) groups.push_back({full, 1, F - full * cs});
+  int T = 0;
+  size_t max_cols = 0, max_a1 = 0, max_a2 = 0, max_a3 = 0;
+  for (auto& g : groups) {
+    int w1 = cw(g.w), w2 = cw(w1), w3 = cw(w2);
+    T += g.nc * w3;
+    max_a1 = std::max(max_a1, (size_t)g.nc * 64 * w1 * H);
+    max_a2 = std::max(max_a2, (size_t)g.nc * 32 * w2 * H);
+    max_a3 = std::max(max_a3, (size_t)g.nc * 16 * w3 * H);
+    max_cols = std::max(max_cols, (size_t)g.nc * 32 * w2 * 9 * H);
+  }
+  if (!act1_.alloc(max_a1) || !act2_.alloc(max_a2) || !act3_.alloc(max_a3) || !cols_.alloc(max_cols) ||
+      !x_enc_.alloc((size_t)T * d) || !xn_enc_.alloc((size_t)T * d) || !qkv_enc_.alloc((size_t)T * 3 * d) ||
+      !att_enc_.alloc((size_t)T * d) || !mid_enc_.alloc((size_t)T * std::max(c.enc_ffn_dim, d)) ||
+      !enc_.alloc((size_t)T * c.enc_output_dim))
+    return 0;
+  cudaEventRecord(ev0_, stream_);
+  int tok = 0;
+  for (auto& g : groups) {
+    int w1 = cw(g.w), w2 = cw(w1), w3 = cw(w2);
+    conv1_gelu(d_mel, F, g.c0 * cs, cs, g.nc, g.w, conv1_w, conv1_b, act1_.p, stream_);
+    im2col_s2(act1_.p, g.nc, 64, w1, cols_.p, false, stream_);
+    GemmArgs a;
+    a.M = g.nc * 32 * w2; a.N = H; a.K = 9 * H;
+    a.A = cols_.p; a.lda = 9 * H; a.B = conv2_w; a.ldb = 9 * H;
+    a.C = act2_.p; a.ldc = H; a.epi = EPI_BIAS_GELU; a.bias = conv2_b;
+    gemm(a, stream_);
+    im2col_s2(act2_.p, g.nc, 32, w2, cols_.p, true, stream_);
+    a.M = g.nc * w3 * 16; a.A = cols_.p; a.B = conv3_w; a.C = act3_.p; a.bias = conv3_b;
+    gemm(a, stream_);
+    GemmArgs o;
+    o.M = g.nc * w3; o.N = d; o.K = 16 * H;
+    o.A = act3_.p; o.lda = 16 * H; o.B = conv_out_w; o.ldb = 16 * H;
+    o.C = x_enc_.p + (size_t)tok * d; o.ldc = d;
+    gemm(o, stream_);
+    add_pe_rows(x_enc_.p + (size_t)tok * d, g.nc * w3, d, w3, pe_, stream_);
+    tok += g.nc * w3;
+  }
+  // attention windows (encoder.rs:292-298)
+  int tpc = cw(cw(cw(cs)));
+  int wts = tpc * (c.enc_n_window_infer / cs);
+  int n_win = (T + wts - 1) / wts;
+  std::vector<int> ws(n_win + 1);
+  for (int w = 0; w < n_win; ++w) ws[w] = w * wts;
+  ws[n_win] = T;
+  int max_win = 0;
+  for (int w = 0; w < n_win; ++w) max_win = std::max(max_win, ws[w + 1] - ws[w]);
+  if (!win_starts_.alloc(n_win + 1)) return 0;
+  CUDA_OK(cudaMemcpyAsync(win_starts_.p, ws.data(), ws.size() * 4, cudaMemcpyHostToDevice, stream_), 0);
+  const float scale = 1.0f / sqrtf((float)c.enc_head_dim);
+  for (auto& L : enc_layers_) {
+    layer_norm_rows(x_enc_.p, xn_enc_.p, T, d, L.ln1w, L.ln1b, 1e-5f, stream_);
+    GemmArgs a;
+    a.M = T; a.N = 3 * d; a.K = d; a.A = xn_enc_.p; a.lda = d; a.B = L.wqkv; a.ldb = d;
+    a.C = qkv_enc_.p; a.ldc = 3 * d; a.epi = EPI_BIAS; a.bias = L.bqkv;
+    gemm(a, stream_);
+    window_attention(qkv_enc_.p, att_enc_.p, T, d, c.enc_heads, win_starts_.p, n_win, max_win, scale, stream_);
+    GemmArgs o;
+    o.M = T; o.N = d; o.K = d; o.A = att_enc_.p; o.lda = d; o.B = L.wo; o.ldb = d;
+    o.C = x_enc_.p; o.ldc = d; o.epi = EPI_RESID; o.resid = x_enc_.p; o.ldr = d; o.bias = L.bo;
+    gemm(o, stream_);
+    layer_norm_rows(x_enc_.p, xn_enc_.p, T, d, L.ln2w, L.ln2b, 1e-5f, stream_);
+    GemmArgs f1;
+    f1.M = T; f1.N = c.enc_ffn_dim; f1.K = d; f1.A = xn_enc_.p; f1.lda = d; f1.B = L.w1; f1.ldb = d;
+    f1.C = mid_enc_.p; f1.ldc = c.enc_ffn_dim; f1.epi = EPI_BIAS_GELU; f1.bias = L.b1;
+    gemm(f1, stream_);
+    GemmArgs f2;
+    f2.M = T; f2.N = d; f2.K = c.enc_ffn_dim; f2.A = mid_enc_.p; f2.lda = c.enc_ffn_dim; f2.B = L.w2;
+    f2.ldb = c.enc_ffn_dim; f2.C = x_enc_.p; f2.ldc = d; f2.epi = EPI_RESID; f2.resid = x_enc_.p; f2.ldr = d;
+    f2.bias = L.b2;
+    gemm(f2, stream_);
+  }
+  layer_norm_rows(x_enc_.p, xn_enc_.p, T, d, ln_post_w, ln_post_b, 1e-5f, stream_);
+  GemmArgs p1;
+  p1.M = T; p1.N = d; p1.K = d; p1.A = xn_enc_.p; p1.lda = d; p1.B = proj1_w; p1.ldb = d;
+  p1.C = mid_enc_.p; p1.ldc = d; p1.epi = EPI_BIAS_GELU; p1.bias = proj1_b;
+  gemm(p1, stream_);
+  GemmArgs p2;
+  p2.M = T; p2.N = c.enc_output_dim; p2.K = d; p2.A = mid_enc_.p; p2.lda = d; p2.B = proj2_w; p2.ldb = d;
+  p2.C = enc_.p; p2.ldc = c.enc_output_dim; p2.epi = EPI_BIAS; p2.bias = proj2_b;
+  gemm(p2, stream_);
+  cudaEventRecord(ev1_, stream_);
+  CUDA_OK(cudaEventSynchronize(ev1_), 0);
+  float ms = 0;
+  cudaEventElapsedTime(&ms, ev0_, ev1_);
+  perf.enc_ms += ms;
+  CUDA_OK(cudaGetLastError(), 0);
+  return T;
+}
+
+// ---------------------------------------------------------------------------- prefill
+bool Engine::prefill_ids(const std::vector<int>& ids, const float* d_enc, int start_pos) {
+  cudaSetDevice(device_);
+  const int h = cfg_.dec_hidden, n = (int)ids.size();
+  if (n < 1) return false;
+  if (!ids_.alloc(n) || !px_.alloc((size_t)n * h)) return false;
+  CUDA_OK(cudaMemcpyAsync(ids_.p, ids.data(), n * 4, cudaMemcpyHostToDevice, stream_), false);
+  gather_embeds(ids_.p, n, embed_, d_enc, h, px_.p, stream_);
+  return run_prefill(n, start_pos);
+}
+
+bool Engine::prefill_rows(const float* rows, int n, int start_pos) {
+  cudaSetDevice(device_);
+  const int h = cfg_.dec_hidden;
+  if (n < 1 || !px_.alloc((size_t)n * h)) return false;
+  CUDA_OK(cudaMemcpyAsync(px_.p, rows, (size_t)n * h * 4, cudaMemcpyHostToDevice, stream_), false);
+  return run_prefill(n, start_pos);
+}
+
+// px_ holds all n prompt rows; rows [start_pos, n-1) are prefilled at positions
+// start_pos.. and row n-1 becomes the first decode input (transcribe.rs:171-185).
+bool Engine::run_prefill(int n, int start_pos) {
+  const Config& c = cfg_;
+  const int h = c.dec_hidden, qd = c.dec_heads * 128, kvd = c.dec_kv_heads * 128, inter = c.dec_intermediate;
+  const int S = n - 1 - start_pos;
+  if (S < 0) return false;
+  if (!ensure_kv(n + 1024)) return false;
+  if (!pxn_.alloc((size_t)std::max(S, 1) * h) || !pqkv_.alloc((size_t)std::max(S, 1) * (qd + 2 * kvd)) ||
+      !patt_.alloc((size_t)std::max(S, 1) * qd) || !pmid_.alloc((size_t)std::max(S, 1) * inter))
+    return false;
+  cudaEventRecord(ev0_, stream_);
+  float* x = px_.p + (size_t)start_pos * h;
+  const float scale = 1.0f / sqrtf(128.f);
+  for (int l = 0; l < c.dec_layers && S > 0; ++l) {
+    const DecLayerW& L = dec_layers_[l];
+    float* kc = kc_.p + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
+    float* vc = vc_.p + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
+    rms_norm_rows(x, pxn_.p, S, h, L.n1, c.dec_rms_norm_eps, stream_);
+    GemmArgs a;
+    a.M = S; a.N = qd + 2 * kvd; a.K = h; a.A = pxn_.p; a.lda = h; a.B = L.wqkv; a.ldb = h;
+    a.C = pqkv_.p; a.ldc = qd + 2 * kvd;
+    gemm(a, stream_);
+    prefill_qk_rope_kv(pqkv_.p, S, start_pos, c.dec_heads, c.dec_kv_heads, L.qn, L.kn, c.dec_rms_norm_eps, rope_cos_,
+                       rope_sin_, kc, vc, max_seq_, stream_);
+    prefill_attention(pqkv_.p, S, start_pos, c.dec_heads, c.dec_kv_heads, kc, vc, max_seq_, scale, patt_.p, stream_);
+    GemmArgs o;
+    o.M = S; o.N = h; o.K = qd; o.A = patt_.p; o.lda = qd; o.B = L.wo; o.ldb = qd;
+    o.C = x; o.ldc = h; o.epi = EPI_RESID; o.resid = x; o.ldr = h;
+    gemm(o, stream_);
+    rms_norm_rows(x, pxn_.p, S, h, L.n2, c.dec_rms_norm_eps, stream_);
+    GemmArgs g;
+    g.M = S; g.N = 2 * inter; g.K = h; g.A = pxn_.p; g.lda = h; g.B = L.wgu; g.ldb = h;
+    g.C = pmid_.p; g.ldc = inter; g.epi = EPI_SWIGLU;
+    gemm(g, stream_);
+    GemmArgs dn;
+    dn.M = S; dn.N = h; dn.K = inter; dn.A = pmid_.p; dn.lda = inter; dn.B = L.wdown; dn.ldb = inter;
+    dn.C = x; dn.ldc = h; dn.epi = EPI_RESID; dn.resid = x; dn.ldr = h;
+    gemm(dn, stream_);
+  }
+  kv_len_ = n - 1;
+  // first decode input: the last prompt row
+  CUDA_OK(cudaMemcpyAsync(dx_.p, px_.p + (size_t)(n - 1) * h, (size_t)h * 4, cudaMemcpyDeviceToDevice, stream_),
+          false);
+  hstate_->pos = n - 1;
+  hstate_->step = 0;
+  hstate_->cur_token = -1;
+  hstate_->forced_mode = 0;
+  CUDA_OK(cudaMemcpyAsync(dstate_.p, hstate_, sizeof(StepState), cudaMemcpyHostToDevice, stream_), false);
+  cudaEventRecord(ev1_, stream_);
+  CUDA_OK(cudaEventSynchronize(ev1_), false);
+  float ms = 0;
+  cudaEventElapsedTime(&ms, ev0_, ev1_);
+  perf.prefill_ms += ms;
+  CUDA_OK(cudaGetLastError(), false);
+  return true;
+}
+
+bool Engine::copy_prefill_hidden(std::vector<float>& out, int rows) {
+  out.resize((size_t)rows * cfg_.dec_hidden);
+  CUDA_OK(cudaMemcpy(out.data(), px_.p, out.size() * 4, cudaMemcpyDeviceToHost), false);
+  return true;
+}
+
+// ---------------------------------------------------------------------------- decode
+DecodeArgs Engine::dargs(const int* forced, float* logits) {
+  const Config& c = cfg_;
+  bool i8 = mode_ == DECODE_INT8;
+  pw_qkv_.clear(); pw_o_.clear(); pw_gu_.clear(); pw_down_.clear();
+  ps_qkv_.clear(); ps_o_.clear(); ps_gu_.clear(); ps_down_.clear();
+  for (auto& L : dec_layers_) {
+    pw_qkv_.push_back(i8 ? (const void*)L.qqkv : (const void*)L.wqkv);
+    pw_o_.push_back(i8 ? (const void*)L.qo : (const void*)L.wo);
+    pw_gu_.push_back(i8 ? (const void*)L.qgu : (const void*)L.wgu);
+    pw_down_.push_back(i8 ? (const void*)L.qdown : (const void*)L.wdown);
+    ps_qkv_.push_back(L.sqkv); ps_o_.push_back(L.so); ps_gu_.push_back(L.sgu); ps_down_.push_back(L.sdown);
+  }
+  DecodeArgs a{};
+  a.hidden = c.dec_hidden; a.q_heads = c.dec_heads; a.kv_heads = c.dec_kv_heads; a.inter = c.dec_intermediate;
+  a.vocab = c.classify_num > 0 ? c.classify_num : c.vocab_size; a.max_seq = max_seq_; a.eps = c.dec_rms_norm_eps;
+  a.int8 = i8;
+  a.w_qkv = pw_qkv_.data(); a.s_qkv = ps_qkv_.data(); a.w_o = pw_o_.data(); a.s_o = ps_o_.data();
+  a.w_gu = pw_gu_.data(); a.s_gu = ps_gu_.data(); a.w_down = pw_down_.data(); a.s_down = ps_down_.data();
+  a.n1 = pn1_.data(); a.n2 = pn2_.data(); a.qn = pqn_.data(); a.kn = pkn_.data();
+  a.lm_w = i8 ? (const void*)lm_q_ : (const void*)lm_bf16_; a.lm_s = lm_s_; a.final_norm = final_norm_;
+  a.embed = embed_; a.rope_cos = rope_cos_; a.rope_sin = rope_sin_;
+  a.k_cache = kc_.p; a.v_cache = vc_.p; a.layers = c.dec_layers;
+  a.x = dx_.p; a.qkv = dqkv_.p; a.attn = dattn_.p; a.ffn = dffn_.p; a.part = dpart_.p; a.ticket = dticket_.p;
+  a.am_ticket = dam_ticket_.p; a.am_part = dam_part_.p; a.st = dstate_.p; a.tokens = dtokens_.p;
+  a.forced = forced; a.logits = logits;
+  return a;
+}
+
+bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, const std::vector<int>* forced,
+                    std::vector<float>* logits) {
+  cudaSetDevice(device_);
+  out.clear();
+  if (max_steps <= 0) return true;
+  const int start_pos = hstate_->pos;
+  if (!ensure_kv(start_pos + max_steps + 1)) return false;
+  if (dtokens_.n < (size_t)max_steps) {
+    if (!dtokens_.alloc(std::max(max_steps, 2048))) return false;
+    graph_ok_ = false;
+  }
+  if (htokens_cap_ < max_steps) {
+    if (htokens_) cudaFreeHost(htokens_);
+    htokens_cap_ = std::max(max_steps, 2048);
+    CUDA_OK(cudaMallocHost(&htokens_, htokens_cap_ * sizeof(int)), false);
+  }
+  cudaEventRecord(ev0_, stream_);
+  const bool direct = forced || logits || !use_graph;
+  if (direct) {
+    // Teacher-forced / logits-recording path: plain launches, one step at a time.
+    if (forced) {
+      if (!dforced_.alloc(std::max<size_t>(forced->size(), 1))) return false;
+      CUDA_OK(cudaMemcpyAsync(dforced_.p, forced->data(), forced->size() * 4, cudaMemcpyHostToDevice, stream_), false);
+      hstate_->forced_mode = 1;
+      CUDA_OK(cudaMemcpyAsync(&dstate_.p->forced_mode, &hstate_->forced_mode, sizeof(int), cudaMemcpyHostToDevice,
+                              stream_),
+              false);
+    }
+    DecodeArgs a = dargs(forced ? dforced_.p : nullptr, logits ? dlogits_.p : nullptr);
+    const int V = a.vocab;
+    if (logits) logits->resize((size_t)max_steps * V);
+    for (int i = 0; i < max_steps; ++i) {
+      decode_step(a, stream_);
+      if (logits)
+        CUDA_OK(cudaMemcpyAsync(logits->data() + (size_t)i * V, dlogits_.p, (size_t)V * 4, cudaMemcpyDeviceToHost,
+                                stream_),
+                false);
+    }
+    CUDA_OK(cudaMemcpyAsync(htokens_, dtokens_.p, max_steps * 4, cudaMemcpyDeviceToHost, stream_), false);
+    CUDA_OK(cudaStreamSynchronize(stream_), false);
+    CUDA_OK(cudaGetLastError(), false);
+    out.assign(htokens_, htokens_ + max_steps);
+  } else {
+    if (!graph_ok_) {
+      if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
+      graph_exec_ = nullptr;
+      DecodeArgs a = dargs(nullptr, nullptr);
+      cudaGraph_t g;
+      CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);
+      decode_step(a, stream_);
+      CUDA_OK(cudaStreamEndCapture(stream_, &g), false);
+      CUDA_OK(cudaGraphInstantiate(&graph_exec_, g, 0), false);
+      cudaGraphDestroy(g);
+      graph_ok_ = true;
+    }
+    // Launch in chunks; after each chunk copy its ids back and look for EOS while the
+    // next chunk runs (transcribe.rs:194-226 stop rule).
+    const int chunk = 16;
+    int launched = 0, checked = 0;
+    bool stop = false;
+    std::vector<cudaEvent_t> evs;
+    auto launch_chunk = [&]() -> bool {
+      int c = std::min(chunk, max_steps - launched);
+      for (int i = 0; i < c; ++i) CUDA_OK(cudaGraphLaunch(graph_exec_, stream_), false);
+      CUDA_OK(cudaMemcpyAsync(htokens_ + launched, dtokens_.p + launched, c * 4, cudaMemcpyDeviceToHost, stream_),
+              false);
+      cudaEvent_t e;
+      cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+      cudaEventRecord(e, stream_);
+      evs.push_back(e);
+      launched += c;
+      return true;
+    };
+    if (!launch_chunk()) return false;
+    size_t ev_i = 0;
+    while (!stop) {
+      if (launched < max_steps && !launch_chunk()) return false;
+      CUDA_OK(cudaEventSynchronize(evs[ev_i]), false);
+      int upto = std::min(max_steps, checked + chunk);
+      for (int i = checked; i < upto; ++i) {
+        out.push_back(htokens_[i]);
+        if (stop_on_eos && (htokens_[i] == kTokEndOfText || htokens_[i] == kTokImEnd)) {
+          stop = true;
+          break;
+        }
+      }
+      checked = upto;
+      ++ev_i;
+      if (checked >= max_steps) stop = true;
+    }
+    CUDA_OK(cudaStreamSynchronize(stream_), false);
+    for (auto e : evs) cudaEventDestroy(e);
+    CUDA_OK(cudaGetLastError(), false);
+  }
+  // KV length after the steps the caller consumes (extra speculative steps are ignored).
+  kv_len_ = start_pos + (int)out.size();
+  hstate_->pos = kv_len_;
+  hstate_->forced_mode = 0;
+  cudaEventRecord(ev1_, stream_);
+  cudaEventSynchronize(ev1_);
+  float ms = 0;
+  cudaEventElapsedTime(&ms, ev0_, ev1_);
+  perf.decode_ms += ms;
+  perf.decode_steps += (int)out.size();
+  return true;
+}
+
+}  // namespace qasr

@@ -1,0 +1,135 @@
+// Device-resident Qwen3-ASR model and its forward stages on one GPU.
+#pragma once
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.h"
+#include "host.h"
+#include "kernels.h"
+
+namespace qasr {
+
+struct EncLayerW {
+  __nv_bfloat16* wqkv;  // [3d][d] (q | k | v)
+  float* bqkv;          // [3d]
+  __nv_bfloat16* wo;
+  float* bo;
+  float *ln1w, *ln1b, *ln2w, *ln2b;
+  __nv_bfloat16 *w1, *w2;
+  float *b1, *b2;
+};
+
+struct DecLayerW {
+  __nv_bfloat16* wqkv;  // [q + 2kv][h]
+  __nv_bfloat16* wo;    // [h][q]
+  __nv_bfloat16* wgu;   // [2*inter][h], rows interleaved gate0, up0, gate1, ... (decoder.rs:91-104)
+  __nv_bfloat16* wdown; // [h][inter]
+  int8_t *qqkv, *qo, *qgu, *qdown;
+  float *sqkv, *so, *sgu, *sdown;
+  float *qn, *kn, *n1, *n2;
+};
+
+enum DecodeMode { DECODE_INT8 = 0, DECODE_BF16 = 1 };
+
+// Per-stage timings of the last call, in milliseconds (CUDA events).
+struct StagePerf {
+  double mel_ms = 0, enc_ms = 0, prefill_ms = 0, decode_ms = 0;
+  int decode_steps = 0;
+};
+
+class Engine {
+ public:
+  ~Engine();
+  bool load(const std::string& dir, int device, bool trunc_quant);
+  const Config& cfg() const { return cfg_; }
+  int device() const { return device_; }
+  cudaStream_t stream() const { return stream_; }
+
+  // Stage 1: samples (host or device) -> mel [F][128] in device memory. Returns F (0 = too short).
+  int mel(const float* samples, int n, bool samples_on_device);
+  // Stage 2: mel (device, [F][128]) -> encoder output rows [T][dec_hidden] in enc_out(). Returns T.
+  int encode(const float* d_mel, int n_frames);
+  float* mel_buf() { return mel_.p; }
+  float* enc_out() { return enc_.p; }
+
+  // Prompt rows: ids >= 0 are token embeddings, id = -(r+1) is encoder row r of `enc`.
+  // Runs decoder_prefill over rows[0, n-1) starting at KV position `start_pos` (rows
+  // before start_pos are not recomputed), then prepares the first decode step from the
+  // last row. `enc` may be null when no id references it.
+  bool prefill_ids(const std::vector<int>& ids, const float* d_enc, int start_pos);
+  // Same with prompt embeddings already materialised on the host (streaming LCP path).
+  bool prefill_rows(const float* h_rows, int n_rows, int start_pos);
+  // Greedy decode: runs up to max_steps decoder_forward steps from the prepared state and
+  // returns the produced ids. With stop_on_eos the loop stops after the first
+  // 151643/151645 (inclusive). forced (teacher forcing) gives the input id of step i+1.
+  bool decode(int max_steps, bool stop_on_eos, std::vector<int>& out, const std::vector<int>* forced = nullptr,
+              std::vector<float>* logits = nullptr);
+  void set_decode_mode(DecodeMode m) { mode_ = m; graph_ok_ = false; }
+  DecodeMode decode_mode() const { return mode_; }
+  StagePerf perf;
+  bool use_graph = true;
+
+  // Debug: final hidden of prefill rows (after the last layer, before final norm).
+  bool copy_prefill_hidden(std::vector<float>& out, int rows);
+
+ private:
+  Config cfg_;
+  int device_ = 0;
+  cudaStream_t stream_ = nullptr;
+  DecodeMode mode_ = DECODE_INT8;
+  std::vector<void*> allocs_;
+  void* dalloc(size_t bytes);
+  template <typename T>
+  T* dalloc_t(size_t n) { return (T*)dalloc(n * sizeof(T)); }
+
+  // encoder weights
+  float *conv1_w = nullptr, *conv1_b = nullptr;
+  __nv_bfloat16 *conv2_w = nullptr, *conv3_w = nullptr, *conv_out_w = nullptr;
+  float *conv2_b = nullptr, *conv3_b = nullptr;
+  std::vector<EncLayerW> enc_layers_;
+  float *ln_post_w = nullptr, *ln_post_b = nullptr, *proj1_b = nullptr, *proj2_b = nullptr;
+  __nv_bfloat16 *proj1_w = nullptr, *proj2_w = nullptr;
+  // decoder weights
+  __nv_bfloat16* embed_ = nullptr;  // [vocab][h]
+  std::vector<DecLayerW> dec_layers_;
+  float* final_norm_ = nullptr;
+  const __nv_bfloat16* lm_bf16_ = nullptr;
+  int8_t* lm_q_ = nullptr;
+  float* lm_s_ = nullptr;
+  // tables
+  float *hann_ = nullptr, *dft_ = nullptr, *mel_filt_ = nullptr, *rope_cos_ = nullptr, *rope_sin_ = nullptr;
+  float* pe_ = nullptr;
+  int rope_cap_ = 0;
+
+  // activations (grow-only)
+  DevBuf<float> samples_, frames_, spec_, power_, mel_;
+  DevBuf<int> gmax_;
+  DevBuf<float> act1_, act2_, act3_, cols_, x_enc_, xn_enc_, qkv_enc_, att_enc_, mid_enc_, enc_;
+  DevBuf<int> win_starts_;
+  DevBuf<float> px_, pxn_, pqkv_, patt_, pmid_;
+  DevBuf<int> ids_;
+  // KV cache [layers][kv][max_seq][128] f32
+  DevBuf<float> kc_, vc_;
+  int max_seq_ = 0;
+  int kv_len_ = 0;
+  bool ensure_kv(int needed);
+  // decode scratch
+  DevBuf<float> dx_, dqkv_, dattn_, dffn_, dpart_, dlogits_;
+  DevBuf<int> dticket_, dam_ticket_, dtokens_, dforced_;
+  DevBuf<unsigned long long> dam_part_;
+  DevBuf<StepState> dstate_;
+  StepState* hstate_ = nullptr;  // pinned
+  int* htokens_ = nullptr;       // pinned
+  int htokens_cap_ = 0;
+  // decode graph
+  cudaGraphExec_t graph_exec_ = nullptr;
+  bool graph_ok_ = false;
+  std::vector<const void*> pw_qkv_, pw_o_, pw_gu_, pw_down_;
+  std::vector<const float*> ps_qkv_, ps_o_, ps_gu_, ps_down_, pn1_, pn2_, pqn_, pkn_;
+  DecodeArgs dargs(const int* forced, float* logits);
+  bool run_prefill(int n_rows, int start_pos);  // rows already in px_
+  cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
+};
+
+}  // namespace qasr

@@ -1,0 +1,137 @@
+// Launchers for the engine's CUDA kernels (sm_100a). All launches are asynchronous on
+// the given stream; pointer arguments are device pointers unless stated otherwise.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+
+namespace qasr {
+
+// ---------------------------------------------------------------- GEMM
+// C[m][n] (ldc) = epilogue( sum_k A[m][k] * B[n][k] ), A f32 [M][lda], B bf16 or f32
+// [N][ldb]. K must be a multiple of 16 and rows of A/B must be 16-byte aligned.
+enum GemmEpi : int {
+  EPI_STORE = 0,       // v = acc
+  EPI_BIAS = 1,        // v = acc + bias[n]
+  EPI_BIAS_GELU = 2,   // v = gelu_tanh(acc + bias[n])
+  EPI_RESID = 3,       // v = (resid[m][n] + bias[n]?) + acc   (resid may alias C)
+  EPI_SWIGLU = 4,      // columns (2j, 2j+1) = (gate, up) -> C[m][j] = silu(gate) * up
+  EPI_LOG10_MAX = 5,   // v = log10(max(acc, 1e-10)); atomic max into *gmax (ordered int)
+};
+
+struct GemmArgs {
+  int M = 0, N = 0, K = 0;
+  const float* A = nullptr;
+  int lda = 0;
+  const void* B = nullptr;
+  bool b_is_f32 = false;
+  int ldb = 0;
+  float* C = nullptr;
+  int ldc = 0;
+  int epi = EPI_STORE;
+  const float* bias = nullptr;   // [N] (EPI_BIAS, EPI_BIAS_GELU, optional for EPI_RESID)
+  const float* resid = nullptr;  // [M][ldr] for EPI_RESID
+  int ldr = 0;
+  int* gmax = nullptr;           // EPI_LOG10_MAX
+};
+void gemm(const GemmArgs& a, cudaStream_t s);
+// Plain SIMT FP32 reference GEMM (kept for parity tests of the tensor-core path).
+void gemm_simt(const GemmArgs& a, cudaStream_t s);
+
+// ---------------------------------------------------------------- mel front end
+// samples [n] -> windowed frames [F][400] (reflect padding, periodic Hann).
+void mel_frames(const float* samples, int n, int n_frames, const float* hann, float* frames, cudaStream_t s);
+// spec [F][ld_spec] (re 0..200, im 201..401) -> power [F][ld_pow] (cols >= 201 zeroed)
+void mel_power(const float* spec, int ld_spec, int n_frames, float* power, int ld_pow, cudaStream_t s);
+void mel_reset_max(int* gmax, cudaStream_t s);
+// logmel [F][128] in place: (max(v, gmax - 8) + 4) / 4
+void mel_normalize(float* logmel, int n_frames, const int* gmax, cudaStream_t s);
+
+// ---------------------------------------------------------------- encoder
+// conv2d1 (1 -> 480, 3x3 s2 p1) + bias + GELU on `n_chunks` chunks of width w taken from
+// mel [F][128] starting at frame f0 + c*cw; output channels-last [c][64][w1][480].
+void conv1_gelu(const float* mel, int n_frames, int f0, int cw, int n_chunks, int w,
+                const float* w1, const float* b1, float* out, cudaStream_t s);
+// im2col for a 3x3 s2 p1 conv over channels-last input [c][H][W][480]; rows ordered
+// (c, oh, ow) or, with col_major_rows, (c, ow, oh); columns k = (ki*3+kj)*480 + ic.
+void im2col_s2(const float* in, int n_chunks, int H, int W, float* cols, bool col_major_rows,
+               cudaStream_t s);
+void add_pe_rows(float* x, int rows, int d, int period, const float* pe, cudaStream_t s);
+void layer_norm_rows(const float* x, float* y, int rows, int d, const float* w, const float* b, float eps,
+                     cudaStream_t s);
+// Windowed bidirectional attention; qkv [T][3d] (q | k | v), out [T][d].
+void window_attention(const float* qkv, float* out, int T, int d, int n_heads, const int* win_starts,
+                      int n_windows, int max_win, float scale, cudaStream_t s);
+
+// ---------------------------------------------------------------- decoder
+void rms_norm_rows(const float* x, float* y, int rows, int d, const float* w, float eps, cudaStream_t s);
+// Prefill: per-head RMSNorm + NeoX RoPE of q/k rows in qkv [S][q_dim + 2*kv_dim] at
+// positions start..start+S-1, then writes k/v into the f32 cache
+// [kv_heads][max_seq][128] of this layer.
+void prefill_qk_rope_kv(float* qkv, int S, int start, int n_heads, int n_kv, const float* qn, const float* kn,
+                        float eps, const float* rope_cos, const float* rope_sin, float* kc, float* vc,
+                        int max_seq, cudaStream_t s);
+// Causal GQA attention of S queries at positions start.. over the cache; out [S][n_heads*128].
+void prefill_attention(const float* qkv, int S, int start, int n_heads, int n_kv, const float* kc,
+                       const float* vc, int max_seq, float scale, float* out, cudaStream_t s);
+// Gathers prompt rows: row r = ids[r] >= 0 ? embed[ids[r]] : enc[-ids[r]-1].
+void gather_embeds(const int* ids, int rows, const __nv_bfloat16* embed, const float* enc, int d, float* out,
+                   cudaStream_t s);
+// Per-row symmetric int8 quantisation of a bf16 [rows][cols] matrix (load time).
+void quantize_rows_int8(const __nv_bfloat16* w, int rows, int cols, bool truncate, int8_t* q, float* scale,
+                        cudaStream_t s);
+
+// Decode-step state living in device memory so that one CUDA graph serves every step.
+struct StepState {
+  int pos;         // KV position of the token being computed
+  int step;        // index into tokens[]
+  int cur_token;   // input token id of this step; < 0: x already holds the input row
+  int forced_mode; // teacher forcing: input token of step i+1 comes from forced[i]
+};
+
+struct DecodeArgs {
+  // model shape
+  int hidden, q_heads, kv_heads, inter, vocab, max_seq;
+  float eps;
+  bool int8;
+  // per-layer weights (arrays of device pointers, host-side)
+  const void* const* w_qkv;    // [layers] int8 or bf16 [q+2kv][hidden]
+  const float* const* s_qkv;   // [layers] int8 scales
+  const void* const* w_o;
+  const float* const* s_o;
+  const void* const* w_gu;     // interleaved gate/up rows
+  const float* const* s_gu;
+  const void* const* w_down;
+  const float* const* s_down;
+  const float* const* n1;
+  const float* const* n2;
+  const float* const* qn;
+  const float* const* kn;
+  const void* lm_w;            // int8 or bf16 [vocab][hidden]
+  const float* lm_s;
+  const float* final_norm;
+  const __nv_bfloat16* embed;
+  const float* rope_cos;
+  const float* rope_sin;
+  float* k_cache;              // [layers][kv][max_seq][128]
+  float* v_cache;
+  int layers;
+  // scratch
+  float* x;        // [hidden] residual stream
+  float* qkv;      // [q_dim + 2 kv_dim]
+  float* attn;     // [q_dim]
+  float* ffn;      // [inter]
+  float* part;     // attention split partials
+  int* ticket;     // [kv_heads] arrival counters (zero at rest)
+  float* amax_part;
+  int* am_ticket;  // [1]
+  unsigned long long* am_part;  // argmax partials
+  StepState* st;
+  int* tokens;     // [max tokens] output ids
+  const int* forced;  // teacher-forced ids or nullptr
+  float* logits;   // optional [vocab] f32 logits of the last step (debug)
+};
+// Enqueues one full decode step (embedding -> layers -> lm_head argmax).
+void decode_step(const DecodeArgs& a, cudaStream_t s);
+
+}  // namespace qasr

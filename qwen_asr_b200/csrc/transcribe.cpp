@@ -1,0 +1,398 @@
+// Transcription orchestration (crates/qwen-asr/src/transcribe.rs), host side. All model
+// math runs on the GPU through Engine; this file only holds the control flow, prompt
+// layout and text handling, which must follow the reference exactly.
+#include "transcribe.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cstring>
+
+namespace qasr {
+
+// transcribe.rs:13-23
+static const int kPrefixHead[] = {151644, 8948, 198};
+static const int kPrefixTail[] = {151645, 198, 151644, 872, 198, 151669};
+static const int kSuffixBase[] = {151670, 151645, 198, 151644, 77091, 198};
+static const int kDegenMaxPeriod = 6, kDegenMinRepeats = 4, kStaleChunks = 4, kResetInterval = 45;
+static const size_t kResetCarry = 24, kMaxEncWindows = 4;
+
+static double now_ms() {
+  using namespace std::chrono;
+  return duration<double, std::milli>(steady_clock::now().time_since_epoch()).count();
+}
+
+void StreamState::reset() {
+  bool keep = prompt_prepared;
+  *this = StreamState();
+  prompt_prepared = keep;
+}
+
+bool Ctx::load(const std::string& dir, int device) {
+  model_dir = dir;
+  const char* q = getenv("QASR_WEIGHT_QUANT");
+  bool trunc = !(q && std::string(q) == "round");
+  if (!eng.load(dir, device, trunc)) return false;
+  if (!tok.load(dir)) return false;
+  return true;
+}
+
+void Ctx::reset_perf() {
+  perf_total_ms = perf_audio_ms = perf_encode_ms = perf_decode_ms = 0;
+  perf_text_tokens = 0;
+  eng.perf = StagePerf();
+}
+
+bool Ctx::set_force_language(const std::string& lang) {
+  if (lang.empty()) {
+    force_language.clear();
+    prompt_tokens_ready = false;
+    return true;
+  }
+  std::string n = normalize_language(lang);
+  if (n.empty()) return false;
+  force_language = n;
+  prompt_tokens_ready = false;
+  return true;
+}
+
+bool Ctx::prepare_prompt_tokens() {  // context.rs:197-231
+  if (prompt_tokens_ready) return true;
+  has_prompt_tokens = has_force_tokens = false;
+  prompt_tokens.clear();
+  force_prompt_tokens.clear();
+  if (!prompt.empty()) {
+    if (!tok.encode(prompt, prompt_tokens)) {
+      set_error("qwen: failed to encode --prompt text");
+      return false;
+    }
+    has_prompt_tokens = true;
+  }
+  if (!force_language.empty()) {
+    if (!tok.encode("language " + force_language, force_prompt_tokens)) {
+      set_error("qwen: failed to encode --language text");
+      return false;
+    }
+    force_prompt_tokens.push_back(kTokAsrText);
+    has_force_tokens = true;
+  }
+  prompt_tokens_ready = true;
+  return true;
+}
+
+bool Ctx::encode_window(const float* samples, size_t n, std::vector<float>& enc, int& seq) {
+  int F = eng.mel(samples, (int)n, false);
+  if (F <= 0) return false;
+  seq = eng.encode(eng.mel_buf(), F);
+  if (seq <= 0) return false;
+  enc.resize((size_t)seq * eng.cfg().dec_hidden);
+  return cudaMemcpy(enc.data(), eng.enc_out(), enc.size() * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+}
+
+// transcribe.rs:63-247
+bool Ctx::transcribe_segment(const float* samples, size_t n, const std::vector<int>* past, std::string& text,
+                             int& n_text) {
+  double t0 = now_ms();
+  n_text = 0;
+  StagePerf before = eng.perf;
+  int F = eng.mel(samples, (int)n, false);
+  if (F <= 0) return false;
+  int T = eng.encode(eng.mel_buf(), F);
+  if (T <= 0) return false;
+  if (!prepare_prompt_tokens()) return false;
+  std::vector<int> ids;
+  ids.insert(ids.end(), std::begin(kPrefixHead), std::end(kPrefixHead));
+  if (has_prompt_tokens) ids.insert(ids.end(), prompt_tokens.begin(), prompt_tokens.end());
+  ids.insert(ids.end(), std::begin(kPrefixTail), std::end(kPrefixTail));
+  for (int i = 0; i < T; ++i) ids.push_back(-(i + 1));
+  ids.insert(ids.end(), std::begin(kSuffixBase), std::end(kSuffixBase));
+  if (has_force_tokens) ids.insert(ids.end(), force_prompt_tokens.begin(), force_prompt_tokens.end());
+  bool has_past = past && !past->empty();
+  if (has_past) {
+    ids.insert(ids.end(), past->begin(), past->end());
+    ids.push_back(kTokAsrText);
+  }
+  if (!eng.prefill_ids(ids, eng.enc_out(), 0)) return false;
+  std::vector<int> gen;
+  int limit = force_n_tokens > 0 ? force_n_tokens : 2048;
+  if (!eng.decode(limit, force_n_tokens <= 0, gen)) return false;
+  bool past_asr = has_force_tokens || has_past;
+  std::string bytes;
+  int processed = 0;
+  for (int t : gen) {
+    if (processed >= limit) break;
+    ++processed;
+    if (force_n_tokens <= 0 && (t == kTokEndOfText || t == kTokImEnd)) break;
+    if (t == kTokAsrText) {
+      past_asr = true;
+    } else if (past_asr) {
+      bytes += tok.decode_bytes(t);
+      ++n_text;
+    }
+  }
+  last_tokens.push_back(gen);
+  text = rust_trim(utf8_lossy(bytes));
+  perf_total_ms += now_ms() - t0;
+  perf_text_tokens += n_text;
+  perf_encode_ms += (eng.perf.mel_ms - before.mel_ms) + (eng.perf.enc_ms - before.enc_ms);
+  perf_decode_ms += (eng.perf.prefill_ms - before.prefill_ms) + (eng.perf.decode_ms - before.decode_ms);
+  return true;
+}
+
+// transcribe.rs:297-426
+bool Ctx::transcribe_audio(const std::vector<float>& in, std::string& result) {
+  reset_perf();
+  last_tokens.clear();
+  perf_audio_ms = 1000.0 * (double)in.size() / kSampleRate;
+  std::vector<float> audio = skip_silence ? compact_silence(in) : in;
+  if (!prepare_prompt_tokens()) return false;
+  std::vector<size_t> splits = split_points(audio, segment_sec, search_sec);
+  result.clear();
+  if (splits.size() == 1) {
+    int nt;
+    return transcribe_segment(audio.data(), audio.size(), nullptr, result, nt);
+  }
+  const size_t min_samples = kSampleRate / 2;
+  for (size_t s = 0; s < splits.size(); ++s) {
+    size_t a = splits[s], b = s + 1 < splits.size() ? splits[s + 1] : audio.size();
+    std::vector<float> seg(audio.begin() + a, audio.begin() + b);
+    if (seg.size() < min_samples) seg.resize(min_samples, 0.f);
+    std::vector<int> past;
+    bool use_past = false;
+    if (past_text_conditioning && !result.empty()) use_past = tok.encode(result, past);
+    std::string st;
+    int nt;
+    if (!transcribe_segment(seg.data(), seg.size(), use_past ? &past : nullptr, st, nt)) continue;
+    if (st.empty()) continue;
+    if (!result.empty() && should_insert_boundary_space((uint8_t)result.back(), (uint8_t)st[0])) result += ' ';
+    result += st;
+  }
+  return true;
+}
+
+// Streaming tail-repetition detector (transcribe.rs:36-55).
+static std::pair<size_t, size_t> tail_repeat_blocks(const std::vector<int>& t, size_t max_period) {
+  size_t n = t.size();
+  if (n < 2) return {1, 0};
+  size_t cap = std::min(n / 2, max_period > 0 ? max_period : n / 2);
+  size_t best_reps = 1, best_p = 0;
+  for (size_t p = 1; p <= cap; ++p) {
+    size_t reps = 1;
+    while ((reps + 1) * p <= n) {
+      bool eq = std::equal(t.begin() + (n - (reps + 1) * p), t.begin() + (n - reps * p), t.begin() + (n - reps * p));
+      if (!eq) break;
+      ++reps;
+    }
+    if (reps > best_reps) {
+      best_reps = reps;
+      best_p = p;
+    }
+  }
+  return {best_reps, best_p};
+}
+
+// stream_push_audio (transcribe.rs:902-1304). `samples` is the full audio so far.
+bool Ctx::stream_push_audio(const std::vector<float>& samples, StreamState& st, bool finalize, std::string& delta) {
+  delta.clear();
+  const size_t chunk_samples = (size_t)(stream_chunk_sec * (float)kSampleRate);
+  const int rollback = stream_rollback, unfixed = stream_unfixed_chunks;
+  const int max_new = stream_max_new_tokens > 0 ? stream_max_new_tokens : 32;
+  const int dim = eng.cfg().dec_hidden;
+  if (!st.prompt_prepared) {
+    if (!prepare_prompt_tokens()) return false;
+    st.prompt_prepared = true;
+  }
+  size_t available = samples.size() > st.audio_cursor ? samples.size() - st.audio_cursor : 0;
+  if (available < chunk_samples && !finalize) return true;
+  if (available == 0) return true;
+  const size_t enc_window_frames = (size_t)std::min(std::max(eng.cfg().enc_n_window_infer, 100), 800);
+  const size_t enc_window_samples = enc_window_frames * kHop;
+
+  while (st.audio_cursor < samples.size()) {
+    size_t remaining = samples.size() - st.audio_cursor;
+    if (remaining < chunk_samples && !finalize) break;
+    double chunk_t0 = now_ms();
+    st.audio_cursor = std::min(st.audio_cursor + chunk_samples, samples.size());
+    bool is_final = finalize && st.audio_cursor >= samples.size();
+    StagePerf before = eng.perf;
+
+    size_t full_end = (st.audio_cursor / enc_window_samples) * enc_window_samples;
+    while ((st.enc_cache_base_windows + st.enc_cache.size()) * enc_window_samples < full_end) {
+      size_t ws = (st.enc_cache_base_windows + st.enc_cache.size()) * enc_window_samples;
+      StreamState::EncWindow w;
+      if (!encode_window(samples.data() + ws, enc_window_samples, w.enc, w.seq_len)) return false;
+      st.enc_cached_seq_total += w.seq_len;
+      st.enc_cache.push_back(std::move(w));
+    }
+    size_t enc_update_threshold = chunk_samples * 2;
+    size_t partial_age = st.audio_cursor > st.last_partial_cursor ? st.audio_cursor - st.last_partial_cursor : 0;
+    bool need_encode = st.last_partial_cursor == 0 || partial_age >= enc_update_threshold || is_final;
+    int partial_seq = 0;
+    const std::vector<float>* partial_enc = nullptr;
+    std::vector<float> fresh;
+    if (need_encode && full_end < st.audio_cursor) {
+      int seq = 0;
+      if (encode_window(samples.data() + full_end, st.audio_cursor - full_end, fresh, seq)) {
+        partial_seq = seq;
+        st.last_partial_cursor = st.audio_cursor;
+        st.last_partial_enc = fresh;
+        st.last_partial_seq = seq;
+        partial_enc = &st.last_partial_enc;
+      } else {
+        partial_seq = st.last_partial_seq;
+        partial_enc = &st.last_partial_enc;
+      }
+    } else if (full_end < st.audio_cursor) {
+      partial_seq = st.last_partial_seq;
+      partial_enc = &st.last_partial_enc;
+    }
+    size_t enc_seq_len = st.enc_cached_seq_total + partial_seq;
+    if (enc_seq_len == 0) {
+      st.chunk_idx += 1;
+      return true;  // the reference returns here (transcribe.rs:1004-1007)
+    }
+    std::vector<float> enc_output(enc_seq_len * dim);
+    size_t off = 0;
+    for (auto& w : st.enc_cache) {
+      memcpy(enc_output.data() + off * dim, w.enc.data(), (size_t)w.seq_len * dim * 4);
+      off += w.seq_len;
+    }
+    if (partial_seq > 0) memcpy(enc_output.data() + off * dim, partial_enc->data(), (size_t)partial_seq * dim * 4);
+
+    size_t n_prefix = 0;
+    if (past_text_conditioning && st.chunk_idx >= unfixed && !st.raw_tokens.empty())
+      n_prefix = (size_t)std::max((int)st.raw_tokens.size() - rollback, 0);
+
+    std::vector<int> ids;
+    ids.insert(ids.end(), std::begin(kPrefixHead), std::end(kPrefixHead));
+    if (has_prompt_tokens) ids.insert(ids.end(), prompt_tokens.begin(), prompt_tokens.end());
+    ids.insert(ids.end(), std::begin(kPrefixTail), std::end(kPrefixTail));
+    for (size_t i = 0; i < enc_seq_len; ++i) ids.push_back(-(int)(i + 1));
+    ids.insert(ids.end(), std::begin(kSuffixBase), std::end(kSuffixBase));
+    if (has_force_tokens) ids.insert(ids.end(), force_prompt_tokens.begin(), force_prompt_tokens.end());
+    for (size_t i = 0; i < n_prefix; ++i) ids.push_back(st.raw_tokens[i]);
+    const size_t total_seq = ids.size(), prefill_len = total_seq - 1;
+
+    // LCP reuse: rows equal as f32 vectors (transcribe.rs:1095-1106). Token rows compare
+    // by id; encoder rows compare element-wise; a token row never equals an encoder row.
+    size_t reused = 0;
+    if (!st.prev_ids.empty() && st.prev_prefill_len > 0) {
+      size_t cmp = std::min(prefill_len, st.prev_prefill_len);
+      while (reused < cmp) {
+        int a = st.prev_ids[reused], b = ids[reused];
+        bool eq;
+        if (a >= 0 || b >= 0) {
+          eq = a == b;
+        } else {
+          const float* ra = st.prev_enc.data() + (size_t)(-a - 1) * dim;
+          const float* rb = enc_output.data() + (size_t)(-b - 1) * dim;
+          eq = true;
+          for (int k = 0; k < dim; ++k)
+            if (!(ra[k] == rb[k])) {
+              eq = false;
+              break;
+            }
+        }
+        if (!eq) break;
+        ++reused;
+      }
+    }
+    // Device copy of the assembled encoder rows for the prompt gather.
+    DevBuf<float> denc;
+    if (!denc.alloc(enc_output.size())) return false;
+    if (cudaMemcpy(denc.p, enc_output.data(), enc_output.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return false;
+    if (!eng.prefill_ids(ids, denc.p, (int)reused)) return false;
+    st.prev_ids.assign(ids.begin(), ids.begin() + prefill_len);
+    st.prev_enc = enc_output;
+    st.prev_prefill_len = prefill_len;
+
+    std::vector<int> gen;
+    if (!eng.decode(max_new, true, gen)) return false;
+    last_tokens.push_back(gen);
+    std::vector<int> chunk_tokens;
+    {
+      int token_i = 0, n_generated = 0;
+      while (n_generated < max_new && token_i < (int)gen.size()) {
+        ++n_generated;
+        int t = gen[token_i++];
+        if (t == kTokEndOfText || t == kTokImEnd) break;
+        chunk_tokens.push_back(t);
+      }
+    }
+
+    bool speech_ended = chunk_tokens.empty() && !st.raw_tokens.empty() && st.chunk_idx >= unfixed;
+    auto text_start_of = [&](const std::vector<int>& rt) -> size_t {
+      if (has_force_tokens) return 0;
+      auto it = std::find(rt.begin(), rt.end(), kTokAsrText);
+      return it == rt.end() ? 0 : (size_t)(it - rt.begin()) + 1;
+    };
+    auto emit = [&](const std::vector<int>& cand, size_t from, size_t to) {
+      for (size_t i = from; i < to; ++i) {
+        if (i < cand.size()) {
+          if (i >= st.stable_text_tokens.size()) st.stable_text_tokens.push_back(cand[i]);
+          const std::string& pb = tok.decode_bytes(cand[i]);
+          perf_text_tokens += 1;
+          st.result_bytes += pb;
+          delta += pb;
+        }
+      }
+    };
+    if (speech_ended) {
+      size_t ts = text_start_of(st.raw_tokens);
+      std::vector<int> cand(st.raw_tokens.begin() + ts, st.raw_tokens.end());
+      emit(cand, st.stable_text_tokens.size(), cand.size());
+    }
+    st.raw_tokens.resize(std::min(st.raw_tokens.size(), n_prefix));
+    st.raw_tokens.insert(st.raw_tokens.end(), chunk_tokens.begin(), chunk_tokens.end());
+
+    auto reset_context = [&]() {
+      size_t carry = std::min(st.stable_text_tokens.size(), kResetCarry);
+      size_t cs = st.stable_text_tokens.size() - carry;
+      st.raw_tokens.clear();
+      if (carry > 0) {
+        st.raw_tokens.push_back(kTokAsrText);
+        st.raw_tokens.insert(st.raw_tokens.end(), st.stable_text_tokens.begin() + cs, st.stable_text_tokens.end());
+      }
+      st.prev_ids.clear();
+      st.prev_enc.clear();
+      st.prev_prefill_len = 0;
+      st.stale_count = 0;
+      st.prev_tail_snapshot.clear();
+      if (st.enc_cache.size() >= kMaxEncWindows) {
+        st.enc_cache_base_windows += st.enc_cache.size();
+        st.enc_cache.clear();
+        st.enc_cached_seq_total = 0;
+      }
+    };
+    if (!speech_ended) {
+      if (st.raw_tokens == st.prev_tail_snapshot) {
+        st.stale_count += 1;
+      } else {
+        st.stale_count = 0;
+        st.prev_tail_snapshot = st.raw_tokens;
+      }
+      auto rep = tail_repeat_blocks(st.raw_tokens, kDegenMaxPeriod);
+      bool is_degen = st.stale_count >= kStaleChunks || rep.first >= (size_t)kDegenMinRepeats;
+      if (is_degen) reset_context();
+      if (st.chunk_idx > 0 && st.chunk_idx % kResetInterval == 0) reset_context();
+
+      size_t ts = text_start_of(st.raw_tokens);
+      size_t n_text_tokens = st.raw_tokens.size() > ts ? st.raw_tokens.size() - ts : 0;
+      size_t candidate_len;
+      if (is_final) candidate_len = n_text_tokens;
+      else if (st.chunk_idx >= unfixed) candidate_len = (size_t)std::max((int)n_text_tokens - rollback, 0);
+      else candidate_len = 0;
+      std::vector<int> cand(st.raw_tokens.begin() + std::min(ts, st.raw_tokens.size()), st.raw_tokens.end());
+      size_t from = st.stable_text_tokens.size();
+      emit(cand, from, std::max(candidate_len, from));
+    }
+    perf_encode_ms += (eng.perf.mel_ms - before.mel_ms) + (eng.perf.enc_ms - before.enc_ms);
+    perf_decode_ms += (eng.perf.prefill_ms - before.prefill_ms) + (eng.perf.decode_ms - before.decode_ms);
+    perf_total_ms += now_ms() - chunk_t0;
+    st.chunk_idx += 1;
+    if (speech_ended) break;
+  }
+  return true;
+}
+
+}  // namespace qasr

@@ -1,0 +1,75 @@
+// Transcription orchestration over one Engine: the QwenCtx settings
+// (crates/qwen-asr/src/context.rs:26-162) and transcribe.rs's offline, segmented and
+// streaming algorithms.
+#pragma once
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+#include "host.h"
+
+namespace qasr {
+
+struct StreamState {  // transcribe.rs:801-893
+  struct EncWindow {
+    int seq_len;
+    std::vector<float> enc;
+  };
+  std::vector<EncWindow> enc_cache;
+  size_t enc_cached_seq_total = 0, enc_cache_base_windows = 0;
+  std::vector<int> raw_tokens, stable_text_tokens;
+  std::string result_bytes;
+  // previous prefill rows: token id (>= 0) or encoder row (< 0 -> index into prev_enc)
+  std::vector<int> prev_ids;
+  std::vector<float> prev_enc;
+  size_t prev_prefill_len = 0;
+  std::vector<int> prev_tail_snapshot;
+  int stale_count = 0;
+  size_t last_partial_cursor = 0;
+  std::vector<float> last_partial_enc;
+  int last_partial_seq = 0;
+  size_t audio_cursor = 0;
+  int chunk_idx = 0;
+  bool prompt_prepared = false;
+  void reset();
+};
+
+class Ctx {
+ public:
+  Engine eng;
+  std::string model_dir;
+  Tokenizer tok;
+  // settings (context.rs:133-162)
+  float segment_sec = 0.0f, search_sec = 3.0f;
+  float stream_chunk_sec = 2.0f;
+  int stream_rollback = 5, stream_unfixed_chunks = 2, stream_max_new_tokens = 32;
+  bool past_text_conditioning = false, skip_silence = false;
+  std::string prompt, force_language;
+  int force_n_tokens = 0;  // benchmark extension: exactly N decode steps, EOS ignored
+  // prompt tokens
+  std::vector<int> prompt_tokens, force_prompt_tokens;
+  bool has_prompt_tokens = false, has_force_tokens = false, prompt_tokens_ready = false;
+  // perf (context.rs:67-73)
+  double perf_total_ms = 0, perf_audio_ms = 0, perf_encode_ms = 0, perf_decode_ms = 0;
+  int perf_text_tokens = 0;
+  std::vector<std::vector<int>> last_tokens;  // generated ids per segment / chunk of the last call
+
+  bool load(const std::string& dir, int device);
+  bool set_force_language(const std::string& lang);
+  void set_prompt(const std::string& p) {
+    prompt = p;
+    prompt_tokens_ready = false;
+  }
+  bool prepare_prompt_tokens();
+  bool transcribe_audio(const std::vector<float>& samples, std::string& out);
+  bool transcribe_segment(const float* samples, size_t n, const std::vector<int>* past, std::string& text,
+                          int& n_text);
+  bool stream_push_audio(const std::vector<float>& samples, StreamState& st, bool finalize, std::string& delta);
+  void reset_perf();
+
+ private:
+  bool encode_window(const float* samples, size_t n, std::vector<float>& enc, int& seq);
+};
+
+}  // namespace qasr

@@ -1,0 +1,177 @@
+"""GPU parity: the CUDA engine (through its C ABI) against the CPU oracle on the same
+seeded weights and audio. Tolerances are stated per test."""
+import numpy as np
+import pytest
+
+from qwen_asr_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def Q():
+    import qwen_asr_b200 as Q
+    return Q
+
+
+@pytest.fixture(scope="module")
+def O():
+    from oracle import qwen_oracle as O
+    return O
+
+
+@pytest.fixture(scope="module")
+def tiny(Q, tiny_dir):
+    return Q.Engine(tiny_dir)
+
+
+@pytest.fixture(scope="module")
+def tiny_oracle(O, tiny_dir):
+    return O.Model(tiny_dir)
+
+
+@pytest.fixture(scope="module")
+def m06(Q, m06_dir):
+    return Q.Engine(m06_dir)
+
+
+@pytest.fixture(scope="module")
+def m06_oracle(O, m06_dir):
+    return O.Model(m06_dir)
+
+
+def rel_err(a, b):
+    return float(np.max(np.abs(a - b)) / max(1e-12, float(np.max(np.abs(b)))))
+
+
+# --------------------------------------------------------------------------- mel
+@pytest.mark.parametrize("n", [161, 401, 8000, 16000 * 3 + 77, 451200])
+def test_mel_matches_oracle(tiny, O, n):
+    x = synth.synth_audio(n, seed=n)
+    ref = O.mel_spectrogram(x)  # [128, F]
+    got = tiny.debug_mel(x)     # [F, 128]
+    assert got.shape == (ref.shape[1], 128)
+    # f32 math in both; summation order differs -> absolute tolerance on values in [-1, 2]
+    assert np.max(np.abs(got.T - ref)) < 2e-4
+
+
+def test_mel_too_short(tiny):
+    with pytest.raises(RuntimeError):
+        tiny.debug_mel(np.zeros(100, dtype=np.float32))  # < one hop: reference returns None
+
+
+# --------------------------------------------------------------------------- encoder
+@pytest.mark.parametrize("seconds", [0.5, 3.0, 9.3])
+def test_encoder_tiny_matches_oracle(tiny, tiny_oracle, O, seconds):
+    x = synth.synth_audio(int(16000 * seconds), seed=7)
+    mel = O.mel_spectrogram(x)
+    ref = tiny_oracle.encode(mel)
+    got = tiny.debug_encode(np.ascontiguousarray(mel.T))
+    assert got.shape == ref.shape
+    assert rel_err(got, ref) < 1e-3
+
+
+@pytest.mark.parametrize("seconds", [1.3, 8.7])
+def test_encoder_06b_matches_oracle(m06, m06_oracle, O, seconds):
+    x = synth.synth_audio(int(16000 * seconds), seed=11)
+    mel = O.mel_spectrogram(x)
+    ref = m06_oracle.encode(mel)
+    got = m06.debug_encode(np.ascontiguousarray(mel.T))
+    assert got.shape == ref.shape
+    assert rel_err(got, ref) < 2e-3
+
+
+# --------------------------------------------------------------------------- decoder
+def _teacher_forced_case(eng, model, O, seconds, n_steps, mode, seed):
+    eng.set_decode_mode(mode)
+    x = synth.synth_audio(int(16000 * seconds), seed=seed)
+    enc = model.encode(O.mel_spectrogram(x))
+    ctx_like = O.Ctx.__new__(O.Ctx)
+    ctx_like.model = model
+    ctx_like.tok = None
+    ctx_like.prompt = None
+    ctx_like.force_language = None
+    rows = O.prompt_rows(ctx_like, enc)
+    rng = np.random.default_rng(seed)
+    forced = rng.integers(0, 151643, n_steps).astype(np.int32)
+    ref_ids, ref_lg = O.teacher_forced(model, rows, forced, n_steps)
+    ids, lg, _ = eng.debug_decode(rows, n_steps, forced=forced, want_logits=True)
+    return ids, lg, ref_ids, ref_lg
+
+
+@pytest.mark.parametrize("mode", ["int8", "bf16"])
+def test_decode_teacher_forced_tiny(tiny, O, tiny_dir, mode):
+    model = O.Model(tiny_dir, decode_mode=mode)
+    ids, lg, ref_ids, ref_lg = _teacher_forced_case(tiny, model, O, 2.0, 24, mode, 5)
+    agree = float(np.mean(ids == ref_ids))
+    assert agree >= 0.995, (agree, ids, ref_ids)
+    # logits: max-rel 2e-2 (bf16 bar of the spec) relative to each step's logit range
+    for s in range(len(ids)):
+        assert rel_err(lg[s], ref_lg[s]) < 2e-2
+
+
+@pytest.mark.parametrize("mode", ["int8", "bf16"])
+def test_decode_teacher_forced_06b(m06, O, m06_dir, mode):
+    model = O.Model(m06_dir, decode_mode=mode)
+    ids, lg, ref_ids, ref_lg = _teacher_forced_case(m06, model, O, 3.0, 16, mode, 9)
+    agree = float(np.mean(ids == ref_ids))
+    assert agree >= 0.995, (agree, ids, ref_ids)
+    for s in range(len(ids)):
+        assert rel_err(lg[s], ref_lg[s]) < 2e-2
+
+
+# --------------------------------------------------------------------------- end to end
+def test_transcribe_offline_tiny(Q, O, tiny_dir):
+    eng = Q.Engine(tiny_dir)
+    ctx = O.Ctx(tiny_dir)
+    x = synth.synth_audio(16000 * 4, seed=21)
+    for e in (eng,):
+        assert e.set_language("english") == 0
+    ctx.set_force_language("english")
+    eng.set_force_n_tokens(20)
+    ctx.force_n_tokens = 20
+    text = eng.transcribe_pcm(x)
+    ref = ctx.transcribe_audio(x)
+    got_tokens = eng.last_tokens()[0]
+    assert got_tokens[:20] == ctx.last_tokens[:20]
+    assert text == ref
+
+
+def test_transcribe_segmented_tiny(Q, O, tiny_dir):
+    eng = Q.Engine(tiny_dir)
+    ctx = O.Ctx(tiny_dir)
+    x = synth.synth_audio(16000 * 70, seed=33)
+    eng.set_segment_sec(30.0)
+    ctx.segment_sec = 30.0
+    eng.set_language("English")
+    ctx.set_force_language("English")
+    eng.set_force_n_tokens(8)
+    ctx.force_n_tokens = 8
+    text = eng.transcribe_pcm(x)
+    ref = ctx.transcribe_audio(x)
+    segs = eng.last_tokens()
+    assert len(segs) == len(ctx.segments_tokens) == len(O.split_points(x, 30.0, 3.0))
+    for a, b in zip(segs, ctx.segments_tokens):
+        assert a[:8] == b[:8]
+    assert text == ref
+
+
+def test_transcribe_without_language_is_empty_text(Q, tiny_dir):
+    # random weights never emit <asr_text>, so nothing is text (transcribe.rs:196-219)
+    eng = Q.Engine(tiny_dir)
+    eng.set_force_n_tokens(6)
+    assert eng.transcribe_pcm(synth.synth_audio(16000, seed=3)) == ""
+
+
+def test_graph_and_direct_decode_agree(Q, tiny_dir):
+    eng = Q.Engine(tiny_dir)
+    eng.set_language("English")
+    eng.set_force_n_tokens(40)
+    x = synth.synth_audio(16000 * 2, seed=44)
+    eng.set_use_graph(True)
+    a = eng.transcribe_pcm(x)
+    ta = eng.last_tokens()
+    eng.set_use_graph(False)
+    b = eng.transcribe_pcm(x)
+    tb = eng.last_tokens()
+    assert a == b and ta == tb

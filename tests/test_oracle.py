@@ -1,0 +1,135 @@
+"""Pins the CPU oracle: the reference's own unit-test envelopes
+(crates/qwen-asr/tests/kernels.rs, tests/audio.rs) re-expressed against the oracle, an
+independent cross-check of the mel front end against transformers'
+WhisperFeatureExtractor, and structural checks of the synthetic checkpoint."""
+import numpy as np
+import pytest
+
+from oracle import qwen_oracle as O
+from qwen_asr_b200 import synth
+
+F32 = np.float32
+
+
+def bf16_round(v):
+    return ((np.float32(v).view(np.uint32) + 0x8000) >> 16).astype(np.uint16)
+
+
+def test_bf16_roundtrip():  # kernels.rs:8-17
+    for v in [0.0, 1.0, -1.0, 3.14, -2.71, 100.5, 0.001, -0.001]:
+        back = O.bf16_to_f32(np.array([bf16_round(v)]))[0]
+        assert abs(v - back) < 0.02 * max(abs(v), 1.0)
+
+
+def test_bf16_matvec_vs_generic():  # kernels.rs:19-44
+    in_dim, out_dim = 128, 16
+    x = (np.arange(in_dim, dtype=F32) * F32(0.01) - F32(0.64)).astype(F32)
+    v = (np.arange(out_dim * in_dim, dtype=F32) * F32(0.001) - F32(0.5)).astype(F32)
+    w_bits = (v.view(np.uint32) >> 16).astype(np.uint16).reshape(out_dim, in_dim)
+    bias = (np.arange(out_dim, dtype=F32) * F32(0.1)).astype(F32)
+    w = O.bf16_to_f32(w_bits)
+    generic = np.array([F32(bias[o]) + sum((w[o, i] * x[i] for i in range(in_dim)), F32(0)) for o in range(out_dim)])
+    dispatch = O.linear(x[None], w)[0] + bias
+    assert np.max(np.abs(generic - dispatch)) < 0.01
+
+
+def test_rms_norm_unit_rms():  # kernels.rs:60-72
+    x = (np.arange(128, dtype=F32) * F32(0.02) - F32(1.28)).astype(F32)
+    out = O.rms_norm(x[None], np.ones(128, F32), F32(1e-6))[0]
+    assert abs(np.sqrt(np.mean(out * out)) - 1.0) < 0.01
+
+
+def test_layer_norm_moments():  # kernels.rs:74-89
+    x = (np.arange(128, dtype=F32) * F32(0.05) - F32(3.2)).astype(F32)
+    out = O.layer_norm(x[None], np.ones(128, F32), np.zeros(128, F32))[0]
+    assert abs(out.mean()) < 0.01 and abs(out.var() - 1.0) < 0.02
+
+
+def test_gelu_silu():  # kernels.rs:105-124
+    g = O.gelu(np.array([0.0, 1.0, -1.0, 2.0, -0.5], F32))
+    assert abs(g[0]) < 1e-5 and g[1] > 0.5 and g[2] < 0.0
+    v = np.array([0.0, 1.0, -1.0, 5.0], F32)
+    s = O.silu_mul(v, np.ones_like(v))
+    assert np.max(np.abs(s - v / (1 + np.exp(-v)))) < 1e-5
+
+
+def test_mel_short_audio_frames():  # audio.rs:47-61
+    n = 8000
+    x = (np.sin(2 * np.pi * 440 * np.arange(n) / 16000) * 0.5).astype(F32)
+    mel = O.mel_spectrogram(x)
+    assert 20 < mel.shape[1] < 80 and mel.shape[0] == 128
+    assert mel.shape[1] == n // 160
+
+
+def test_mel_range():  # audio.rs:23-45 (value range after (log10 + 4) / 4)
+    mel = O.mel_spectrogram(synth.synth_audio(16000 * 11, seed=4))
+    assert mel.min() >= -1.0 and mel.max() <= 2.0
+    assert 1000 < mel.shape[1] < 1200
+
+
+def test_mel_too_short_is_none():
+    assert O.mel_spectrogram(np.zeros(159, F32)) is None
+
+
+def test_mel_matches_whisper_feature_extractor():
+    """Independent pin: the reference restates the Whisper/Qwen log-mel recipe; the
+    transformers implementation of that recipe must agree with the oracle."""
+    tr = pytest.importorskip("transformers")
+    fe = tr.WhisperFeatureExtractor(feature_size=128, sampling_rate=16000, hop_length=160, chunk_length=30,
+                                    n_fft=400)
+    for n, seed in ((16000 * 3 + 77, 5), (40000, 6)):
+        x = synth.synth_audio(n, seed)
+        ref = fe._np_extract_fbank_features(x[None].astype(F32), "cpu")[0]
+        got = O.mel_spectrogram(x)
+        assert got.shape == ref.shape
+        assert np.max(np.abs(got - ref)) < 3e-3
+
+
+def test_quantizers():
+    # activation quantiser (kernels/mod.rs:1795-1802): round half away, absmax 127
+    q, s = O.quantize_act(np.array([0.5, -1.0, 0.25, 127.0 / 254.0], F32))
+    assert s == F32(1.0) / F32(127.0) and list(q[:3]) == [64, -127, 32]
+    q, s = O.quantize_act(np.zeros(4, F32))
+    assert s == 1.0 and not q.any()
+    # weight quantiser: trunc (neon.rs:672-684) vs round (mod.rs:1805-1829)
+    w = np.array([[1.0, 0.5, -0.3, 0.0]], F32)
+    bits = (w.view(np.uint32) >> 16).astype(np.uint16)
+    qt, st = O.quantize_weights(bits, "trunc")
+    qr, sr = O.quantize_weights(bits, "round")
+    assert st[0] == sr[0] and qt[0, 0] == 127 and qr[0, 0] == 127
+    assert qt[0, 1] == 63 and qr[0, 1] == 64
+
+
+def test_int8_dot_is_exact():
+    rng = np.random.default_rng(0)
+    w = rng.integers(-127, 128, (64, 3072)).astype(np.int8)
+    x = rng.integers(-127, 128, 3072).astype(np.int8)
+    ref = w.astype(np.int64) @ x.astype(np.int64)
+    assert np.array_equal(O.int8_dot(O.int8_chunks(w), x), ref)
+
+
+def test_synthetic_checkpoint_layout(tiny_dir):
+    st = O.SafeTensors(tiny_dir)
+    cfg = O.detect_config(st)
+    assert (cfg.enc_d_model, cfg.enc_layers, cfg.dec_hidden, cfg.dec_layers) == (128, 2, 256, 2)
+    assert not st.has("thinker.lm_head.weight")  # tied lm_head (decoder.rs:145-151)
+    names = [n for n, _, _ in synth.tensor_specs("0.6b")]
+    assert "thinker.audio_tower.layers.17.fc1.weight" in names
+    assert "thinker.audio_tower.layers.18.fc1.weight" not in names  # 0.6B detection (context.rs:95)
+    n06 = sum(int(np.prod(s)) for _, s, _ in synth.tensor_specs("0.6b"))
+    assert 0.75e9 < n06 < 0.8e9
+
+
+def test_oracle_transcribe_tiny_runs(tiny_dir):
+    ctx = O.Ctx(tiny_dir)
+    ctx.set_force_language("English")
+    ctx.force_n_tokens = 5
+    text = ctx.transcribe_audio(synth.synth_audio(16000, seed=2))
+    assert isinstance(text, str) and len(ctx.last_tokens) == 5
+
+
+def test_synth_audio_properties():
+    x = synth.synth_audio(16000 * 2, seed=1)
+    assert x.dtype == np.float32 and abs(np.max(np.abs(x)) - 10 ** (-3 / 20)) < 2e-3
+    assert np.array_equal(x, synth.synth_audio(16000 * 2, seed=1))
+    assert np.all(np.round(x * 32768) == x * 32768)  # s16 quantised
