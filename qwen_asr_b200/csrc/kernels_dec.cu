@@ -260,6 +260,7 @@ __device__ __forceinline__ float mv_prologue(const MvArgs& a, float* xs, int8_t*
     ss = fmaf(v.z, v.z, ss);
     ss = fmaf(v.w, v.w, ss);
   }
+  __syncthreads();  // xs is read below with a different thread mapping
   if (a.norm_w) {
     float tot = block_sum(ss, red);
     float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
