@@ -30,6 +30,18 @@ int32_t qwen_asr_set_decode_mode(QwenAsrEngine* engine, int32_t mode);
 void qwen_asr_set_force_n_tokens(QwenAsrEngine* engine, int32_t n);
 /* 1 (default): decode steps replay a CUDA graph; 0: plain launches. */
 void qwen_asr_set_use_graph(QwenAsrEngine* engine, int32_t on);
+/* Per-op decode profiler (the reference's --profile counters, kernels/mod.rs:78-168): when
+ * on, decode steps run as plain launches with CUDA events around each kernel. */
+void qwen_asr_set_profile(QwenAsrEngine* engine, int32_t on);
+/* Accumulated GPU ms and launch counts per op: qkv, attention, o_proj, gate_up, down,
+ * lm_head_argmax. Returns 6. */
+int32_t qwen_asr_profile_report(QwenAsrEngine* engine, double* ms, int64_t* counts, int32_t cap);
+/* Kernel timeline of the next decode calls: CTA 0 of every decode kernel records
+ * {kind, t_entry, t_after_dependency_wait, t_exit} (GPU %globaltimer, ns); kinds as in
+ * qwen_asr_profile_report. Works with the CUDA-graph path. */
+void qwen_asr_set_timeline(QwenAsrEngine* engine, int32_t on);
+/* Copies the last decode call's timeline (4 values per kernel); returns the value count. */
+int64_t qwen_asr_get_timeline(QwenAsrEngine* engine, uint64_t* out, int64_t cap);
 /* Generated ids of segment/chunk `segment` of the last call (including the stop token);
  * returns the count (copies at most cap), -1 if out of range. */
 int32_t qwen_asr_last_tokens(QwenAsrEngine* engine, int32_t segment, int32_t* out, int32_t cap);

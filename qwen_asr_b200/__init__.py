@@ -52,6 +52,10 @@ SIGNATURES = {
     "qwen_asr_set_force_n_tokens": (None, [_VP, C.c_int32]),
     "qwen_asr_set_use_graph": (None, [_VP, C.c_int32]),
     "qwen_asr_last_tokens": (C.c_int32, [_VP, C.c_int32, _I32P, C.c_int32]),
+    "qwen_asr_set_profile": (None, [_VP, C.c_int32]),
+    "qwen_asr_set_timeline": (None, [_VP, C.c_int32]),
+    "qwen_asr_get_timeline": (C.c_int64, [_VP, C.POINTER(C.c_uint64), C.c_int64]),
+    "qwen_asr_profile_report": (C.c_int32, [_VP, C.POINTER(C.c_double), _I64P, C.c_int32]),
     "qwen_asr_last_segments": (C.c_int32, [_VP]),
     "qwen_asr_get_perf": (C.c_int32, [_VP, C.POINTER(C.c_double), C.c_int32]),
     "qwen_asr_model_info": (C.c_int32, [_VP, _I32P, C.c_int32]),
@@ -165,6 +169,26 @@ class Engine:
 
     def set_use_graph(self, on: bool):
         lib().qwen_asr_set_use_graph(self._h, int(on))
+
+    def set_profile(self, on: bool):
+        lib().qwen_asr_set_profile(self._h, int(on))
+
+    def profile_report(self) -> dict:
+        ms = (C.c_double * 6)()
+        n = (C.c_int64 * 6)()
+        lib().qwen_asr_profile_report(self._h, ms, n, 6)
+        names = ["qkv", "attention", "o_proj", "gate_up", "down", "lm_head_argmax"]
+        return {k: (ms[i], n[i]) for i, k in enumerate(names)}
+
+    def set_timeline(self, on: bool):
+        lib().qwen_asr_set_timeline(self._h, int(on))
+
+    def timeline(self) -> np.ndarray:
+        """[n_kernels, 4] = kind, t_entry, t_after_wait, t_exit (ns) of the last decode."""
+        n = lib().qwen_asr_get_timeline(self._h, None, 0)
+        buf = np.zeros(max(n, 4), dtype=np.uint64)
+        lib().qwen_asr_get_timeline(self._h, buf.ctypes.data_as(C.POINTER(C.c_uint64)), n)
+        return buf[:n].reshape(-1, 4)
 
     def last_tokens(self):
         L = lib()

@@ -191,6 +191,36 @@ void qwen_asr_set_use_graph(QwenAsrEngine* e, int32_t on) {
   if (e) e->ctx.eng.use_graph = on != 0;
 }
 
+void qwen_asr_set_profile(QwenAsrEngine* e, int32_t on) {
+  if (!e) return;
+  e->ctx.eng.profile = on != 0;
+  for (int i = 0; i < 6; ++i) {
+    e->ctx.eng.prof_ms[i] = 0;
+    e->ctx.eng.prof_n[i] = 0;
+  }
+}
+
+int32_t qwen_asr_profile_report(QwenAsrEngine* e, double* ms, int64_t* counts, int32_t cap) {
+  if (!e) return -1;
+  for (int i = 0; i < 6 && i < cap; ++i) {
+    if (ms) ms[i] = e->ctx.eng.prof_ms[i];
+    if (counts) counts[i] = e->ctx.eng.prof_n[i];
+  }
+  return 6;
+}
+
+void qwen_asr_set_timeline(QwenAsrEngine* e, int32_t on) {
+  if (e) e->ctx.eng.set_timeline(on != 0);
+}
+
+int64_t qwen_asr_get_timeline(QwenAsrEngine* e, uint64_t* out, int64_t cap) {
+  if (!e) return -1;
+  const auto& t = e->ctx.eng.last_timeline;
+  if (out)
+    for (int64_t i = 0; i < (int64_t)t.size() && i < cap; ++i) out[i] = t[i];
+  return (int64_t)t.size();
+}
+
 int32_t qwen_asr_last_tokens(QwenAsrEngine* e, int32_t segment, int32_t* out, int32_t cap) {
   if (!e || segment < 0 || segment >= (int)e->ctx.last_tokens.size()) return -1;
   const auto& v = e->ctx.last_tokens[segment];

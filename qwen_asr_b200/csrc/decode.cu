@@ -1,0 +1,648 @@
+// Single-token decode step (decoder_forward, crates/qwen-asr/src/decoder.rs:550-645) as a
+// chain of programmatic-dependent launches. Every weight matvec CTA owns a contiguous
+// slab of rows; its first tiles are pulled into shared memory with cp.async.bulk BEFORE
+// griddepcontrol.wait, so the HBM stream of kernel i+1 overlaps the tail of kernel i.
+//
+// Numerics follow the reference's int8 path exactly: per-vector activation quantisation
+// (kernels/mod.rs:1795-1802), exact int32 dot products (dp4a), then
+// (float)sum * x_scale * w_scale[row] (+ residual) (kernels/neon.rs:716-800).
+#include "bulk.cuh"
+#include "common.h"
+#include "dev_util.cuh"
+#include "kernels.h"
+
+namespace qasr {
+
+constexpr int kHd = 128;
+constexpr int kWarps = 8;
+constexpr int kSplits = 16;  // attention split-K CTAs per kv head
+constexpr int kMaxG = 4;     // q heads per kv head
+
+enum MvEpi { MV_STORE = 0, MV_RESID = 1, MV_SWIGLU = 2, MV_ARGMAX = 3 };
+
+struct MvArgs {
+  const float* x;              // input vector [K]
+  const __nv_bfloat16* embed;  // optional: take x from embed[st->cur_token] when >= 0
+  float* x_out;                // written with the gathered embedding row by CTA 0
+  const float* norm_w;         // fused RMSNorm weight or null
+  float eps;
+  int K, N;
+  const void* W;               // [N][K] int8 or bf16
+  const float* ws;             // int8 row scales
+  float* out;
+  const float* resid;          // may alias out
+  int rows_per_cta, tile_rows, stages, tile_bytes;
+  unsigned long long* am_part;
+  int* am_ticket;
+  StepState* st;
+  int* tokens;
+  const int* forced;
+  float* logits;
+  int* err;
+  unsigned long long* tl;
+  int* tl_count;
+  int kind;
+};
+
+__device__ __forceinline__ unsigned long long am_key(float v, int idx) {
+  unsigned int hv = (unsigned int)float_to_ordered(v) ^ 0x80000000u;
+  return ((unsigned long long)hv << 32) | (unsigned int)(0xFFFFFFFFu - (unsigned int)idx);
+}
+
+struct Timeline {
+  unsigned long long* slot = nullptr;
+  __device__ __forceinline__ void begin(unsigned long long* tl, int* cnt, int kind) {
+    if (tl && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+      slot = tl + 4 * (size_t)atomicAdd(cnt, 1);
+      slot[0] = (unsigned long long)kind;
+      slot[1] = global_timer_ns();
+    }
+  }
+  __device__ __forceinline__ void mark(int i) {
+    if (slot) slot[i] = global_timer_ns();
+  }
+};
+
+template <bool INT8, int EPI>
+__global__ void __launch_bounds__(256, 1) mv_kernel(MvArgs a) {
+  Timeline tline;
+  tline.begin(a.tl, a.tl_count, a.kind);
+  extern __shared__ __align__(128) unsigned char sm[];
+  __shared__ float red[32];
+  __shared__ unsigned long long am_warp[kWarps];
+  __shared__ int is_last;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = a.K;
+  const size_t row_bytes = (size_t)K * (INT8 ? 1 : 2);
+  unsigned char* wst = sm;
+  float* xs = reinterpret_cast<float*>(sm + (size_t)a.stages * a.tile_bytes);
+  int8_t* xq = reinterpret_cast<int8_t*>(xs + K);
+  uint64_t* full =
+      reinterpret_cast<uint64_t*>(sm + (((size_t)a.stages * a.tile_bytes + (size_t)K * 5 + 63) & ~(size_t)63));
+  uint64_t* empty = full + a.stages;
+  float* sws = reinterpret_cast<float*>(empty + a.stages);  // [rows_per_cta] row scales
+  float* snw = sws + a.rows_per_cta;                         // [K] RMSNorm weight
+
+  const int r0 = blockIdx.x * a.rows_per_cta;
+  const int nrows = max(0, min(a.N, r0 + a.rows_per_cta) - r0);
+  const int ntiles = (nrows + a.tile_rows - 1) / a.tile_rows;
+  const unsigned char* wbase = reinterpret_cast<const unsigned char*>(a.W) + (size_t)r0 * row_bytes;
+  auto issue = [&](int t) {
+    int s = t % a.stages;
+    int rows_t = min(a.tile_rows, nrows - t * a.tile_rows);
+    uint32_t bytes = (uint32_t)(rows_t * row_bytes);
+    mbar_expect_tx(&full[s], bytes);
+    bulk_g2s(wst + (size_t)s * a.tile_bytes, wbase + (size_t)t * a.tile_rows * row_bytes, bytes, &full[s]);
+  };
+  if (tid == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kWarps);
+    }
+    fence_mbar_init();
+    for (int t = 0; t < min(a.stages, ntiles); ++t) issue(t);  // weights do not depend on x
+  }
+  // Immutable per-row scales and norm weights: stage them before waiting on the producer.
+  if (INT8)
+    for (int i = tid; i < nrows; i += 256) sws[i] = a.ws[r0 + i];
+  if (a.norm_w)
+    for (int i = tid; i < K; i += 256) snw[i] = a.norm_w[i];
+  pdl_launch_dependents();
+  pdl_wait();
+  tline.mark(2);
+
+  // ---- prologue: x (optionally gathered / RMS-normalised), per-vector int8 quantisation
+  const float* xsrc = a.x;
+  const uint16_t* erow = nullptr;
+  if (a.embed) {
+    int tok = a.st->cur_token;
+    if (tok >= 0) erow = reinterpret_cast<const uint16_t*>(a.embed) + (size_t)tok * K;
+  }
+  float ss = 0.f;
+  for (int i = tid * 4; i < K; i += 256 * 4) {
+    float4 v;
+    if (erow) {
+      uint2 b = *reinterpret_cast<const uint2*>(erow + i);
+      v = make_float4(__uint_as_float(b.x << 16), __uint_as_float(b.x & 0xFFFF0000u), __uint_as_float(b.y << 16),
+                      __uint_as_float(b.y & 0xFFFF0000u));
+      if (blockIdx.x == 0) *reinterpret_cast<float4*>(a.x_out + i) = v;
+    } else {
+      v = *reinterpret_cast<const float4*>(xsrc + i);
+    }
+    *reinterpret_cast<float4*>(xs + i) = v;
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
+  }
+  __syncthreads();
+  if (a.norm_w) {
+    float tot = block_sum(ss, red);
+    float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+    for (int i = tid; i < K; i += 256) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), snw[i]);
+  }
+  float xscale = 1.0f;
+  if (INT8) {
+    float mx = 0.f;
+    for (int i = tid; i < K; i += 256) mx = fmaxf(mx, fabsf(xs[i]));
+    mx = block_max(mx, red);
+    xscale = mx > 0.f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+    float inv = __fdiv_rn(127.0f, fmaxf(mx, 1e-10f));
+    for (int i = tid; i < K; i += 256) {
+      float r = roundf(__fmul_rn(xs[i], inv));
+      xq[i] = (int8_t)fminf(fmaxf(r, -127.f), 127.f);
+    }
+  }
+  __syncthreads();
+
+  // ---- main loop over weight tiles
+  unsigned long long best = 0ull;
+  for (int t = 0; t < ntiles; ++t) {
+    const int s = t % a.stages;
+    const uint32_t phase = (uint32_t)(t / a.stages) & 1u;
+    mbar_wait(&full[s], phase, a.err, 1);
+    const int rows_t = min(a.tile_rows, nrows - t * a.tile_rows);
+    const unsigned char* tw = wst + (size_t)s * a.tile_bytes;
+    for (int rr = warp * 2; rr < rows_t; rr += 2 * kWarps) {
+      const bool two = rr + 1 < rows_t;
+      float v0, v1 = 0.f;
+      if (INT8) {
+        int acc0 = 0, acc1 = 0;
+        const int8_t* w0 = reinterpret_cast<const int8_t*>(tw) + (size_t)rr * K;
+        const int8_t* w1 = w0 + K;
+#pragma unroll 4
+        for (int k0 = lane * 16; k0 < K; k0 += 512) {
+          int4 xv = *reinterpret_cast<const int4*>(xq + k0);
+          int4 wa = *reinterpret_cast<const int4*>(w0 + k0);
+          acc0 = __dp4a(wa.x, xv.x, acc0);
+          acc0 = __dp4a(wa.y, xv.y, acc0);
+          acc0 = __dp4a(wa.z, xv.z, acc0);
+          acc0 = __dp4a(wa.w, xv.w, acc0);
+          if (two) {
+            int4 wb = *reinterpret_cast<const int4*>(w1 + k0);
+            acc1 = __dp4a(wb.x, xv.x, acc1);
+            acc1 = __dp4a(wb.y, xv.y, acc1);
+            acc1 = __dp4a(wb.z, xv.z, acc1);
+            acc1 = __dp4a(wb.w, xv.w, acc1);
+          }
+        }
+        acc0 = warp_sum_i(acc0);
+        acc1 = warp_sum_i(acc1);
+        const int lr = t * a.tile_rows + rr;
+        v0 = __fmul_rn(__fmul_rn((float)acc0, xscale), sws[lr]);
+        if (two) v1 = __fmul_rn(__fmul_rn((float)acc1, xscale), sws[lr + 1]);
+      } else {
+        float acc0 = 0.f, acc1 = 0.f;
+        const uint16_t* w0 = reinterpret_cast<const uint16_t*>(tw) + (size_t)rr * K;
+        const uint16_t* w1 = w0 + K;
+#pragma unroll 4
+        for (int k0 = lane * 8; k0 < K; k0 += 256) {
+          float4 x0 = *reinterpret_cast<const float4*>(xs + k0);
+          float4 x1 = *reinterpret_cast<const float4*>(xs + k0 + 4);
+          float f[8];
+          bf16x8_to_f32(*reinterpret_cast<const uint4*>(w0 + k0), f);
+          acc0 = fmaf(f[0], x0.x, acc0); acc0 = fmaf(f[1], x0.y, acc0);
+          acc0 = fmaf(f[2], x0.z, acc0); acc0 = fmaf(f[3], x0.w, acc0);
+          acc0 = fmaf(f[4], x1.x, acc0); acc0 = fmaf(f[5], x1.y, acc0);
+          acc0 = fmaf(f[6], x1.z, acc0); acc0 = fmaf(f[7], x1.w, acc0);
+          if (two) {
+            bf16x8_to_f32(*reinterpret_cast<const uint4*>(w1 + k0), f);
+            acc1 = fmaf(f[0], x0.x, acc1); acc1 = fmaf(f[1], x0.y, acc1);
+            acc1 = fmaf(f[2], x0.z, acc1); acc1 = fmaf(f[3], x0.w, acc1);
+            acc1 = fmaf(f[4], x1.x, acc1); acc1 = fmaf(f[5], x1.y, acc1);
+            acc1 = fmaf(f[6], x1.z, acc1); acc1 = fmaf(f[7], x1.w, acc1);
+          }
+        }
+        v0 = warp_sum(acc0);
+        v1 = warp_sum(acc1);
+      }
+      const int row = r0 + t * a.tile_rows + rr;
+      if (lane == 0) {
+        if (EPI == MV_SWIGLU) {
+          if (two) a.out[row / 2] = silu_mul(v0, v1);
+        } else if (EPI == MV_ARGMAX) {
+          if (a.logits) {
+            a.logits[row] = v0;
+            if (two) a.logits[row + 1] = v1;
+          }
+          unsigned long long k0 = am_key(v0, row);
+          best = k0 > best ? k0 : best;
+          if (two) {
+            unsigned long long k1 = am_key(v1, row + 1);
+            best = k1 > best ? k1 : best;
+          }
+        } else if (EPI == MV_RESID) {
+          a.out[row] = __fadd_rn(v0, a.resid[row]);
+          if (two) a.out[row + 1] = __fadd_rn(v1, a.resid[row + 1]);
+        } else {
+          a.out[row] = v0;
+          if (two) a.out[row + 1] = v1;
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (tid == 0 && t + a.stages < ntiles) {
+      mbar_wait(&empty[s], phase, a.err, 2);  // every warp is done with this stage
+      issue(t + a.stages);
+    }
+  }
+
+  if (EPI == MV_ARGMAX) {
+    if (lane == 0) am_warp[warp] = best;
+    __syncthreads();
+    if (tid == 0) {
+      unsigned long long b = 0ull;
+      for (int w = 0; w < kWarps; ++w) b = am_warp[w] > b ? am_warp[w] : b;
+      a.am_part[blockIdx.x] = b;
+      __threadfence();
+      is_last = (atomicAdd(a.am_ticket, 1) == (int)gridDim.x - 1);
+    }
+    __syncthreads();
+    if (is_last) {
+      __threadfence();
+      unsigned long long b = 0ull;
+      for (int i = tid; i < (int)gridDim.x; i += 256) {
+        unsigned long long v = *((volatile unsigned long long*)a.am_part + i);
+        b = v > b ? v : b;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        unsigned long long t2 = __shfl_xor_sync(0xffffffffu, b, o);
+        b = t2 > b ? t2 : b;
+      }
+      if (lane == 0) am_warp[warp] = b;
+      __syncthreads();
+      if (tid == 0) {
+        for (int w = 0; w < kWarps; ++w) b = am_warp[w] > b ? am_warp[w] : b;
+        int tok = (int)(0xFFFFFFFFu - (unsigned int)(b & 0xFFFFFFFFull));
+        StepState* st = a.st;
+        int step = st->step;
+        a.tokens[step] = tok;
+        st->cur_token = (st->forced_mode && a.forced) ? a.forced[step] : tok;
+        st->step = step + 1;
+        st->pos = st->pos + 1;
+        *a.am_ticket = 0;
+      }
+    }
+  }
+  tline.mark(3);
+}
+
+// ------------------------------------------------------------------ attention
+// grid (kv_heads, kSplits), block 128 (one thread per head dimension). q/k RMSNorm
+// (kernels/mod.rs:1214-1240) + NeoX RoPE + KV append at `pos`, then split-K
+// online-softmax attention over positions 0..pos (kernels/mod.rs:1492-1534); the last
+// CTA of a kv head to arrive merges the split partials (arrival ticket, no spinning).
+struct AttnArgs {
+  const float* qkv;
+  int n_heads, n_kv;
+  const float* qn;
+  const float* kn;
+  float eps;
+  const float* rc;
+  const float* rs;
+  float* kc;
+  float* vc;
+  int max_seq;
+  float scale;
+  StepState* st;
+  float* part;
+  int* ticket;
+  float* out;
+  unsigned long long* tl;
+  int* tl_count;
+};
+
+__global__ void __launch_bounds__(128) attn_kernel(AttnArgs a) {
+  Timeline tline;
+  tline.begin(a.tl, a.tl_count, 1);
+  __shared__ __align__(16) float hv[kMaxG + 2][kHd];  // normalised q heads, k, v
+  __shared__ float red[4][kMaxG + 1];
+  __shared__ float wm[4][kMaxG], wl[4][kMaxG];
+  __shared__ __align__(16) float wo[4][kMaxG][kHd];
+  __shared__ float sM[kMaxG][kSplits], sF[kMaxG][kSplits], sL[kMaxG];
+  __shared__ int is_last;
+  const int kvh = blockIdx.x, split = blockIdx.y, d = threadIdx.x;
+  const int warp = d >> 5, lane = d & 31;
+  const int G = a.n_heads / a.n_kv;
+  const float qn = a.qn[d], kn = a.kn[d];
+  pdl_launch_dependents();
+  pdl_wait();
+  tline.mark(2);
+  // Issue every independent load first.
+  const int pos = a.st->pos;
+  float raw[kMaxG + 2];
+#pragma unroll
+  for (int g = 0; g < kMaxG; ++g) raw[g] = g < G ? a.qkv[(kvh * G + g) * kHd + d] : 0.f;
+  raw[kMaxG] = a.qkv[(a.n_heads + kvh) * kHd + d];
+  raw[kMaxG + 1] = a.qkv[(a.n_heads + a.n_kv + kvh) * kHd + d];
+  const float c = a.rc[(size_t)pos * (kHd / 2) + (d & 63)], sn = a.rs[(size_t)pos * (kHd / 2) + (d & 63)];
+  // One reduction pass for the G q-head norms and the k norm.
+#pragma unroll
+  for (int g = 0; g <= kMaxG; ++g) {
+    float v = raw[g];
+    float ss = warp_sum(v * v);
+    if (lane == 0 && (g < G || g == kMaxG)) red[warp][g < G ? g : G] = ss;
+  }
+  __syncthreads();
+  float nv[kMaxG + 1];
+#pragma unroll
+  for (int g = 0; g <= kMaxG; ++g) {
+    if (g < G || g == kMaxG) {
+      int r = g < G ? g : G;
+      float tot = red[0][r] + red[1][r] + red[2][r] + red[3][r];
+      float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)kHd), a.eps)));
+      nv[g] = __fmul_rn(__fmul_rn(raw[g], inv), g < G ? qn : kn);
+      hv[g < G ? g : kMaxG][d] = nv[g];
+    }
+  }
+  __syncthreads();
+  // NeoX rotation (generic path, kernels/mod.rs:1780-1788): pairs (d, d + 64).
+  float rot[kMaxG + 1];
+#pragma unroll
+  for (int g = 0; g <= kMaxG; ++g) {
+    if (g < G || g == kMaxG) {
+      int h = g < G ? g : kMaxG;
+      if (d < kHd / 2) rot[g] = __fadd_rn(__fmul_rn(nv[g], c), __fmul_rn(-hv[h][d + kHd / 2], sn));
+      else rot[g] = __fadd_rn(__fmul_rn(nv[g], c), __fmul_rn(hv[h][d - kHd / 2], sn));
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g <= kMaxG; ++g)
+    if (g < G || g == kMaxG) hv[g < G ? g : kMaxG][d] = rot[g];
+  hv[kMaxG + 1][d] = raw[kMaxG + 1];
+  float* kb = a.kc + (size_t)kvh * a.max_seq * kHd;
+  float* vb = a.vc + (size_t)kvh * a.max_seq * kHd;
+  if (split == 0) {
+    kb[(size_t)pos * kHd + d] = rot[kMaxG];
+    vb[(size_t)pos * kHd + d] = raw[kMaxG + 1];
+  }
+  __syncthreads();
+  const float* ks = hv[kMaxG];
+  const float* vs = hv[kMaxG + 1];
+  const int total = pos + 1;
+  const int chunk = (total + kSplits - 1) / kSplits;
+  const int j0 = split * chunk, j1 = min(total, j0 + chunk);
+  float m[kMaxG], l[kMaxG], o[kMaxG][4];
+#pragma unroll
+  for (int g = 0; g < kMaxG; ++g) {
+    m[g] = -3.0e38f;
+    l[g] = 0.f;
+    o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+  }
+  // Keys in groups of 4 per warp so several row loads are in flight at once.
+  for (int jb = j0 + warp * 4; jb < j1; jb += 16) {
+    float4 kv[4], vv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      int j = jb + u;
+      if (j < j1 && j != pos) {
+        kv[u] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)j * kHd) + lane);
+        vv[u] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)j * kHd) + lane);
+      } else {
+        kv[u] = *reinterpret_cast<const float4*>(&ks[lane * 4]);
+        vv[u] = *reinterpret_cast<const float4*>(&vs[lane * 4]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (jb + u >= j1) break;
+#pragma unroll
+      for (int g = 0; g < kMaxG; ++g) {
+        if (g >= G) break;
+        float4 q = *reinterpret_cast<const float4*>(&hv[g][lane * 4]);
+        float p = q.x * kv[u].x;
+        p = fmaf(q.y, kv[u].y, p);
+        p = fmaf(q.z, kv[u].z, p);
+        p = fmaf(q.w, kv[u].w, p);
+        float sc = __fmul_rn(warp_sum(p), a.scale);
+        float mn = fmaxf(m[g], sc);
+        float corr = expf(__fsub_rn(m[g], mn));
+        float e = expf(__fsub_rn(sc, mn));
+        l[g] = fmaf(l[g], corr, e);
+        o[g][0] = fmaf(o[g][0], corr, e * vv[u].x);
+        o[g][1] = fmaf(o[g][1], corr, e * vv[u].y);
+        o[g][2] = fmaf(o[g][2], corr, e * vv[u].z);
+        o[g][3] = fmaf(o[g][3], corr, e * vv[u].w);
+        m[g] = mn;
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < kMaxG; ++g) {
+    if (g >= G) break;
+    if (lane == 0) {
+      wm[warp][g] = m[g];
+      wl[warp][g] = l[g];
+    }
+    *reinterpret_cast<float4*>(&wo[warp][g][lane * 4]) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+  }
+  __syncthreads();
+  // CTA partial per head: {M, L, O[128]} at part[((h * kSplits) + split) * 130]
+  for (int g = 0; g < G; ++g) {
+    float M = fmaxf(fmaxf(wm[0][g], wm[1][g]), fmaxf(wm[2][g], wm[3][g]));
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      float f = wl[w][g] > 0.f ? expf(__fsub_rn(wm[w][g], M)) : 0.f;
+      L = fmaf(wl[w][g], f, L);
+      O = fmaf(wo[w][g][d], f, O);
+    }
+    float* pp = a.part + ((size_t)(kvh * G + g) * kSplits + split) * (kHd + 2);
+    pp[2 + d] = O;
+    if (d == 0) {
+      pp[0] = M;
+      pp[1] = L;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (d == 0) is_last = (atomicAdd(&a.ticket[kvh], 1) == kSplits - 1);
+  __syncthreads();
+  tline.mark(3);
+  if (!is_last) return;
+  __threadfence();
+  // Merge: split scalars through shared memory, then every thread reads its column of
+  // all splits with independent L2 loads.
+  if (d < G * kSplits) {
+    int g = d / kSplits, sp = d % kSplits;
+    const float* pp = a.part + ((size_t)(kvh * G + g) * kSplits + sp) * (kHd + 2);
+    float M = __ldcg(pp), L = __ldcg(pp + 1);
+    sM[g][sp] = L > 0.f ? M : -3.0e38f;
+    sF[g][sp] = L;
+  }
+  __syncthreads();
+  if (d < G) {
+    float M = -3.0e38f;
+    for (int sp = 0; sp < kSplits; ++sp) M = fmaxf(M, sM[d][sp]);
+    float L = 0.f;
+    for (int sp = 0; sp < kSplits; ++sp) {
+      float f = sF[d][sp] > 0.f ? expf(__fsub_rn(sM[d][sp], M)) : 0.f;
+      L = fmaf(sF[d][sp], f, L);
+      sF[d][sp] = f;
+    }
+    sL[d] = L;
+  }
+  __syncthreads();
+  for (int g = 0; g < G; ++g) {
+    const float* base = a.part + (size_t)(kvh * G + g) * kSplits * (kHd + 2) + 2 + d;
+    float vals[kSplits];
+#pragma unroll
+    for (int sp = 0; sp < kSplits; ++sp) vals[sp] = __ldcg(base + sp * (kHd + 2));
+    float O = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < kSplits; ++sp) O = fmaf(vals[sp], sF[g][sp], O);
+    a.out[(kvh * G + g) * kHd + d] = __fdiv_rn(O, sL[g]);
+  }
+  if (d == 0) a.ticket[kvh] = 0;
+}
+
+// ------------------------------------------------------------------ host side
+namespace {
+constexpr int kStageBytes = 24 * 1024;
+constexpr int kSmemBudget = 112 * 1024;  // two decode kernels co-reside on one SM
+
+struct MvPlan {
+  int grid, rows_per_cta, tile_rows, stages, tile_bytes;
+  size_t smem;
+};
+
+MvPlan plan_mv(int N, int K, bool int8, int num_sms) {
+  MvPlan p{};
+  const int row_bytes = K * (int8 ? 1 : 2);
+  int rpc = (N + num_sms - 1) / num_sms;
+  rpc += rpc & 1;
+  p.rows_per_cta = rpc;
+  p.grid = (N + rpc - 1) / rpc;
+  int cta_bytes = rpc * row_bytes;
+  int ntiles = (cta_bytes + kStageBytes - 1) / kStageBytes;
+  int tr = (rpc + ntiles - 1) / ntiles;
+  tr += tr & 1;
+  if (tr * row_bytes > kStageBytes && tr > 2) tr = std::max(2, (kStageBytes / row_bytes) & ~1);
+  p.tile_rows = tr;
+  p.tile_bytes = (tr * row_bytes + 127) & ~127;
+  ntiles = (rpc + tr - 1) / tr;
+  size_t fixed = (size_t)K * 9 + 64 + 16 * 8 + (size_t)rpc * 4;
+  int st = (int)((kSmemBudget - fixed) / p.tile_bytes);
+  p.stages = std::max(1, std::min(std::min(st, 4), ntiles));
+  p.smem = (size_t)p.stages * p.tile_bytes + fixed;
+  return p;
+}
+
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+template <int EPI>
+void mv(bool int8, MvArgs m, int num_sms, cudaStream_t s) {
+  MvPlan p = plan_mv(m.N, m.K, int8, num_sms);
+  m.rows_per_cta = p.rows_per_cta;
+  m.tile_rows = p.tile_rows;
+  m.stages = p.stages;
+  m.tile_bytes = p.tile_bytes;
+  if (int8) launch_pdl(mv_kernel<true, EPI>, dim3(p.grid), dim3(256), p.smem, s, m);
+  else launch_pdl(mv_kernel<false, EPI>, dim3(p.grid), dim3(256), p.smem, s, m);
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+}  // namespace
+
+void decode_kernels_init() {
+  const int kMax = 200 * 1024;
+  cudaFuncSetAttribute(mv_kernel<true, MV_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+  cudaFuncSetAttribute(mv_kernel<true, MV_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+  cudaFuncSetAttribute(mv_kernel<true, MV_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+  cudaFuncSetAttribute(mv_kernel<true, MV_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+  cudaFuncSetAttribute(mv_kernel<false, MV_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+  cudaFuncSetAttribute(mv_kernel<false, MV_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+  cudaFuncSetAttribute(mv_kernel<false, MV_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+  cudaFuncSetAttribute(mv_kernel<false, MV_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+}
+
+void decode_step(const DecodeArgs& a, cudaStream_t s) {
+  static thread_local int cached_dev = -1, cached_sms = 148;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != cached_dev) {
+    cached_dev = dev;
+    cached_sms = sm_count();
+  }
+  const int nsm = cached_sms;
+  const int qd = a.q_heads * kHd, kvd = a.kv_heads * kHd;
+  for (int l = 0; l < a.layers; ++l) {
+    MvArgs m{};
+    m.eps = a.eps;
+    m.err = a.err;
+    m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 0;
+    // QKV (+ token embedding gather on layer 0, input RMSNorm fused)
+    m.x = a.x;
+    if (l == 0) {
+      m.embed = a.embed;
+      m.st = a.st;
+      m.x_out = a.x;
+    }
+    m.norm_w = a.n1[l]; m.K = a.hidden; m.N = qd + 2 * kvd;
+    m.W = a.w_qkv[l]; m.ws = a.s_qkv[l]; m.out = a.qkv;
+    mv<MV_STORE>(a.int8, m, nsm, s);
+    if (a.on_launch) a.on_launch(a.hook_ctx, 0);
+    AttnArgs at{a.qkv, a.q_heads, a.kv_heads, a.qn[l], a.kn[l], a.eps, a.rope_cos, a.rope_sin,
+                a.k_cache + (size_t)l * a.kv_heads * a.max_seq * kHd,
+                a.v_cache + (size_t)l * a.kv_heads * a.max_seq * kHd, a.max_seq, 1.0f / sqrtf((float)kHd), a.st,
+                a.part, a.ticket, a.attn, a.tl, a.tl_count};
+    launch_pdl(attn_kernel, dim3(a.kv_heads, kSplits), dim3(128), 0, s, at);
+    if (a.on_launch) a.on_launch(a.hook_ctx, 1);
+    // O projection + residual
+    m = MvArgs{};
+    m.eps = a.eps; m.err = a.err;
+    m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 2;
+    m.x = a.attn; m.K = qd; m.N = a.hidden;
+    m.W = a.w_o[l]; m.ws = a.s_o[l]; m.out = a.x; m.resid = a.x;
+    mv<MV_RESID>(a.int8, m, nsm, s);
+    if (a.on_launch) a.on_launch(a.hook_ctx, 2);
+    // gate/up (post-attention RMSNorm fused) + SwiGLU
+    m = MvArgs{};
+    m.eps = a.eps; m.err = a.err;
+    m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 3;
+    m.x = a.x; m.norm_w = a.n2[l]; m.K = a.hidden; m.N = 2 * a.inter;
+    m.W = a.w_gu[l]; m.ws = a.s_gu[l]; m.out = a.ffn;
+    mv<MV_SWIGLU>(a.int8, m, nsm, s);
+    if (a.on_launch) a.on_launch(a.hook_ctx, 3);
+    // down projection + residual
+    m = MvArgs{};
+    m.eps = a.eps; m.err = a.err;
+    m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 4;
+    m.x = a.ffn; m.K = a.inter; m.N = a.hidden;
+    m.W = a.w_down[l]; m.ws = a.s_down[l]; m.out = a.x; m.resid = a.x;
+    mv<MV_RESID>(a.int8, m, nsm, s);
+    if (a.on_launch) a.on_launch(a.hook_ctx, 4);
+  }
+  MvArgs m{};
+  m.eps = a.eps; m.err = a.err;
+  m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 5;
+  m.x = a.x; m.norm_w = a.final_norm; m.K = a.hidden; m.N = a.vocab;
+  m.W = a.lm_w; m.ws = a.lm_s;
+  m.am_part = a.am_part; m.am_ticket = a.am_ticket; m.st = a.st; m.tokens = a.tokens; m.forced = a.forced;
+  m.logits = a.logits;
+  mv<MV_ARGMAX>(a.int8, m, nsm, s);
+  if (a.on_launch) a.on_launch(a.hook_ctx, 5);
+}
+
+}  // namespace qasr

@@ -78,6 +78,8 @@ bool Engine::load(const std::string& dir, int device, bool trunc_quant) {
   if (!st.open(dir)) return false;
   if (!detect_config(st, cfg_)) return false;
   CUDA_OK(cudaSetDevice(device), false);
+  decode_kernels_init();
+  enc_kernels_init();
   CUDA_OK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), false);
   CUDA_OK(cudaEventCreate(&ev0_), false);
   CUDA_OK(cudaEventCreate(&ev1_), false);
@@ -278,10 +280,11 @@ bool Engine::load(const std::string& dir, int device, bool trunc_quant) {
   CUDA_OK(cudaMallocHost(&hstate_, sizeof(StepState)), false);
   if (!dx_.alloc(h) || !dqkv_.alloc(qd + 2 * kvd) || !dattn_.alloc(qd) || !dffn_.alloc(inter) ||
       !dpart_.alloc((size_t)c.dec_heads * 16 * 130) || !dticket_.alloc(c.dec_kv_heads) || !dam_ticket_.alloc(1) ||
-      !dam_part_.alloc(4096) || !dstate_.alloc(1) || !dlogits_.alloc(c.vocab_size))
+      !dam_part_.alloc(4096) || !dstate_.alloc(1) || !dlogits_.alloc(c.vocab_size) || !derr_.alloc(1))
     return false;
   CUDA_OK(cudaMemset(dticket_.p, 0, c.dec_kv_heads * sizeof(int)), false);
   CUDA_OK(cudaMemset(dam_ticket_.p, 0, sizeof(int)), false);
+  CUDA_OK(cudaMemset(derr_.p, 0, sizeof(int)), false);
   for (auto& L : dec_layers_) {
     pn1_.push_back(L.n1);
     pn2_.push_back(L.n2);
@@ -587,7 +590,11 @@ DecodeArgs Engine::dargs(const int* forced, float* logits) {
   a.k_cache = kc_.p; a.v_cache = vc_.p; a.layers = c.dec_layers;
   a.x = dx_.p; a.qkv = dqkv_.p; a.attn = dattn_.p; a.ffn = dffn_.p; a.part = dpart_.p; a.ticket = dticket_.p;
   a.am_ticket = dam_ticket_.p; a.am_part = dam_part_.p; a.st = dstate_.p; a.tokens = dtokens_.p;
-  a.forced = forced; a.logits = logits;
+  a.forced = forced; a.logits = logits; a.err = derr_.p;
+  if (timeline_) {
+    a.tl = dtl_.p;
+    a.tl_count = dtl_count_.p;
+  }
   return a;
 }
 
@@ -607,8 +614,17 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     htokens_cap_ = std::max(max_steps, 2048);
     CUDA_OK(cudaMallocHost(&htokens_, htokens_cap_ * sizeof(int)), false);
   }
+  if (timeline_) {
+    size_t need = (size_t)max_steps * (cfg_.dec_layers * 5 + 1) * 4 + 64;
+    if (dtl_.n < need) {
+      if (!dtl_.alloc(need)) return false;
+      graph_ok_ = false;
+    }
+    if (!dtl_count_.alloc(1)) return false;
+    CUDA_OK(cudaMemsetAsync(dtl_count_.p, 0, sizeof(int), stream_), false);
+  }
   cudaEventRecord(ev0_, stream_);
-  const bool direct = forced || logits || !use_graph;
+  const bool direct = forced || logits || !use_graph || profile;
   if (direct) {
     // Teacher-forced / logits-recording path: plain launches, one step at a time.
     if (forced) {
@@ -620,9 +636,20 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
               false);
     }
     DecodeArgs a = dargs(forced ? dforced_.p : nullptr, logits ? dlogits_.p : nullptr);
+    if (profile) {
+      a.on_launch = [](void* ctx, int kind) {
+        Engine* e = (Engine*)ctx;
+        cudaEvent_t ev;
+        cudaEventCreate(&ev);
+        cudaEventRecord(ev, e->stream_);
+        e->prof_ev_.push_back({kind, ev});
+      };
+      a.hook_ctx = this;
+    }
     const int V = a.vocab;
     if (logits) logits->resize((size_t)max_steps * V);
     for (int i = 0; i < max_steps; ++i) {
+      if (profile) a.on_launch(this, -1);
       decode_step(a, stream_);
       if (logits)
         CUDA_OK(cudaMemcpyAsync(logits->data() + (size_t)i * V, dlogits_.p, (size_t)V * 4, cudaMemcpyDeviceToHost,
@@ -633,6 +660,16 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     CUDA_OK(cudaStreamSynchronize(stream_), false);
     CUDA_OK(cudaGetLastError(), false);
     out.assign(htokens_, htokens_ + max_steps);
+    for (size_t i = 1; i < prof_ev_.size(); ++i) {
+      int k = prof_ev_[i].first;
+      if (k < 0) continue;
+      float ms = 0;
+      cudaEventElapsedTime(&ms, prof_ev_[i - 1].second, prof_ev_[i].second);
+      prof_ms[k] += ms;
+      prof_n[k] += 1;
+    }
+    for (auto& pe : prof_ev_) cudaEventDestroy(pe.second);
+    prof_ev_.clear();
   } else {
     if (!graph_ok_) {
       if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
@@ -684,6 +721,22 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     CUDA_OK(cudaStreamSynchronize(stream_), false);
     for (auto e : evs) cudaEventDestroy(e);
     CUDA_OK(cudaGetLastError(), false);
+  }
+  {
+    int herr = 0;
+    CUDA_OK(cudaMemcpy(&herr, derr_.p, sizeof(int), cudaMemcpyDeviceToHost), false);
+    if (herr) {
+      cudaMemset(derr_.p, 0, sizeof(int));
+      set_error("decode: a device-side wait timed out (code " + std::to_string(herr) + ")");
+      return false;
+    }
+  }
+  if (timeline_) {
+    int cnt = 0;
+    CUDA_OK(cudaMemcpy(&cnt, dtl_count_.p, sizeof(int), cudaMemcpyDeviceToHost), false);
+    cnt = std::min<int>(cnt, (int)(dtl_.n / 4));
+    last_timeline.resize((size_t)cnt * 4);
+    CUDA_OK(cudaMemcpy(last_timeline.data(), dtl_.p, last_timeline.size() * 8, cudaMemcpyDeviceToHost), false);
   }
   // KV length after the steps the caller consumes (extra speculative steps are ignored).
   kv_len_ = start_pos + (int)out.size();

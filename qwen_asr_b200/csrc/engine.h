@@ -69,6 +69,14 @@ class Engine {
   DecodeMode decode_mode() const { return mode_; }
   StagePerf perf;
   bool use_graph = true;
+  // Per-op decode profiler (CUDA events around every launch; disables the graph).
+  bool profile = false;
+  double prof_ms[6] = {0, 0, 0, 0, 0, 0};
+  long prof_n[6] = {0, 0, 0, 0, 0, 0};
+  std::vector<std::pair<int, cudaEvent_t>> prof_ev_;
+  // Kernel timeline (in-kernel %globaltimer stamps; graph-compatible).
+  void set_timeline(bool on) { timeline_ = on; graph_ok_ = false; }
+  std::vector<unsigned long long> last_timeline;
 
   // Debug: final hidden of prefill rows (after the last layer, before final norm).
   bool copy_prefill_hidden(std::vector<float>& out, int rows);
@@ -116,9 +124,12 @@ class Engine {
   bool ensure_kv(int needed);
   // decode scratch
   DevBuf<float> dx_, dqkv_, dattn_, dffn_, dpart_, dlogits_;
-  DevBuf<int> dticket_, dam_ticket_, dtokens_, dforced_;
+  DevBuf<int> dticket_, dam_ticket_, dtokens_, dforced_, derr_;
   DevBuf<unsigned long long> dam_part_;
   DevBuf<StepState> dstate_;
+  bool timeline_ = false;
+  DevBuf<unsigned long long> dtl_;
+  DevBuf<int> dtl_count_;
   StepState* hstate_ = nullptr;  // pinned
   int* htokens_ = nullptr;       // pinned
   int htokens_cap_ = 0;

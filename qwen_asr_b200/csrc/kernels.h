@@ -130,7 +130,19 @@ struct DecodeArgs {
   int* tokens;     // [max tokens] output ids
   const int* forced;  // teacher-forced ids or nullptr
   float* logits;   // optional [vocab] f32 logits of the last step (debug)
+  int* err;        // device error flag (bounded waits that gave up)
+  // Optional host hook called after each launch (kind: 0 qkv, 1 attention, 2 o-proj,
+  // 3 gate/up, 4 down, 5 lm_head) - used by the per-op profiler.
+  void (*on_launch)(void* ctx, int kind) = nullptr;
+  void* hook_ctx = nullptr;
+  // Optional timeline: CTA 0 of every kernel appends {kind, t_entry, t_after_wait, t_exit}
+  // (%globaltimer ns) at tl[4 * atomicAdd(tl_count, 1)].
+  unsigned long long* tl = nullptr;
+  int* tl_count = nullptr;
 };
+// Per-device kernel attributes (dynamic shared memory limits); call once per device.
+void decode_kernels_init();
+void enc_kernels_init();
 // Enqueues one full decode step (embedding -> layers -> lm_head argmax).
 void decode_step(const DecodeArgs& a, cudaStream_t s);
 

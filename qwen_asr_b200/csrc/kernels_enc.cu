@@ -241,15 +241,14 @@ __global__ void __launch_bounds__(256) window_attention_kernel(const float* __re
   }
 }
 
+void enc_kernels_init() {
+  cudaFuncSetAttribute(window_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+}
+
 void window_attention(const float* qkv, float* out, int T, int d, int n_heads, const int* win_starts, int n_windows,
                       int max_win, float scale, cudaStream_t s) {
   (void)T;
   size_t smem = (size_t)(2 * max_win * 65 + 8 * max_win + 8 * kEncHd) * sizeof(float);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(window_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr_set = true;
-  }
   dim3 grid(n_windows, n_heads);
   window_attention_kernel<<<grid, 256, smem, s>>>(qkv, out, d, win_starts, scale);
 }
