@@ -1,0 +1,360 @@
+#!/usr/bin/env python
+"""Benchmark of the Qwen3-ASR transcription path on B200 (one process per GPU).
+
+A step is one offline transcription of one clip (mel -> encoder -> prefill -> greedy
+decode) on each GPU. Default workload ("C2"): Qwen3-ASR-0.6B,
+28.2 s seeded synthetic clip, int8 decode of 256 tokens (EOS ignored), weights
+random-init in the reference's safetensors layout. Every rank transcribes its own clip
+(replicas, weak scaling, no collective on the data path; NCCL only carries the
+barrier and the max-over-ranks timing).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c1|c2|c3]
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: (preset, samples, audio seed, decode tokens, decode mode, weight seed)
+    "c1": ("0.6b", 451200, 1, 128, "bf16", 0),
+    "c2": ("0.6b", 451200, 1, 256, "int8", 0),
+    "c3": ("1.7b", 960000, 2, 512, "bf16", 1),
+}
+PRESET_DIMS = {"0.6b": (1024, 3072), "1.7b": (2048, 6144)}  # dec hidden, intermediate
+N_LAYERS, KV_HEADS, HEAD_DIM, VOCAB, Q_DIM = 28, 8, 128, 151936, 2048
+
+
+def decode_step_bytes(preset: str, mode: str, pos: float) -> float:
+    """Algorithmic HBM bytes of one decode step: every decoder weight once (int8 or bf16),
+    the int8 row scales, and the f32 KV cache rows 0..pos of every layer."""
+    h, inter = PRESET_DIMS[preset]
+    per_layer = (Q_DIM + 2 * KV_HEADS * HEAD_DIM) * h + h * Q_DIM + 2 * inter * h + h * inter
+    n_w = N_LAYERS * per_layer + VOCAB * h
+    esz = 1 if mode == "int8" else 2
+    scales = (N_LAYERS * (Q_DIM + 2 * KV_HEADS * HEAD_DIM + h + 2 * inter + h) + VOCAB) * 4 if mode == "int8" else 0
+    kv = N_LAYERS * KV_HEADS * HEAD_DIM * 4 * 2 * (pos + 1)
+    return n_w * esz + scales + kv
+
+
+def measured_hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic():
+    """Per-step DRAM bytes of the decode kernels from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "decode_step_int8_c2.md")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_step:"):
+                return float(line.split(":")[1].strip())
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.seek(0)
+        rows = [r.split(", ") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(world, v: float, local: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local}")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def model_dir(preset, seed, world, rank, local):
+    from qwen_asr_b200 import synth
+    d = os.path.join(os.environ.get("QASR_BENCH_DIR", "/tmp/qasr_bench"), f"{preset}-s{seed}")
+    if rank == 0:
+        synth.write_model(d, preset, seed, device="cpu")  # identical weights for both arms
+    barrier(world)
+    return d
+
+
+# ------------------------------------------------------------------------ CPU baseline
+def cpu_sample(preset, n_samples, seed, tokens, mode, wseed, model_path, n_decode=2, model=None):
+    """One bounded sample of the workload on the host with the oracle (the numpy
+    restatement of the reference's CPU path): mel + encoder + prefill of the full clip,
+    then `n_decode` greedy decode steps; decode time is extrapolated to `tokens`.
+    Returns (audio-sec/sec, seconds measured, model)."""
+    from oracle import qwen_oracle as O
+    from qwen_asr_b200 import synth
+    if model is None:
+        model = O.Model(model_path, decode_mode=mode)
+    x = synth.synth_audio(n_samples, seed)
+    t0 = time.perf_counter()
+    mel = O.mel_spectrogram(x)
+    enc = model.encode(mel)
+    ctx = O.Ctx.__new__(O.Ctx)
+    ctx.model, ctx.tok, ctx.prompt, ctx.force_language = model, None, None, None
+    rows = O.prompt_rows(ctx, enc)
+    dec = O.Decoder(model)
+    dec.prefill(rows[:-1])
+    t1 = time.perf_counter()
+    tok = dec.forward(rows[-1])
+    for _ in range(n_decode - 1):
+        tok = dec.forward(model.embed(tok))
+    t2 = time.perf_counter()
+    per_tok = (t2 - t1) / n_decode
+    total = (t1 - t0) + tokens * per_tok
+    return (n_samples / 16000.0) / total, t2 - t0, model
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        return max(int(i.get("num_threads", 1)) for i in threadpool_info()) or os.cpu_count()
+    except Exception:
+        return os.cpu_count()
+
+
+# ------------------------------------------------------------------------ main arms
+def run_reference(args, world, rank, local):
+    if rank != 0:
+        return
+    preset, n, seed, tokens, mode, wseed = CONFIGS[args.config]
+    from qwen_asr_b200 import synth
+    d = os.path.join(os.environ.get("QASR_BENCH_DIR", "/tmp/qasr_bench"), f"{preset}-s{wseed}")
+    synth.write_model(d, preset, wseed, device="cpu")  # same file as the GPU arm writes
+    model = None
+    for _ in range(args.warmup):
+        _, _, model = cpu_sample(preset, n, seed, tokens, mode, wseed, d, model=model)
+    vals, secs = [], []
+    for _ in range(args.steps):
+        v, s, model = cpu_sample(preset, n, seed, tokens, mode, wseed, d, model=model)
+        vals.append(v)
+        secs.append(s)
+    value = statistics.mean(vals)
+    sample = (f"per step: mel+encoder+prefill of the full {n / 16000:.1f} s clip + 2 decode steps, decode "
+              f"extrapolated to {tokens} tokens")
+    line = {
+        "impl": "reference", "metric": "audio-sec/sec", "value": round(value, 4), "unit": "audio-s/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000 * (n / 16000.0) / value, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8+f32" if mode == "int8" else "bf16+f32", "data": "synthetic",
+        "config": config_dict(args.config, world),
+        "cpu_baseline": {"value": round(value, 4), "unit": "audio-s/s", "cores": cpu_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference = numpy restatement of the reference CPU path (oracle/); the Rust reference cannot be "
+                "built here (no cargo) and its int8 decode is unimplemented on x86_64",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(name, world):
+    preset, n, seed, tokens, mode, wseed = CONFIGS[name]
+    return {"workload": f"{name.upper()}: Qwen3-ASR-{preset.upper()} offline transcription of a {n / 16000:.1f} s "
+                        f"clip, {mode} decode of {tokens} tokens (EOS ignored), one clip per GPU",
+            "clip_sec": n / 16000.0, "decode_tokens": tokens, "decode_weights": mode,
+            "l2": "no flush: each step streams >1 GB of weights, far larger than the 126 MB L2",
+            "parallelism": f"replicas x{world}"}
+
+
+def run_ours(args, world, rank, local):
+    import numpy as np
+    import torch
+    import qwen_asr_b200 as Q
+    from qwen_asr_b200 import synth
+
+    preset, n, seed, tokens, mode, wseed = CONFIGS[args.config]
+    if args.tokens:
+        tokens = args.tokens
+    d = model_dir(preset, wseed, world, rank, local)
+    torch.cuda.set_device(local)
+    eng = Q.Engine(d, device=local)
+    eng.set_decode_mode(mode)
+    eng.set_force_n_tokens(tokens)
+    x = synth.synth_audio(n, seed + rank)
+    x_dev = torch.from_numpy(x).to(f"cuda:{local}")
+    x_pin = torch.from_numpy(x).pin_memory()
+    stream = torch.cuda.ExternalStream(eng.cuda_stream(), device=f"cuda:{local}")
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        eng.transcribe_device(x_dev.data_ptr(), n)
+
+    # ---- device-resident timed region
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    l0 = eng.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    dec_ms, steps_done = 0.0, 0
+    for _ in range(args.steps):
+        eng.transcribe_device(x_dev.data_ptr(), n)
+        p = eng.perf()
+        dec_ms += p["gpu_decode_ms"]
+        steps_done += int(p["decode_steps"])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = eng.launch_count() - l0
+    clk = clocks.stop()
+    barrier(world)
+    ms = max_over_ranks(world, e0.elapsed_time(e1), local)
+    ms_step = ms / args.steps
+    value = world * args.steps * (n / 16000.0) / (ms / 1000.0)
+
+    # ---- end to end through the C ABI with host buffers (H2D inside the timed region)
+    barrier(world)
+    torch.cuda.synchronize()
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0.record(stream)
+    lib = Q.lib()
+    host_ptr = ctypes.cast(x_pin.data_ptr(), Q._F32P)  # pinned host samples
+    for _ in range(args.steps):
+        Q._take_string(lib.qwen_asr_transcribe_pcm(eng._h, host_ptr, n))
+    h1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(world, h0.elapsed_time(h1), local)
+    e2e_value = world * args.steps * (n / 16000.0) / (e2e_ms / 1000.0)
+
+    # ---- roofline of the int8 decode step (HBM-bound), timed by the engine's CUDA events
+    perf = eng.perf()
+    step_ms = dec_ms / max(steps_done, 1)
+    # prompt rows = 9 prefix + T_enc + 6 suffix (transcribe.rs:96-169)
+    frames = n // 160
+    def cw(w):
+        return (w + 2 - 3) // 2 + 1
+    t_enc = (frames // 100) * 13 + (cw(cw(cw(frames % 100))) if frames % 100 else 0)
+    prompt = 9 + t_enc + 6
+    avg_pos = prompt - 1 + tokens / 2.0
+    bytes_step = decode_step_bytes(preset, mode, avg_pos)
+    achieved = bytes_step / (step_ms / 1000.0) / 1e9
+    peak, peak_kind = measured_hbm_peak()
+    traffic = profile_traffic()
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "kernel": f"decode step ({mode} weight matvec chain + attention + lm_head argmax)",
+                "algorithmic_bytes_per_step": int(bytes_step), "avg_step_ms": round(step_ms, 4),
+                "peak_source": peak_kind}
+
+    line = None
+    if rank == 0:
+        cb = None
+        if not args.no_cpu_baseline:
+            try:
+                v1, s1, model = cpu_sample(preset, n, seed, tokens, mode, wseed, d)
+                cb = {"value": round(v1, 4), "unit": "audio-s/s", "cores": cpu_threads(), "kind": "port",
+                      "sample": f"mel+encoder+prefill of the full {n / 16000:.1f} s clip + 2 decode steps on the host "
+                                f"({s1:.1f} s), decode extrapolated to {tokens} tokens"}
+            except Exception as ex:  # the baseline must not break the GPU line
+                cb = {"value": None, "unit": "audio-s/s", "cores": cpu_threads(), "kind": "port",
+                      "sample": f"failed: {ex}"}
+        line = {
+            "metric": "audio-sec/sec", "value": round(value, 3), "unit": "audio-s/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8+f32" if mode == "int8" else "bf16+f32",
+            "data": "synthetic: seeded random-init weights in the reference safetensors layout + seeded speech-like audio",
+            "config": config_dict(args.config, world),
+            "decode_tok_s_per_gpu": round(1000.0 / step_ms, 1),
+            "stage_ms": {k: round(perf[k], 3) for k in ("gpu_mel_ms", "gpu_enc_ms", "gpu_prefill_ms", "gpu_decode_ms")},
+            "e2e": {"value": round(e2e_value, 3), "unit": "audio-s/s", "h2d_bytes_per_step": 4 * n,
+                    "d2h_bytes_per_step": 4 * tokens},
+            "gpu_launches": int(launches),
+            "roofline": roofline,
+            "cpu_baseline": cb,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    barrier(world)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--tokens", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, world, rank, local)
+    else:
+        run_ours(args, world, rank, local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -36,6 +36,13 @@ void qwen_asr_set_profile(QwenAsrEngine* engine, int32_t on);
 /* Accumulated GPU ms and launch counts per op: qkv, attention, o_proj, gate_up, down,
  * lm_head_argmax. Returns 6. */
 int32_t qwen_asr_profile_report(QwenAsrEngine* engine, double* ms, int64_t* counts, int32_t cap);
+/* Offline transcription of f32 16 kHz samples already in this engine's device memory
+ * (same result as qwen_asr_transcribe_pcm on the same samples). */
+char* qwen_asr_transcribe_device(QwenAsrEngine* engine, const float* d_samples, int32_t n_samples);
+/* The engine's CUDA stream (cudaStream_t): every kernel of the engine runs on it. */
+void* qwen_asr_cuda_stream(QwenAsrEngine* engine);
+/* Number of kernels this engine has enqueued so far (graph replays count their nodes). */
+int64_t qwen_asr_launch_count(QwenAsrEngine* engine);
 /* Kernel timeline of the next decode calls: CTA 0 of every decode kernel records
  * {kind, t_entry, t_after_dependency_wait, t_exit} (GPU %globaltimer, ns); kinds as in
  * qwen_asr_profile_report. Works with the CUDA-graph path. */

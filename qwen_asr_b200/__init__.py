@@ -54,6 +54,9 @@ SIGNATURES = {
     "qwen_asr_last_tokens": (C.c_int32, [_VP, C.c_int32, _I32P, C.c_int32]),
     "qwen_asr_set_profile": (None, [_VP, C.c_int32]),
     "qwen_asr_set_timeline": (None, [_VP, C.c_int32]),
+    "qwen_asr_transcribe_device": (_VP, [_VP, C.c_void_p, C.c_int32]),
+    "qwen_asr_cuda_stream": (C.c_void_p, [_VP]),
+    "qwen_asr_launch_count": (C.c_int64, [_VP]),
     "qwen_asr_get_timeline": (C.c_int64, [_VP, C.POINTER(C.c_uint64), C.c_int64]),
     "qwen_asr_profile_report": (C.c_int32, [_VP, C.POINTER(C.c_double), _I64P, C.c_int32]),
     "qwen_asr_last_segments": (C.c_int32, [_VP]),
@@ -179,6 +182,16 @@ class Engine:
         lib().qwen_asr_profile_report(self._h, ms, n, 6)
         names = ["qkv", "attention", "o_proj", "gate_up", "down", "lm_head_argmax"]
         return {k: (ms[i], n[i]) for i, k in enumerate(names)}
+
+    def transcribe_device(self, d_ptr: int, n: int) -> str | None:
+        """Samples already in this engine's device memory (e.g. a torch CUDA tensor's data_ptr())."""
+        return _take_string(lib().qwen_asr_transcribe_device(self._h, C.c_void_p(d_ptr), n))
+
+    def cuda_stream(self) -> int:
+        return lib().qwen_asr_cuda_stream(self._h) or 0
+
+    def launch_count(self) -> int:
+        return lib().qwen_asr_launch_count(self._h)
 
     def set_timeline(self, on: bool):
         lib().qwen_asr_set_timeline(self._h, int(on))

@@ -209,6 +209,22 @@ int32_t qwen_asr_profile_report(QwenAsrEngine* e, double* ms, int64_t* counts, i
   return 6;
 }
 
+char* qwen_asr_transcribe_device(QwenAsrEngine* e, const float* d_samples, int32_t n_samples) {
+  if (!e || !d_samples || n_samples <= 0) return nullptr;
+  std::string out;
+  try {
+    if (!e->ctx.transcribe_device(d_samples, (size_t)n_samples, out)) return nullptr;
+  } catch (const std::exception& ex) {
+    qasr::set_error(std::string("transcribe: ") + ex.what());
+    return nullptr;
+  }
+  return to_c_string(out);
+}
+
+void* qwen_asr_cuda_stream(QwenAsrEngine* e) { return e ? (void*)e->ctx.eng.stream() : nullptr; }
+
+int64_t qwen_asr_launch_count(QwenAsrEngine* e) { return e ? (int64_t)e->ctx.eng.launches : -1; }
+
 void qwen_asr_set_timeline(QwenAsrEngine* e, int32_t on) {
   if (e) e->ctx.eng.set_timeline(on != 0);
 }

@@ -359,6 +359,7 @@ int Engine::mel(const float* samples, int n, bool on_device) {
       !power_.alloc((size_t)n_frames * 208) || !mel_.alloc((size_t)n_frames * kMelBins) || !gmax_.alloc(1))
     return 0;
   cudaEventRecord(ev0_, stream_);
+  launches += 6;
   mel_frames(dsamp, n, n_frames, hann_, frames_.p, stream_);
   GemmArgs g;
   g.M = n_frames; g.N = 408; g.K = kNfft;
@@ -409,6 +410,7 @@ int Engine::encode(const float* d_mel, int F) {
       !enc_.alloc((size_t)T * c.enc_output_dim))
     return 0;
   cudaEventRecord(ev0_, stream_);
+  launches += 7 * (long)groups.size() + 7 * (long)enc_layers_.size() + 3;
   int tok = 0;
   for (auto& g : groups) {
     int w1 = cw(g.w), w2 = cw(w1), w3 = cw(w2);
@@ -490,6 +492,7 @@ bool Engine::prefill_ids(const std::vector<int>& ids, const float* d_enc, int st
   if (!ids_.alloc(n) || !px_.alloc((size_t)n * h)) return false;
   CUDA_OK(cudaMemcpyAsync(ids_.p, ids.data(), n * 4, cudaMemcpyHostToDevice, stream_), false);
   gather_embeds(ids_.p, n, embed_, d_enc, h, px_.p, stream_);
+  launches += 1;
   return run_prefill(n, start_pos);
 }
 
@@ -513,6 +516,7 @@ bool Engine::run_prefill(int n, int start_pos) {
       !patt_.alloc((size_t)std::max(S, 1) * qd) || !pmid_.alloc((size_t)std::max(S, 1) * inter))
     return false;
   cudaEventRecord(ev0_, stream_);
+  if (S > 0) launches += 8 * (long)c.dec_layers;
   float* x = px_.p + (size_t)start_pos * h;
   const float scale = 1.0f / sqrtf(128.f);
   for (int l = 0; l < c.dec_layers && S > 0; ++l) {
@@ -660,6 +664,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     CUDA_OK(cudaStreamSynchronize(stream_), false);
     CUDA_OK(cudaGetLastError(), false);
     out.assign(htokens_, htokens_ + max_steps);
+    launches += (long)max_steps * (5 * cfg_.dec_layers + 1);
     for (size_t i = 1; i < prof_ev_.size(); ++i) {
       int k = prof_ev_[i].first;
       if (k < 0) continue;
@@ -719,6 +724,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
       if (checked >= max_steps) stop = true;
     }
     CUDA_OK(cudaStreamSynchronize(stream_), false);
+    launches += (long)launched * (5 * cfg_.dec_layers + 1);
     for (auto e : evs) cudaEventDestroy(e);
     CUDA_OK(cudaGetLastError(), false);
   }

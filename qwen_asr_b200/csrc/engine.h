@@ -69,6 +69,7 @@ class Engine {
   DecodeMode decode_mode() const { return mode_; }
   StagePerf perf;
   bool use_graph = true;
+  long launches = 0;  // kernels enqueued by this engine (graph replays count their nodes)
   // Per-op decode profiler (CUDA events around every launch; disables the graph).
   bool profile = false;
   double prof_ms[6] = {0, 0, 0, 0, 0, 0};

@@ -90,11 +90,11 @@ bool Ctx::encode_window(const float* samples, size_t n, std::vector<float>& enc,
 
 // transcribe.rs:63-247
 bool Ctx::transcribe_segment(const float* samples, size_t n, const std::vector<int>* past, std::string& text,
-                             int& n_text) {
+                             int& n_text, bool on_device) {
   double t0 = now_ms();
   n_text = 0;
   StagePerf before = eng.perf;
-  int F = eng.mel(samples, (int)n, false);
+  int F = eng.mel(samples, (int)n, on_device);
   if (F <= 0) return false;
   int T = eng.encode(eng.mel_buf(), F);
   if (T <= 0) return false;
@@ -167,6 +167,21 @@ bool Ctx::transcribe_audio(const std::vector<float>& in, std::string& result) {
     result += st;
   }
   return true;
+}
+
+bool Ctx::transcribe_device(const float* d_samples, size_t n, std::string& out) {
+  if (segment_sec > 0.0f || skip_silence) {
+    // Segmentation and silence compaction are host algorithms: bring the samples back.
+    std::vector<float> h(n);
+    if (cudaMemcpy(h.data(), d_samples, n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return false;
+    return transcribe_audio(h, out);
+  }
+  reset_perf();
+  last_tokens.clear();
+  perf_audio_ms = 1000.0 * (double)n / kSampleRate;
+  if (!prepare_prompt_tokens()) return false;
+  int nt;
+  return transcribe_segment(d_samples, n, nullptr, out, nt, true);
 }
 
 // Streaming tail-repetition detector (transcribe.rs:36-55).

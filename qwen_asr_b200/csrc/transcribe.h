@@ -63,8 +63,10 @@ class Ctx {
   }
   bool prepare_prompt_tokens();
   bool transcribe_audio(const std::vector<float>& samples, std::string& out);
+  // Offline transcription of samples already resident in device memory.
+  bool transcribe_device(const float* d_samples, size_t n, std::string& out);
   bool transcribe_segment(const float* samples, size_t n, const std::vector<int>* past, std::string& text,
-                          int& n_text);
+                          int& n_text, bool on_device = false);
   bool stream_push_audio(const std::vector<float>& samples, StreamState& st, bool finalize, std::string& delta);
   void reset_perf();
 
