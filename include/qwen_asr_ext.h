@@ -73,6 +73,25 @@ int32_t qwen_asr_debug_encode(QwenAsrEngine* engine, const float* mel, int32_t n
 int32_t qwen_asr_debug_decode(QwenAsrEngine* engine, const float* rows, int32_t n_rows, const int32_t* forced,
                               int32_t n_steps, int32_t* out_ids, float* out_logits, float* out_hidden);
 
+/* ---- allocation-free mel front end (no counterpart in the reference) ----
+ * For callers that must not allocate device memory during a call: processes holding a
+ * fixed device-memory budget, real-time audio threads that may not block in the
+ * allocator, or hosts that forbid device allocations after start-up. Computes the same
+ * features as qwen_asr_debug_mel (mel_spectrogram, audio.rs:273-372), but from samples
+ * already in device memory into a caller-owned device buffer d_mel [F][128] (frame-major,
+ * capacity mel_cap floats), F = n_samples / 160, and keeps its intermediate buffers in one
+ * library-owned device array (about 4 MB, held on every GPU that loads the library until
+ * the process exits). It calls no cudaMalloc/cudaFree. Limit: F <= QWEN_ASR_MEL_NOALLOC_MAX_FRAMES
+ * (10 s of 16 kHz audio); longer input returns -1 with a message in qwen_asr_last_error().
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress),
+ * so make that first call before any stream capture. All calls share the one array: calls
+ * whose GPU work overlaps (other engines or threads on the same device) race and must be
+ * serialised by the caller. Runs on the engine's stream and returns after it completes;
+ * returns F or -1. */
+#define QWEN_ASR_MEL_NOALLOC_MAX_FRAMES 1000
+int32_t qwen_asr_mel_noalloc(QwenAsrEngine* engine, const float* d_samples, int32_t n_samples, float* d_mel,
+                             int64_t mel_cap);
+
 /* ---- host-only hooks (no GPU needed) ---- */
 /* QwenTokenizer::encode (tokenizer.rs:227-279): returns the id count, -2 if unencodable. */
 int32_t qwen_asr_debug_tokenize(const char* model_dir, const char* text, int32_t* out, int32_t cap);

@@ -12,14 +12,7 @@
 #include "../../include/qwen_asr_ext.h"
 #include "transcribe.h"
 
-struct QwenAsrEngine {
-  qasr::Ctx ctx;
-};
-
-struct QwenAsrStreamState {
-  qasr::StreamState state;
-  std::vector<float> audio_buf;  // the reference passes the full accumulated buffer (c_api.rs:171-175)
-};
+#include "c_api_types.h"
 
 namespace {
 // Returns a malloc'ed copy, or NULL when the text holds an interior NUL (CString::new).

@@ -51,6 +51,11 @@ class Engine {
   // Stage 2: mel (device, [F][128]) -> encoder output rows [T][dec_hidden] in enc_out(). Returns T.
   int encode(const float* d_mel, int n_frames);
   float* mel_buf() { return mel_.p; }
+  // Read-only device tables of the mel front end (Hann window, DFT matrix [408][400],
+  // mel filterbank [128][208]).
+  const float* hann_table() const { return hann_; }
+  const float* dft_table() const { return dft_; }
+  const float* mel_filter_table() const { return mel_filt_; }
   float* enc_out() { return enc_.p; }
 
   // Prompt rows: ids >= 0 are token embeddings, id = -(r+1) is encoder row r of `enc`.
