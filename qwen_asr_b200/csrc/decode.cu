@@ -6,6 +6,8 @@
 // Numerics follow the reference's int8 path exactly: per-vector activation quantisation
 // (kernels/mod.rs:1795-1802), exact int32 dot products (dp4a), then
 // (float)sum * x_scale * w_scale[row] (+ residual) (kernels/neon.rs:716-800).
+#include <cooperative_groups.h>
+
 #include "bulk.cuh"
 #include "common.h"
 #include "dev_util.cuh"
@@ -290,10 +292,15 @@ __global__ void __launch_bounds__(256, 1) mv_kernel(MvArgs a) {
 }
 
 // ------------------------------------------------------------------ attention
-// grid (kv_heads, kSplits), block 128 (one thread per head dimension). q/k RMSNorm
-// (kernels/mod.rs:1214-1240) + NeoX RoPE + KV append at `pos`, then split-K
-// online-softmax attention over positions 0..pos (kernels/mod.rs:1492-1534); the last
-// CTA of a kv head to arrive merges the split partials (arrival ticket, no spinning).
+// grid (kv_heads, kSplits) launched as clusters of kSplits CTAs (one cluster per kv
+// head), block 128 (one thread per head dimension). q/k RMSNorm (kernels/mod.rs:1214-1240)
+// + NeoX RoPE + KV append at `pos`, then split-K online-softmax attention over positions
+// 0..pos (kernels/mod.rs:1492-1534). The K/V rows of earlier positions were written by
+// earlier steps and StepState is constant within a step, so each CTA pulls its rows into
+// shared memory with cp.async.bulk BEFORE the dependency wait. The split partials are
+// merged through distributed shared memory inside the cluster (no global atomics).
+constexpr int kPrefRows = 64;  // K/V rows per CTA staged in shared memory (64 KB)
+
 struct AttnArgs {
   const float* qkv;
   int n_heads, n_kv;
@@ -307,37 +314,58 @@ struct AttnArgs {
   int max_seq;
   float scale;
   StepState* st;
-  float* part;
-  int* ticket;
   float* out;
+  int* err;
   unsigned long long* tl;
   int* tl_count;
 };
 
 __global__ void __launch_bounds__(128) attn_kernel(AttnArgs a) {
+  namespace cg = cooperative_groups;
   Timeline tline;
   tline.begin(a.tl, a.tl_count, 1);
-  __shared__ __align__(16) float hv[kMaxG + 2][kHd];  // normalised q heads, k, v
+  extern __shared__ __align__(128) float kvs[];  // K [kPrefRows][128] then V [kPrefRows][128]
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ __align__(16) float hv[kMaxG + 2][kHd];  // normalised q heads, k, v of `pos`
   __shared__ float red[4][kMaxG + 1];
   __shared__ float wm[4][kMaxG], wl[4][kMaxG];
   __shared__ __align__(16) float wo[4][kMaxG][kHd];
-  __shared__ float sM[kMaxG][kSplits], sF[kMaxG][kSplits], sL[kMaxG];
-  __shared__ int is_last;
+  __shared__ float pm[kMaxG], pl[kMaxG];           // this CTA's partial, read by cluster peers
+  __shared__ __align__(16) float po[kMaxG][kHd];
+  cg::cluster_group cluster = cg::this_cluster();
   const int kvh = blockIdx.x, split = blockIdx.y, d = threadIdx.x;
   const int warp = d >> 5, lane = d & 31;
   const int G = a.n_heads / a.n_kv;
+  // ---- before the dependency wait: everything that does not depend on this step's q/k/v
+  const int pos = a.st->pos;
+  const int total = pos + 1;
+  const int chunk = (total + kSplits - 1) / kSplits;
+  const int j0 = split * chunk, j1 = min(total, j0 + chunk);
+  const int npre = max(0, min(min(j1, pos) - j0, kPrefRows));  // rows j0..j0+npre-1, all < pos
+  float* kb = a.kc + (size_t)kvh * a.max_seq * kHd;
+  float* vb = a.vc + (size_t)kvh * a.max_seq * kHd;
+  float* ksm = kvs;
+  float* vsm = kvs + kPrefRows * kHd;
+  if (d == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    if (npre > 0) {
+      const uint32_t bytes = (uint32_t)(npre * kHd * sizeof(float));
+      mbar_expect_tx(&bar, 2 * bytes);
+      bulk_g2s(ksm, kb + (size_t)j0 * kHd, bytes, &bar);
+      bulk_g2s(vsm, vb + (size_t)j0 * kHd, bytes, &bar);
+    }
+  }
   const float qn = a.qn[d], kn = a.kn[d];
+  const float c = a.rc[(size_t)pos * (kHd / 2) + (d & 63)], sn = a.rs[(size_t)pos * (kHd / 2) + (d & 63)];
   pdl_launch_dependents();
   pdl_wait();
   tline.mark(2);
-  // Issue every independent load first.
-  const int pos = a.st->pos;
   float raw[kMaxG + 2];
 #pragma unroll
   for (int g = 0; g < kMaxG; ++g) raw[g] = g < G ? a.qkv[(kvh * G + g) * kHd + d] : 0.f;
   raw[kMaxG] = a.qkv[(a.n_heads + kvh) * kHd + d];
   raw[kMaxG + 1] = a.qkv[(a.n_heads + a.n_kv + kvh) * kHd + d];
-  const float c = a.rc[(size_t)pos * (kHd / 2) + (d & 63)], sn = a.rs[(size_t)pos * (kHd / 2) + (d & 63)];
   // One reduction pass for the G q-head norms and the k norm.
 #pragma unroll
   for (int g = 0; g <= kMaxG; ++g) {
@@ -373,18 +401,14 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs a) {
   for (int g = 0; g <= kMaxG; ++g)
     if (g < G || g == kMaxG) hv[g < G ? g : kMaxG][d] = rot[g];
   hv[kMaxG + 1][d] = raw[kMaxG + 1];
-  float* kb = a.kc + (size_t)kvh * a.max_seq * kHd;
-  float* vb = a.vc + (size_t)kvh * a.max_seq * kHd;
   if (split == 0) {
     kb[(size_t)pos * kHd + d] = rot[kMaxG];
     vb[(size_t)pos * kHd + d] = raw[kMaxG + 1];
   }
   __syncthreads();
+  if (npre > 0) mbar_wait(&bar, 0, a.err, 3);
   const float* ks = hv[kMaxG];
   const float* vs = hv[kMaxG + 1];
-  const int total = pos + 1;
-  const int chunk = (total + kSplits - 1) / kSplits;
-  const int j0 = split * chunk, j1 = min(total, j0 + chunk);
   float m[kMaxG], l[kMaxG], o[kMaxG][4];
 #pragma unroll
   for (int g = 0; g < kMaxG; ++g) {
@@ -392,15 +416,21 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs a) {
     l[g] = 0.f;
     o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
   }
-  // Keys in groups of 4 per warp so several row loads are in flight at once.
+  // Keys in groups of 4 per warp: staged rows from shared memory, the current position
+  // from `hv`, rows beyond the staging window straight from L2/HBM.
   for (int jb = j0 + warp * 4; jb < j1; jb += 16) {
     float4 kv[4], vv[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      int j = jb + u;
+      const int j = jb + u;
       if (j < j1 && j != pos) {
-        kv[u] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)j * kHd) + lane);
-        vv[u] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)j * kHd) + lane);
+        if (j - j0 < npre) {
+          kv[u] = reinterpret_cast<const float4*>(ksm + (size_t)(j - j0) * kHd)[lane];
+          vv[u] = reinterpret_cast<const float4*>(vsm + (size_t)(j - j0) * kHd)[lane];
+        } else {
+          kv[u] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)j * kHd) + lane);
+          vv[u] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)j * kHd) + lane);
+        }
       } else {
         kv[u] = *reinterpret_cast<const float4*>(&ks[lane * 4]);
         vv[u] = *reinterpret_cast<const float4*>(&vs[lane * 4]);
@@ -440,7 +470,7 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs a) {
     *reinterpret_cast<float4*>(&wo[warp][g][lane * 4]) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
   }
   __syncthreads();
-  // CTA partial per head: {M, L, O[128]} at part[((h * kSplits) + split) * 130]
+  // CTA partial per head {M, L, O[128]}, kept in this CTA's shared memory.
   for (int g = 0; g < G; ++g) {
     float M = fmaxf(fmaxf(wm[0][g], wm[1][g]), fmaxf(wm[2][g], wm[3][g]));
     float L = 0.f, O = 0.f;
@@ -450,53 +480,41 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs a) {
       L = fmaf(wl[w][g], f, L);
       O = fmaf(wo[w][g][d], f, O);
     }
-    float* pp = a.part + ((size_t)(kvh * G + g) * kSplits + split) * (kHd + 2);
-    pp[2 + d] = O;
+    po[g][d] = O;
     if (d == 0) {
-      pp[0] = M;
-      pp[1] = L;
+      pm[g] = M;
+      pl[g] = L;
     }
   }
-  __threadfence();
-  __syncthreads();
-  if (d == 0) is_last = (atomicAdd(&a.ticket[kvh], 1) == kSplits - 1);
-  __syncthreads();
+  cluster.sync();
   tline.mark(3);
-  if (!is_last) return;
-  __threadfence();
-  // Merge: split scalars through shared memory, then every thread reads its column of
-  // all splits with independent L2 loads.
-  if (d < G * kSplits) {
-    int g = d / kSplits, sp = d % kSplits;
-    const float* pp = a.part + ((size_t)(kvh * G + g) * kSplits + sp) * (kHd + 2);
-    float M = __ldcg(pp), L = __ldcg(pp + 1);
-    sM[g][sp] = L > 0.f ? M : -3.0e38f;
-    sF[g][sp] = L;
-  }
-  __syncthreads();
-  if (d < G) {
-    float M = -3.0e38f;
-    for (int sp = 0; sp < kSplits; ++sp) M = fmaxf(M, sM[d][sp]);
-    float L = 0.f;
-    for (int sp = 0; sp < kSplits; ++sp) {
-      float f = sF[d][sp] > 0.f ? expf(__fsub_rn(sM[d][sp], M)) : 0.f;
-      L = fmaf(sF[d][sp], f, L);
-      sF[d][sp] = f;
+  // Merge across the cluster: CTA `split` finalises dims [split*8, split*8 + 8) of every head.
+  constexpr int kDimsPerCta = kHd / kSplits;
+  if (d < G * kDimsPerCta) {
+    const int g = d / kDimsPerCta, dim = split * kDimsPerCta + d % kDimsPerCta;
+    float Ms[kSplits], Ls[kSplits], Os[kSplits];
+#pragma unroll
+    for (int r = 0; r < kSplits; ++r) {
+      Ms[r] = *cluster.map_shared_rank(&pm[g], r);
+      Ls[r] = *cluster.map_shared_rank(&pl[g], r);
+      Os[r] = *cluster.map_shared_rank(&po[g][dim], r);
     }
-    sL[d] = L;
-  }
-  __syncthreads();
-  for (int g = 0; g < G; ++g) {
-    const float* base = a.part + (size_t)(kvh * G + g) * kSplits * (kHd + 2) + 2 + d;
-    float vals[kSplits];
+    float M = -3.0e38f;
 #pragma unroll
-    for (int sp = 0; sp < kSplits; ++sp) vals[sp] = __ldcg(base + sp * (kHd + 2));
-    float O = 0.f;
+    for (int r = 0; r < kSplits; ++r)
+      if (Ls[r] > 0.f) M = fmaxf(M, Ms[r]);
+    float L = 0.f, O = 0.f;
 #pragma unroll
-    for (int sp = 0; sp < kSplits; ++sp) O = fmaf(vals[sp], sF[g][sp], O);
-    a.out[(kvh * G + g) * kHd + d] = __fdiv_rn(O, sL[g]);
+    for (int r = 0; r < kSplits; ++r) {
+      if (Ls[r] > 0.f) {
+        float f = expf(__fsub_rn(Ms[r], M));
+        L = fmaf(Ls[r], f, L);
+        O = fmaf(Os[r], f, O);
+      }
+    }
+    a.out[(kvh * G + g) * kHd + dim] = __fdiv_rn(O, L);
   }
-  if (d == 0) a.ticket[kvh] = 0;
+  cluster.sync();  // peers may still be reading this CTA's partial
 }
 
 // ------------------------------------------------------------------ host side
@@ -509,7 +527,7 @@ struct MvPlan {
   size_t smem;
 };
 
-MvPlan plan_mv(int N, int K, bool int8, int num_sms) {
+MvPlan plan_mv(int N, int K, bool int8, int num_sms, bool last_kernel = false) {
   MvPlan p{};
   const int row_bytes = K * (int8 ? 1 : 2);
   int rpc = (N + num_sms - 1) / num_sms;
@@ -525,36 +543,51 @@ MvPlan plan_mv(int N, int K, bool int8, int num_sms) {
   p.tile_bytes = (tr * row_bytes + 127) & ~127;
   ntiles = (rpc + tr - 1) / tr;
   size_t fixed = (size_t)K * 9 + 64 + 16 * 8 + (size_t)rpc * 4;
-  int st = (int)((kSmemBudget - fixed) / p.tile_bytes);
-  p.stages = std::max(1, std::min(std::min(st, 4), ntiles));
+  // The step's last kernel (lm_head) has no successor to share the SM with: deeper ring.
+  const size_t budget = last_kernel ? 200 * 1024 : kSmemBudget;
+  int st = (int)((budget - fixed) / p.tile_bytes);
+  p.stages = std::max(1, std::min(std::min(st, last_kernel ? 8 : 4), ntiles));
   p.smem = (size_t)p.stages * p.tile_bytes + fixed;
   return p;
 }
 
+// Launch with programmatic stream serialisation (PDL) and an optional cluster shape.
 template <typename... KArgs, typename... Args>
-void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+void launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+               int cluster_y, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_y > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = cluster_y;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = n;
   cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 template <int EPI>
-void mv(bool int8, MvArgs m, int num_sms, cudaStream_t s) {
-  MvPlan p = plan_mv(m.N, m.K, int8, num_sms);
+void mv(bool int8, MvArgs m, int num_sms, cudaStream_t s, bool pdl = true) {
+  MvPlan p = plan_mv(m.N, m.K, int8, num_sms, EPI == MV_ARGMAX);
   m.rows_per_cta = p.rows_per_cta;
   m.tile_rows = p.tile_rows;
   m.stages = p.stages;
   m.tile_bytes = p.tile_bytes;
-  if (int8) launch_pdl(mv_kernel<true, EPI>, dim3(p.grid), dim3(256), p.smem, s, m);
-  else launch_pdl(mv_kernel<false, EPI>, dim3(p.grid), dim3(256), p.smem, s, m);
+  if (int8) launch_ex(mv_kernel<true, EPI>, dim3(p.grid), dim3(256), p.smem, s, pdl, 1, m);
+  else launch_ex(mv_kernel<false, EPI>, dim3(p.grid), dim3(256), p.smem, s, pdl, 1, m);
 }
 
 int sm_count() {
@@ -575,6 +608,8 @@ void decode_kernels_init() {
   cudaFuncSetAttribute(mv_kernel<false, MV_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
   cudaFuncSetAttribute(mv_kernel<false, MV_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
   cudaFuncSetAttribute(mv_kernel<false, MV_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+  cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrefRows * kHd * 8);
+  cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
 }
 
 void decode_step(const DecodeArgs& a, cudaStream_t s) {
@@ -601,13 +636,16 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
     }
     m.norm_w = a.n1[l]; m.K = a.hidden; m.N = qd + 2 * kvd;
     m.W = a.w_qkv[l]; m.ws = a.s_qkv[l]; m.out = a.qkv;
-    mv<MV_STORE>(a.int8, m, nsm, s);
+    // The first kernel of a step is a plain launch: it starts only after the previous
+    // step (which advanced StepState and wrote the last KV row) has completed, so every
+    // later kernel of the step may read StepState and earlier KV rows before its wait.
+    mv<MV_STORE>(a.int8, m, nsm, s, l != 0);
     if (a.on_launch) a.on_launch(a.hook_ctx, 0);
     AttnArgs at{a.qkv, a.q_heads, a.kv_heads, a.qn[l], a.kn[l], a.eps, a.rope_cos, a.rope_sin,
                 a.k_cache + (size_t)l * a.kv_heads * a.max_seq * kHd,
                 a.v_cache + (size_t)l * a.kv_heads * a.max_seq * kHd, a.max_seq, 1.0f / sqrtf((float)kHd), a.st,
-                a.part, a.ticket, a.attn, a.tl, a.tl_count};
-    launch_pdl(attn_kernel, dim3(a.kv_heads, kSplits), dim3(128), 0, s, at);
+                a.attn, a.err, a.tl, a.tl_count};
+    launch_ex(attn_kernel, dim3(a.kv_heads, kSplits), dim3(128), (size_t)kPrefRows * kHd * 8, s, true, kSplits, at);
     if (a.on_launch) a.on_launch(a.hook_ctx, 1);
     // O projection + residual
     m = MvArgs{};
