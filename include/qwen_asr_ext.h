@@ -73,6 +73,13 @@ int32_t qwen_asr_debug_encode(QwenAsrEngine* engine, const float* mel, int32_t n
 int32_t qwen_asr_debug_decode(QwenAsrEngine* engine, const float* rows, int32_t n_rows, const int32_t* forced,
                               int32_t n_steps, int32_t* out_ids, float* out_logits, float* out_hidden);
 
+/* One GEMM of the engine on the current device: C = epi(A[M][K] f32 * B[N][K]^T bf16 bits),
+ * epi as the engine's GemmEpi (0 store, 1 +bias, 2 gelu(+bias), 3 resid(+bias)+acc,
+ * 4 swiglu -> C[M][N/2]); impl 0 = SIMT FP32 kernel, 1 = tcgen05 tensor-core kernel.
+ * Host buffers. Returns 0, or < 0 on error. (Parity hook for the contraction kernels.) */
+int32_t qwen_asr_debug_gemm(int32_t M, int32_t N, int32_t K, const float* A, const uint16_t* B, const float* bias,
+                            const float* resid, int32_t epi, int32_t impl, float* C);
+
 /* ---- allocation-free mel front end (no counterpart in the reference) ----
  * For callers that must not allocate device memory during a call: processes holding a
  * fixed device-memory budget, real-time audio threads that may not block in the

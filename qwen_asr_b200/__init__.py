@@ -57,6 +57,8 @@ SIGNATURES = {
     "qwen_asr_transcribe_device": (_VP, [_VP, C.c_void_p, C.c_int32]),
     "qwen_asr_cuda_stream": (C.c_void_p, [_VP]),
     "qwen_asr_launch_count": (C.c_int64, [_VP]),
+    "qwen_asr_debug_gemm": (C.c_int32, [C.c_int32, C.c_int32, C.c_int32, _F32P, C.POINTER(C.c_uint16), _F32P,
+                                         _F32P, C.c_int32, C.c_int32, _F32P]),
     "qwen_asr_mel_noalloc": (C.c_int32, [_VP, C.c_void_p, C.c_int32, C.c_void_p, C.c_int64]),
     "qwen_asr_get_timeline": (C.c_int64, [_VP, C.POINTER(C.c_uint64), C.c_int64]),
     "qwen_asr_profile_report": (C.c_int32, [_VP, C.POINTER(C.c_double), _I64P, C.c_int32]),

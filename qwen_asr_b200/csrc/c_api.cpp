@@ -306,6 +306,39 @@ int32_t qwen_asr_debug_decode(QwenAsrEngine* e, const float* rows, int32_t n_row
   return (int32_t)ids.size();
 }
 
+int32_t qwen_asr_debug_gemm(int32_t M, int32_t N, int32_t K, const float* A, const uint16_t* B, const float* bias,
+                            const float* resid, int32_t epi, int32_t impl, float* C) {
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) return -1;
+  int ncols = epi == qasr::EPI_SWIGLU ? N / 2 : N;
+  qasr::DevBuf<float> dA, dC, dbias, dres;
+  qasr::DevBuf<uint16_t> dB;
+  qasr::DevBuf<int> dg;
+  if (!dA.upload(A, (size_t)M * K) || !dB.upload(B, (size_t)N * K) || !dC.alloc((size_t)M * ncols) || !dg.alloc(1))
+    return -1;
+  qasr::GemmArgs g;
+  g.M = M; g.N = N; g.K = K; g.A = dA.p; g.lda = K; g.B = dB.p; g.ldb = K; g.C = dC.p; g.ldc = ncols; g.epi = epi;
+  if (bias) {
+    if (!dbias.upload(bias, N)) return -1;
+    g.bias = dbias.p;
+  }
+  if (resid) {
+    if (!dres.upload(resid, (size_t)M * N)) return -1;
+    if (cudaMemcpy(dC.p, resid, (size_t)M * N * 4, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
+    g.resid = dC.p; g.ldr = N;
+  }
+  g.gmax = dg.p;
+  cudaDeviceSynchronize();
+  if (impl == 1) {
+    if (!qasr::gemm_tc(g, 0)) return -2;
+  } else {
+    qasr::gemm_simt(g, 0);
+  }
+  if (cudaDeviceSynchronize() != cudaSuccess || cudaGetLastError() != cudaSuccess) return -3;
+  if (qasr::gemm_tc_error()) return -4;
+  if (cudaMemcpy(C, dC.p, (size_t)M * ncols * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  return 0;
+}
+
 // ---- host-only hooks (no GPU needed): tokenizer, WAV, segmentation, text handling ----
 int32_t qwen_asr_debug_tokenize(const char* model_dir, const char* text, int32_t* out, int32_t cap) {
   if (!model_dir || !text) return -1;

@@ -480,6 +480,10 @@ int Engine::encode(const float* d_mel, int F) {
   float ms = 0;
   cudaEventElapsedTime(&ms, ev0_, ev1_);
   perf.enc_ms += ms;
+  if (int e = gemm_tc_error()) {
+    set_error("tensor-core GEMM: a device-side wait timed out (code " + std::to_string(e) + ")");
+    return 0;
+  }
   CUDA_OK(cudaGetLastError(), 0);
   return T;
 }
@@ -559,6 +563,10 @@ bool Engine::run_prefill(int n, int start_pos) {
   float ms = 0;
   cudaEventElapsedTime(&ms, ev0_, ev1_);
   perf.prefill_ms += ms;
+  if (int e = gemm_tc_error()) {
+    set_error("tensor-core GEMM: a device-side wait timed out (code " + std::to_string(e) + ")");
+    return false;
+  }
   CUDA_OK(cudaGetLastError(), false);
   return true;
 }

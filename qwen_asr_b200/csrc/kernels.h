@@ -37,6 +37,12 @@ struct GemmArgs {
 void gemm(const GemmArgs& a, cudaStream_t s);
 // Plain SIMT FP32 reference GEMM (kept for parity tests of the tensor-core path).
 void gemm_simt(const GemmArgs& a, cudaStream_t s);
+// tcgen05/TMEM tensor-core GEMM (bf16 B, f32 A split into bf16 hi + lo). Returns false
+// when the shape is unsupported (the caller then uses the SIMT kernel).
+bool gemm_tc(const GemmArgs& a, cudaStream_t s);
+bool gemm_tc_available();
+// Nonzero when a bounded wait inside the tensor-core GEMM gave up (clears the flag).
+int gemm_tc_error();
 
 // ---------------------------------------------------------------- mel front end
 // samples [n] -> windowed frames [F][400] (reflect padding, periodic Hann).
