@@ -291,87 +291,235 @@ __global__ void __launch_bounds__(256, 1) mv_kernel(MvArgs a) {
   tline.mark(3);
 }
 
-// ------------------------------------------------------------------ attention
-// grid (kv_heads, kSplits) launched as clusters of kSplits CTAs (one cluster per kv
-// head), block 128 (one thread per head dimension). q/k RMSNorm (kernels/mod.rs:1214-1240)
-// + NeoX RoPE + KV append at `pos`, then split-K online-softmax attention over positions
-// 0..pos (kernels/mod.rs:1492-1534). The K/V rows of earlier positions were written by
-// earlier steps and StepState is constant within a step, so each CTA pulls its rows into
-// shared memory with cp.async.bulk BEFORE the dependency wait. The split partials are
-// merged through distributed shared memory inside the cluster (no global atomics).
-constexpr int kPrefRows = 64;  // K/V rows per CTA staged in shared memory (64 KB)
-
-struct AttnArgs {
-  const float* qkv;
+// ------------------------------------------------------------------ QKV + attention
+// One cluster of kSplits CTAs per kv head, block 128 (one thread per head dimension).
+// Phase 1 (QKV projection of this kv head's group, kernels/mod.rs:884-967): the group's
+// (G+2)*128 rows (G q heads, k, v) are split evenly over the cluster; each CTA pulls its
+// weight rows into shared memory with cp.async.bulk before the dependency wait, then
+// RMS-normalises and (int8) quantises x and computes its rows. The cluster exchanges the
+// q/k/v vectors through distributed shared memory.
+// Phase 2: q/k RMSNorm (kernels/mod.rs:1214-1240) + NeoX RoPE + KV append at `pos`, then
+// split-K online-softmax attention over positions 0..pos (kernels/mod.rs:1492-1534). K/V
+// rows of earlier positions (written by earlier steps; StepState is constant within a
+// step) are also pulled into shared memory before the wait. Split partials are merged
+// through distributed shared memory (no global atomics).
+struct QkvAttnArgs {
+  const float* x;              // residual stream [K]
+  const __nv_bfloat16* embed;  // layer 0: take x from embed[st->cur_token] when >= 0
+  float* x_out;                // layer 0: gathered embedding row written by CTA (0, 0)
+  const float* norm_w;         // input RMSNorm weight [K]
+  float eps;
+  int K;
+  const void* W;               // [q + 2kv][K] int8 or bf16
+  const float* ws;             // int8 row scales
   int n_heads, n_kv;
   const float* qn;
   const float* kn;
-  float eps;
   const float* rc;
   const float* rs;
   float* kc;
   float* vc;
   int max_seq;
   float scale;
+  int rows_per_cta;            // (G + 2) * 128 / kSplits
+  int kv_rows;                 // K/V rows per CTA staged in shared memory
   StepState* st;
-  float* out;
+  float* out;                  // attention output [n_heads * 128]
   int* err;
   unsigned long long* tl;
   int* tl_count;
 };
 
-__global__ void __launch_bounds__(128) attn_kernel(AttnArgs a) {
+template <bool INT8>
+__global__ void __launch_bounds__(128) qkv_attn_kernel(QkvAttnArgs a) {
   namespace cg = cooperative_groups;
   Timeline tline;
   tline.begin(a.tl, a.tl_count, 1);
-  extern __shared__ __align__(128) float kvs[];  // K [kPrefRows][128] then V [kPrefRows][128]
-  __shared__ __align__(8) uint64_t bar;
+  extern __shared__ __align__(128) unsigned char dsm[];
+  __shared__ __align__(8) uint64_t wbar, kvbar;
+  __shared__ float red32[32];
+  __shared__ float vals[64];                          // this CTA's projected rows
   __shared__ __align__(16) float hv[kMaxG + 2][kHd];  // normalised q heads, k, v of `pos`
   __shared__ float red[4][kMaxG + 1];
   __shared__ float wm[4][kMaxG], wl[4][kMaxG];
   __shared__ __align__(16) float wo[4][kMaxG][kHd];
-  __shared__ float pm[kMaxG], pl[kMaxG];           // this CTA's partial, read by cluster peers
+  __shared__ float pm[kMaxG], pl[kMaxG];
   __shared__ __align__(16) float po[kMaxG][kHd];
   cg::cluster_group cluster = cg::this_cluster();
-  const int kvh = blockIdx.x, split = blockIdx.y, d = threadIdx.x;
+  const int kvh = blockIdx.x, rank = blockIdx.y, d = threadIdx.x;
   const int warp = d >> 5, lane = d & 31;
   const int G = a.n_heads / a.n_kv;
-  // ---- before the dependency wait: everything that does not depend on this step's q/k/v
+  const int K = a.K;
+  const size_t row_bytes = (size_t)K * (INT8 ? 1 : 2);
+  const int rpc = a.rows_per_cta;
+  // shared-memory carve-up: weight rows | K rows | V rows | x f32 | x int8 | scales | norm w
+  unsigned char* wsm = dsm;
+  float* ksm = reinterpret_cast<float*>(dsm + (((size_t)rpc * row_bytes + 127) & ~(size_t)127));
+  float* vsm = ksm + (size_t)a.kv_rows * kHd;
+  float* xs = vsm + (size_t)a.kv_rows * kHd;
+  int8_t* xq = reinterpret_cast<int8_t*>(xs + K);
+  float* sws = reinterpret_cast<float*>(xq + ((K + 15) & ~15));
+  float* snw = sws + 64;
+
+  // ---- before the dependency wait
   const int pos = a.st->pos;
   const int total = pos + 1;
   const int chunk = (total + kSplits - 1) / kSplits;
-  const int j0 = split * chunk, j1 = min(total, j0 + chunk);
-  const int npre = max(0, min(min(j1, pos) - j0, kPrefRows));  // rows j0..j0+npre-1, all < pos
+  const int j0 = rank * chunk, j1 = min(total, j0 + chunk);
+  const int npre = max(0, min(min(j1, pos) - j0, a.kv_rows));
   float* kb = a.kc + (size_t)kvh * a.max_seq * kHd;
   float* vb = a.vc + (size_t)kvh * a.max_seq * kHd;
-  float* ksm = kvs;
-  float* vsm = kvs + kPrefRows * kHd;
+  // Group row gi in [0, (G+2)*128) -> weight row (q heads, then k, then v of this kv head).
+  auto wrow = [&](int gi) -> int {
+    if (gi < G * kHd) return kvh * G * kHd + gi;
+    if (gi < (G + 1) * kHd) return a.n_heads * kHd + kvh * kHd + (gi - G * kHd);
+    return (a.n_heads + a.n_kv) * kHd + kvh * kHd + (gi - (G + 1) * kHd);
+  };
+  const int g0 = rank * rpc;
   if (d == 0) {
-    mbar_init(&bar, 1);
+    mbar_init(&wbar, 1);
+    mbar_init(&kvbar, 1);
     fence_mbar_init();
+    mbar_expect_tx(&wbar, (uint32_t)(rpc * row_bytes));
+    // the CTA's rows form at most two runs (a q/k/v segment boundary may fall inside)
+    int i = 0;
+    while (i < rpc) {
+      int gi = g0 + i;
+      int seg_end = (gi / kHd + 1) * kHd;
+      int n = min(rpc - i, seg_end - gi);
+      bulk_g2s(wsm + (size_t)i * row_bytes, reinterpret_cast<const unsigned char*>(a.W) + (size_t)wrow(gi) * row_bytes,
+               (uint32_t)(n * row_bytes), &wbar);
+      i += n;
+    }
     if (npre > 0) {
       const uint32_t bytes = (uint32_t)(npre * kHd * sizeof(float));
-      mbar_expect_tx(&bar, 2 * bytes);
-      bulk_g2s(ksm, kb + (size_t)j0 * kHd, bytes, &bar);
-      bulk_g2s(vsm, vb + (size_t)j0 * kHd, bytes, &bar);
+      mbar_expect_tx(&kvbar, 2 * bytes);
+      bulk_g2s(ksm, kb + (size_t)j0 * kHd, bytes, &kvbar);
+      bulk_g2s(vsm, vb + (size_t)j0 * kHd, bytes, &kvbar);
     }
   }
+  if (INT8 && d < rpc) sws[d] = a.ws[wrow(g0 + d)];
+  for (int i = d; i < K; i += 128) snw[i] = a.norm_w[i];
   const float qn = a.qn[d], kn = a.kn[d];
   const float c = a.rc[(size_t)pos * (kHd / 2) + (d & 63)], sn = a.rs[(size_t)pos * (kHd / 2) + (d & 63)];
   pdl_launch_dependents();
   pdl_wait();
   tline.mark(2);
+
+  // ---- phase 1: x -> RMSNorm -> (int8) -> this CTA's rows of q/k/v
+  const uint16_t* erow = nullptr;
+  if (a.embed) {
+    int tok = a.st->cur_token;
+    if (tok >= 0) erow = reinterpret_cast<const uint16_t*>(a.embed) + (size_t)tok * K;
+  }
+  float ss = 0.f;
+  for (int i = d * 4; i < K; i += 128 * 4) {
+    float4 v;
+    if (erow) {
+      uint2 b = *reinterpret_cast<const uint2*>(erow + i);
+      v = make_float4(__uint_as_float(b.x << 16), __uint_as_float(b.x & 0xFFFF0000u), __uint_as_float(b.y << 16),
+                      __uint_as_float(b.y & 0xFFFF0000u));
+      if (kvh == 0 && rank == 0) *reinterpret_cast<float4*>(a.x_out + i) = v;
+    } else {
+      v = *reinterpret_cast<const float4*>(a.x + i);
+    }
+    *reinterpret_cast<float4*>(xs + i) = v;
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
+  }
+  __syncthreads();
+  {
+    float tot = block_sum(ss, red32);
+    float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+    for (int i = d; i < K; i += 128) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), snw[i]);
+  }
+  float xscale = 1.0f;
+  if (INT8) {
+    float mx = 0.f;
+    for (int i = d; i < K; i += 128) mx = fmaxf(mx, fabsf(xs[i]));
+    mx = block_max(mx, red32);
+    xscale = mx > 0.f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+    float inv = __fdiv_rn(127.0f, fmaxf(mx, 1e-10f));
+    for (int i = d; i < K; i += 128) {
+      float r = roundf(__fmul_rn(xs[i], inv));
+      xq[i] = (int8_t)fminf(fmaxf(r, -127.f), 127.f);
+    }
+  }
+  __syncthreads();
+  mbar_wait(&wbar, 0, a.err, 4);
+  for (int rr = warp * 2; rr < rpc; rr += 8) {
+    const bool two = rr + 1 < rpc;
+    float v0, v1 = 0.f;
+    if (INT8) {
+      int acc0 = 0, acc1 = 0;
+      const int8_t* w0 = reinterpret_cast<const int8_t*>(wsm) + (size_t)rr * K;
+      const int8_t* w1 = w0 + K;
+#pragma unroll 4
+      for (int k0 = lane * 16; k0 < K; k0 += 512) {
+        int4 xv = *reinterpret_cast<const int4*>(xq + k0);
+        int4 wa = *reinterpret_cast<const int4*>(w0 + k0);
+        acc0 = __dp4a(wa.x, xv.x, acc0);
+        acc0 = __dp4a(wa.y, xv.y, acc0);
+        acc0 = __dp4a(wa.z, xv.z, acc0);
+        acc0 = __dp4a(wa.w, xv.w, acc0);
+        if (two) {
+          int4 wb = *reinterpret_cast<const int4*>(w1 + k0);
+          acc1 = __dp4a(wb.x, xv.x, acc1);
+          acc1 = __dp4a(wb.y, xv.y, acc1);
+          acc1 = __dp4a(wb.z, xv.z, acc1);
+          acc1 = __dp4a(wb.w, xv.w, acc1);
+        }
+      }
+      acc0 = warp_sum_i(acc0);
+      acc1 = warp_sum_i(acc1);
+      v0 = __fmul_rn(__fmul_rn((float)acc0, xscale), sws[rr]);
+      if (two) v1 = __fmul_rn(__fmul_rn((float)acc1, xscale), sws[rr + 1]);
+    } else {
+      float acc0 = 0.f, acc1 = 0.f;
+      const uint16_t* w0 = reinterpret_cast<const uint16_t*>(wsm) + (size_t)rr * K;
+      const uint16_t* w1 = w0 + K;
+#pragma unroll 4
+      for (int k0 = lane * 8; k0 < K; k0 += 256) {
+        float4 x0 = *reinterpret_cast<const float4*>(xs + k0);
+        float4 x1 = *reinterpret_cast<const float4*>(xs + k0 + 4);
+        float f[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(w0 + k0), f);
+        acc0 = fmaf(f[0], x0.x, acc0); acc0 = fmaf(f[1], x0.y, acc0);
+        acc0 = fmaf(f[2], x0.z, acc0); acc0 = fmaf(f[3], x0.w, acc0);
+        acc0 = fmaf(f[4], x1.x, acc0); acc0 = fmaf(f[5], x1.y, acc0);
+        acc0 = fmaf(f[6], x1.z, acc0); acc0 = fmaf(f[7], x1.w, acc0);
+        if (two) {
+          bf16x8_to_f32(*reinterpret_cast<const uint4*>(w1 + k0), f);
+          acc1 = fmaf(f[0], x0.x, acc1); acc1 = fmaf(f[1], x0.y, acc1);
+          acc1 = fmaf(f[2], x0.z, acc1); acc1 = fmaf(f[3], x0.w, acc1);
+          acc1 = fmaf(f[4], x1.x, acc1); acc1 = fmaf(f[5], x1.y, acc1);
+          acc1 = fmaf(f[6], x1.z, acc1); acc1 = fmaf(f[7], x1.w, acc1);
+        }
+      }
+      v0 = warp_sum(acc0);
+      v1 = warp_sum(acc1);
+    }
+    if (lane == 0) {
+      vals[rr] = v0;
+      if (two) vals[rr + 1] = v1;
+    }
+  }
+  cluster.sync();  // every CTA's rows are ready
+
+  // ---- phase 2: gather this head group's raw q/k/v from the cluster
   float raw[kMaxG + 2];
 #pragma unroll
-  for (int g = 0; g < kMaxG; ++g) raw[g] = g < G ? a.qkv[(kvh * G + g) * kHd + d] : 0.f;
-  raw[kMaxG] = a.qkv[(a.n_heads + kvh) * kHd + d];
-  raw[kMaxG + 1] = a.qkv[(a.n_heads + a.n_kv + kvh) * kHd + d];
-  // One reduction pass for the G q-head norms and the k norm.
+  for (int g = 0; g < kMaxG + 2; ++g) {
+    int gi = g < G ? g * kHd + d : (g == kMaxG ? G * kHd + d : (g == kMaxG + 1 ? (G + 1) * kHd + d : -1));
+    raw[g] = gi >= 0 ? *cluster.map_shared_rank(&vals[gi % rpc], gi / rpc) : 0.f;
+  }
 #pragma unroll
   for (int g = 0; g <= kMaxG; ++g) {
     float v = raw[g];
-    float ss = warp_sum(v * v);
-    if (lane == 0 && (g < G || g == kMaxG)) red[warp][g < G ? g : G] = ss;
+    float s2 = warp_sum(v * v);
+    if (lane == 0 && (g < G || g == kMaxG)) red[warp][g < G ? g : G] = s2;
   }
   __syncthreads();
   float nv[kMaxG + 1];
@@ -401,12 +549,12 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs a) {
   for (int g = 0; g <= kMaxG; ++g)
     if (g < G || g == kMaxG) hv[g < G ? g : kMaxG][d] = rot[g];
   hv[kMaxG + 1][d] = raw[kMaxG + 1];
-  if (split == 0) {
+  if (rank == 0) {
     kb[(size_t)pos * kHd + d] = rot[kMaxG];
     vb[(size_t)pos * kHd + d] = raw[kMaxG + 1];
   }
   __syncthreads();
-  if (npre > 0) mbar_wait(&bar, 0, a.err, 3);
+  if (npre > 0) mbar_wait(&kvbar, 0, a.err, 3);
   const float* ks = hv[kMaxG];
   const float* vs = hv[kMaxG + 1];
   float m[kMaxG], l[kMaxG], o[kMaxG][4];
@@ -416,8 +564,6 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs a) {
     l[g] = 0.f;
     o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
   }
-  // Keys in groups of 4 per warp: staged rows from shared memory, the current position
-  // from `hv`, rows beyond the staging window straight from L2/HBM.
   for (int jb = j0 + warp * 4; jb < j1; jb += 16) {
     float4 kv[4], vv[4];
 #pragma unroll
@@ -470,7 +616,6 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs a) {
     *reinterpret_cast<float4*>(&wo[warp][g][lane * 4]) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
   }
   __syncthreads();
-  // CTA partial per head {M, L, O[128]}, kept in this CTA's shared memory.
   for (int g = 0; g < G; ++g) {
     float M = fmaxf(fmaxf(wm[0][g], wm[1][g]), fmaxf(wm[2][g], wm[3][g]));
     float L = 0.f, O = 0.f;
@@ -488,10 +633,10 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs a) {
   }
   cluster.sync();
   tline.mark(3);
-  // Merge across the cluster: CTA `split` finalises dims [split*8, split*8 + 8) of every head.
+  // CTA `rank` finalises dims [rank*8, rank*8 + 8) of every head of the group.
   constexpr int kDimsPerCta = kHd / kSplits;
   if (d < G * kDimsPerCta) {
-    const int g = d / kDimsPerCta, dim = split * kDimsPerCta + d % kDimsPerCta;
+    const int g = d / kDimsPerCta, dim = rank * kDimsPerCta + d % kDimsPerCta;
     float Ms[kSplits], Ls[kSplits], Os[kSplits];
 #pragma unroll
     for (int r = 0; r < kSplits; ++r) {
@@ -514,7 +659,7 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs a) {
     }
     a.out[(kvh * G + g) * kHd + dim] = __fdiv_rn(O, L);
   }
-  cluster.sync();  // peers may still be reading this CTA's partial
+  cluster.sync();  // peers may still be reading this CTA's shared memory
 }
 
 // ------------------------------------------------------------------ host side
@@ -608,8 +753,10 @@ void decode_kernels_init() {
   cudaFuncSetAttribute(mv_kernel<false, MV_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
   cudaFuncSetAttribute(mv_kernel<false, MV_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
   cudaFuncSetAttribute(mv_kernel<false, MV_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
-  cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrefRows * kHd * 8);
-  cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  for (auto k : {qkv_attn_kernel<true>, qkv_attn_kernel<false>}) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+    cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  }
 }
 
 void decode_step(const DecodeArgs& a, cudaStream_t s) {
@@ -623,32 +770,36 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
   const int nsm = cached_sms;
   const int qd = a.q_heads * kHd, kvd = a.kv_heads * kHd;
   for (int l = 0; l < a.layers; ++l) {
-    MvArgs m{};
-    m.eps = a.eps;
-    m.err = a.err;
-    m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 0;
-    // QKV (+ token embedding gather on layer 0, input RMSNorm fused)
-    m.x = a.x;
-    if (l == 0) {
-      m.embed = a.embed;
-      m.st = a.st;
-      m.x_out = a.x;
+    // QKV projection + attention, one cluster per kv head. The first kernel of a step is a
+    // plain launch: it starts only after the previous step (which advanced StepState and
+    // wrote the last KV row) has completed, so every kernel of the step may read StepState
+    // and earlier KV rows before its dependency wait.
+    {
+      QkvAttnArgs q{};
+      q.x = a.x;
+      if (l == 0) {
+        q.embed = a.embed;
+        q.x_out = a.x;
+      }
+      q.norm_w = a.n1[l]; q.eps = a.eps; q.K = a.hidden; q.W = a.w_qkv[l]; q.ws = a.s_qkv[l];
+      q.n_heads = a.q_heads; q.n_kv = a.kv_heads; q.qn = a.qn[l]; q.kn = a.kn[l];
+      q.rc = a.rope_cos; q.rs = a.rope_sin;
+      q.kc = a.k_cache + (size_t)l * a.kv_heads * a.max_seq * kHd;
+      q.vc = a.v_cache + (size_t)l * a.kv_heads * a.max_seq * kHd;
+      q.max_seq = a.max_seq; q.scale = 1.0f / sqrtf((float)kHd);
+      q.rows_per_cta = (a.q_heads / a.kv_heads + 2) * kHd / kSplits;
+      q.st = a.st; q.out = a.attn; q.err = a.err; q.tl = a.tl; q.tl_count = a.tl_count;
+      const size_t wbytes = ((size_t)q.rows_per_cta * a.hidden * (a.int8 ? 1 : 2) + 127) & ~(size_t)127;
+      const size_t tail = (size_t)a.hidden * 5 + 16 + 64 * 4 + (size_t)a.hidden * 4;
+      const size_t budget = 200 * 1024;
+      q.kv_rows = (int)std::max<long>(0, std::min<long>(24, ((long)budget - (long)(wbytes + tail)) / (2 * kHd * 4)));
+      const size_t smem = wbytes + (size_t)q.kv_rows * kHd * 8 + tail;
+      if (a.int8) launch_ex(qkv_attn_kernel<true>, dim3(a.kv_heads, kSplits), dim3(128), smem, s, l != 0, kSplits, q);
+      else launch_ex(qkv_attn_kernel<false>, dim3(a.kv_heads, kSplits), dim3(128), smem, s, l != 0, kSplits, q);
+      if (a.on_launch) a.on_launch(a.hook_ctx, 1);
     }
-    m.norm_w = a.n1[l]; m.K = a.hidden; m.N = qd + 2 * kvd;
-    m.W = a.w_qkv[l]; m.ws = a.s_qkv[l]; m.out = a.qkv;
-    // The first kernel of a step is a plain launch: it starts only after the previous
-    // step (which advanced StepState and wrote the last KV row) has completed, so every
-    // later kernel of the step may read StepState and earlier KV rows before its wait.
-    mv<MV_STORE>(a.int8, m, nsm, s, l != 0);
-    if (a.on_launch) a.on_launch(a.hook_ctx, 0);
-    AttnArgs at{a.qkv, a.q_heads, a.kv_heads, a.qn[l], a.kn[l], a.eps, a.rope_cos, a.rope_sin,
-                a.k_cache + (size_t)l * a.kv_heads * a.max_seq * kHd,
-                a.v_cache + (size_t)l * a.kv_heads * a.max_seq * kHd, a.max_seq, 1.0f / sqrtf((float)kHd), a.st,
-                a.attn, a.err, a.tl, a.tl_count};
-    launch_ex(attn_kernel, dim3(a.kv_heads, kSplits), dim3(128), (size_t)kPrefRows * kHd * 8, s, true, kSplits, at);
-    if (a.on_launch) a.on_launch(a.hook_ctx, 1);
+    MvArgs m{};
     // O projection + residual
-    m = MvArgs{};
     m.eps = a.eps; m.err = a.err;
     m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 2;
     m.x = a.attn; m.K = qd; m.N = a.hidden;
