@@ -16,7 +16,8 @@
 namespace qasr {
 
 constexpr int kHd = 128;
-constexpr int kWarps = 8;
+constexpr int kWarps = 16;  // decode matvec CTA: 512 threads
+constexpr int kThreads = kWarps * 32;
 constexpr int kSplits = 16;  // attention split-K CTAs per kv head
 constexpr int kMaxG = 4;     // q heads per kv head
 
@@ -66,7 +67,7 @@ struct Timeline {
 };
 
 template <bool INT8, int EPI>
-__global__ void __launch_bounds__(256, 1) mv_kernel(MvArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) mv_kernel(MvArgs a) {
   Timeline tline;
   tline.begin(a.tl, a.tl_count, a.kind);
   extern __shared__ __align__(128) unsigned char sm[];
@@ -106,9 +107,9 @@ __global__ void __launch_bounds__(256, 1) mv_kernel(MvArgs a) {
   }
   // Immutable per-row scales and norm weights: stage them before waiting on the producer.
   if (INT8)
-    for (int i = tid; i < nrows; i += 256) sws[i] = a.ws[r0 + i];
+    for (int i = tid; i < nrows; i += kThreads) sws[i] = a.ws[r0 + i];
   if (a.norm_w)
-    for (int i = tid; i < K; i += 256) snw[i] = a.norm_w[i];
+    for (int i = tid; i < K; i += kThreads) snw[i] = a.norm_w[i];
   pdl_launch_dependents();
   pdl_wait();
   tline.mark(2);
@@ -121,7 +122,7 @@ __global__ void __launch_bounds__(256, 1) mv_kernel(MvArgs a) {
     if (tok >= 0) erow = reinterpret_cast<const uint16_t*>(a.embed) + (size_t)tok * K;
   }
   float ss = 0.f;
-  for (int i = tid * 4; i < K; i += 256 * 4) {
+  for (int i = tid * 4; i < K; i += kThreads * 4) {
     float4 v;
     if (erow) {
       uint2 b = *reinterpret_cast<const uint2*>(erow + i);
@@ -141,16 +142,16 @@ __global__ void __launch_bounds__(256, 1) mv_kernel(MvArgs a) {
   if (a.norm_w) {
     float tot = block_sum(ss, red);
     float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
-    for (int i = tid; i < K; i += 256) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), snw[i]);
+    for (int i = tid; i < K; i += kThreads) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), snw[i]);
   }
   float xscale = 1.0f;
   if (INT8) {
     float mx = 0.f;
-    for (int i = tid; i < K; i += 256) mx = fmaxf(mx, fabsf(xs[i]));
+    for (int i = tid; i < K; i += kThreads) mx = fmaxf(mx, fabsf(xs[i]));
     mx = block_max(mx, red);
     xscale = mx > 0.f ? __fdiv_rn(mx, 127.0f) : 1.0f;
     float inv = __fdiv_rn(127.0f, fmaxf(mx, 1e-10f));
-    for (int i = tid; i < K; i += 256) {
+    for (int i = tid; i < K; i += kThreads) {
       float r = roundf(__fmul_rn(xs[i], inv));
       xq[i] = (int8_t)fminf(fmaxf(r, -127.f), 127.f);
     }
@@ -165,81 +166,88 @@ __global__ void __launch_bounds__(256, 1) mv_kernel(MvArgs a) {
     mbar_wait(&full[s], phase, a.err, 1);
     const int rows_t = min(a.tile_rows, nrows - t * a.tile_rows);
     const unsigned char* tw = wst + (size_t)s * a.tile_bytes;
-    for (int rr = warp * 2; rr < rows_t; rr += 2 * kWarps) {
-      const bool two = rr + 1 < rows_t;
-      float v0, v1 = 0.f;
+    // Four rows per warp iteration: the x chunk is loaded once per four weight rows and
+    // the four dot products are reduced together with a transposing butterfly (6
+    // shuffles). Afterwards lane 8*r holds row r (r = 0..3).
+    for (int rr = warp * 4; rr < rows_t; rr += 4 * kWarps) {
+      float acc[4];
       if (INT8) {
-        int acc0 = 0, acc1 = 0;
+        int ia[4] = {0, 0, 0, 0};
         const int8_t* w0 = reinterpret_cast<const int8_t*>(tw) + (size_t)rr * K;
-        const int8_t* w1 = w0 + K;
-#pragma unroll 4
+#pragma unroll 2
         for (int k0 = lane * 16; k0 < K; k0 += 512) {
           int4 xv = *reinterpret_cast<const int4*>(xq + k0);
-          int4 wa = *reinterpret_cast<const int4*>(w0 + k0);
-          acc0 = __dp4a(wa.x, xv.x, acc0);
-          acc0 = __dp4a(wa.y, xv.y, acc0);
-          acc0 = __dp4a(wa.z, xv.z, acc0);
-          acc0 = __dp4a(wa.w, xv.w, acc0);
-          if (two) {
-            int4 wb = *reinterpret_cast<const int4*>(w1 + k0);
-            acc1 = __dp4a(wb.x, xv.x, acc1);
-            acc1 = __dp4a(wb.y, xv.y, acc1);
-            acc1 = __dp4a(wb.z, xv.z, acc1);
-            acc1 = __dp4a(wb.w, xv.w, acc1);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            if (rr + r < rows_t) {
+              int4 w = *reinterpret_cast<const int4*>(w0 + (size_t)r * K + k0);
+              ia[r] = __dp4a(w.x, xv.x, ia[r]);
+              ia[r] = __dp4a(w.y, xv.y, ia[r]);
+              ia[r] = __dp4a(w.z, xv.z, ia[r]);
+              ia[r] = __dp4a(w.w, xv.w, ia[r]);
+            }
           }
         }
-        acc0 = warp_sum_i(acc0);
-        acc1 = warp_sum_i(acc1);
-        const int lr = t * a.tile_rows + rr;
-        v0 = __fmul_rn(__fmul_rn((float)acc0, xscale), sws[lr]);
-        if (two) v1 = __fmul_rn(__fmul_rn((float)acc1, xscale), sws[lr + 1]);
+        // int32 sums are exact in any order; reduce as ints, convert once
+        int s0 = (lane & 16) ? ia[2] : ia[0], s1 = (lane & 16) ? ia[3] : ia[1];
+        int t0 = (lane & 16) ? ia[0] : ia[2], t1 = (lane & 16) ? ia[1] : ia[3];
+        s0 += __shfl_xor_sync(0xffffffffu, t0, 16);
+        s1 += __shfl_xor_sync(0xffffffffu, t1, 16);
+        int u = (lane & 8) ? s1 : s0, w = (lane & 8) ? s0 : s1;
+        u += __shfl_xor_sync(0xffffffffu, w, 8);
+        u += __shfl_xor_sync(0xffffffffu, u, 4);
+        u += __shfl_xor_sync(0xffffffffu, u, 2);
+        u += __shfl_xor_sync(0xffffffffu, u, 1);
+        const int myr = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
+        const int lr = t * a.tile_rows + rr + myr;
+        acc[0] = (rr + myr < rows_t) ? __fmul_rn(__fmul_rn((float)u, xscale), sws[lr]) : 0.f;
       } else {
-        float acc0 = 0.f, acc1 = 0.f;
+        float fa[4] = {0.f, 0.f, 0.f, 0.f};
         const uint16_t* w0 = reinterpret_cast<const uint16_t*>(tw) + (size_t)rr * K;
-        const uint16_t* w1 = w0 + K;
-#pragma unroll 4
+#pragma unroll 2
         for (int k0 = lane * 8; k0 < K; k0 += 256) {
           float4 x0 = *reinterpret_cast<const float4*>(xs + k0);
           float4 x1 = *reinterpret_cast<const float4*>(xs + k0 + 4);
-          float f[8];
-          bf16x8_to_f32(*reinterpret_cast<const uint4*>(w0 + k0), f);
-          acc0 = fmaf(f[0], x0.x, acc0); acc0 = fmaf(f[1], x0.y, acc0);
-          acc0 = fmaf(f[2], x0.z, acc0); acc0 = fmaf(f[3], x0.w, acc0);
-          acc0 = fmaf(f[4], x1.x, acc0); acc0 = fmaf(f[5], x1.y, acc0);
-          acc0 = fmaf(f[6], x1.z, acc0); acc0 = fmaf(f[7], x1.w, acc0);
-          if (two) {
-            bf16x8_to_f32(*reinterpret_cast<const uint4*>(w1 + k0), f);
-            acc1 = fmaf(f[0], x0.x, acc1); acc1 = fmaf(f[1], x0.y, acc1);
-            acc1 = fmaf(f[2], x0.z, acc1); acc1 = fmaf(f[3], x0.w, acc1);
-            acc1 = fmaf(f[4], x1.x, acc1); acc1 = fmaf(f[5], x1.y, acc1);
-            acc1 = fmaf(f[6], x1.z, acc1); acc1 = fmaf(f[7], x1.w, acc1);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            if (rr + r < rows_t) {
+              float f[8];
+              bf16x8_to_f32(*reinterpret_cast<const uint4*>(w0 + (size_t)r * K + k0), f);
+              fa[r] = fmaf(f[0], x0.x, fa[r]); fa[r] = fmaf(f[1], x0.y, fa[r]);
+              fa[r] = fmaf(f[2], x0.z, fa[r]); fa[r] = fmaf(f[3], x0.w, fa[r]);
+              fa[r] = fmaf(f[4], x1.x, fa[r]); fa[r] = fmaf(f[5], x1.y, fa[r]);
+              fa[r] = fmaf(f[6], x1.z, fa[r]); fa[r] = fmaf(f[7], x1.w, fa[r]);
+            }
           }
         }
-        v0 = warp_sum(acc0);
-        v1 = warp_sum(acc1);
+        float s0 = (lane & 16) ? fa[2] : fa[0], s1 = (lane & 16) ? fa[3] : fa[1];
+        float t0 = (lane & 16) ? fa[0] : fa[2], t1 = (lane & 16) ? fa[1] : fa[3];
+        s0 += __shfl_xor_sync(0xffffffffu, t0, 16);
+        s1 += __shfl_xor_sync(0xffffffffu, t1, 16);
+        float u = (lane & 8) ? s1 : s0, w = (lane & 8) ? s0 : s1;
+        u += __shfl_xor_sync(0xffffffffu, w, 8);
+        u += __shfl_xor_sync(0xffffffffu, u, 4);
+        u += __shfl_xor_sync(0xffffffffu, u, 2);
+        u += __shfl_xor_sync(0xffffffffu, u, 1);
+        acc[0] = u;
       }
-      const int row = r0 + t * a.tile_rows + rr;
-      if (lane == 0) {
-        if (EPI == MV_SWIGLU) {
-          if (two) a.out[row / 2] = silu_mul(v0, v1);
-        } else if (EPI == MV_ARGMAX) {
-          if (a.logits) {
-            a.logits[row] = v0;
-            if (two) a.logits[row + 1] = v1;
-          }
-          unsigned long long k0 = am_key(v0, row);
-          best = k0 > best ? k0 : best;
-          if (two) {
-            unsigned long long k1 = am_key(v1, row + 1);
-            best = k1 > best ? k1 : best;
-          }
-        } else if (EPI == MV_RESID) {
-          a.out[row] = __fadd_rn(v0, a.resid[row]);
-          if (two) a.out[row + 1] = __fadd_rn(v1, a.resid[row + 1]);
-        } else {
-          a.out[row] = v0;
-          if (two) a.out[row + 1] = v1;
+      const float v = acc[0];
+      const int myr = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
+      const int row = r0 + t * a.tile_rows + rr + myr;
+      const bool valid = (lane & 7) == 0 && rr + myr < rows_t;
+      if (EPI == MV_SWIGLU) {
+        const float up = __shfl_down_sync(0xffffffffu, v, 8);  // row myr + 1 (the "up" row)
+        if (valid && (myr & 1) == 0 && rr + myr + 1 < rows_t) a.out[row / 2] = silu_mul(v, up);
+      } else if (EPI == MV_ARGMAX) {
+        if (valid) {
+          if (a.logits) a.logits[row] = v;
+          unsigned long long k = am_key(v, row);
+          best = k > best ? k : best;
         }
+      } else if (EPI == MV_RESID) {
+        if (valid) a.out[row] = __fadd_rn(v, a.resid[row]);
+      } else {
+        if (valid) a.out[row] = v;
       }
     }
     __syncwarp();
@@ -251,6 +259,11 @@ __global__ void __launch_bounds__(256, 1) mv_kernel(MvArgs a) {
   }
 
   if (EPI == MV_ARGMAX) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      unsigned long long t2 = __shfl_xor_sync(0xffffffffu, best, o);
+      best = t2 > best ? t2 : best;
+    }
     if (lane == 0) am_warp[warp] = best;
     __syncthreads();
     if (tid == 0) {
@@ -264,7 +277,7 @@ __global__ void __launch_bounds__(256, 1) mv_kernel(MvArgs a) {
     if (is_last) {
       __threadfence();
       unsigned long long b = 0ull;
-      for (int i = tid; i < (int)gridDim.x; i += 256) {
+      for (int i = tid; i < (int)gridDim.x; i += kThreads) {
         unsigned long long v = *((volatile unsigned long long*)a.am_part + i);
         b = v > b ? v : b;
       }
@@ -731,8 +744,8 @@ void mv(bool int8, MvArgs m, int num_sms, cudaStream_t s, bool pdl = true) {
   m.tile_rows = p.tile_rows;
   m.stages = p.stages;
   m.tile_bytes = p.tile_bytes;
-  if (int8) launch_ex(mv_kernel<true, EPI>, dim3(p.grid), dim3(256), p.smem, s, pdl, 1, m);
-  else launch_ex(mv_kernel<false, EPI>, dim3(p.grid), dim3(256), p.smem, s, pdl, 1, m);
+  if (int8) launch_ex(mv_kernel<true, EPI>, dim3(p.grid), dim3(kThreads), p.smem, s, pdl, 1, m);
+  else launch_ex(mv_kernel<false, EPI>, dim3(p.grid), dim3(kThreads), p.smem, s, pdl, 1, m);
 }
 
 int sm_count() {
