@@ -1098,3 +1098,166 @@ def prompt_rows(ctx: "Ctx", enc: np.ndarray) -> np.ndarray:
     """Prompt embeddings of transcribe_segment (transcribe.rs:96-169) for the ctx settings."""
     pt, ft = ctx.prompt_tokens()
     return ctx.build_embeds(enc, pt, ft, None, False)
+
+
+# ---------------------------------------------------------------------------
+# Incremental streaming (transcribe.rs:801-1304)
+# ---------------------------------------------------------------------------
+
+def stream_tail_repeat_blocks(tokens, max_period):
+    """transcribe.rs:36-55."""
+    n = len(tokens)
+    if n < 2:
+        return 1, 0
+    cap = min(n // 2, max_period if max_period > 0 else n // 2)
+    best_reps, best_p = 1, 0
+    for p in range(1, cap + 1):
+        reps = 1
+        while (reps + 1) * p <= n:
+            if tokens[n - (reps + 1) * p:n - reps * p] != tokens[n - reps * p:n - (reps - 1) * p]:
+                break
+            reps += 1
+        if reps > best_reps:
+            best_reps, best_p = reps, p
+    return best_reps, best_p
+
+
+class StreamState:
+    """transcribe.rs:801-893 (the oracle keeps one decoder per stream)."""
+
+    def __init__(self):
+        self.enc_cache = []          # list of encoder outputs per completed window
+        self.enc_cache_base_windows = 0
+        self.raw_tokens = []
+        self.stable_text_tokens = []
+        self.result_bytes = b""
+        self.prev_prefill = None     # f32 rows of the previous prefill
+        self.prev_tail_snapshot = []
+        self.stale_count = 0
+        self.last_partial_cursor = 0
+        self.last_partial_enc = None
+        self.audio_cursor = 0
+        self.chunk_idx = 0
+        self.dec = None
+
+
+def stream_push_audio(ctx: "Ctx", samples, st: StreamState, finalize: bool) -> bytes:
+    """transcribe.rs:902-1304: processes every full chunk of `samples` (the whole buffer so
+    far) from st.audio_cursor, plus the tail when finalising; returns the emitted bytes."""
+    m = ctx.model
+    if st.dec is None:
+        st.dec = Decoder(m)
+    dec = st.dec
+    chunk_samples = int(F32(ctx.stream_chunk_sec) * F32(SAMPLE_RATE))
+    rollback, unfixed = ctx.stream_rollback, ctx.stream_unfixed_chunks
+    max_new = ctx.stream_max_new_tokens if ctx.stream_max_new_tokens > 0 else 32
+    pt, ft = ctx.prompt_tokens()
+    n_force = len(ft) if ft else 0
+    x = np.asarray(samples, dtype=F32)
+    available = max(0, len(x) - st.audio_cursor)
+    if (available < chunk_samples and not finalize) or available == 0:
+        return b""
+    win = min(max(m.cfg.enc_n_window_infer, 100), 800) * HOP_LENGTH
+    delta = b""
+
+    def text_start(rt):
+        if n_force:
+            return 0
+        return rt.index(TOKEN_ASR_TEXT) + 1 if TOKEN_ASR_TEXT in rt else 0
+
+    def emit(cand, a, b):
+        nonlocal delta
+        for i in range(a, b):
+            if i < len(cand):
+                if i >= len(st.stable_text_tokens):
+                    st.stable_text_tokens.append(cand[i])
+                pb = ctx.tok.decode_bytes(cand[i])
+                st.result_bytes += pb
+                delta += pb
+
+    def reset_context():
+        carry = min(len(st.stable_text_tokens), STREAM_RESET_CARRY_TOKENS)
+        st.raw_tokens = ([TOKEN_ASR_TEXT] + st.stable_text_tokens[len(st.stable_text_tokens) - carry:]) if carry else []
+        st.prev_prefill = None
+        st.stale_count = 0
+        st.prev_tail_snapshot = []
+        if len(st.enc_cache) >= STREAM_MAX_ENC_WINDOWS:
+            st.enc_cache_base_windows += len(st.enc_cache)
+            st.enc_cache = []
+
+    while st.audio_cursor < len(x):
+        if len(x) - st.audio_cursor < chunk_samples and not finalize:
+            break
+        st.audio_cursor = min(st.audio_cursor + chunk_samples, len(x))
+        is_final = finalize and st.audio_cursor >= len(x)
+        full_end = (st.audio_cursor // win) * win
+        while (st.enc_cache_base_windows + len(st.enc_cache)) * win < full_end:
+            ws = (st.enc_cache_base_windows + len(st.enc_cache)) * win
+            st.enc_cache.append(m.encode(mel_spectrogram(x[ws:ws + win])))
+        need = st.last_partial_cursor == 0 or (st.audio_cursor - st.last_partial_cursor) >= 2 * chunk_samples or is_final
+        partial = None
+        if full_end < st.audio_cursor:
+            if need:
+                mel = mel_spectrogram(x[full_end:st.audio_cursor])
+                if mel is not None:
+                    st.last_partial_enc = m.encode(mel)
+                    st.last_partial_cursor = st.audio_cursor
+            partial = st.last_partial_enc
+        parts = list(st.enc_cache) + ([partial] if partial is not None and len(partial) else [])
+        if not parts:
+            st.chunk_idx += 1
+            return b""  # the reference returns an empty delta here (transcribe.rs:1004-1007)
+        enc = np.concatenate(parts).astype(F32)
+        n_prefix = max(len(st.raw_tokens) - rollback, 0) if (ctx.past_text_conditioning and st.chunk_idx >= unfixed
+                                                              and st.raw_tokens) else 0
+        emb = ctx.build_embeds(enc, pt, ft, st.raw_tokens[:n_prefix], False)
+        prefill_len = emb.shape[0] - 1
+        reused = 0
+        if st.prev_prefill is not None and len(st.prev_prefill):
+            cmp = min(prefill_len, len(st.prev_prefill))
+            while reused < cmp and np.array_equal(st.prev_prefill[reused], emb[reused]):
+                reused += 1
+        dec.kv.len = reused
+        if prefill_len - reused > 0:
+            dec.prefill(emb[reused:prefill_len])
+        token = dec.forward(emb[prefill_len])
+        st.prev_prefill = emb[:prefill_len].copy()
+        chunk_tokens = []
+        n_gen = 0
+        while n_gen < max_new:
+            n_gen += 1
+            if token in (TOKEN_ENDOFTEXT, TOKEN_IM_END):
+                break
+            chunk_tokens.append(token)
+            token = dec.forward(m.embed(token))
+        speech_ended = not chunk_tokens and bool(st.raw_tokens) and st.chunk_idx >= unfixed
+        if speech_ended:
+            cand = st.raw_tokens[text_start(st.raw_tokens):]
+            emit(cand, len(st.stable_text_tokens), len(cand))
+        st.raw_tokens = st.raw_tokens[:n_prefix] + chunk_tokens
+        if not speech_ended:
+            if st.raw_tokens == st.prev_tail_snapshot:
+                st.stale_count += 1
+            else:
+                st.stale_count = 0
+                st.prev_tail_snapshot = list(st.raw_tokens)
+            reps, _ = stream_tail_repeat_blocks(st.raw_tokens, STREAM_DEGEN_MAX_PERIOD)
+            if st.stale_count >= STREAM_STALE_CHUNKS or reps >= STREAM_DEGEN_MIN_REPEATS:
+                reset_context()
+            if st.chunk_idx > 0 and st.chunk_idx % STREAM_RESET_INTERVAL_CHUNKS == 0:
+                reset_context()
+            ts = text_start(st.raw_tokens)
+            n_text = max(len(st.raw_tokens) - ts, 0)
+            if is_final:
+                cand_len = n_text
+            elif st.chunk_idx >= unfixed:
+                cand_len = max(n_text - rollback, 0)
+            else:
+                cand_len = 0
+            cand = st.raw_tokens[ts:]
+            a = len(st.stable_text_tokens)
+            emit(cand, a, max(cand_len, a))
+        st.chunk_idx += 1
+        if speech_ended:
+            break
+    return delta

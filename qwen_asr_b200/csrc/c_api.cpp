@@ -290,6 +290,7 @@ int32_t qwen_asr_debug_decode(QwenAsrEngine* e, const float* rows, int32_t n_row
                               int32_t n_steps, int32_t* out_ids, float* out_logits, float* out_hidden) {
   if (!e || !rows || n_rows <= 0 || n_steps < 0) return -1;
   auto& eng = e->ctx.eng;
+  e->ctx.kv_owner = nullptr;
   if (!eng.prefill_rows(rows, n_rows, 0)) return -1;
   if (out_hidden) {
     std::vector<float> h;

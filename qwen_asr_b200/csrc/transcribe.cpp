@@ -112,6 +112,7 @@ bool Ctx::transcribe_segment(const float* samples, size_t n, const std::vector<i
     ids.push_back(kTokAsrText);
   }
   if (!eng.prefill_ids(ids, eng.enc_out(), 0)) return false;
+  kv_owner = nullptr;
   std::vector<int> gen;
   int limit = force_n_tokens > 0 ? force_n_tokens : 2048;
   if (!eng.decode(limit, force_n_tokens <= 0, gen)) return false;
@@ -263,7 +264,8 @@ bool Ctx::stream_push_audio(const std::vector<float>& samples, StreamState& st, 
     size_t enc_seq_len = st.enc_cached_seq_total + partial_seq;
     if (enc_seq_len == 0) {
       st.chunk_idx += 1;
-      return true;  // the reference returns here (transcribe.rs:1004-1007)
+      delta.clear();  // the reference returns an empty delta here (transcribe.rs:1004-1007)
+      return true;
     }
     std::vector<float> enc_output(enc_seq_len * dim);
     size_t off = 0;
@@ -290,6 +292,10 @@ bool Ctx::stream_push_audio(const std::vector<float>& samples, StreamState& st, 
     // LCP reuse: rows equal as f32 vectors (transcribe.rs:1095-1106). Token rows compare
     // by id; encoder rows compare element-wise; a token row never equals an encoder row.
     size_t reused = 0;
+    if (kv_owner != &st) {  // another stream or an offline call overwrote the KV cache
+      st.prev_ids.clear();
+      st.prev_prefill_len = 0;
+    }
     if (!st.prev_ids.empty() && st.prev_prefill_len > 0) {
       size_t cmp = std::min(prefill_len, st.prev_prefill_len);
       while (reused < cmp) {
@@ -317,6 +323,7 @@ bool Ctx::stream_push_audio(const std::vector<float>& samples, StreamState& st, 
     if (cudaMemcpy(denc.p, enc_output.data(), enc_output.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
       return false;
     if (!eng.prefill_ids(ids, denc.p, (int)reused)) return false;
+    kv_owner = &st;
     st.prev_ids.assign(ids.begin(), ids.begin() + prefill_len);
     st.prev_enc = enc_output;
     st.prev_prefill_len = prefill_len;

@@ -46,7 +46,8 @@ class Ctx {
   int stream_rollback = 5, stream_unfixed_chunks = 2, stream_max_new_tokens = 32;
   bool past_text_conditioning = false, skip_silence = false;
   std::string prompt, force_language;
-  int force_n_tokens = 0;  // benchmark extension: exactly N decode steps, EOS ignored
+  int force_n_tokens = 0;
+  const void* kv_owner = nullptr;  // stream whose prompt rows the KV cache currently holds  // benchmark extension: exactly N decode steps, EOS ignored
   // prompt tokens
   std::vector<int> prompt_tokens, force_prompt_tokens;
   bool has_prompt_tokens = false, has_force_tokens = false, prompt_tokens_ready = false;
