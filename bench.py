@@ -297,7 +297,8 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
 
     for _ in range(args.warmup):
-        eng.transcribe_device(x_dev.data_ptr(), n)
+        if eng.transcribe_device(x_dev.data_ptr(), n) is None:
+            raise RuntimeError(f"transcription failed: {Q.last_error()}")
 
     # ---- device-resident timed region
     barrier(world)

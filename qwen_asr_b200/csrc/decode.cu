@@ -7,6 +7,7 @@
 // (kernels/mod.rs:1795-1802), exact int32 dot products (dp4a), then
 // (float)sum * x_scale * w_scale[row] (+ residual) (kernels/neon.rs:716-800).
 #include <cooperative_groups.h>
+#include <cuda.h>
 
 #include "bulk.cuh"
 #include "common.h"
@@ -30,11 +31,13 @@ struct MvArgs {
   const float* norm_w;         // fused RMSNorm weight or null
   float eps;
   int K, N;
-  const void* W;               // [N][K] int8 or bf16
   const float* ws;             // int8 row scales
   float* out;
   const float* resid;          // may alias out
-  int rows_per_cta, tile_rows, stages, tile_bytes;
+  int rows_per_cta;            // multiple of block_rows
+  int block_rows;              // R: 16, 32 or 64 weight rows per stage (R / 16 per warp)
+  int nkc;                     // 512-byte column chunks per row
+  int stages;
   unsigned long long* am_part;
   int* am_ticket;
   StepState* st;
@@ -66,36 +69,87 @@ struct Timeline {
   }
 };
 
-template <bool INT8, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) mv_kernel(MvArgs a) {
+constexpr int kChunk = 512;  // bytes of a weight row per stage (32 lanes x 16 bytes)
+
+__device__ __forceinline__ void tma_box(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Reduces v[0..RPW) over the warp; afterwards lane `row_lane(r)` holds row r's sum.
+template <int RPW, typename T>
+__device__ __forceinline__ T warp_reduce_rows(const T (&v)[4], int lane) {
+  if (RPW == 4) {
+    T s0 = (lane & 16) ? v[2] : v[0], s1 = (lane & 16) ? v[3] : v[1];
+    T t0 = (lane & 16) ? v[0] : v[2], t1 = (lane & 16) ? v[1] : v[3];
+    s0 += __shfl_xor_sync(0xffffffffu, t0, 16);
+    s1 += __shfl_xor_sync(0xffffffffu, t1, 16);
+    T u = (lane & 8) ? s1 : s0, w = (lane & 8) ? s0 : s1;
+    u += __shfl_xor_sync(0xffffffffu, w, 8);
+    u += __shfl_xor_sync(0xffffffffu, u, 4);
+    u += __shfl_xor_sync(0xffffffffu, u, 2);
+    u += __shfl_xor_sync(0xffffffffu, u, 1);
+    return u;
+  } else if (RPW == 2) {
+    T s = (lane & 16) ? v[1] : v[0], t = (lane & 16) ? v[0] : v[1];
+    s += __shfl_xor_sync(0xffffffffu, t, 16);
+    s += __shfl_xor_sync(0xffffffffu, s, 8);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    return s;
+  } else {
+    T s = v[0];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    return s;
+  }
+}
+template <int RPW>
+__device__ __forceinline__ int lane_row(int lane) {
+  return RPW == 4 ? ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1) : (RPW == 2 ? (lane >> 4) : 0);
+}
+template <int RPW>
+__device__ __forceinline__ bool row_lane(int lane) {
+  return RPW == 4 ? (lane & 7) == 0 : (RPW == 2 ? (lane & 15) == 0 : lane == 0);
+}
+
+// Decode matvec y = epi(W x). Each CTA owns rows_per_cta rows; the rows stream through a
+// ring of shared-memory stages holding R rows x 512 bytes each (2-D TMA boxes, the first
+// ones issued before the dependency wait). Every warp owns R/16 rows of a stage, so all 16
+// warps work on every stage, accumulating across the row's 512-byte chunks.
+template <bool INT8, int EPI, int RPW>
+__global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__ CUtensorMap wmap, MvArgs a) {
   Timeline tline;
   tline.begin(a.tl, a.tl_count, a.kind);
-  extern __shared__ __align__(128) unsigned char sm[];
+  extern __shared__ unsigned char sm_raw[];
   __shared__ float red[32];
   __shared__ unsigned long long am_warp[kWarps];
   __shared__ int is_last;
+  unsigned char* sm = (unsigned char*)(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int K = a.K;
-  const size_t row_bytes = (size_t)K * (INT8 ? 1 : 2);
+  const int K = a.K, R = a.block_rows, nkc = a.nkc;
+  const int kpad = nkc * kChunk / (INT8 ? 1 : 2);  // padded vector length in elements
+  const int stage_bytes = R * kChunk;
   unsigned char* wst = sm;
-  float* xs = reinterpret_cast<float*>(sm + (size_t)a.stages * a.tile_bytes);
-  int8_t* xq = reinterpret_cast<int8_t*>(xs + K);
-  uint64_t* full =
-      reinterpret_cast<uint64_t*>(sm + (((size_t)a.stages * a.tile_bytes + (size_t)K * 5 + 63) & ~(size_t)63));
+  float* xs = reinterpret_cast<float*>(sm + (size_t)a.stages * stage_bytes);
+  int8_t* xq = reinterpret_cast<int8_t*>(xs + kpad);
+  uint64_t* full = reinterpret_cast<uint64_t*>(xq + ((kpad + 15) & ~15));
   uint64_t* empty = full + a.stages;
-  float* sws = reinterpret_cast<float*>(empty + a.stages);  // [rows_per_cta] row scales
-  float* snw = sws + a.rows_per_cta;                         // [K] RMSNorm weight
+  float* sws = reinterpret_cast<float*>(empty + a.stages);
+  float* snw = sws + a.rows_per_cta;
 
   const int r0 = blockIdx.x * a.rows_per_cta;
   const int nrows = max(0, min(a.N, r0 + a.rows_per_cta) - r0);
-  const int ntiles = (nrows + a.tile_rows - 1) / a.tile_rows;
-  const unsigned char* wbase = reinterpret_cast<const unsigned char*>(a.W) + (size_t)r0 * row_bytes;
+  const int nblocks = (nrows + R - 1) / R;
+  const int nt = nblocks * nkc;
   auto issue = [&](int t) {
-    int s = t % a.stages;
-    int rows_t = min(a.tile_rows, nrows - t * a.tile_rows);
-    uint32_t bytes = (uint32_t)(rows_t * row_bytes);
-    mbar_expect_tx(&full[s], bytes);
-    bulk_g2s(wst + (size_t)s * a.tile_bytes, wbase + (size_t)t * a.tile_rows * row_bytes, bytes, &full[s]);
+    const int s = t % a.stages;
+    mbar_expect_tx(&full[s], (uint32_t)stage_bytes);
+    tma_box(wst + (size_t)s * stage_bytes, &wmap, (t % nkc) * (kChunk / 2), r0 + (t / nkc) * R, &full[s]);
   };
   if (tid == 0) {
     for (int s = 0; s < a.stages; ++s) {
@@ -103,9 +157,8 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(MvArgs a) {
       mbar_init(&empty[s], kWarps);
     }
     fence_mbar_init();
-    for (int t = 0; t < min(a.stages, ntiles); ++t) issue(t);  // weights do not depend on x
+    for (int t = 0; t < min(a.stages, nt); ++t) issue(t);  // weights do not depend on x
   }
-  // Immutable per-row scales and norm weights: stage them before waiting on the producer.
   if (INT8)
     for (int i = tid; i < nrows; i += kThreads) sws[i] = a.ws[r0 + i];
   if (a.norm_w)
@@ -115,7 +168,6 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(MvArgs a) {
   tline.mark(2);
 
   // ---- prologue: x (optionally gathered / RMS-normalised), per-vector int8 quantisation
-  const float* xsrc = a.x;
   const uint16_t* erow = nullptr;
   if (a.embed) {
     int tok = a.st->cur_token;
@@ -130,13 +182,17 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(MvArgs a) {
                       __uint_as_float(b.y & 0xFFFF0000u));
       if (blockIdx.x == 0) *reinterpret_cast<float4*>(a.x_out + i) = v;
     } else {
-      v = *reinterpret_cast<const float4*>(xsrc + i);
+      v = *reinterpret_cast<const float4*>(a.x + i);
     }
     *reinterpret_cast<float4*>(xs + i) = v;
     ss = fmaf(v.x, v.x, ss);
     ss = fmaf(v.y, v.y, ss);
     ss = fmaf(v.z, v.z, ss);
     ss = fmaf(v.w, v.w, ss);
+  }
+  for (int i = K + tid; i < kpad; i += kThreads) {  // padding past K multiplies zero weights
+    xs[i] = 0.f;
+    xq[i] = 0;
   }
   __syncthreads();
   if (a.norm_w) {
@@ -158,86 +214,64 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(MvArgs a) {
   }
   __syncthreads();
 
-  // ---- main loop over weight tiles
+  // ---- main loop over stages (row block b, column chunk kc)
   unsigned long long best = 0ull;
-  for (int t = 0; t < ntiles; ++t) {
-    const int s = t % a.stages;
-    const uint32_t phase = (uint32_t)(t / a.stages) & 1u;
-    mbar_wait(&full[s], phase, a.err, 1);
-    const int rows_t = min(a.tile_rows, nrows - t * a.tile_rows);
-    const unsigned char* tw = wst + (size_t)s * a.tile_bytes;
-    // Four rows per warp iteration: the x chunk is loaded once per four weight rows and
-    // the four dot products are reduced together with a transposing butterfly (6
-    // shuffles). Afterwards lane 8*r holds row r (r = 0..3).
-    for (int rr = warp * 4; rr < rows_t; rr += 4 * kWarps) {
-      float acc[4];
-      if (INT8) {
-        int ia[4] = {0, 0, 0, 0};
-        const int8_t* w0 = reinterpret_cast<const int8_t*>(tw) + (size_t)rr * K;
-#pragma unroll 2
-        for (int k0 = lane * 16; k0 < K; k0 += 512) {
-          int4 xv = *reinterpret_cast<const int4*>(xq + k0);
+  int iacc[4] = {0, 0, 0, 0};
+  float facc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int t = 0; t < nt; ++t) {
+    const int s = t % a.stages, b = t / nkc, kc = t % nkc;
+    mbar_wait(&full[s], (uint32_t)(t / a.stages) & 1u, a.err, 1);
+    const unsigned char* tw = wst + (size_t)s * stage_bytes + (size_t)(warp * RPW) * kChunk + lane * 16;
+    if (INT8) {
+      const int4 xv = *reinterpret_cast<const int4*>(xq + kc * kChunk + lane * 16);
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            if (rr + r < rows_t) {
-              int4 w = *reinterpret_cast<const int4*>(w0 + (size_t)r * K + k0);
-              ia[r] = __dp4a(w.x, xv.x, ia[r]);
-              ia[r] = __dp4a(w.y, xv.y, ia[r]);
-              ia[r] = __dp4a(w.z, xv.z, ia[r]);
-              ia[r] = __dp4a(w.w, xv.w, ia[r]);
-            }
-          }
-        }
-        // int32 sums are exact in any order; reduce as ints, convert once
-        int s0 = (lane & 16) ? ia[2] : ia[0], s1 = (lane & 16) ? ia[3] : ia[1];
-        int t0 = (lane & 16) ? ia[0] : ia[2], t1 = (lane & 16) ? ia[1] : ia[3];
-        s0 += __shfl_xor_sync(0xffffffffu, t0, 16);
-        s1 += __shfl_xor_sync(0xffffffffu, t1, 16);
-        int u = (lane & 8) ? s1 : s0, w = (lane & 8) ? s0 : s1;
-        u += __shfl_xor_sync(0xffffffffu, w, 8);
-        u += __shfl_xor_sync(0xffffffffu, u, 4);
-        u += __shfl_xor_sync(0xffffffffu, u, 2);
-        u += __shfl_xor_sync(0xffffffffu, u, 1);
-        const int myr = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
-        const int lr = t * a.tile_rows + rr + myr;
-        acc[0] = (rr + myr < rows_t) ? __fmul_rn(__fmul_rn((float)u, xscale), sws[lr]) : 0.f;
-      } else {
-        float fa[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint16_t* w0 = reinterpret_cast<const uint16_t*>(tw) + (size_t)rr * K;
-#pragma unroll 2
-        for (int k0 = lane * 8; k0 < K; k0 += 256) {
-          float4 x0 = *reinterpret_cast<const float4*>(xs + k0);
-          float4 x1 = *reinterpret_cast<const float4*>(xs + k0 + 4);
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            if (rr + r < rows_t) {
-              float f[8];
-              bf16x8_to_f32(*reinterpret_cast<const uint4*>(w0 + (size_t)r * K + k0), f);
-              fa[r] = fmaf(f[0], x0.x, fa[r]); fa[r] = fmaf(f[1], x0.y, fa[r]);
-              fa[r] = fmaf(f[2], x0.z, fa[r]); fa[r] = fmaf(f[3], x0.w, fa[r]);
-              fa[r] = fmaf(f[4], x1.x, fa[r]); fa[r] = fmaf(f[5], x1.y, fa[r]);
-              fa[r] = fmaf(f[6], x1.z, fa[r]); fa[r] = fmaf(f[7], x1.w, fa[r]);
-            }
-          }
-        }
-        float s0 = (lane & 16) ? fa[2] : fa[0], s1 = (lane & 16) ? fa[3] : fa[1];
-        float t0 = (lane & 16) ? fa[0] : fa[2], t1 = (lane & 16) ? fa[1] : fa[3];
-        s0 += __shfl_xor_sync(0xffffffffu, t0, 16);
-        s1 += __shfl_xor_sync(0xffffffffu, t1, 16);
-        float u = (lane & 8) ? s1 : s0, w = (lane & 8) ? s0 : s1;
-        u += __shfl_xor_sync(0xffffffffu, w, 8);
-        u += __shfl_xor_sync(0xffffffffu, u, 4);
-        u += __shfl_xor_sync(0xffffffffu, u, 2);
-        u += __shfl_xor_sync(0xffffffffu, u, 1);
-        acc[0] = u;
+      for (int r = 0; r < RPW; ++r) {
+        const int4 w = *reinterpret_cast<const int4*>(tw + r * kChunk);
+        iacc[r] = __dp4a(w.x, xv.x, iacc[r]);
+        iacc[r] = __dp4a(w.y, xv.y, iacc[r]);
+        iacc[r] = __dp4a(w.z, xv.z, iacc[r]);
+        iacc[r] = __dp4a(w.w, xv.w, iacc[r]);
       }
-      const float v = acc[0];
-      const int myr = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
-      const int row = r0 + t * a.tile_rows + rr + myr;
-      const bool valid = (lane & 7) == 0 && rr + myr < rows_t;
+    } else {
+      const float4 x0 = *reinterpret_cast<const float4*>(xs + kc * (kChunk / 2) + lane * 8);
+      const float4 x1 = *reinterpret_cast<const float4*>(xs + kc * (kChunk / 2) + lane * 8 + 4);
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        float f[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(tw + r * kChunk), f);
+        facc[r] = fmaf(f[0], x0.x, facc[r]); facc[r] = fmaf(f[1], x0.y, facc[r]);
+        facc[r] = fmaf(f[2], x0.z, facc[r]); facc[r] = fmaf(f[3], x0.w, facc[r]);
+        facc[r] = fmaf(f[4], x1.x, facc[r]); facc[r] = fmaf(f[5], x1.y, facc[r]);
+        facc[r] = fmaf(f[6], x1.z, facc[r]); facc[r] = fmaf(f[7], x1.w, facc[r]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (tid == 0 && t + a.stages < nt) {
+      mbar_wait(&empty[s], (uint32_t)(t / a.stages) & 1u, a.err, 2);  // every warp is done with it
+      issue(t + a.stages);
+    }
+    if (kc == nkc - 1) {
+      // row block finished: reduce, scale, epilogue
+      float v;
+      if (INT8) {
+        const int u = warp_reduce_rows<RPW>(iacc, lane);  // exact int32 sum
+        const int lr = b * R + warp * RPW + lane_row<RPW>(lane);
+        v = lr < nrows ? __fmul_rn(__fmul_rn((float)u, xscale), sws[lr]) : 0.f;
+      } else {
+        v = warp_reduce_rows<RPW>(facc, lane);
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        iacc[r] = 0;
+        facc[r] = 0.f;
+      }
+      const int lr = b * R + warp * RPW + lane_row<RPW>(lane);
+      const int row = r0 + lr;
+      const bool valid = row_lane<RPW>(lane) && lr < nrows;
       if (EPI == MV_SWIGLU) {
-        const float up = __shfl_down_sync(0xffffffffu, v, 8);  // row myr + 1 (the "up" row)
-        if (valid && (myr & 1) == 0 && rr + myr + 1 < rows_t) a.out[row / 2] = silu_mul(v, up);
+        const float up = __shfl_down_sync(0xffffffffu, v, RPW == 4 ? 8 : 16);  // the paired "up" row
+        if (valid && (lane_row<RPW>(lane) & 1) == 0 && lr + 1 < nrows) a.out[row / 2] = silu_mul(v, up);
       } else if (EPI == MV_ARGMAX) {
         if (valid) {
           if (a.logits) a.logits[row] = v;
@@ -250,12 +284,6 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(MvArgs a) {
         if (valid) a.out[row] = v;
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    if (tid == 0 && t + a.stages < ntiles) {
-      mbar_wait(&empty[s], phase, a.err, 2);  // every warp is done with this stage
-      issue(t + a.stages);
-    }
   }
 
   if (EPI == MV_ARGMAX) {
@@ -267,30 +295,30 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(MvArgs a) {
     if (lane == 0) am_warp[warp] = best;
     __syncthreads();
     if (tid == 0) {
-      unsigned long long b = 0ull;
-      for (int w = 0; w < kWarps; ++w) b = am_warp[w] > b ? am_warp[w] : b;
-      a.am_part[blockIdx.x] = b;
+      unsigned long long bb = 0ull;
+      for (int w = 0; w < kWarps; ++w) bb = am_warp[w] > bb ? am_warp[w] : bb;
+      a.am_part[blockIdx.x] = bb;
       __threadfence();
       is_last = (atomicAdd(a.am_ticket, 1) == (int)gridDim.x - 1);
     }
     __syncthreads();
     if (is_last) {
       __threadfence();
-      unsigned long long b = 0ull;
+      unsigned long long bb = 0ull;
       for (int i = tid; i < (int)gridDim.x; i += kThreads) {
-        unsigned long long v = *((volatile unsigned long long*)a.am_part + i);
-        b = v > b ? v : b;
+        unsigned long long v = __ldcg(a.am_part + i);
+        bb = v > bb ? v : bb;
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
-        unsigned long long t2 = __shfl_xor_sync(0xffffffffu, b, o);
-        b = t2 > b ? t2 : b;
+        unsigned long long t2 = __shfl_xor_sync(0xffffffffu, bb, o);
+        bb = t2 > bb ? t2 : bb;
       }
-      if (lane == 0) am_warp[warp] = b;
+      if (lane == 0) am_warp[warp] = bb;
       __syncthreads();
       if (tid == 0) {
-        for (int w = 0; w < kWarps; ++w) b = am_warp[w] > b ? am_warp[w] : b;
-        int tok = (int)(0xFFFFFFFFu - (unsigned int)(b & 0xFFFFFFFFull));
+        for (int w = 0; w < kWarps; ++w) bb = am_warp[w] > bb ? am_warp[w] : bb;
+        int tok = (int)(0xFFFFFFFFu - (unsigned int)(bb & 0xFFFFFFFFull));
         StepState* st = a.st;
         int step = st->step;
         a.tokens[step] = tok;
@@ -300,6 +328,122 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(MvArgs a) {
         *a.am_ticket = 0;
       }
     }
+  }
+  tline.mark(3);
+}
+
+// Small decode matvec (<= 48 rows per CTA: the o, gate/up and down projections): the CTA's whole
+// weight slab arrives in ONE stage (one TMA box per 512-byte column chunk) issued before
+// the dependency wait; the 16 warps split the (row, chunk) dot products, and each row's
+// chunk partials are summed in a fixed order (deterministic for f32 as well).
+template <bool INT8, int EPI>
+__global__ void __launch_bounds__(kThreads, 1) mv_small_kernel(const __grid_constant__ CUtensorMap wmap, MvArgs a) {
+  Timeline tline;
+  tline.begin(a.tl, a.tl_count, a.kind);
+  extern __shared__ unsigned char sm_raw[];
+  __shared__ float red[32];
+  __shared__ __align__(8) uint64_t bar;
+  unsigned char* sm = (unsigned char*)(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = a.K, nkc = a.nkc, R = a.rows_per_cta;
+  const int kpad = nkc * kChunk / (INT8 ? 1 : 2);
+  unsigned char* wst = sm;  // [kc][R rows][512 B]
+  float* xs = reinterpret_cast<float*>(sm + (size_t)nkc * R * kChunk);
+  int8_t* xq = reinterpret_cast<int8_t*>(xs + kpad);
+  float* sws = reinterpret_cast<float*>(xq + ((kpad + 15) & ~15));
+  float* snw = sws + R;
+  float* part = snw + K;  // [R][nkc] chunk partials (int32 bit patterns for int8)
+  const int r0 = blockIdx.x * R;
+  const int nrows = max(0, min(a.N, r0 + R) - r0);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_expect_tx(&bar, (uint32_t)(nkc * R * kChunk));
+    for (int kc = 0; kc < nkc; ++kc) tma_box(wst + (size_t)kc * R * kChunk, &wmap, kc * (kChunk / 2), r0, &bar);
+  }
+  if (INT8)
+    for (int i = tid; i < nrows; i += kThreads) sws[i] = a.ws[r0 + i];
+  if (a.norm_w)
+    for (int i = tid; i < K; i += kThreads) snw[i] = a.norm_w[i];
+  pdl_launch_dependents();
+  pdl_wait();
+  tline.mark(2);
+  float ss = 0.f;
+  for (int i = tid * 4; i < K; i += kThreads * 4) {
+    float4 v = *reinterpret_cast<const float4*>(a.x + i);
+    *reinterpret_cast<float4*>(xs + i) = v;
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
+  }
+  for (int i = K + tid; i < kpad; i += kThreads) {
+    xs[i] = 0.f;
+    xq[i] = 0;
+  }
+  __syncthreads();
+  if (a.norm_w) {
+    float tot = block_sum(ss, red);
+    float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+    for (int i = tid; i < K; i += kThreads) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), snw[i]);
+  }
+  float xscale = 1.0f;
+  if (INT8) {
+    float mx = 0.f;
+    for (int i = tid; i < K; i += kThreads) mx = fmaxf(mx, fabsf(xs[i]));
+    mx = block_max(mx, red);
+    xscale = mx > 0.f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+    float inv = __fdiv_rn(127.0f, fmaxf(mx, 1e-10f));
+    for (int i = tid; i < K; i += kThreads) {
+      float r = roundf(__fmul_rn(xs[i], inv));
+      xq[i] = (int8_t)fminf(fmaxf(r, -127.f), 127.f);
+    }
+  }
+  __syncthreads();
+  mbar_wait(&bar, 0, a.err, 5);
+  for (int it = warp; it < R * nkc; it += kWarps) {
+    const int r = it / nkc, kc = it % nkc;
+    const unsigned char* w = wst + ((size_t)kc * R + r) * kChunk + lane * 16;
+    if (INT8) {
+      const int4 xv = *reinterpret_cast<const int4*>(xq + kc * kChunk + lane * 16);
+      const int4 wv = *reinterpret_cast<const int4*>(w);
+      int acc = __dp4a(wv.x, xv.x, 0);
+      acc = __dp4a(wv.y, xv.y, acc);
+      acc = __dp4a(wv.z, xv.z, acc);
+      acc = __dp4a(wv.w, xv.w, acc);
+      acc = warp_sum_i(acc);
+      if (lane == 0) part[r * nkc + kc] = __int_as_float(acc);
+    } else {
+      const float4 x0 = *reinterpret_cast<const float4*>(xs + kc * (kChunk / 2) + lane * 8);
+      const float4 x1 = *reinterpret_cast<const float4*>(xs + kc * (kChunk / 2) + lane * 8 + 4);
+      float f[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(w), f);
+      float acc = f[0] * x0.x;
+      acc = fmaf(f[1], x0.y, acc); acc = fmaf(f[2], x0.z, acc); acc = fmaf(f[3], x0.w, acc);
+      acc = fmaf(f[4], x1.x, acc); acc = fmaf(f[5], x1.y, acc); acc = fmaf(f[6], x1.z, acc);
+      acc = fmaf(f[7], x1.w, acc);
+      acc = warp_sum(acc);
+      if (lane == 0) part[r * nkc + kc] = acc;
+    }
+  }
+  __syncthreads();
+  auto row_value = [&](int r) -> float {
+    if (INT8) {
+      int s = 0;
+      for (int kc = 0; kc < nkc; ++kc) s += __float_as_int(part[r * nkc + kc]);
+      return __fmul_rn(__fmul_rn((float)s, xscale), sws[r]);
+    }
+    float v = 0.f;
+    for (int kc = 0; kc < nkc; ++kc) v += part[r * nkc + kc];
+    return v;
+  };
+  if (EPI == MV_SWIGLU) {  // rows (2j, 2j+1) = (gate, up), r0 is even
+    if (2 * tid + 1 < nrows) a.out[(r0 >> 1) + tid] = silu_mul(row_value(2 * tid), row_value(2 * tid + 1));
+  } else if (tid < nrows) {
+    const float v = row_value(tid);
+    const int row = r0 + tid;
+    if (EPI == MV_RESID) a.out[row] = __fadd_rn(v, a.resid[row]);
+    else a.out[row] = v;
   }
   tline.mark(3);
 }
@@ -681,31 +825,27 @@ constexpr int kStageBytes = 24 * 1024;
 constexpr int kSmemBudget = 112 * 1024;  // two decode kernels co-reside on one SM
 
 struct MvPlan {
-  int grid, rows_per_cta, tile_rows, stages, tile_bytes;
+  int grid, rows_per_cta, block_rows, nkc, stages;
   size_t smem;
 };
 
-MvPlan plan_mv(int N, int K, bool int8, int num_sms, bool last_kernel = false) {
+MvPlan plan_mv(int N, int K, bool int8, int num_sms, bool swiglu, bool last_kernel) {
   MvPlan p{};
   const int row_bytes = K * (int8 ? 1 : 2);
-  int rpc = (N + num_sms - 1) / num_sms;
-  rpc += rpc & 1;
-  p.rows_per_cta = rpc;
-  p.grid = (N + rpc - 1) / rpc;
-  int cta_bytes = rpc * row_bytes;
-  int ntiles = (cta_bytes + kStageBytes - 1) / kStageBytes;
-  int tr = (rpc + ntiles - 1) / ntiles;
-  tr += tr & 1;
-  if (tr * row_bytes > kStageBytes && tr > 2) tr = std::max(2, (kStageBytes / row_bytes) & ~1);
-  p.tile_rows = tr;
-  p.tile_bytes = (tr * row_bytes + 127) & ~127;
-  ntiles = (rpc + tr - 1) / tr;
-  size_t fixed = (size_t)K * 9 + 64 + 16 * 8 + (size_t)rpc * 4;
+  const int raw = (N + num_sms - 1) / num_sms;
+  p.block_rows = raw >= 48 ? 64 : (raw >= 24 || swiglu) ? 32 : 16;
+  p.rows_per_cta = (raw + p.block_rows - 1) / p.block_rows * p.block_rows;
+  p.grid = (N + p.rows_per_cta - 1) / p.rows_per_cta;
+  p.nkc = (row_bytes + kChunk - 1) / kChunk;
+  const int kpad = p.nkc * kChunk / (int8 ? 1 : 2);
+  const size_t fixed = 1024 + (size_t)kpad * 4 + kpad + 16 + 16 * 8 + (size_t)p.rows_per_cta * 4 + (size_t)K * 4;
   // The step's last kernel (lm_head) has no successor to share the SM with: deeper ring.
   const size_t budget = last_kernel ? 200 * 1024 : kSmemBudget;
-  int st = (int)((budget - fixed) / p.tile_bytes);
-  p.stages = std::max(1, std::min(std::min(st, last_kernel ? 8 : 4), ntiles));
-  p.smem = (size_t)p.stages * p.tile_bytes + fixed;
+  const size_t stage = (size_t)p.block_rows * kChunk;
+  const int total = (p.rows_per_cta / p.block_rows) * p.nkc;
+  p.stages = (int)std::max<size_t>(2, std::min<size_t>((budget - fixed) / stage, last_kernel ? 8 : 6));
+  p.stages = std::min(p.stages, std::max(total, 1));
+  p.smem = (size_t)p.stages * stage + fixed;
   return p;
 }
 
@@ -737,15 +877,58 @@ void launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
   cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+template <bool INT8, int EPI>
+void mv_launch(const CUtensorMap& map, const MvArgs& m, const MvPlan& p, cudaStream_t s, bool pdl) {
+  const int rpw = p.block_rows / kWarps;
+  if (rpw == 4) launch_ex(mv_kernel<INT8, EPI, 4>, dim3(p.grid), dim3(kThreads), p.smem, s, pdl, 1, map, m);
+  else if (rpw == 2) launch_ex(mv_kernel<INT8, EPI, 2>, dim3(p.grid), dim3(kThreads), p.smem, s, pdl, 1, map, m);
+  else launch_ex(mv_kernel<INT8, EPI, 1>, dim3(p.grid), dim3(kThreads), p.smem, s, pdl, 1, map, m);
+}
+
 template <int EPI>
-void mv(bool int8, MvArgs m, int num_sms, cudaStream_t s, bool pdl = true) {
-  MvPlan p = plan_mv(m.N, m.K, int8, num_sms, EPI == MV_ARGMAX);
+void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pdl = true) {
+  const int row_bytes = m.K * (int8 ? 1 : 2);
+  const int raw = (m.N + num_sms - 1) / num_sms;
+  const int rpc_small = raw + (raw & 1);
+  const int nkc_small = (row_bytes + kChunk - 1) / kChunk;
+  const int kpad_small = nkc_small * kChunk / (int8 ? 1 : 2);
+  const size_t smem_small = 1024 + (size_t)nkc_small * rpc_small * kChunk + (size_t)kpad_small * 5 + 16 +
+                            (size_t)rpc_small * 4 + (size_t)m.K * 4 + (size_t)rpc_small * nkc_small * 4 + 64;
+  if (EPI != MV_ARGMAX && raw <= 48 && smem_small <= 200 * 1024) {
+    // small matrix: one stage per CTA holding the whole slab, K split across warps
+    const int rpc = rpc_small, nkc = nkc_small;
+    const size_t smem = smem_small;
+    m.rows_per_cta = rpc;
+    m.nkc = nkc;
+    CUtensorMap map;
+    if (!make_tma_2d_u16(&map, W, m.N, row_bytes / 2, kChunk / 2, rpc)) {
+      set_error("decode: cannot encode the weight tensor map");
+      return;
+    }
+    dim3 grid((m.N + rpc - 1) / rpc);
+    if (int8) launch_ex(mv_small_kernel<true, EPI>, grid, dim3(kThreads), smem, s, pdl, 1, map, m);
+    else launch_ex(mv_small_kernel<false, EPI>, grid, dim3(kThreads), smem, s, pdl, 1, map, m);
+    return;
+  }
+  MvPlan p = plan_mv(m.N, m.K, int8, num_sms, EPI == MV_SWIGLU, EPI == MV_ARGMAX);
   m.rows_per_cta = p.rows_per_cta;
-  m.tile_rows = p.tile_rows;
+  m.block_rows = p.block_rows;
+  m.nkc = p.nkc;
   m.stages = p.stages;
-  m.tile_bytes = p.tile_bytes;
-  if (int8) launch_ex(mv_kernel<true, EPI>, dim3(p.grid), dim3(kThreads), p.smem, s, pdl, 1, m);
-  else launch_ex(mv_kernel<false, EPI>, dim3(p.grid), dim3(kThreads), p.smem, s, pdl, 1, m);
+  CUtensorMap map;
+  if (!make_tma_2d_u16(&map, W, m.N, row_bytes / 2, kChunk / 2, p.block_rows)) {
+    set_error("decode: cannot encode the weight tensor map");
+    return;
+  }
+  if (int8) mv_launch<true, EPI>(map, m, p, s, pdl);
+  else mv_launch<false, EPI>(map, m, p, s, pdl);
+}
+
+template <bool INT8, int EPI>
+void mv_attr(int bytes) {
+  cudaFuncSetAttribute(mv_kernel<INT8, EPI, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  cudaFuncSetAttribute(mv_kernel<INT8, EPI, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  cudaFuncSetAttribute(mv_kernel<INT8, EPI, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 int sm_count() {
@@ -757,15 +940,19 @@ int sm_count() {
 }  // namespace
 
 void decode_kernels_init() {
-  const int kMax = 200 * 1024;
-  cudaFuncSetAttribute(mv_kernel<true, MV_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
-  cudaFuncSetAttribute(mv_kernel<true, MV_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
-  cudaFuncSetAttribute(mv_kernel<true, MV_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
-  cudaFuncSetAttribute(mv_kernel<true, MV_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
-  cudaFuncSetAttribute(mv_kernel<false, MV_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
-  cudaFuncSetAttribute(mv_kernel<false, MV_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
-  cudaFuncSetAttribute(mv_kernel<false, MV_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
-  cudaFuncSetAttribute(mv_kernel<false, MV_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+  const int kMax = 210 * 1024;
+  for (auto k : {mv_small_kernel<true, MV_RESID>, mv_small_kernel<false, MV_RESID>, mv_small_kernel<true, MV_STORE>,
+                 mv_small_kernel<false, MV_STORE>, mv_small_kernel<true, MV_SWIGLU>,
+                 mv_small_kernel<false, MV_SWIGLU>})
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+  mv_attr<true, MV_STORE>(kMax);
+  mv_attr<true, MV_RESID>(kMax);
+  mv_attr<true, MV_SWIGLU>(kMax);
+  mv_attr<true, MV_ARGMAX>(kMax);
+  mv_attr<false, MV_STORE>(kMax);
+  mv_attr<false, MV_RESID>(kMax);
+  mv_attr<false, MV_SWIGLU>(kMax);
+  mv_attr<false, MV_ARGMAX>(kMax);
   for (auto k : {qkv_attn_kernel<true>, qkv_attn_kernel<false>}) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
     cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -816,34 +1003,34 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
     m.eps = a.eps; m.err = a.err;
     m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 2;
     m.x = a.attn; m.K = qd; m.N = a.hidden;
-    m.W = a.w_o[l]; m.ws = a.s_o[l]; m.out = a.x; m.resid = a.x;
-    mv<MV_RESID>(a.int8, m, nsm, s);
+    m.ws = a.s_o[l]; m.out = a.x; m.resid = a.x;
+    mv<MV_RESID>(a.int8, a.w_o[l], m, nsm, s);
     if (a.on_launch) a.on_launch(a.hook_ctx, 2);
     // gate/up (post-attention RMSNorm fused) + SwiGLU
     m = MvArgs{};
     m.eps = a.eps; m.err = a.err;
     m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 3;
     m.x = a.x; m.norm_w = a.n2[l]; m.K = a.hidden; m.N = 2 * a.inter;
-    m.W = a.w_gu[l]; m.ws = a.s_gu[l]; m.out = a.ffn;
-    mv<MV_SWIGLU>(a.int8, m, nsm, s);
+    m.ws = a.s_gu[l]; m.out = a.ffn;
+    mv<MV_SWIGLU>(a.int8, a.w_gu[l], m, nsm, s);
     if (a.on_launch) a.on_launch(a.hook_ctx, 3);
     // down projection + residual
     m = MvArgs{};
     m.eps = a.eps; m.err = a.err;
     m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 4;
     m.x = a.ffn; m.K = a.inter; m.N = a.hidden;
-    m.W = a.w_down[l]; m.ws = a.s_down[l]; m.out = a.x; m.resid = a.x;
-    mv<MV_RESID>(a.int8, m, nsm, s);
+    m.ws = a.s_down[l]; m.out = a.x; m.resid = a.x;
+    mv<MV_RESID>(a.int8, a.w_down[l], m, nsm, s);
     if (a.on_launch) a.on_launch(a.hook_ctx, 4);
   }
   MvArgs m{};
   m.eps = a.eps; m.err = a.err;
   m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 5;
   m.x = a.x; m.norm_w = a.final_norm; m.K = a.hidden; m.N = a.vocab;
-  m.W = a.lm_w; m.ws = a.lm_s;
+  m.ws = a.lm_s;
   m.am_part = a.am_part; m.am_ticket = a.am_ticket; m.st = a.st; m.tokens = a.tokens; m.forced = a.forced;
   m.logits = a.logits;
-  mv<MV_ARGMAX>(a.int8, m, nsm, s);
+  mv<MV_ARGMAX>(a.int8, a.lm_w, m, nsm, s);
   if (a.on_launch) a.on_launch(a.hook_ctx, 5);
 }
 
