@@ -174,6 +174,12 @@ def cpu_sample(preset, n_samples, seed, tokens, mode, wseed, model_path, n_decod
     return (n_samples / 16000.0) / total, t2 - t0, model
 
 
+def all_host_threads():
+    """BLAS thread pool sized to every host core (torchrun sets OMP_NUM_THREADS=1)."""
+    from threadpoolctl import threadpool_limits
+    return threadpool_limits(limits=os.cpu_count())
+
+
 def cpu_threads():
     try:
         from threadpoolctl import threadpool_info
@@ -190,6 +196,7 @@ def run_reference(args, world, rank, local):
     from qwen_asr_b200 import synth
     d = os.path.join(os.environ.get("QASR_BENCH_DIR", "/tmp/qasr_bench"), f"{preset}-s{wseed}")
     synth.write_model(d, preset, wseed, device="cpu")  # same file as the GPU arm writes
+    all_host_threads()
     model = None
     for _ in range(args.warmup):
         _, _, model = cpu_sample(preset, n, seed, tokens, mode, wseed, d, model=model)
@@ -362,6 +369,7 @@ def run_ours(args, world, rank, local):
         cb = None
         if not args.no_cpu_baseline:
             try:
+                all_host_threads()
                 v1, s1, model = cpu_sample(preset, n, seed, tokens, mode, wseed, d)
                 cb = {"value": round(v1, 4), "unit": "audio-s/s", "cores": cpu_threads(), "kind": "port",
                       "sample": f"mel+encoder+prefill of the full {n / 16000:.1f} s clip + 2 decode steps on the host "
