@@ -28,6 +28,17 @@ void qwen_asr_set_skip_silence(QwenAsrEngine* engine, int32_t on);
 int32_t qwen_asr_set_decode_mode(QwenAsrEngine* engine, int32_t mode);
 /* Benchmark mode: run exactly n decode steps per segment, ignoring EOS (0 = off). */
 void qwen_asr_set_force_n_tokens(QwenAsrEngine* engine, int32_t n);
+/* Transcribes `count` independent segments [starts[i], ends[i]) of one buffer (each padded
+ * to 0.5 s like the -S loop, transcribe.rs:374-384), decoding them in batches. texts_out[i]
+ * receives segment i's text (free with qwen_asr_free_string). Returns 0, or -1 on error
+ * (qwen_asr_last_error). Used to shard one clip's segments over several GPUs. */
+int32_t qwen_asr_transcribe_segments(QwenAsrEngine* engine, const float* samples, int64_t n_samples,
+                                     const int64_t* starts, const int64_t* ends, int32_t count, char** texts_out);
+/* Segmented transcription (segment_sec > 0, past-text conditioning off) decodes up to n
+ * segments together, reading the decoder weights once per step for all of them; the text
+ * is identical to one-at-a-time decoding. 0 (default) = the largest batch the decode
+ * kernels admit for the loaded model, 1 = sequential. Returns the batch that will be used. */
+int32_t qwen_asr_set_decode_batch(QwenAsrEngine* engine, int32_t n);
 /* 1 (default): decode steps replay a CUDA graph; 0: plain launches. */
 void qwen_asr_set_use_graph(QwenAsrEngine* engine, int32_t on);
 /* Per-op decode profiler (the reference's --profile counters, kernels/mod.rs:78-168): when

@@ -51,6 +51,9 @@ SIGNATURES = {
     "qwen_asr_set_decode_mode": (C.c_int32, [_VP, C.c_int32]),
     "qwen_asr_set_force_n_tokens": (None, [_VP, C.c_int32]),
     "qwen_asr_set_use_graph": (None, [_VP, C.c_int32]),
+    "qwen_asr_set_decode_batch": (C.c_int32, [_VP, C.c_int32]),
+    "qwen_asr_transcribe_segments": (C.c_int32, [_VP, _F32P, C.c_int64, C.POINTER(C.c_int64), C.POINTER(C.c_int64),
+                                                 C.c_int32, C.POINTER(C.c_void_p)]),
     "qwen_asr_last_tokens": (C.c_int32, [_VP, C.c_int32, _I32P, C.c_int32]),
     "qwen_asr_set_profile": (None, [_VP, C.c_int32]),
     "qwen_asr_set_timeline": (None, [_VP, C.c_int32]),
@@ -172,6 +175,20 @@ class Engine:
 
     def set_force_n_tokens(self, n: int):
         lib().qwen_asr_set_force_n_tokens(self._h, n)
+
+    def transcribe_segments(self, samples, bounds) -> list[str | None]:
+        """Texts of the independent segments [a, b) of `samples`, decoded in batches."""
+        a, p = _f32(samples)
+        k = len(bounds)
+        st = (C.c_int64 * max(k, 1))(*[int(s) for s, _ in bounds])
+        en = (C.c_int64 * max(k, 1))(*[int(e) for _, e in bounds])
+        out = (C.c_void_p * max(k, 1))()
+        if lib().qwen_asr_transcribe_segments(self._h, p, len(a), st, en, k, out) != 0:
+            raise RuntimeError(last_error())
+        return [_take_string(out[i]) for i in range(k)]
+
+    def set_decode_batch(self, n: int) -> int:
+        return lib().qwen_asr_set_decode_batch(self._h, n)
 
     def set_use_graph(self, on: bool):
         lib().qwen_asr_set_use_graph(self._h, int(on))

@@ -180,6 +180,37 @@ int32_t qwen_asr_set_decode_mode(QwenAsrEngine* e, int32_t mode) {
 void qwen_asr_set_force_n_tokens(QwenAsrEngine* e, int32_t n) {
   if (e) e->ctx.force_n_tokens = n > 0 ? n : 0;
 }
+int32_t qwen_asr_transcribe_segments(QwenAsrEngine* e, const float* samples, int64_t n_samples, const int64_t* starts,
+                                     const int64_t* ends, int32_t count, char** texts_out) {
+  if (!e || !samples || n_samples <= 0 || !starts || !ends || count < 0 || (count > 0 && !texts_out)) return -1;
+  std::vector<std::pair<size_t, size_t>> bounds;
+  for (int32_t i = 0; i < count; ++i) {
+    if (starts[i] < 0 || ends[i] < starts[i] || ends[i] > n_samples) {
+      qasr::set_error("transcribe_segments: segment " + std::to_string(i) + " is out of range");
+      return -1;
+    }
+    bounds.emplace_back((size_t)starts[i], (size_t)ends[i]);
+  }
+  std::vector<std::string> texts;
+  try {
+    e->ctx.reset_perf();
+    e->ctx.last_tokens.clear();
+    e->ctx.perf_audio_ms = 1000.0 * (double)n_samples / qasr::kSampleRate;
+    if (!e->ctx.transcribe_segment_list(samples, (size_t)n_samples, bounds, texts)) return -1;
+  } catch (const std::exception& ex) {
+    qasr::set_error(std::string("transcribe_segments: ") + ex.what());
+    return -1;
+  }
+  for (int32_t i = 0; i < count; ++i) texts_out[i] = to_c_string(texts[i]);
+  return 0;
+}
+
+int32_t qwen_asr_set_decode_batch(QwenAsrEngine* e, int32_t n) {
+  if (!e) return 0;
+  e->ctx.decode_batch = n > 0 ? n : 0;
+  const int lim = e->ctx.eng.max_decode_batch();
+  return n > 0 ? std::min<int32_t>(n, lim) : lim;
+}
 void qwen_asr_set_use_graph(QwenAsrEngine* e, int32_t on) {
   if (e) e->ctx.eng.use_graph = on != 0;
 }

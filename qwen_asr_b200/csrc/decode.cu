@@ -24,24 +24,28 @@ constexpr int kMaxG = 4;     // q heads per kv head
 
 enum MvEpi { MV_STORE = 0, MV_RESID = 1, MV_SWIGLU = 2, MV_ARGMAX = 3 };
 
+constexpr int kMaxB = 8;  // sequences per batched decode launch
+
 struct MvArgs {
-  const float* x;              // input vector [K]
-  const __nv_bfloat16* embed;  // optional: take x from embed[st->cur_token] when >= 0
-  float* x_out;                // written with the gathered embedding row by CTA 0
+  const float* x;              // input vectors [B][ldx]
+  const __nv_bfloat16* embed;  // optional: take x_b from embed[st[b].cur_token] when >= 0
+  float* x_out;                // the gathered embedding rows are written here by CTA 0
   const float* norm_w;         // fused RMSNorm weight or null
   float eps;
   int K, N;
+  int B, ldx, ldo;             // batch, row stride of x (and x_out) and of out/resid
   const float* ws;             // int8 row scales
-  float* out;
-  const float* resid;          // may alias out
+  float* out;                  // [B][ldo]
+  const float* resid;          // [B][ldo], may alias out
   int rows_per_cta;            // multiple of block_rows
   int block_rows;              // R: 16, 32 or 64 weight rows per stage (R / 16 per warp)
   int nkc;                     // 512-byte column chunks per row
   int stages;
-  unsigned long long* am_part;
+  unsigned long long* am_part; // [B][gridDim.x]
   int* am_ticket;
-  StepState* st;
-  int* tokens;
+  StepState* st;               // [B]
+  int* tokens;                 // [B][tokens_ld]
+  int tokens_ld;
   const int* forced;
   float* logits;
   int* err;
@@ -58,7 +62,7 @@ __device__ __forceinline__ unsigned long long am_key(float v, int idx) {
 struct Timeline {
   unsigned long long* slot = nullptr;
   __device__ __forceinline__ void begin(unsigned long long* tl, int* cnt, int kind) {
-    if (tl && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+    if (tl && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0) {
       slot = tl + 4 * (size_t)atomicAdd(cnt, 1);
       slot[0] = (unsigned long long)kind;
       slot[1] = global_timer_ns();
@@ -79,9 +83,9 @@ __device__ __forceinline__ void tma_box(void* dst, const CUtensorMap* map, int x
       : "memory");
 }
 
-// Reduces v[0..RPW) over the warp; afterwards lane `row_lane(r)` holds row r's sum.
+// Reduces v[0..RPW) over the warp; afterwards lane `row_lane` holds row r's sum.
 template <int RPW, typename T>
-__device__ __forceinline__ T warp_reduce_rows(const T (&v)[4], int lane) {
+__device__ __forceinline__ T warp_reduce_rows(const T* v, int lane) {
   if (RPW == 4) {
     T s0 = (lane & 16) ? v[2] : v[0], s1 = (lane & 16) ? v[3] : v[1];
     T t0 = (lane & 16) ? v[0] : v[2], t1 = (lane & 16) ? v[1] : v[3];
@@ -117,27 +121,141 @@ __device__ __forceinline__ bool row_lane(int lane) {
   return RPW == 4 ? (lane & 7) == 0 : (RPW == 2 ? (lane & 15) == 0 : lane == 0);
 }
 
-// Decode matvec y = epi(W x). Each CTA owns rows_per_cta rows; the rows stream through a
-// ring of shared-memory stages holding R rows x 512 bytes each (2-D TMA boxes, the first
-// ones issued before the dependency wait). Every warp owns R/16 rows of a stage, so all 16
-// warps work on every stage, accumulating across the row's 512-byte chunks.
+// Stages sequence b's input vector in shared memory: gathered from the embedding (layer 0)
+// or read from x, RMS-normalised when norm_w is set, and for int8 weights quantised per
+// vector (kernels/mod.rs:1795-1802) into xq_b; returns the activation scale (1 for bf16).
+template <bool INT8>
+__device__ float stage_x(const MvArgs& a, int b, float* xs_b, int8_t* xq_b, const float* snw, float* red, int kpad) {
+  const int tid = threadIdx.x, K = a.K;
+  const uint16_t* erow = nullptr;
+  if (a.embed) {
+    int tok = a.st[b].cur_token;
+    if (tok >= 0) erow = reinterpret_cast<const uint16_t*>(a.embed) + (size_t)tok * K;
+  }
+  const float* xsrc = a.x + (size_t)b * a.ldx;
+  float ss = 0.f;
+  for (int i = tid * 4; i < K; i += kThreads * 4) {
+    float4 v;
+    if (erow) {
+      uint2 u = *reinterpret_cast<const uint2*>(erow + i);
+      v = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                      __uint_as_float(u.y & 0xFFFF0000u));
+      if (blockIdx.x == 0) *reinterpret_cast<float4*>(a.x_out + (size_t)b * a.ldx + i) = v;
+    } else {
+      v = *reinterpret_cast<const float4*>(xsrc + i);
+    }
+    *reinterpret_cast<float4*>(xs_b + i) = v;
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
+  }
+  for (int i = K + tid; i < kpad; i += kThreads) {  // padding past K multiplies zero weights
+    xs_b[i] = 0.f;
+    if (INT8) xq_b[i] = 0;
+  }
+  __syncthreads();
+  if (a.norm_w) {
+    float tot = block_sum(ss, red);
+    float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+    for (int i = tid; i < K; i += kThreads) xs_b[i] = __fmul_rn(__fmul_rn(xs_b[i], inv), snw[i]);
+  }
+  float xscale = 1.0f;
+  if (INT8) {
+    float mx = 0.f;
+    for (int i = tid; i < K; i += kThreads) mx = fmaxf(mx, fabsf(xs_b[i]));
+    mx = block_max(mx, red);
+    xscale = mx > 0.f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+    float inv = __fdiv_rn(127.0f, fmaxf(mx, 1e-10f));
+    for (int i = tid; i < K; i += kThreads) {
+      float r = roundf(__fmul_rn(xs_b[i], inv));
+      xq_b[i] = (int8_t)fminf(fmaxf(r, -127.f), 127.f);
+    }
+  }
+  __syncthreads();
+  return xscale;
+}
+
+// Greedy-token bookkeeping of sequence b after its argmax (decoder.rs:550-645 returns the
+// token; transcribe.rs feeds it back as the next input).
+__device__ __forceinline__ void commit_token(const MvArgs& a, int b, unsigned long long key) {
+  const int tok = (int)(0xFFFFFFFFu - (unsigned int)(key & 0xFFFFFFFFull));
+  StepState* st = a.st + b;
+  const int step = st->step;
+  a.tokens[(size_t)b * a.tokens_ld + step] = tok;
+  st->cur_token = (st->forced_mode && a.forced) ? a.forced[step] : tok;
+  st->step = step + 1;
+  st->pos = st->pos + 1;
+}
+
+// Argmax finish shared by the matvec kernels: per-CTA best keys (best[b] in lane 0 of each
+// warp after a warp reduction) -> am_part -> the last CTA to arrive reduces per sequence.
+__device__ __forceinline__ void argmax_finish(const MvArgs& a, const unsigned long long (&best)[kMaxB],
+                                              unsigned long long (*am_warp)[kMaxB], int* is_last) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+  for (int b = 0; b < kMaxB; ++b) {
+    if (b >= a.B) break;
+    unsigned long long v = best[b];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      unsigned long long t2 = __shfl_xor_sync(0xffffffffu, v, o);
+      v = t2 > v ? t2 : v;
+    }
+    if (lane == 0) am_warp[warp][b] = v;
+  }
+  __syncthreads();
+  if (tid < a.B) {
+    unsigned long long v = 0ull;
+    for (int w = 0; w < kWarps; ++w) v = am_warp[w][tid] > v ? am_warp[w][tid] : v;
+    a.am_part[(size_t)tid * gridDim.x + blockIdx.x] = v;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) *is_last = (atomicAdd(a.am_ticket, 1) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (!*is_last) return;
+  __threadfence();
+  for (int b = warp; b < a.B; b += kWarps) {
+    unsigned long long v = 0ull;
+    for (int i = lane; i < (int)gridDim.x; i += 32) {
+      unsigned long long u = __ldcg(a.am_part + (size_t)b * gridDim.x + i);
+      v = u > v ? u : v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      unsigned long long t2 = __shfl_xor_sync(0xffffffffu, v, o);
+      v = t2 > v ? t2 : v;
+    }
+    if (lane == 0) commit_token(a, b, v);
+  }
+  __syncthreads();
+  if (tid == 0) *a.am_ticket = 0;
+}
+
+// Decode matvec y_b = epi(W x_b) for B sequences sharing one weight stream. Each CTA owns
+// rows_per_cta rows; the rows stream through a ring of shared-memory stages holding R rows
+// x 512 bytes each (2-D TMA boxes; the first ones issued before the dependency wait).
+// Every warp owns R/16 rows of a stage and accumulates them for every sequence across the
+// row's 512-byte chunks, so all 16 warps work on every stage.
 template <bool INT8, int EPI, int RPW>
 __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__ CUtensorMap wmap, MvArgs a) {
   Timeline tline;
   tline.begin(a.tl, a.tl_count, a.kind);
   extern __shared__ unsigned char sm_raw[];
   __shared__ float red[32];
-  __shared__ unsigned long long am_warp[kWarps];
+  __shared__ unsigned long long am_warp[kWarps][kMaxB];
+  __shared__ float xscale[kMaxB];
   __shared__ int is_last;
   unsigned char* sm = (unsigned char*)(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int K = a.K, R = a.block_rows, nkc = a.nkc;
+  const int K = a.K, R = a.block_rows, nkc = a.nkc, B = a.B;
   const int kpad = nkc * kChunk / (INT8 ? 1 : 2);  // padded vector length in elements
   const int stage_bytes = R * kChunk;
   unsigned char* wst = sm;
-  float* xs = reinterpret_cast<float*>(sm + (size_t)a.stages * stage_bytes);
-  int8_t* xq = reinterpret_cast<int8_t*>(xs + kpad);
-  uint64_t* full = reinterpret_cast<uint64_t*>(xq + ((kpad + 15) & ~15));
+  float* xs = reinterpret_cast<float*>(sm + (size_t)a.stages * stage_bytes);  // int8: [kpad]; bf16: [B][kpad]
+  int8_t* xq = reinterpret_cast<int8_t*>(xs + (INT8 ? kpad : B * kpad));    // int8: [B][kpad]
+  uint64_t* full = reinterpret_cast<uint64_t*>(xq + (INT8 ? ((B * kpad + 15) & ~15) : 0));
   uint64_t* empty = full + a.stages;
   float* sws = reinterpret_cast<float*>(empty + a.stages);
   float* snw = sws + a.rows_per_cta;
@@ -166,83 +284,63 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__
   pdl_launch_dependents();
   pdl_wait();
   tline.mark(2);
-
-  // ---- prologue: x (optionally gathered / RMS-normalised), per-vector int8 quantisation
-  const uint16_t* erow = nullptr;
-  if (a.embed) {
-    int tok = a.st->cur_token;
-    if (tok >= 0) erow = reinterpret_cast<const uint16_t*>(a.embed) + (size_t)tok * K;
-  }
-  float ss = 0.f;
-  for (int i = tid * 4; i < K; i += kThreads * 4) {
-    float4 v;
-    if (erow) {
-      uint2 b = *reinterpret_cast<const uint2*>(erow + i);
-      v = make_float4(__uint_as_float(b.x << 16), __uint_as_float(b.x & 0xFFFF0000u), __uint_as_float(b.y << 16),
-                      __uint_as_float(b.y & 0xFFFF0000u));
-      if (blockIdx.x == 0) *reinterpret_cast<float4*>(a.x_out + i) = v;
-    } else {
-      v = *reinterpret_cast<const float4*>(a.x + i);
-    }
-    *reinterpret_cast<float4*>(xs + i) = v;
-    ss = fmaf(v.x, v.x, ss);
-    ss = fmaf(v.y, v.y, ss);
-    ss = fmaf(v.z, v.z, ss);
-    ss = fmaf(v.w, v.w, ss);
-  }
-  for (int i = K + tid; i < kpad; i += kThreads) {  // padding past K multiplies zero weights
-    xs[i] = 0.f;
-    xq[i] = 0;
-  }
-  __syncthreads();
-  if (a.norm_w) {
-    float tot = block_sum(ss, red);
-    float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
-    for (int i = tid; i < K; i += kThreads) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), snw[i]);
-  }
-  float xscale = 1.0f;
-  if (INT8) {
-    float mx = 0.f;
-    for (int i = tid; i < K; i += kThreads) mx = fmaxf(mx, fabsf(xs[i]));
-    mx = block_max(mx, red);
-    xscale = mx > 0.f ? __fdiv_rn(mx, 127.0f) : 1.0f;
-    float inv = __fdiv_rn(127.0f, fmaxf(mx, 1e-10f));
-    for (int i = tid; i < K; i += kThreads) {
-      float r = roundf(__fmul_rn(xs[i], inv));
-      xq[i] = (int8_t)fminf(fmaxf(r, -127.f), 127.f);
-    }
+  for (int b = 0; b < B; ++b) {
+    float sc = stage_x<INT8>(a, b, INT8 ? xs : xs + (size_t)b * kpad, xq + (size_t)b * kpad, snw, red, kpad);
+    if (tid == 0) xscale[b] = sc;
   }
   __syncthreads();
 
-  // ---- main loop over stages (row block b, column chunk kc)
-  unsigned long long best = 0ull;
-  int iacc[4] = {0, 0, 0, 0};
-  float facc[4] = {0.f, 0.f, 0.f, 0.f};
+  unsigned long long best[kMaxB];
+  int iacc[4][kMaxB];
+  float facc[4][kMaxB];
+#pragma unroll
+  for (int b = 0; b < kMaxB; ++b) {
+    best[b] = 0ull;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      iacc[r][b] = 0;
+      facc[r][b] = 0.f;
+    }
+  }
   for (int t = 0; t < nt; ++t) {
-    const int s = t % a.stages, b = t / nkc, kc = t % nkc;
+    const int s = t % a.stages, blk = t / nkc, kc = t % nkc;
     mbar_wait(&full[s], (uint32_t)(t / a.stages) & 1u, a.err, 1);
     const unsigned char* tw = wst + (size_t)s * stage_bytes + (size_t)(warp * RPW) * kChunk + lane * 16;
     if (INT8) {
-      const int4 xv = *reinterpret_cast<const int4*>(xq + kc * kChunk + lane * 16);
+      int4 w[RPW];
 #pragma unroll
-      for (int r = 0; r < RPW; ++r) {
-        const int4 w = *reinterpret_cast<const int4*>(tw + r * kChunk);
-        iacc[r] = __dp4a(w.x, xv.x, iacc[r]);
-        iacc[r] = __dp4a(w.y, xv.y, iacc[r]);
-        iacc[r] = __dp4a(w.z, xv.z, iacc[r]);
-        iacc[r] = __dp4a(w.w, xv.w, iacc[r]);
+      for (int r = 0; r < RPW; ++r) w[r] = *reinterpret_cast<const int4*>(tw + r * kChunk);
+#pragma unroll
+      for (int b = 0; b < kMaxB; ++b) {
+        if (b >= B) break;
+        const int4 xv = *reinterpret_cast<const int4*>(xq + (size_t)b * kpad + kc * kChunk + lane * 16);
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+          iacc[r][b] = __dp4a(w[r].x, xv.x, iacc[r][b]);
+          iacc[r][b] = __dp4a(w[r].y, xv.y, iacc[r][b]);
+          iacc[r][b] = __dp4a(w[r].z, xv.z, iacc[r][b]);
+          iacc[r][b] = __dp4a(w[r].w, xv.w, iacc[r][b]);
+        }
       }
     } else {
-      const float4 x0 = *reinterpret_cast<const float4*>(xs + kc * (kChunk / 2) + lane * 8);
-      const float4 x1 = *reinterpret_cast<const float4*>(xs + kc * (kChunk / 2) + lane * 8 + 4);
+      float f[RPW][8];
 #pragma unroll
-      for (int r = 0; r < RPW; ++r) {
-        float f[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(tw + r * kChunk), f);
-        facc[r] = fmaf(f[0], x0.x, facc[r]); facc[r] = fmaf(f[1], x0.y, facc[r]);
-        facc[r] = fmaf(f[2], x0.z, facc[r]); facc[r] = fmaf(f[3], x0.w, facc[r]);
-        facc[r] = fmaf(f[4], x1.x, facc[r]); facc[r] = fmaf(f[5], x1.y, facc[r]);
-        facc[r] = fmaf(f[6], x1.z, facc[r]); facc[r] = fmaf(f[7], x1.w, facc[r]);
+      for (int r = 0; r < RPW; ++r) bf16x8_to_f32(*reinterpret_cast<const uint4*>(tw + r * kChunk), f[r]);
+#pragma unroll
+      for (int b = 0; b < kMaxB; ++b) {
+        if (b >= B) break;
+        const float* xb = xs + (size_t)b * kpad + kc * (kChunk / 2) + lane * 8;
+        const float4 x0 = *reinterpret_cast<const float4*>(xb);
+        const float4 x1 = *reinterpret_cast<const float4*>(xb + 4);
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+          float acc = facc[r][b];
+          acc = fmaf(f[r][0], x0.x, acc); acc = fmaf(f[r][1], x0.y, acc);
+          acc = fmaf(f[r][2], x0.z, acc); acc = fmaf(f[r][3], x0.w, acc);
+          acc = fmaf(f[r][4], x1.x, acc); acc = fmaf(f[r][5], x1.y, acc);
+          acc = fmaf(f[r][6], x1.z, acc); acc = fmaf(f[r][7], x1.w, acc);
+          facc[r][b] = acc;
+        }
       }
     }
     __syncwarp();
@@ -252,107 +350,74 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__
       issue(t + a.stages);
     }
     if (kc == nkc - 1) {
-      // row block finished: reduce, scale, epilogue
-      float v;
-      if (INT8) {
-        const int u = warp_reduce_rows<RPW>(iacc, lane);  // exact int32 sum
-        const int lr = b * R + warp * RPW + lane_row<RPW>(lane);
-        v = lr < nrows ? __fmul_rn(__fmul_rn((float)u, xscale), sws[lr]) : 0.f;
-      } else {
-        v = warp_reduce_rows<RPW>(facc, lane);
-      }
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        iacc[r] = 0;
-        facc[r] = 0.f;
-      }
-      const int lr = b * R + warp * RPW + lane_row<RPW>(lane);
+      // row block finished: reduce, scale, epilogue for every sequence
+      const int lr = blk * R + warp * RPW + lane_row<RPW>(lane);
       const int row = r0 + lr;
       const bool valid = row_lane<RPW>(lane) && lr < nrows;
-      if (EPI == MV_SWIGLU) {
-        const float up = __shfl_down_sync(0xffffffffu, v, RPW == 4 ? 8 : 16);  // the paired "up" row
-        if (valid && (lane_row<RPW>(lane) & 1) == 0 && lr + 1 < nrows) a.out[row / 2] = silu_mul(v, up);
-      } else if (EPI == MV_ARGMAX) {
-        if (valid) {
-          if (a.logits) a.logits[row] = v;
-          unsigned long long k = am_key(v, row);
-          best = k > best ? k : best;
+#pragma unroll
+      for (int b = 0; b < kMaxB; ++b) {
+        if (b >= B) break;
+        float v;
+        if (INT8) {
+          int col[4] = {iacc[0][b], RPW > 1 ? iacc[1][b] : 0, RPW > 2 ? iacc[2][b] : 0, RPW > 3 ? iacc[3][b] : 0};
+          const int u = warp_reduce_rows<RPW>(col, lane);  // exact int32 sum
+          v = lr < nrows ? __fmul_rn(__fmul_rn((float)u, xscale[b]), sws[lr]) : 0.f;
+        } else {
+          float col[4] = {facc[0][b], RPW > 1 ? facc[1][b] : 0.f, RPW > 2 ? facc[2][b] : 0.f,
+                          RPW > 3 ? facc[3][b] : 0.f};
+          v = warp_reduce_rows<RPW>(col, lane);
         }
-      } else if (EPI == MV_RESID) {
-        if (valid) a.out[row] = __fadd_rn(v, a.resid[row]);
-      } else {
-        if (valid) a.out[row] = v;
-      }
-    }
-  }
-
-  if (EPI == MV_ARGMAX) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      unsigned long long t2 = __shfl_xor_sync(0xffffffffu, best, o);
-      best = t2 > best ? t2 : best;
-    }
-    if (lane == 0) am_warp[warp] = best;
-    __syncthreads();
-    if (tid == 0) {
-      unsigned long long bb = 0ull;
-      for (int w = 0; w < kWarps; ++w) bb = am_warp[w] > bb ? am_warp[w] : bb;
-      a.am_part[blockIdx.x] = bb;
-      __threadfence();
-      is_last = (atomicAdd(a.am_ticket, 1) == (int)gridDim.x - 1);
-    }
-    __syncthreads();
-    if (is_last) {
-      __threadfence();
-      unsigned long long bb = 0ull;
-      for (int i = tid; i < (int)gridDim.x; i += kThreads) {
-        unsigned long long v = __ldcg(a.am_part + i);
-        bb = v > bb ? v : bb;
+        float* ob = a.out + (size_t)b * a.ldo;
+        if (EPI == MV_SWIGLU) {
+          const float up = __shfl_down_sync(0xffffffffu, v, RPW == 4 ? 8 : 16);  // the paired "up" row
+          if (valid && (lane_row<RPW>(lane) & 1) == 0 && lr + 1 < nrows) ob[row / 2] = silu_mul(v, up);
+        } else if (EPI == MV_ARGMAX) {
+          if (valid) {
+            if (a.logits) a.logits[(size_t)b * a.N + row] = v;
+            unsigned long long k = am_key(v, row);
+            best[b] = k > best[b] ? k : best[b];
+          }
+        } else if (EPI == MV_RESID) {
+          if (valid) ob[row] = __fadd_rn(v, a.resid[(size_t)b * a.ldo + row]);
+        } else {
+          if (valid) ob[row] = v;
+        }
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        unsigned long long t2 = __shfl_xor_sync(0xffffffffu, bb, o);
-        bb = t2 > bb ? t2 : bb;
-      }
-      if (lane == 0) am_warp[warp] = bb;
-      __syncthreads();
-      if (tid == 0) {
-        for (int w = 0; w < kWarps; ++w) bb = am_warp[w] > bb ? am_warp[w] : bb;
-        int tok = (int)(0xFFFFFFFFu - (unsigned int)(bb & 0xFFFFFFFFull));
-        StepState* st = a.st;
-        int step = st->step;
-        a.tokens[step] = tok;
-        st->cur_token = (st->forced_mode && a.forced) ? a.forced[step] : tok;
-        st->step = step + 1;
-        st->pos = st->pos + 1;
-        *a.am_ticket = 0;
-      }
+      for (int b = 0; b < kMaxB; ++b)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          iacc[r][b] = 0;
+          facc[r][b] = 0.f;
+        }
     }
   }
+  if (EPI == MV_ARGMAX) argmax_finish(a, best, am_warp, &is_last);
   tline.mark(3);
 }
 
-// Small decode matvec (<= 48 rows per CTA: the o, gate/up and down projections): the CTA's whole
-// weight slab arrives in ONE stage (one TMA box per 512-byte column chunk) issued before
-// the dependency wait; the 16 warps split the (row, chunk) dot products, and each row's
-// chunk partials are summed in a fixed order (deterministic for f32 as well).
+// Small decode matvec (<= 48 rows per CTA: the o, gate/up and down projections): the CTA's
+// whole weight slab arrives in ONE stage (one TMA box per 512-byte column chunk) issued
+// before the dependency wait; the 16 warps split the (sequence, row, chunk) dot products,
+// and each row's chunk partials are summed in a fixed order (deterministic for f32 too).
 template <bool INT8, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) mv_small_kernel(const __grid_constant__ CUtensorMap wmap, MvArgs a) {
   Timeline tline;
   tline.begin(a.tl, a.tl_count, a.kind);
   extern __shared__ unsigned char sm_raw[];
   __shared__ float red[32];
+  __shared__ float xscale[kMaxB];
   __shared__ __align__(8) uint64_t bar;
   unsigned char* sm = (unsigned char*)(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int K = a.K, nkc = a.nkc, R = a.rows_per_cta;
+  const int K = a.K, nkc = a.nkc, R = a.rows_per_cta, B = a.B;
   const int kpad = nkc * kChunk / (INT8 ? 1 : 2);
   unsigned char* wst = sm;  // [kc][R rows][512 B]
-  float* xs = reinterpret_cast<float*>(sm + (size_t)nkc * R * kChunk);
-  int8_t* xq = reinterpret_cast<int8_t*>(xs + kpad);
-  float* sws = reinterpret_cast<float*>(xq + ((kpad + 15) & ~15));
+  float* xs = reinterpret_cast<float*>(sm + (size_t)nkc * R * kChunk);  // int8: [kpad]; bf16: [B][kpad]
+  int8_t* xq = reinterpret_cast<int8_t*>(xs + (INT8 ? kpad : B * kpad));
+  float* sws = reinterpret_cast<float*>(xq + (INT8 ? ((B * kpad + 15) & ~15) : 0));
   float* snw = sws + R;
-  float* part = snw + K;  // [R][nkc] chunk partials (int32 bit patterns for int8)
+  float* part = snw + K;  // [B][R][nkc] chunk partials (int32 bit patterns for int8)
   const int r0 = blockIdx.x * R;
   const int nrows = max(0, min(a.N, r0 + R) - r0);
   if (tid == 0) {
@@ -368,54 +433,28 @@ __global__ void __launch_bounds__(kThreads, 1) mv_small_kernel(const __grid_cons
   pdl_launch_dependents();
   pdl_wait();
   tline.mark(2);
-  float ss = 0.f;
-  for (int i = tid * 4; i < K; i += kThreads * 4) {
-    float4 v = *reinterpret_cast<const float4*>(a.x + i);
-    *reinterpret_cast<float4*>(xs + i) = v;
-    ss = fmaf(v.x, v.x, ss);
-    ss = fmaf(v.y, v.y, ss);
-    ss = fmaf(v.z, v.z, ss);
-    ss = fmaf(v.w, v.w, ss);
+  for (int b = 0; b < B; ++b) {
+    float sc = stage_x<INT8>(a, b, INT8 ? xs : xs + (size_t)b * kpad, xq + (size_t)b * kpad, snw, red, kpad);
+    if (tid == 0) xscale[b] = sc;
   }
-  for (int i = K + tid; i < kpad; i += kThreads) {
-    xs[i] = 0.f;
-    xq[i] = 0;
-  }
-  __syncthreads();
-  if (a.norm_w) {
-    float tot = block_sum(ss, red);
-    float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
-    for (int i = tid; i < K; i += kThreads) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), snw[i]);
-  }
-  float xscale = 1.0f;
-  if (INT8) {
-    float mx = 0.f;
-    for (int i = tid; i < K; i += kThreads) mx = fmaxf(mx, fabsf(xs[i]));
-    mx = block_max(mx, red);
-    xscale = mx > 0.f ? __fdiv_rn(mx, 127.0f) : 1.0f;
-    float inv = __fdiv_rn(127.0f, fmaxf(mx, 1e-10f));
-    for (int i = tid; i < K; i += kThreads) {
-      float r = roundf(__fmul_rn(xs[i], inv));
-      xq[i] = (int8_t)fminf(fmaxf(r, -127.f), 127.f);
-    }
-  }
-  __syncthreads();
   mbar_wait(&bar, 0, a.err, 5);
-  for (int it = warp; it < R * nkc; it += kWarps) {
-    const int r = it / nkc, kc = it % nkc;
+  const int items = B * R * nkc;
+  for (int it = warp; it < items; it += kWarps) {
+    const int b = it / (R * nkc), r = (it / nkc) % R, kc = it % nkc;
     const unsigned char* w = wst + ((size_t)kc * R + r) * kChunk + lane * 16;
     if (INT8) {
-      const int4 xv = *reinterpret_cast<const int4*>(xq + kc * kChunk + lane * 16);
+      const int4 xv = *reinterpret_cast<const int4*>(xq + (size_t)b * kpad + kc * kChunk + lane * 16);
       const int4 wv = *reinterpret_cast<const int4*>(w);
       int acc = __dp4a(wv.x, xv.x, 0);
       acc = __dp4a(wv.y, xv.y, acc);
       acc = __dp4a(wv.z, xv.z, acc);
       acc = __dp4a(wv.w, xv.w, acc);
       acc = warp_sum_i(acc);
-      if (lane == 0) part[r * nkc + kc] = __int_as_float(acc);
+      if (lane == 0) part[it] = __int_as_float(acc);
     } else {
-      const float4 x0 = *reinterpret_cast<const float4*>(xs + kc * (kChunk / 2) + lane * 8);
-      const float4 x1 = *reinterpret_cast<const float4*>(xs + kc * (kChunk / 2) + lane * 8 + 4);
+      const float* xb = xs + (size_t)b * kpad + kc * (kChunk / 2) + lane * 8;
+      const float4 x0 = *reinterpret_cast<const float4*>(xb);
+      const float4 x1 = *reinterpret_cast<const float4*>(xb + 4);
       float f[8];
       bf16x8_to_f32(*reinterpret_cast<const uint4*>(w), f);
       float acc = f[0] * x0.x;
@@ -423,27 +462,36 @@ __global__ void __launch_bounds__(kThreads, 1) mv_small_kernel(const __grid_cons
       acc = fmaf(f[4], x1.x, acc); acc = fmaf(f[5], x1.y, acc); acc = fmaf(f[6], x1.z, acc);
       acc = fmaf(f[7], x1.w, acc);
       acc = warp_sum(acc);
-      if (lane == 0) part[r * nkc + kc] = acc;
+      if (lane == 0) part[it] = acc;
     }
   }
   __syncthreads();
-  auto row_value = [&](int r) -> float {
+  auto row_value = [&](int b, int r) -> float {
+    const float* p = part + ((size_t)b * R + r) * nkc;
     if (INT8) {
       int s = 0;
-      for (int kc = 0; kc < nkc; ++kc) s += __float_as_int(part[r * nkc + kc]);
-      return __fmul_rn(__fmul_rn((float)s, xscale), sws[r]);
+      for (int kc = 0; kc < nkc; ++kc) s += __float_as_int(p[kc]);
+      return __fmul_rn(__fmul_rn((float)s, xscale[b]), sws[r]);
     }
     float v = 0.f;
-    for (int kc = 0; kc < nkc; ++kc) v += part[r * nkc + kc];
+    for (int kc = 0; kc < nkc; ++kc) v += p[kc];
     return v;
   };
   if (EPI == MV_SWIGLU) {  // rows (2j, 2j+1) = (gate, up), r0 is even
-    if (2 * tid + 1 < nrows) a.out[(r0 >> 1) + tid] = silu_mul(row_value(2 * tid), row_value(2 * tid + 1));
-  } else if (tid < nrows) {
-    const float v = row_value(tid);
-    const int row = r0 + tid;
-    if (EPI == MV_RESID) a.out[row] = __fadd_rn(v, a.resid[row]);
-    else a.out[row] = v;
+    const int half = R / 2;
+    for (int i = tid; i < B * half; i += kThreads) {
+      const int b = i / half, j = i % half;
+      if (2 * j + 1 < nrows) a.out[(size_t)b * a.ldo + (r0 >> 1) + j] = silu_mul(row_value(b, 2 * j), row_value(b, 2 * j + 1));
+    }
+  } else {
+    for (int i = tid; i < B * R; i += kThreads) {
+      const int b = i / R, r = i % R;
+      if (r >= nrows) continue;
+      const float v = row_value(b, r);
+      const int row = r0 + r;
+      if (EPI == MV_RESID) a.out[(size_t)b * a.ldo + row] = __fadd_rn(v, a.resid[(size_t)b * a.ldo + row]);
+      else a.out[(size_t)b * a.ldo + row] = v;
+    }
   }
   tline.mark(3);
 }
@@ -482,14 +530,25 @@ struct QkvAttnArgs {
   int kv_rows;                 // K/V rows per CTA staged in shared memory
   StepState* st;
   float* out;                  // attention output [n_heads * 128]
+  int ldx, ldo;                // per-sequence strides of x / x_out and out (blockIdx.z = sequence)
+  size_t kv_slot_stride;       // floats between the KV caches of consecutive sequences
   int* err;
   unsigned long long* tl;
   int* tl_count;
 };
 
 template <bool INT8>
-__global__ void __launch_bounds__(128) qkv_attn_kernel(QkvAttnArgs a) {
+__global__ void __launch_bounds__(128, 1) qkv_attn_kernel(QkvAttnArgs a) {
   namespace cg = cooperative_groups;
+  {  // sequence blockIdx.z of a batched step: its own residual row, state and KV slot
+    const int b = blockIdx.z;
+    a.x += (size_t)b * a.ldx;
+    if (a.x_out) a.x_out += (size_t)b * a.ldx;
+    a.out += (size_t)b * a.ldo;
+    a.st += b;
+    a.kc += (size_t)b * a.kv_slot_stride;
+    a.vc += (size_t)b * a.kv_slot_stride;
+  }
   Timeline tline;
   tline.begin(a.tl, a.tl_count, 1);
   extern __shared__ __align__(128) unsigned char dsm[];
@@ -821,15 +880,15 @@ __global__ void __launch_bounds__(128) qkv_attn_kernel(QkvAttnArgs a) {
 
 // ------------------------------------------------------------------ host side
 namespace {
-constexpr int kStageBytes = 24 * 1024;
 constexpr int kSmemBudget = 112 * 1024;  // two decode kernels co-reside on one SM
+constexpr size_t kSmallSmemMax = 200 * 1024;
 
 struct MvPlan {
   int grid, rows_per_cta, block_rows, nkc, stages;
   size_t smem;
 };
 
-MvPlan plan_mv(int N, int K, bool int8, int num_sms, bool swiglu, bool last_kernel) {
+MvPlan plan_mv(int N, int K, bool int8, int B, int num_sms, bool swiglu, bool last_kernel) {
   MvPlan p{};
   const int row_bytes = K * (int8 ? 1 : 2);
   const int raw = (N + num_sms - 1) / num_sms;
@@ -838,11 +897,18 @@ MvPlan plan_mv(int N, int K, bool int8, int num_sms, bool swiglu, bool last_kern
   p.grid = (N + p.rows_per_cta - 1) / p.rows_per_cta;
   p.nkc = (row_bytes + kChunk - 1) / kChunk;
   const int kpad = p.nkc * kChunk / (int8 ? 1 : 2);
-  const size_t fixed = 1024 + (size_t)kpad * 4 + kpad + 16 + 16 * 8 + (size_t)p.rows_per_cta * 4 + (size_t)K * 4;
+  const size_t xbytes = int8 ? (size_t)kpad * 4 + (((size_t)B * kpad + 15) & ~(size_t)15) : (size_t)B * kpad * 4;
+  const size_t fixed = 1024 + xbytes + 16 * 8 + (size_t)p.rows_per_cta * 4 + (size_t)K * 4;
   // The step's last kernel (lm_head) has no successor to share the SM with: deeper ring.
-  const size_t budget = last_kernel ? 200 * 1024 : kSmemBudget;
+  // Batched steps read each weight stage for several sequences, so they take the larger
+  // budget as well (fewer resident successors matter less than the longer compute).
+  const size_t budget = (last_kernel || B > 1) ? kSmallSmemMax : kSmemBudget;
   const size_t stage = (size_t)p.block_rows * kChunk;
   const int total = (p.rows_per_cta / p.block_rows) * p.nkc;
+  if (fixed + 2 * stage > budget) {
+    p.stages = 0;
+    return p;
+  }
   p.stages = (int)std::max<size_t>(2, std::min<size_t>((budget - fixed) / stage, last_kernel ? 8 : 6));
   p.stages = std::min(p.stages, std::max(total, 1));
   p.smem = (size_t)p.stages * stage + fixed;
@@ -885,19 +951,27 @@ void mv_launch(const CUtensorMap& map, const MvArgs& m, const MvPlan& p, cudaStr
   else launch_ex(mv_kernel<INT8, EPI, 1>, dim3(p.grid), dim3(kThreads), p.smem, s, pdl, 1, map, m);
 }
 
+// Shared memory of the single-stage small matvec for B sequences (0 when it does not apply).
+size_t small_smem(int N, int K, bool int8, int B, int num_sms, int* rpc_out, int* nkc_out) {
+  const int row_bytes = K * (int8 ? 1 : 2);
+  const int raw = (N + num_sms - 1) / num_sms;
+  const int rpc = raw + (raw & 1);
+  const int nkc = (row_bytes + kChunk - 1) / kChunk;
+  const int kpad = nkc * kChunk / (int8 ? 1 : 2);
+  const size_t xbytes = int8 ? (size_t)kpad * 4 + (((size_t)B * kpad + 15) & ~(size_t)15) : (size_t)B * kpad * 4;
+  if (rpc_out) *rpc_out = rpc;
+  if (nkc_out) *nkc_out = nkc;
+  return 1024 + (size_t)nkc * rpc * kChunk + xbytes + (size_t)rpc * 4 + (size_t)K * 4 + (size_t)B * rpc * nkc * 4 + 64;
+}
+
 template <int EPI>
 void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pdl = true) {
   const int row_bytes = m.K * (int8 ? 1 : 2);
   const int raw = (m.N + num_sms - 1) / num_sms;
-  const int rpc_small = raw + (raw & 1);
-  const int nkc_small = (row_bytes + kChunk - 1) / kChunk;
-  const int kpad_small = nkc_small * kChunk / (int8 ? 1 : 2);
-  const size_t smem_small = 1024 + (size_t)nkc_small * rpc_small * kChunk + (size_t)kpad_small * 5 + 16 +
-                            (size_t)rpc_small * 4 + (size_t)m.K * 4 + (size_t)rpc_small * nkc_small * 4 + 64;
-  if (EPI != MV_ARGMAX && raw <= 48 && smem_small <= 200 * 1024) {
+  int rpc = 0, nkc = 0;
+  const size_t smem_small = small_smem(m.N, m.K, int8, m.B, num_sms, &rpc, &nkc);
+  if (EPI != MV_ARGMAX && raw <= 48 && smem_small <= kSmallSmemMax) {
     // small matrix: one stage per CTA holding the whole slab, K split across warps
-    const int rpc = rpc_small, nkc = nkc_small;
-    const size_t smem = smem_small;
     m.rows_per_cta = rpc;
     m.nkc = nkc;
     CUtensorMap map;
@@ -906,11 +980,15 @@ void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pd
       return;
     }
     dim3 grid((m.N + rpc - 1) / rpc);
-    if (int8) launch_ex(mv_small_kernel<true, EPI>, grid, dim3(kThreads), smem, s, pdl, 1, map, m);
-    else launch_ex(mv_small_kernel<false, EPI>, grid, dim3(kThreads), smem, s, pdl, 1, map, m);
+    if (int8) launch_ex(mv_small_kernel<true, EPI>, grid, dim3(kThreads), smem_small, s, pdl, 1, map, m);
+    else launch_ex(mv_small_kernel<false, EPI>, grid, dim3(kThreads), smem_small, s, pdl, 1, map, m);
     return;
   }
-  MvPlan p = plan_mv(m.N, m.K, int8, num_sms, EPI == MV_SWIGLU, EPI == MV_ARGMAX);
+  MvPlan p = plan_mv(m.N, m.K, int8, m.B, num_sms, EPI == MV_SWIGLU, EPI == MV_ARGMAX);
+  if (p.stages == 0) {
+    set_error("decode: batch too large for the matvec shared memory");
+    return;
+  }
   m.rows_per_cta = p.rows_per_cta;
   m.block_rows = p.block_rows;
   m.nkc = p.nkc;
@@ -959,6 +1037,30 @@ void decode_kernels_init() {
   }
 }
 
+int decode_max_batch(int hidden, int inter, int q_heads, bool int8) {
+  const int nsm = sm_count();
+  const int qd = q_heads * kHd;
+  int best = 1;
+  for (int B = 2; B <= kDecodeMaxBatch; ++B) {
+    bool ok = true;
+    // every matvec must fit either the small kernel or a streaming ring of >= 2 stages
+    const int shapes[4][2] = {{hidden, qd}, {2 * inter, hidden}, {hidden, inter}, {1 << 17, hidden}};
+    for (int i = 0; i < 4 && ok; ++i) {
+      const int N = shapes[i][0], K = shapes[i][1];
+      const int raw = (N + nsm - 1) / nsm;
+      auto small_at = [&](int b) {
+        return i < 3 && raw <= 48 && small_smem(N, K, int8, b, nsm, nullptr, nullptr) <= kSmallSmemMax;
+      };
+      // the kernel (and so the summation order) must be the one a single sequence gets
+      if (small_at(1) != small_at(B)) ok = false;
+      if (!small_at(B) && plan_mv(N, K, int8, B, nsm, i == 1, i == 3).stages == 0) ok = false;
+    }
+    if (!ok) break;
+    best = B;
+  }
+  return best;
+}
+
 void decode_step(const DecodeArgs& a, cudaStream_t s) {
   static thread_local int cached_dev = -1, cached_sms = 148;
   int dev = 0;
@@ -968,12 +1070,21 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
     cached_sms = sm_count();
   }
   const int nsm = cached_sms;
+  const int B = std::max(1, a.batch);
   const int qd = a.q_heads * kHd, kvd = a.kv_heads * kHd;
+  (void)kvd;
+  auto base = [&](int kind) {
+    MvArgs m{};
+    m.eps = a.eps; m.err = a.err;
+    m.tl = a.tl; m.tl_count = a.tl_count; m.kind = kind;
+    m.B = B;
+    return m;
+  };
   for (int l = 0; l < a.layers; ++l) {
-    // QKV projection + attention, one cluster per kv head. The first kernel of a step is a
-    // plain launch: it starts only after the previous step (which advanced StepState and
-    // wrote the last KV row) has completed, so every kernel of the step may read StepState
-    // and earlier KV rows before its dependency wait.
+    // QKV projection + attention, one cluster per (kv head, sequence). The first kernel of a
+    // step is a plain launch: it starts only after the previous step (which advanced
+    // StepState and wrote the last KV row) has completed, so every kernel of the step may
+    // read StepState and earlier KV rows before its dependency wait.
     {
       QkvAttnArgs q{};
       q.x = a.x;
@@ -989,46 +1100,41 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
       q.max_seq = a.max_seq; q.scale = 1.0f / sqrtf((float)kHd);
       q.rows_per_cta = (a.q_heads / a.kv_heads + 2) * kHd / kSplits;
       q.st = a.st; q.out = a.attn; q.err = a.err; q.tl = a.tl; q.tl_count = a.tl_count;
+      q.ldx = a.hidden; q.ldo = qd; q.kv_slot_stride = a.kv_slot_stride;
       const size_t wbytes = ((size_t)q.rows_per_cta * a.hidden * (a.int8 ? 1 : 2) + 127) & ~(size_t)127;
       const size_t tail = (size_t)a.hidden * 5 + 16 + 64 * 4 + (size_t)a.hidden * 4;
       const size_t budget = 200 * 1024;
       q.kv_rows = (int)std::max<long>(0, std::min<long>(24, ((long)budget - (long)(wbytes + tail)) / (2 * kHd * 4)));
       const size_t smem = wbytes + (size_t)q.kv_rows * kHd * 8 + tail;
-      if (a.int8) launch_ex(qkv_attn_kernel<true>, dim3(a.kv_heads, kSplits), dim3(128), smem, s, l != 0, kSplits, q);
-      else launch_ex(qkv_attn_kernel<false>, dim3(a.kv_heads, kSplits), dim3(128), smem, s, l != 0, kSplits, q);
+      const dim3 grid(a.kv_heads, kSplits, B);
+      if (a.int8) launch_ex(qkv_attn_kernel<true>, grid, dim3(128), smem, s, l != 0, kSplits, q);
+      else launch_ex(qkv_attn_kernel<false>, grid, dim3(128), smem, s, l != 0, kSplits, q);
       if (a.on_launch) a.on_launch(a.hook_ctx, 1);
     }
-    MvArgs m{};
     // O projection + residual
-    m.eps = a.eps; m.err = a.err;
-    m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 2;
-    m.x = a.attn; m.K = qd; m.N = a.hidden;
-    m.ws = a.s_o[l]; m.out = a.x; m.resid = a.x;
+    MvArgs m = base(2);
+    m.x = a.attn; m.ldx = qd; m.K = qd; m.N = a.hidden;
+    m.ws = a.s_o[l]; m.out = a.x; m.resid = a.x; m.ldo = a.hidden;
     mv<MV_RESID>(a.int8, a.w_o[l], m, nsm, s);
     if (a.on_launch) a.on_launch(a.hook_ctx, 2);
     // gate/up (post-attention RMSNorm fused) + SwiGLU
-    m = MvArgs{};
-    m.eps = a.eps; m.err = a.err;
-    m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 3;
-    m.x = a.x; m.norm_w = a.n2[l]; m.K = a.hidden; m.N = 2 * a.inter;
-    m.ws = a.s_gu[l]; m.out = a.ffn;
+    m = base(3);
+    m.x = a.x; m.ldx = a.hidden; m.norm_w = a.n2[l]; m.K = a.hidden; m.N = 2 * a.inter;
+    m.ws = a.s_gu[l]; m.out = a.ffn; m.ldo = a.inter;
     mv<MV_SWIGLU>(a.int8, a.w_gu[l], m, nsm, s);
     if (a.on_launch) a.on_launch(a.hook_ctx, 3);
     // down projection + residual
-    m = MvArgs{};
-    m.eps = a.eps; m.err = a.err;
-    m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 4;
-    m.x = a.ffn; m.K = a.inter; m.N = a.hidden;
-    m.ws = a.s_down[l]; m.out = a.x; m.resid = a.x;
+    m = base(4);
+    m.x = a.ffn; m.ldx = a.inter; m.K = a.inter; m.N = a.hidden;
+    m.ws = a.s_down[l]; m.out = a.x; m.resid = a.x; m.ldo = a.hidden;
     mv<MV_RESID>(a.int8, a.w_down[l], m, nsm, s);
     if (a.on_launch) a.on_launch(a.hook_ctx, 4);
   }
-  MvArgs m{};
-  m.eps = a.eps; m.err = a.err;
-  m.tl = a.tl; m.tl_count = a.tl_count; m.kind = 5;
-  m.x = a.x; m.norm_w = a.final_norm; m.K = a.hidden; m.N = a.vocab;
+  MvArgs m = base(5);
+  m.x = a.x; m.ldx = a.hidden; m.norm_w = a.final_norm; m.K = a.hidden; m.N = a.vocab;
   m.ws = a.lm_s;
   m.am_part = a.am_part; m.am_ticket = a.am_ticket; m.st = a.st; m.tokens = a.tokens; m.forced = a.forced;
+  m.tokens_ld = a.tokens_ld;
   m.logits = a.logits;
   mv<MV_ARGMAX>(a.int8, a.lm_w, m, nsm, s);
   if (a.on_launch) a.on_launch(a.hook_ctx, 5);

@@ -9,7 +9,8 @@ namespace qasr {
 
 Engine::~Engine() {
   if (device_ >= 0) cudaSetDevice(device_);
-  if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
+  for (auto& g : graph_exec_)
+    if (g) cudaGraphExecDestroy(g);
   for (void* p : allocs_) cudaFree(p);
   if (hstate_) cudaFreeHost(hstate_);
   if (htokens_) cudaFreeHost(htokens_);
@@ -277,10 +278,12 @@ bool Engine::load(const std::string& dir, int device, bool trunc_quant) {
 
   // ---- decode state
   if (!ensure_kv(4096)) return false;
-  CUDA_OK(cudaMallocHost(&hstate_, sizeof(StepState)), false);
-  if (!dx_.alloc(h) || !dqkv_.alloc(qd + 2 * kvd) || !dattn_.alloc(qd) || !dffn_.alloc(inter) ||
-      !dpart_.alloc((size_t)c.dec_heads * 16 * 130) || !dticket_.alloc(c.dec_kv_heads) || !dam_ticket_.alloc(1) ||
-      !dam_part_.alloc(4096) || !dstate_.alloc(1) || !dlogits_.alloc(c.vocab_size) || !derr_.alloc(1))
+  CUDA_OK(cudaMallocHost(&hstate_, kDecodeMaxBatch * sizeof(StepState)), false);
+  const int mb = kDecodeMaxBatch;
+  if (!dx_.alloc((size_t)mb * h) || !dqkv_.alloc(qd + 2 * kvd) || !dattn_.alloc((size_t)mb * qd) ||
+      !dffn_.alloc((size_t)mb * inter) || !dpart_.alloc((size_t)c.dec_heads * 16 * 130) ||
+      !dticket_.alloc(c.dec_kv_heads) || !dam_ticket_.alloc(1) || !dam_part_.alloc((size_t)mb * 1024) ||
+      !dstate_.alloc(mb) || !dlogits_.alloc(c.vocab_size) || !derr_.alloc(1))
     return false;
   CUDA_OK(cudaMemset(dticket_.p, 0, c.dec_kv_heads * sizeof(int)), false);
   CUDA_OK(cudaMemset(dam_ticket_.p, 0, sizeof(int)), false);
@@ -301,20 +304,23 @@ bool Engine::ensure_kv(int needed) {
   if (needed <= max_seq_ && rope_cap_ >= max_seq_) return true;
   int nm = max_seq_ > 0 ? max_seq_ : 2048;
   while (nm < needed) nm *= 2;
-  size_t per = (size_t)c.dec_layers * c.dec_kv_heads * nm * 128;
+  size_t per = (size_t)slots_ * c.dec_layers * c.dec_kv_heads * nm * 128;
   float *nk = nullptr, *nv = nullptr;
   CUDA_OK(cudaMalloc(&nk, per * 4), false);
   CUDA_OK(cudaMalloc(&nv, per * 4), false);
-  if (kc_.p && kv_len_ > 0) {
-    // copy [layer][head][0..len) rows into the wider layout (decoder.rs:199-231)
-    size_t rows = (size_t)c.dec_layers * c.dec_kv_heads;
-    CUDA_OK(cudaMemcpy2DAsync(nk, (size_t)nm * 128 * 4, kc_.p, (size_t)max_seq_ * 128 * 4, (size_t)kv_len_ * 128 * 4,
-                              rows, cudaMemcpyDeviceToDevice, stream_),
-            false);
-    CUDA_OK(cudaMemcpy2DAsync(nv, (size_t)nm * 128 * 4, vc_.p, (size_t)max_seq_ * 128 * 4, (size_t)kv_len_ * 128 * 4,
-                              rows, cudaMemcpyDeviceToDevice, stream_),
-            false);
-    CUDA_OK(cudaStreamSynchronize(stream_), false);
+  if (kc_.p && max_seq_ > 0) {
+    // copy every (slot, layer, head) row run into the wider layout (decoder.rs:199-231)
+    size_t rows = (size_t)slots_ * c.dec_layers * c.dec_kv_heads;
+    size_t used = (size_t)(slots_ > 1 ? max_seq_ : kv_len_) * 128 * 4;
+    if (used > 0) {
+      CUDA_OK(cudaMemcpy2DAsync(nk, (size_t)nm * 128 * 4, kc_.p, (size_t)max_seq_ * 128 * 4, used, rows,
+                                cudaMemcpyDeviceToDevice, stream_),
+              false);
+      CUDA_OK(cudaMemcpy2DAsync(nv, (size_t)nm * 128 * 4, vc_.p, (size_t)max_seq_ * 128 * 4, used, rows,
+                                cudaMemcpyDeviceToDevice, stream_),
+              false);
+      CUDA_OK(cudaStreamSynchronize(stream_), false);
+    }
   }
   kc_.release();
   vc_.release();
@@ -337,7 +343,31 @@ bool Engine::ensure_kv(int needed) {
   CUDA_OK(cudaMemcpy(rope_cos_, rc.data(), rc.size() * 4, cudaMemcpyHostToDevice), false);
   CUDA_OK(cudaMemcpy(rope_sin_, rs.data(), rs.size() * 4, cudaMemcpyHostToDevice), false);
   rope_cap_ = nm;
-  graph_ok_ = false;
+  ++graph_gen_;
+  return true;
+}
+
+bool Engine::ensure_slots(int n) {
+  if (n <= slots_) return true;
+  const size_t old = (size_t)slots_ * kv_slot_stride(), per = (size_t)n * kv_slot_stride();
+  float *nk = nullptr, *nv = nullptr;
+  CUDA_OK(cudaMalloc(&nk, per * 4), false);
+  if (cudaMalloc(&nv, per * 4) != cudaSuccess) {
+    cudaFree(nk);
+    set_error("cudaMalloc failed for the KV cache slots");
+    return false;
+  }
+  CUDA_OK(cudaMemcpyAsync(nk, kc_.p, old * 4, cudaMemcpyDeviceToDevice, stream_), false);
+  CUDA_OK(cudaMemcpyAsync(nv, vc_.p, old * 4, cudaMemcpyDeviceToDevice, stream_), false);
+  CUDA_OK(cudaStreamSynchronize(stream_), false);
+  kc_.release();
+  vc_.release();
+  kc_.p = nk;
+  kc_.n = per;
+  vc_.p = nv;
+  vc_.n = per;
+  slots_ = n;
+  ++graph_gen_;
   return true;
 }
 
@@ -489,7 +519,7 @@ int Engine::encode(const float* d_mel, int F) {
 }
 
 // ---------------------------------------------------------------------------- prefill
-bool Engine::prefill_ids(const std::vector<int>& ids, const float* d_enc, int start_pos) {
+bool Engine::prefill_ids(const std::vector<int>& ids, const float* d_enc, int start_pos, int slot) {
   cudaSetDevice(device_);
   const int h = cfg_.dec_hidden, n = (int)ids.size();
   if (n < 1) return false;
@@ -497,7 +527,7 @@ bool Engine::prefill_ids(const std::vector<int>& ids, const float* d_enc, int st
   CUDA_OK(cudaMemcpyAsync(ids_.p, ids.data(), n * 4, cudaMemcpyHostToDevice, stream_), false);
   gather_embeds(ids_.p, n, embed_, d_enc, h, px_.p, stream_);
   launches += 1;
-  return run_prefill(n, start_pos);
+  return run_prefill(n, start_pos, slot);
 }
 
 bool Engine::prefill_rows(const float* rows, int n, int start_pos) {
@@ -510,12 +540,12 @@ bool Engine::prefill_rows(const float* rows, int n, int start_pos) {
 
 // px_ holds all n prompt rows; rows [start_pos, n-1) are prefilled at positions
 // start_pos.. and row n-1 becomes the first decode input (transcribe.rs:171-185).
-bool Engine::run_prefill(int n, int start_pos) {
+bool Engine::run_prefill(int n, int start_pos, int slot) {
   const Config& c = cfg_;
   const int h = c.dec_hidden, qd = c.dec_heads * 128, kvd = c.dec_kv_heads * 128, inter = c.dec_intermediate;
   const int S = n - 1 - start_pos;
-  if (S < 0) return false;
-  if (!ensure_kv(n + 1024)) return false;
+  if (S < 0 || slot < 0 || slot >= kDecodeMaxBatch) return false;
+  if (!ensure_slots(slot + 1) || !ensure_kv(n + 1024)) return false;
   if (!pxn_.alloc((size_t)std::max(S, 1) * h) || !pqkv_.alloc((size_t)std::max(S, 1) * (qd + 2 * kvd)) ||
       !patt_.alloc((size_t)std::max(S, 1) * qd) || !pmid_.alloc((size_t)std::max(S, 1) * inter))
     return false;
@@ -525,8 +555,8 @@ bool Engine::run_prefill(int n, int start_pos) {
   const float scale = 1.0f / sqrtf(128.f);
   for (int l = 0; l < c.dec_layers && S > 0; ++l) {
     const DecLayerW& L = dec_layers_[l];
-    float* kc = kc_.p + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
-    float* vc = vc_.p + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
+    float* kc = kc_.p + slot * kv_slot_stride() + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
+    float* vc = vc_.p + slot * kv_slot_stride() + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
     rms_norm_rows(x, pxn_.p, S, h, L.n1, c.dec_rms_norm_eps, stream_);
     GemmArgs a;
     a.M = S; a.N = qd + 2 * kvd; a.K = h; a.A = pxn_.p; a.lda = h; a.B = L.wqkv; a.ldb = h;
@@ -549,15 +579,17 @@ bool Engine::run_prefill(int n, int start_pos) {
     dn.C = x; dn.ldc = h; dn.epi = EPI_RESID; dn.resid = x; dn.ldr = h;
     gemm(dn, stream_);
   }
-  kv_len_ = n - 1;
+  if (slot == 0) kv_len_ = n - 1;
   // first decode input: the last prompt row
-  CUDA_OK(cudaMemcpyAsync(dx_.p, px_.p + (size_t)(n - 1) * h, (size_t)h * 4, cudaMemcpyDeviceToDevice, stream_),
+  CUDA_OK(cudaMemcpyAsync(dx_.p + (size_t)slot * h, px_.p + (size_t)(n - 1) * h, (size_t)h * 4,
+                          cudaMemcpyDeviceToDevice, stream_),
           false);
-  hstate_->pos = n - 1;
-  hstate_->step = 0;
-  hstate_->cur_token = -1;
-  hstate_->forced_mode = 0;
-  CUDA_OK(cudaMemcpyAsync(dstate_.p, hstate_, sizeof(StepState), cudaMemcpyHostToDevice, stream_), false);
+  StepState* hs = hstate_ + slot;
+  hs->pos = n - 1;
+  hs->step = 0;
+  hs->cur_token = -1;
+  hs->forced_mode = 0;
+  CUDA_OK(cudaMemcpyAsync(dstate_.p + slot, hs, sizeof(StepState), cudaMemcpyHostToDevice, stream_), false);
   cudaEventRecord(ev1_, stream_);
   CUDA_OK(cudaEventSynchronize(ev1_), false);
   float ms = 0;
@@ -602,6 +634,7 @@ DecodeArgs Engine::dargs(const int* forced, float* logits) {
   a.k_cache = kc_.p; a.v_cache = vc_.p; a.layers = c.dec_layers;
   a.x = dx_.p; a.qkv = dqkv_.p; a.attn = dattn_.p; a.ffn = dffn_.p; a.part = dpart_.p; a.ticket = dticket_.p;
   a.am_ticket = dam_ticket_.p; a.am_part = dam_part_.p; a.st = dstate_.p; a.tokens = dtokens_.p;
+  a.kv_slot_stride = kv_slot_stride(); a.tokens_ld = tokens_ld_; a.batch = 1;
   a.forced = forced; a.logits = logits; a.err = derr_.p;
   if (timeline_) {
     a.tl = dtl_.p;
@@ -617,20 +650,12 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
   if (max_steps <= 0) return true;
   const int start_pos = hstate_->pos;
   if (!ensure_kv(start_pos + max_steps + 1)) return false;
-  if (dtokens_.n < (size_t)max_steps) {
-    if (!dtokens_.alloc(std::max(max_steps, 2048))) return false;
-    graph_ok_ = false;
-  }
-  if (htokens_cap_ < max_steps) {
-    if (htokens_) cudaFreeHost(htokens_);
-    htokens_cap_ = std::max(max_steps, 2048);
-    CUDA_OK(cudaMallocHost(&htokens_, htokens_cap_ * sizeof(int)), false);
-  }
+  if (!ensure_tokens(max_steps, 1)) return false;
   if (timeline_) {
     size_t need = (size_t)max_steps * (cfg_.dec_layers * 5 + 1) * 4 + 64;
     if (dtl_.n < need) {
       if (!dtl_.alloc(need)) return false;
-      graph_ok_ = false;
+      ++graph_gen_;
     }
     if (!dtl_count_.alloc(1)) return false;
     CUDA_OK(cudaMemsetAsync(dtl_count_.p, 0, sizeof(int), stream_), false);
@@ -684,18 +709,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     for (auto& pe : prof_ev_) cudaEventDestroy(pe.second);
     prof_ev_.clear();
   } else {
-    if (!graph_ok_) {
-      if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
-      graph_exec_ = nullptr;
-      DecodeArgs a = dargs(nullptr, nullptr);
-      cudaGraph_t g;
-      CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);
-      decode_step(a, stream_);
-      CUDA_OK(cudaStreamEndCapture(stream_, &g), false);
-      CUDA_OK(cudaGraphInstantiate(&graph_exec_, g, 0), false);
-      cudaGraphDestroy(g);
-      graph_ok_ = true;
-    }
+    if (!graph_for(1)) return false;
     // Launch in chunks; after each chunk copy its ids back and look for EOS while the
     // next chunk runs (transcribe.rs:194-226 stop rule).
     const int chunk = 16;
@@ -704,7 +718,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     std::vector<cudaEvent_t> evs;
     auto launch_chunk = [&]() -> bool {
       int c = std::min(chunk, max_steps - launched);
-      for (int i = 0; i < c; ++i) CUDA_OK(cudaGraphLaunch(graph_exec_, stream_), false);
+      for (int i = 0; i < c; ++i) CUDA_OK(cudaGraphLaunch(graph_exec_[1], stream_), false);
       CUDA_OK(cudaMemcpyAsync(htokens_ + launched, dtokens_.p + launched, c * 4, cudaMemcpyDeviceToHost, stream_),
               false);
       cudaEvent_t e;
@@ -762,6 +776,153 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
   cudaEventElapsedTime(&ms, ev0_, ev1_);
   perf.decode_ms += ms;
   perf.decode_steps += (int)out.size();
+  return true;
+}
+
+bool Engine::ensure_tokens(int max_steps, int B) {
+  const int ld = std::max(tokens_ld_, std::max(max_steps, 2048));
+  const int rows = std::max(B, tokens_rows_);
+  if (ld == tokens_ld_ && rows == tokens_rows_) return true;
+  if (!dtokens_.alloc((size_t)rows * ld)) return false;
+  if (htokens_) cudaFreeHost(htokens_);
+  htokens_ = nullptr;
+  CUDA_OK(cudaMallocHost(&htokens_, (size_t)rows * ld * sizeof(int)), false);
+  tokens_ld_ = ld;
+  tokens_rows_ = rows;
+  ++graph_gen_;
+  return true;
+}
+
+// One captured decode step for batch size B (re-captured after any buffer moved).
+bool Engine::graph_for(int B) {
+  if (built_gen_[B] == graph_gen_ && graph_exec_[B]) return true;
+  if (graph_exec_[B]) cudaGraphExecDestroy(graph_exec_[B]);
+  graph_exec_[B] = nullptr;
+  DecodeArgs a = dargs(nullptr, nullptr);
+  a.batch = B;
+  cudaGraph_t g;
+  CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);
+  decode_step(a, stream_);
+  CUDA_OK(cudaStreamEndCapture(stream_, &g), false);
+  CUDA_OK(cudaGraphInstantiate(&graph_exec_[B], g, 0), false);
+  cudaGraphDestroy(g);
+  built_gen_[B] = graph_gen_;
+  return true;
+}
+
+int Engine::max_decode_batch() {
+  if (max_batch_ == 0) {
+    cudaSetDevice(device_);
+    const Config& c = cfg_;
+    max_batch_ = decode_max_batch(c.dec_hidden, c.dec_intermediate, c.dec_heads, mode_ == DECODE_INT8);
+  }
+  return max_batch_;
+}
+
+bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<std::vector<int>>& out) {
+  cudaSetDevice(device_);
+  out.assign(std::max(B, 0), {});
+  if (B <= 0 || max_steps <= 0) return true;
+  if (B == 1) return decode(max_steps, stop_on_eos, out[0]);
+  if (B > max_decode_batch() || B > slots_) {
+    set_error("decode_batch: batch " + std::to_string(B) + " exceeds the prefilled slots or the kernel limit");
+    return false;
+  }
+  int maxpos = 0;
+  for (int b = 0; b < B; ++b) maxpos = std::max(maxpos, hstate_[b].pos);
+  if (!ensure_kv(maxpos + max_steps + 1) || !ensure_tokens(max_steps, B)) return false;
+  if (timeline_) {
+    size_t need = (size_t)max_steps * (cfg_.dec_layers * 5 + 1) * 4 + 64;
+    if (dtl_.n < need) {
+      if (!dtl_.alloc(need)) return false;
+      ++graph_gen_;
+    }
+    if (!dtl_count_.alloc(1)) return false;
+    CUDA_OK(cudaMemsetAsync(dtl_count_.p, 0, sizeof(int), stream_), false);
+  }
+  if (!graph_for(B)) return false;
+  cudaEventRecord(ev0_, stream_);
+  // Chunks of steps; after each chunk the ids of every sequence come back (one 2-D copy)
+  // and are scanned for EOS while the next chunk runs (transcribe.rs:194-226 per sequence).
+  const int chunk = 16, ld = tokens_ld_;
+  int launched = 0, checked = 0;
+  std::vector<char> done(B, 0);
+  int n_done = 0;
+  std::vector<cudaEvent_t> evs;
+  auto launch_chunk = [&]() -> bool {
+    int c = std::min(chunk, max_steps - launched);
+    for (int i = 0; i < c; ++i) CUDA_OK(cudaGraphLaunch(graph_exec_[B], stream_), false);
+    CUDA_OK(cudaMemcpy2DAsync(htokens_ + launched, (size_t)ld * 4, dtokens_.p + launched, (size_t)ld * 4,
+                              (size_t)c * 4, B, cudaMemcpyDeviceToHost, stream_),
+            false);
+    cudaEvent_t e;
+    cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+    cudaEventRecord(e, stream_);
+    evs.push_back(e);
+    launched += c;
+    return true;
+  };
+  bool ok = launch_chunk();
+  size_t ev_i = 0;
+  bool stop = !ok;
+  while (!stop) {
+    if (launched < max_steps && !launch_chunk()) {
+      ok = false;
+      break;
+    }
+    if (cudaEventSynchronize(evs[ev_i]) != cudaSuccess) {
+      ok = false;
+      break;
+    }
+    const int upto = std::min(max_steps, checked + chunk);
+    for (int b = 0; b < B; ++b) {
+      for (int i = checked; i < upto && !done[b]; ++i) {
+        const int t = htokens_[(size_t)b * ld + i];
+        out[b].push_back(t);
+        if (stop_on_eos && (t == kTokEndOfText || t == kTokImEnd)) {
+          done[b] = 1;
+          ++n_done;
+        }
+      }
+    }
+    checked = upto;
+    ++ev_i;
+    if (checked >= max_steps || n_done == B) stop = true;
+  }
+  cudaStreamSynchronize(stream_);
+  for (auto e : evs) cudaEventDestroy(e);
+  if (!ok) {
+    set_error("decode_batch: launch or copy failed");
+    return false;
+  }
+  CUDA_OK(cudaGetLastError(), false);
+  launches += (long)launched * (5 * cfg_.dec_layers + 1);
+  int herr = 0;
+  CUDA_OK(cudaMemcpy(&herr, derr_.p, sizeof(int), cudaMemcpyDeviceToHost), false);
+  if (herr) {
+    cudaMemset(derr_.p, 0, sizeof(int));
+    set_error("decode: a device-side wait timed out (code " + std::to_string(herr) + ")");
+    return false;
+  }
+  if (timeline_) {
+    int cnt = 0;
+    CUDA_OK(cudaMemcpy(&cnt, dtl_count_.p, sizeof(int), cudaMemcpyDeviceToHost), false);
+    cnt = std::min<int>(cnt, (int)(dtl_.n / 4));
+    last_timeline.resize((size_t)cnt * 4);
+    CUDA_OK(cudaMemcpy(last_timeline.data(), dtl_.p, last_timeline.size() * 8, cudaMemcpyDeviceToHost), false);
+  }
+  size_t longest = 0;
+  for (int b = 0; b < B; ++b) {
+    hstate_[b].pos += (int)out[b].size();
+    longest = std::max(longest, out[b].size());
+  }
+  kv_len_ = hstate_[0].pos;
+  cudaEventRecord(ev1_, stream_);
+  cudaEventSynchronize(ev1_);
+  float ms = 0;
+  cudaEventElapsedTime(&ms, ev0_, ev1_);
+  perf.decode_ms += ms;
+  perf.decode_steps += (int)longest;
   return true;
 }
 

@@ -62,7 +62,9 @@ class Engine {
   // Runs decoder_prefill over rows[0, n-1) starting at KV position `start_pos` (rows
   // before start_pos are not recomputed), then prepares the first decode step from the
   // last row. `enc` may be null when no id references it.
-  bool prefill_ids(const std::vector<int>& ids, const float* d_enc, int start_pos);
+  // `slot` selects the KV cache / decode state of one sequence of a batched decode
+  // (slot 0 is the one decode() continues).
+  bool prefill_ids(const std::vector<int>& ids, const float* d_enc, int start_pos, int slot = 0);
   // Same with prompt embeddings already materialised on the host (streaming LCP path).
   bool prefill_rows(const float* h_rows, int n_rows, int start_pos);
   // Greedy decode: runs up to max_steps decoder_forward steps from the prepared state and
@@ -70,7 +72,18 @@ class Engine {
   // 151643/151645 (inclusive). forced (teacher forcing) gives the input id of step i+1.
   bool decode(int max_steps, bool stop_on_eos, std::vector<int>& out, const std::vector<int>* forced = nullptr,
               std::vector<float>* logits = nullptr);
-  void set_decode_mode(DecodeMode m) { mode_ = m; graph_ok_ = false; }
+  // Batched greedy decode of the sequences prefilled into slots 0..B-1: every step reads
+  // the weights once for all B sequences. Runs until every sequence has produced EOS (with
+  // stop_on_eos) or max_steps; out[b] holds sequence b's ids exactly as decode() would
+  // return them for that sequence alone.
+  bool decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<std::vector<int>>& out);
+  // Largest B decode_batch accepts for this model (shared-memory bound, <= kDecodeMaxBatch).
+  int max_decode_batch();
+  void set_decode_mode(DecodeMode m) {
+    mode_ = m;
+    max_batch_ = 0;
+    ++graph_gen_;
+  }
   DecodeMode decode_mode() const { return mode_; }
   StagePerf perf;
   bool use_graph = true;
@@ -81,7 +94,7 @@ class Engine {
   long prof_n[6] = {0, 0, 0, 0, 0, 0};
   std::vector<std::pair<int, cudaEvent_t>> prof_ev_;
   // Kernel timeline (in-kernel %globaltimer stamps; graph-compatible).
-  void set_timeline(bool on) { timeline_ = on; graph_ok_ = false; }
+  void set_timeline(bool on) { timeline_ = on; ++graph_gen_; }
   std::vector<unsigned long long> last_timeline;
 
   // Debug: final hidden of prefill rows (after the last layer, before final norm).
@@ -123,11 +136,14 @@ class Engine {
   DevBuf<int> win_starts_;
   DevBuf<float> px_, pxn_, pqkv_, patt_, pmid_;
   DevBuf<int> ids_;
-  // KV cache [layers][kv][max_seq][128] f32
+  // KV cache [slot][layers][kv][max_seq][128] f32
   DevBuf<float> kc_, vc_;
   int max_seq_ = 0;
   int kv_len_ = 0;
+  int slots_ = 1;
   bool ensure_kv(int needed);
+  bool ensure_slots(int n);
+  size_t kv_slot_stride() const { return (size_t)cfg_.dec_layers * cfg_.dec_kv_heads * max_seq_ * 128; }
   // decode scratch
   DevBuf<float> dx_, dqkv_, dattn_, dffn_, dpart_, dlogits_;
   DevBuf<int> dticket_, dam_ticket_, dtokens_, dforced_, derr_;
@@ -136,16 +152,20 @@ class Engine {
   bool timeline_ = false;
   DevBuf<unsigned long long> dtl_;
   DevBuf<int> dtl_count_;
-  StepState* hstate_ = nullptr;  // pinned
-  int* htokens_ = nullptr;       // pinned
-  int htokens_cap_ = 0;
-  // decode graph
-  cudaGraphExec_t graph_exec_ = nullptr;
-  bool graph_ok_ = false;
+  StepState* hstate_ = nullptr;  // pinned [kDecodeMaxBatch]
+  int* htokens_ = nullptr;       // pinned [kDecodeMaxBatch][tokens_ld_]
+  int tokens_ld_ = 0;            // per-sequence capacity of dtokens_ / htokens_
+  int tokens_rows_ = 0;
+  bool ensure_tokens(int max_steps, int B);
+  int max_batch_ = 0;
+  // decode graphs, one per batch size; valid while built_gen_[B] == graph_gen_
+  cudaGraphExec_t graph_exec_[kDecodeMaxBatch + 1] = {};
+  unsigned graph_gen_ = 1, built_gen_[kDecodeMaxBatch + 1] = {};
+  bool graph_for(int B);
   std::vector<const void*> pw_qkv_, pw_o_, pw_gu_, pw_down_;
   std::vector<const float*> ps_qkv_, ps_o_, ps_gu_, ps_down_, pn1_, pn2_, pqn_, pkn_;
   DecodeArgs dargs(const int* forced, float* logits);
-  bool run_prefill(int n_rows, int start_pos);  // rows already in px_
+  bool run_prefill(int n_rows, int start_pos, int slot = 0);  // rows already in px_
   cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
 };
 

@@ -149,7 +149,16 @@ struct DecodeArgs {
   // (%globaltimer ns) at tl[4 * atomicAdd(tl_count, 1)].
   unsigned long long* tl = nullptr;
   int* tl_count = nullptr;
+  // Batched step: `batch` sequences (<= kDecodeMaxBatch) share every weight read. x, attn,
+  // ffn, logits, st and am_part hold one row per sequence; sequence b's KV cache starts
+  // kv_slot_stride floats after sequence b-1's, and its tokens at tokens + b * tokens_ld.
+  int batch = 1;
+  size_t kv_slot_stride = 0;
+  int tokens_ld = 0;
 };
+constexpr int kDecodeMaxBatch = 8;
+// Largest batch the decode kernels' shared memory admits for this model shape.
+int decode_max_batch(int hidden, int inter, int q_heads, bool int8);
 // Per-device kernel attributes (dynamic shared memory limits); call once per device.
 void decode_kernels_init();
 void enc_kernels_init();

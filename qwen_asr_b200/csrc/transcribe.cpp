@@ -88,17 +88,7 @@ bool Ctx::encode_window(const float* samples, size_t n, std::vector<float>& enc,
   return cudaMemcpy(enc.data(), eng.enc_out(), enc.size() * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
 }
 
-// transcribe.rs:63-247
-bool Ctx::transcribe_segment(const float* samples, size_t n, const std::vector<int>* past, std::string& text,
-                             int& n_text, bool on_device) {
-  double t0 = now_ms();
-  n_text = 0;
-  StagePerf before = eng.perf;
-  int F = eng.mel(samples, (int)n, on_device);
-  if (F <= 0) return false;
-  int T = eng.encode(eng.mel_buf(), F);
-  if (T <= 0) return false;
-  if (!prepare_prompt_tokens()) return false;
+std::vector<int> Ctx::segment_ids(int T, const std::vector<int>* past) const {
   std::vector<int> ids;
   ids.insert(ids.end(), std::begin(kPrefixHead), std::end(kPrefixHead));
   if (has_prompt_tokens) ids.insert(ids.end(), prompt_tokens.begin(), prompt_tokens.end());
@@ -106,19 +96,18 @@ bool Ctx::transcribe_segment(const float* samples, size_t n, const std::vector<i
   for (int i = 0; i < T; ++i) ids.push_back(-(i + 1));
   ids.insert(ids.end(), std::begin(kSuffixBase), std::end(kSuffixBase));
   if (has_force_tokens) ids.insert(ids.end(), force_prompt_tokens.begin(), force_prompt_tokens.end());
-  bool has_past = past && !past->empty();
-  if (has_past) {
+  if (past && !past->empty()) {
     ids.insert(ids.end(), past->begin(), past->end());
     ids.push_back(kTokAsrText);
   }
-  if (!eng.prefill_ids(ids, eng.enc_out(), 0)) return false;
-  kv_owner = nullptr;
-  std::vector<int> gen;
-  int limit = force_n_tokens > 0 ? force_n_tokens : 2048;
-  if (!eng.decode(limit, force_n_tokens <= 0, gen)) return false;
+  return ids;
+}
+
+int Ctx::segment_text(const std::vector<int>& gen, bool has_past, std::string& text) const {
+  const int limit = force_n_tokens > 0 ? force_n_tokens : 2048;
   bool past_asr = has_force_tokens || has_past;
   std::string bytes;
-  int processed = 0;
+  int processed = 0, n_text = 0;
   for (int t : gen) {
     if (processed >= limit) break;
     ++processed;
@@ -130,10 +119,64 @@ bool Ctx::transcribe_segment(const float* samples, size_t n, const std::vector<i
       ++n_text;
     }
   }
-  last_tokens.push_back(gen);
   text = rust_trim(utf8_lossy(bytes));
+  return n_text;
+}
+
+// transcribe.rs:63-247
+bool Ctx::transcribe_segment(const float* samples, size_t n, const std::vector<int>* past, std::string& text,
+                             int& n_text, bool on_device) {
+  double t0 = now_ms();
+  n_text = 0;
+  StagePerf before = eng.perf;
+  int F = eng.mel(samples, (int)n, on_device);
+  if (F <= 0) return false;
+  int T = eng.encode(eng.mel_buf(), F);
+  if (T <= 0) return false;
+  if (!prepare_prompt_tokens()) return false;
+  const bool has_past = past && !past->empty();
+  if (!eng.prefill_ids(segment_ids(T, past), eng.enc_out(), 0)) return false;
+  kv_owner = nullptr;
+  std::vector<int> gen;
+  const int limit = force_n_tokens > 0 ? force_n_tokens : 2048;
+  if (!eng.decode(limit, force_n_tokens <= 0, gen)) return false;
+  n_text = segment_text(gen, has_past, text);
+  last_tokens.push_back(gen);
   perf_total_ms += now_ms() - t0;
   perf_text_tokens += n_text;
+  perf_encode_ms += (eng.perf.mel_ms - before.mel_ms) + (eng.perf.enc_ms - before.enc_ms);
+  perf_decode_ms += (eng.perf.prefill_ms - before.prefill_ms) + (eng.perf.decode_ms - before.decode_ms);
+  return true;
+}
+
+// Independent segments decoded as one batch: each segment's mel, encoder and prefill run
+// into its own KV slot, then one batched greedy decode serves all of them. A segment whose
+// mel or encoder yields nothing gets an empty text, as transcribe_segment's failure does
+// in the sequential loop (transcribe.rs:386-398 skips it).
+bool Ctx::transcribe_segments_batched(const std::vector<std::vector<float>>& segs, std::vector<std::string>& texts) {
+  double t0 = now_ms();
+  StagePerf before = eng.perf;
+  texts.assign(segs.size(), std::string());
+  std::vector<int> slot_of(segs.size(), -1);
+  int B = 0;
+  for (size_t i = 0; i < segs.size(); ++i) {
+    int F = eng.mel(segs[i].data(), (int)segs[i].size(), false);
+    if (F <= 0) continue;
+    int T = eng.encode(eng.mel_buf(), F);
+    if (T <= 0) continue;
+    if (!eng.prefill_ids(segment_ids(T, nullptr), eng.enc_out(), 0, B)) return false;
+    slot_of[i] = B++;
+  }
+  kv_owner = nullptr;
+  std::vector<std::vector<int>> gen;
+  const int limit = force_n_tokens > 0 ? force_n_tokens : 2048;
+  if (B > 0 && !eng.decode_batch(B, limit, force_n_tokens <= 0, gen)) return false;
+  for (size_t i = 0; i < segs.size(); ++i) {
+    if (slot_of[i] < 0) continue;
+    perf_text_tokens += segment_text(gen[slot_of[i]], false, texts[i]);
+    last_tokens.push_back(gen[slot_of[i]]);
+  }
+  perf_total_ms += now_ms() - t0;
   perf_encode_ms += (eng.perf.mel_ms - before.mel_ms) + (eng.perf.enc_ms - before.enc_ms);
   perf_decode_ms += (eng.perf.prefill_ms - before.prefill_ms) + (eng.perf.decode_ms - before.decode_ms);
   return true;
@@ -153,6 +196,19 @@ bool Ctx::transcribe_audio(const std::vector<float>& in, std::string& result) {
     return transcribe_segment(audio.data(), audio.size(), nullptr, result, nt);
   }
   const size_t min_samples = kSampleRate / 2;
+  if (!past_text_conditioning && (decode_batch == 0 || decode_batch > 1)) {
+    std::vector<std::pair<size_t, size_t>> bounds;
+    for (size_t s = 0; s < splits.size(); ++s)
+      bounds.emplace_back(splits[s], s + 1 < splits.size() ? splits[s + 1] : audio.size());
+    std::vector<std::string> texts;
+    if (!transcribe_segment_list(audio.data(), audio.size(), bounds, texts)) return false;
+    for (const std::string& st : texts) {
+      if (st.empty()) continue;
+      if (!result.empty() && should_insert_boundary_space((uint8_t)result.back(), (uint8_t)st[0])) result += ' ';
+      result += st;
+    }
+    return true;
+  }
   for (size_t s = 0; s < splits.size(); ++s) {
     size_t a = splits[s], b = s + 1 < splits.size() ? splits[s + 1] : audio.size();
     std::vector<float> seg(audio.begin() + a, audio.begin() + b);
@@ -166,6 +222,26 @@ bool Ctx::transcribe_audio(const std::vector<float>& in, std::string& result) {
     if (st.empty()) continue;
     if (!result.empty() && should_insert_boundary_space((uint8_t)result.back(), (uint8_t)st[0])) result += ' ';
     result += st;
+  }
+  return true;
+}
+
+bool Ctx::transcribe_segment_list(const float* samples, size_t n, const std::vector<std::pair<size_t, size_t>>& bounds,
+                                  std::vector<std::string>& texts) {
+  if (!prepare_prompt_tokens()) return false;
+  const size_t min_samples = kSampleRate / 2;
+  const int batch = std::max(1, decode_batch > 0 ? std::min(decode_batch, eng.max_decode_batch()) : eng.max_decode_batch());
+  texts.clear();
+  for (size_t g = 0; g < bounds.size(); g += batch) {
+    std::vector<std::vector<float>> group;
+    for (size_t s = g; s < std::min(bounds.size(), g + batch); ++s) {
+      size_t a = std::min(bounds[s].first, n), b = std::min(std::max(bounds[s].second, a), n);
+      group.emplace_back(samples + a, samples + b);
+      if (group.back().size() < min_samples) group.back().resize(min_samples, 0.f);
+    }
+    std::vector<std::string> part;
+    if (!transcribe_segments_batched(group, part)) return false;
+    texts.insert(texts.end(), part.begin(), part.end());
   }
   return true;
 }

@@ -46,8 +46,12 @@ class Ctx {
   int stream_rollback = 5, stream_unfixed_chunks = 2, stream_max_new_tokens = 32;
   bool past_text_conditioning = false, skip_silence = false;
   std::string prompt, force_language;
-  int force_n_tokens = 0;
-  const void* kv_owner = nullptr;  // stream whose prompt rows the KV cache currently holds  // benchmark extension: exactly N decode steps, EOS ignored
+  int force_n_tokens = 0;          // benchmark extension: exactly N decode steps, EOS ignored
+  // Segments of one transcribe_audio call decoded together (one weight read per step for
+  // all of them); 0 = the engine's largest batch, 1 = one segment at a time. Only used
+  // when past-text conditioning is off (the segments are then independent).
+  int decode_batch = 0;
+  const void* kv_owner = nullptr;  // stream whose prompt rows the KV cache currently holds
   // prompt tokens
   std::vector<int> prompt_tokens, force_prompt_tokens;
   bool has_prompt_tokens = false, has_force_tokens = false, prompt_tokens_ready = false;
@@ -70,9 +74,19 @@ class Ctx {
                           int& n_text, bool on_device = false);
   bool stream_push_audio(const std::vector<float>& samples, StreamState& st, bool finalize, std::string& delta);
   void reset_perf();
+  // Transcribes the independent segments [starts[i], ends[i]) of `samples` (each padded to
+  // 0.5 s as transcribe.rs:374-384 does), batching their decodes; texts[i] per segment.
+  bool transcribe_segment_list(const float* samples, size_t n, const std::vector<std::pair<size_t, size_t>>& bounds,
+                               std::vector<std::string>& texts);
 
  private:
   bool encode_window(const float* samples, size_t n, std::vector<float>& enc, int& seq);
+  // Prompt ids of one segment (transcribe.rs:110-150): chat prefix, optional user prompt,
+  // T encoder rows (ids -1..-T), assistant prefix, forced language, past text.
+  std::vector<int> segment_ids(int T, const std::vector<int>* past) const;
+  // Generated ids -> text (transcribe.rs:194-247); returns the text-token count.
+  int segment_text(const std::vector<int>& gen, bool has_past, std::string& text) const;
+  bool transcribe_segments_batched(const std::vector<std::vector<float>>& segs, std::vector<std::string>& texts);
 };
 
 }  // namespace qasr

@@ -77,13 +77,18 @@ def padded(samples: np.ndarray, a: int, b: int) -> np.ndarray:
 
 
 def transcribe_sharded(transcribe_one, samples: np.ndarray, segment_sec: float, rank: int, world: int,
-                       search_sec: float = 3.0, segs=None):
-    """Every rank transcribes its segments with `transcribe_one(segment_samples) -> str`;
-    returns the joined text on rank 0 (None elsewhere). Collective: all ranks must call."""
+                       search_sec: float = 3.0, segs=None, transcribe_many=None):
+    """Every rank transcribes its segments with `transcribe_one(segment_samples) -> str`, or
+    all of them at once with `transcribe_many(samples, [(a, b), ...]) -> [str]` (the engine's
+    batched-decode entry point); returns the joined text on rank 0 (None elsewhere).
+    Collective: all ranks must call."""
     if segs is None:
         segs = segments(samples, segment_sec, search_sec)
     mine = assign(segs, world)[rank]
-    local = [(i, transcribe_one(padded(samples, *segs[i]))) for i in mine]
+    if transcribe_many is not None:
+        local = list(zip(mine, transcribe_many(samples, [segs[i] for i in mine]) if mine else []))
+    else:
+        local = [(i, transcribe_one(padded(samples, *segs[i]))) for i in mine]
     if world == 1:
         gathered = [local]
     else:

@@ -27,13 +27,18 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, x, q):
+def fake_many(x, bounds):
+    return [fake_text(shard.padded(x, a, b)) for a, b in bounds]
+
+
+def _worker(rank, world, port, x, q, many=False):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     segs = shard.segments(x, 30.0)
-    out = shard.transcribe_sharded(fake_text, x, 30.0, rank, world, segs=segs)
+    out = shard.transcribe_sharded(fake_text, x, 30.0, rank, world, segs=segs,
+                                   transcribe_many=fake_many if many else None)
     if rank == 0:
         q.put(out)
     dist.destroy_process_group()
@@ -67,14 +72,15 @@ def test_join_matches_oracle_rule():
     assert shard.join_texts(texts) == want
 
 
-def test_two_gloo_ranks_match_single_process():
+@pytest.mark.parametrize("many", [False, True])
+def test_two_gloo_ranks_match_single_process(many):
     x = synth.synth_audio(16000 * 130, seed=9)
     segs = shard.segments(x, 30.0)
     single = shard.join_texts([fake_text(shard.padded(x, a, b)) for a, b in segs])
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, x, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, x, q, many)) for r in range(2)]
     for p in procs:
         p.start()
     out = q.get(timeout=120)
