@@ -9,6 +9,10 @@
 #include <cooperative_groups.h>
 #include <cuda.h>
 
+#include <cstdio>
+#include <cstdlib>
+#include <type_traits>
+
 #include "bulk.cuh"
 #include "common.h"
 #include "dev_util.cuh"
@@ -1071,8 +1075,20 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
   }
   const int nsm = cached_sms;
   const int B = std::max(1, a.batch);
-  const int qd = a.q_heads * kHd, kvd = a.kv_heads * kHd;
-  (void)kvd;
+  const int qd = a.q_heads * kHd;
+  static const bool sync_check = getenv("QASR_SYNC_CHECK") != nullptr;
+  auto check = [&](const char* what, int layer) {  // debugging aid: plain launches only
+    if (!sync_check) return;
+    const cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) fprintf(stderr, "decode_step: %s (layer %d, batch %d): %s\n", what, layer, B, cudaGetErrorString(e));
+  };
+  auto run = [&](auto epi_tag, const void* W, const MvArgs& m) {
+    constexpr int EPI = decltype(epi_tag)::value;
+    mv<EPI>(a.int8, W, m, nsm, s);
+  };
+  using Resid = std::integral_constant<int, MV_RESID>;
+  using Swiglu = std::integral_constant<int, MV_SWIGLU>;
+  using Argmax = std::integral_constant<int, MV_ARGMAX>;
   auto base = [&](int kind) {
     MvArgs m{};
     m.eps = a.eps; m.err = a.err;
@@ -1110,25 +1126,29 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
       if (a.int8) launch_ex(qkv_attn_kernel<true>, grid, dim3(128), smem, s, l != 0, kSplits, q);
       else launch_ex(qkv_attn_kernel<false>, grid, dim3(128), smem, s, l != 0, kSplits, q);
       if (a.on_launch) a.on_launch(a.hook_ctx, 1);
+      check("qkv_attn", l);
     }
     // O projection + residual
     MvArgs m = base(2);
     m.x = a.attn; m.ldx = qd; m.K = qd; m.N = a.hidden;
     m.ws = a.s_o[l]; m.out = a.x; m.resid = a.x; m.ldo = a.hidden;
-    mv<MV_RESID>(a.int8, a.w_o[l], m, nsm, s);
+    run(Resid{}, a.w_o[l], m);
     if (a.on_launch) a.on_launch(a.hook_ctx, 2);
+    check("o_proj", l);
     // gate/up (post-attention RMSNorm fused) + SwiGLU
     m = base(3);
     m.x = a.x; m.ldx = a.hidden; m.norm_w = a.n2[l]; m.K = a.hidden; m.N = 2 * a.inter;
     m.ws = a.s_gu[l]; m.out = a.ffn; m.ldo = a.inter;
-    mv<MV_SWIGLU>(a.int8, a.w_gu[l], m, nsm, s);
+    run(Swiglu{}, a.w_gu[l], m);
     if (a.on_launch) a.on_launch(a.hook_ctx, 3);
+    check("gate_up", l);
     // down projection + residual
     m = base(4);
     m.x = a.ffn; m.ldx = a.inter; m.K = a.inter; m.N = a.hidden;
     m.ws = a.s_down[l]; m.out = a.x; m.resid = a.x; m.ldo = a.hidden;
-    mv<MV_RESID>(a.int8, a.w_down[l], m, nsm, s);
+    run(Resid{}, a.w_down[l], m);
     if (a.on_launch) a.on_launch(a.hook_ctx, 4);
+    check("down", l);
   }
   MvArgs m = base(5);
   m.x = a.x; m.ldx = a.hidden; m.norm_w = a.final_norm; m.K = a.hidden; m.N = a.vocab;
@@ -1136,8 +1156,9 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
   m.am_part = a.am_part; m.am_ticket = a.am_ticket; m.st = a.st; m.tokens = a.tokens; m.forced = a.forced;
   m.tokens_ld = a.tokens_ld;
   m.logits = a.logits;
-  mv<MV_ARGMAX>(a.int8, a.lm_w, m, nsm, s);
+  run(Argmax{}, a.lm_w, m);
   if (a.on_launch) a.on_launch(a.hook_ctx, 5);
+  check("lm_head", -1);
 }
 
 }  // namespace qasr

@@ -80,6 +80,7 @@ bool Engine::load(const std::string& dir, int device, bool trunc_quant) {
   if (!detect_config(st, cfg_)) return false;
   CUDA_OK(cudaSetDevice(device), false);
   decode_kernels_init();
+
   enc_kernels_init();
   CUDA_OK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), false);
   CUDA_OK(cudaEventCreate(&ev0_), false);
@@ -709,7 +710,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     for (auto& pe : prof_ev_) cudaEventDestroy(pe.second);
     prof_ev_.clear();
   } else {
-    if (!graph_for(1)) return false;
+    if (!graph_for(0)) return false;
     // Launch in chunks; after each chunk copy its ids back and look for EOS while the
     // next chunk runs (transcribe.rs:194-226 stop rule).
     const int chunk = 16;
@@ -718,7 +719,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     std::vector<cudaEvent_t> evs;
     auto launch_chunk = [&]() -> bool {
       int c = std::min(chunk, max_steps - launched);
-      for (int i = 0; i < c; ++i) CUDA_OK(cudaGraphLaunch(graph_exec_[1], stream_), false);
+      for (int i = 0; i < c; ++i) CUDA_OK(cudaGraphLaunch(graph_exec_[0], stream_), false);
       CUDA_OK(cudaMemcpyAsync(htokens_ + launched, dtokens_.p + launched, c * 4, cudaMemcpyDeviceToHost, stream_),
               false);
       cudaEvent_t e;
@@ -794,12 +795,14 @@ bool Engine::ensure_tokens(int max_steps, int B) {
 }
 
 // One captured decode step for batch size B (re-captured after any buffer moved).
+// Slot 0 holds the single-sequence step of decode(); slot B >= 1 the batched step of
+// decode_batch().
 bool Engine::graph_for(int B) {
   if (built_gen_[B] == graph_gen_ && graph_exec_[B]) return true;
   if (graph_exec_[B]) cudaGraphExecDestroy(graph_exec_[B]);
   graph_exec_[B] = nullptr;
   DecodeArgs a = dargs(nullptr, nullptr);
-  a.batch = B;
+  a.batch = std::max(B, 1);
   cudaGraph_t g;
   CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);
   decode_step(a, stream_);
@@ -823,7 +826,6 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
   cudaSetDevice(device_);
   out.assign(std::max(B, 0), {});
   if (B <= 0 || max_steps <= 0) return true;
-  if (B == 1) return decode(max_steps, stop_on_eos, out[0]);
   if (B > max_decode_batch() || B > slots_) {
     set_error("decode_batch: batch " + std::to_string(B) + " exceeds the prefilled slots or the kernel limit");
     return false;
@@ -840,7 +842,9 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
     if (!dtl_count_.alloc(1)) return false;
     CUDA_OK(cudaMemsetAsync(dtl_count_.p, 0, sizeof(int), stream_), false);
   }
-  if (!graph_for(B)) return false;
+  if (use_graph && !graph_for(B)) return false;
+  DecodeArgs direct_args = dargs(nullptr, nullptr);
+  direct_args.batch = B;
   cudaEventRecord(ev0_, stream_);
   // Chunks of steps; after each chunk the ids of every sequence come back (one 2-D copy)
   // and are scanned for EOS while the next chunk runs (transcribe.rs:194-226 per sequence).
@@ -851,7 +855,10 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
   std::vector<cudaEvent_t> evs;
   auto launch_chunk = [&]() -> bool {
     int c = std::min(chunk, max_steps - launched);
-    for (int i = 0; i < c; ++i) CUDA_OK(cudaGraphLaunch(graph_exec_[B], stream_), false);
+    for (int i = 0; i < c; ++i) {
+      if (use_graph) CUDA_OK(cudaGraphLaunch(graph_exec_[B], stream_), false);
+      else decode_step(direct_args, stream_);
+    }
     CUDA_OK(cudaMemcpy2DAsync(htokens_ + launched, (size_t)ld * 4, dtokens_.p + launched, (size_t)ld * 4,
                               (size_t)c * 4, B, cudaMemcpyDeviceToHost, stream_),
             false);

@@ -226,7 +226,7 @@ std::mutex g_tc_mu;
 
 bool gemm_tc_available() { return get_encode() != nullptr; }
 
-bool make_tma_2d_u16(void* map, const void* base, int rows, int cols, int box_cols, int box_rows) {
+bool make_tma_2d_u16(void* map, const void* base, int rows, int cols, int box_cols, int box_rows, bool swizzle128) {
   EncodeTiledFn enc = get_encode();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -234,8 +234,8 @@ bool make_tma_2d_u16(void* map, const void* base, int rows, int cols, int box_co
   cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   return enc((CUtensorMap*)map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool gemm_tc(const GemmArgs& a, cudaStream_t s) {

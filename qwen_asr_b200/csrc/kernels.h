@@ -43,10 +43,11 @@ bool gemm_tc(const GemmArgs& a, cudaStream_t s);
 bool gemm_tc_available();
 // Nonzero when a bounded wait inside the tensor-core GEMM gave up (clears the flag).
 int gemm_tc_error();
-// 2-D TMA map over a row-major matrix of 16-bit elements [rows][cols] (no swizzle),
-// box = box_cols x box_rows; out-of-range boxes read zeros.
+// 2-D TMA map over a row-major matrix of 16-bit elements [rows][cols], box = box_cols x
+// box_rows; out-of-range boxes read zeros. swizzle128: 128-byte swizzle (box_cols = 64),
+// the K-major operand layout of tcgen05.mma.
 bool make_tma_2d_u16(void* map /* CUtensorMap* */, const void* base, int rows, int cols, int box_cols,
-                     int box_rows);
+                     int box_rows, bool swizzle128 = false);
 
 // ---------------------------------------------------------------- mel front end
 // samples [n] -> windowed frames [F][400] (reflect padding, periodic Hann).
