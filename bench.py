@@ -60,16 +60,21 @@ def measured_hbm_peak():
         return 6650.0, "fallback"
 
 
-def profile_traffic():
-    """Per-step DRAM bytes of the decode kernels from the committed ncu summary, if any."""
+def profile_traffic(avg_pos: float):
+    """DRAM bytes of one decode step, from the committed ncu capture of a step at a known KV
+    position scaled to avg_pos: the weight bytes are fixed, the KV part grows with position."""
     p = os.path.join(ROOT, "profiles", "decode_step_int8_c2.md")
+    vals = {}
     try:
         for line in open(p):
-            if line.startswith("traffic_bytes_per_step:"):
-                return float(line.split(":")[1].strip())
-    except Exception:
-        pass
-    return None
+            k, _, v = line.partition(":")
+            if k in ("captured_bytes_per_step", "captured_pos", "kv_bytes_per_position"):
+                vals[k] = float(v.strip())
+    except OSError:
+        return None
+    if len(vals) != 3:
+        return None
+    return int(vals["captured_bytes_per_step"] + vals["kv_bytes_per_position"] * (avg_pos - vals["captured_pos"]))
 
 
 class ClockSampler:
@@ -361,7 +366,7 @@ def run_ours(args, world, rank, local):
     bytes_step = decode_step_bytes(preset, mode, avg_pos)
     achieved = bytes_step / (step_ms / 1000.0) / 1e9
     peak, peak_kind = measured_hbm_peak()
-    traffic = profile_traffic()
+    traffic = profile_traffic(avg_pos) if (preset, mode) == ("0.6b", "int8") else None
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic,
                 "kernel": f"decode step ({mode} weight matvec chain + attention + lm_head argmax)",
