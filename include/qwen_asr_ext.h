@@ -28,6 +28,12 @@ void qwen_asr_set_skip_silence(QwenAsrEngine* engine, int32_t on);
 int32_t qwen_asr_set_decode_mode(QwenAsrEngine* engine, int32_t mode);
 /* Benchmark mode: run exactly n decode steps per segment, ignoring EOS (0 = off). */
 void qwen_asr_set_force_n_tokens(QwenAsrEngine* engine, int32_t n);
+/* 1 (default): a single sequence decodes through the persistent one-launch-per-step kernel
+ * (one CTA per SM, a TMA producer warp streaming the step's weights, grid barriers between
+ * the phases of a layer) when the device supports it; 0: the multi-kernel chain. */
+void qwen_asr_set_persistent_decode(QwenAsrEngine* engine, int32_t on);
+/* 1 when the last single-sequence decode ran on the persistent kernel. */
+int32_t qwen_asr_persistent_decode_active(QwenAsrEngine* engine);
 /* Transcribes `count` independent segments [starts[i], ends[i]) of one buffer (each padded
  * to 0.5 s like the -S loop, transcribe.rs:374-384), decoding them in batches. texts_out[i]
  * receives segment i's text (free with qwen_asr_free_string). Returns 0, or -1 on error

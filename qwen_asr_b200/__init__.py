@@ -52,6 +52,8 @@ SIGNATURES = {
     "qwen_asr_set_force_n_tokens": (None, [_VP, C.c_int32]),
     "qwen_asr_set_use_graph": (None, [_VP, C.c_int32]),
     "qwen_asr_set_decode_batch": (C.c_int32, [_VP, C.c_int32]),
+    "qwen_asr_set_persistent_decode": (None, [_VP, C.c_int32]),
+    "qwen_asr_persistent_decode_active": (C.c_int32, [_VP]),
     "qwen_asr_transcribe_segments": (C.c_int32, [_VP, _F32P, C.c_int64, C.POINTER(C.c_int64), C.POINTER(C.c_int64),
                                                  C.c_int32, C.POINTER(C.c_void_p)]),
     "qwen_asr_last_tokens": (C.c_int32, [_VP, C.c_int32, _I32P, C.c_int32]),
@@ -186,6 +188,12 @@ class Engine:
         if lib().qwen_asr_transcribe_segments(self._h, p, len(a), st, en, k, out) != 0:
             raise RuntimeError(last_error())
         return [_take_string(out[i]) for i in range(k)]
+
+    def set_persistent_decode(self, on: bool):
+        lib().qwen_asr_set_persistent_decode(self._h, int(on))
+
+    def persistent_decode_active(self) -> bool:
+        return bool(lib().qwen_asr_persistent_decode_active(self._h))
 
     def set_decode_batch(self, n: int) -> int:
         return lib().qwen_asr_set_decode_batch(self._h, n)

@@ -11,6 +11,7 @@ Engine::~Engine() {
   if (device_ >= 0) cudaSetDevice(device_);
   for (auto& g : graph_exec_)
     if (g) cudaGraphExecDestroy(g);
+  if (mega_) mega_destroy(mega_);
   for (void* p : allocs_) cudaFree(p);
   if (hstate_) cudaFreeHost(hstate_);
   if (htokens_) cudaFreeHost(htokens_);
@@ -80,6 +81,7 @@ bool Engine::load(const std::string& dir, int device, bool trunc_quant) {
   if (!detect_config(st, cfg_)) return false;
   CUDA_OK(cudaSetDevice(device), false);
   decode_kernels_init();
+  if (const char* pm = getenv("QASR_DECODE_MEGA")) persistent_ = strcmp(pm, "0") != 0;
 
   enc_kernels_init();
   CUDA_OK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), false);
@@ -644,6 +646,25 @@ DecodeArgs Engine::dargs(const int* forced, float* logits) {
   return a;
 }
 
+bool Engine::mega_usable() {
+  if (!persistent_) return false;
+  if (!mega_ && !mega_tried_) {
+    mega_tried_ = true;
+    mega_ = mega_create(dargs(nullptr, nullptr));
+    cudaGetLastError();
+  }
+  return mega_ != nullptr;
+}
+
+bool Engine::persistent_decode_active() { return persistent_ && !profile && mega_ != nullptr; }
+
+void Engine::enqueue_step(const DecodeArgs& a) {
+  if (persistent_ && a.on_launch == nullptr && mega_ && mega_step(mega_, a, stream_)) return;
+  decode_step(a, stream_);
+}
+
+int Engine::decode_step_launches_1() const { return 5 * cfg_.dec_layers + 1; }
+
 bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, const std::vector<int>* forced,
                     std::vector<float>* logits) {
   cudaSetDevice(device_);
@@ -653,7 +674,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
   if (!ensure_kv(start_pos + max_steps + 1)) return false;
   if (!ensure_tokens(max_steps, 1)) return false;
   if (timeline_) {
-    size_t need = (size_t)max_steps * (cfg_.dec_layers * 5 + 1) * 4 + 64;
+    size_t need = (size_t)max_steps * (cfg_.dec_layers * 10 + 4) * 4 + 64;
     if (dtl_.n < need) {
       if (!dtl_.alloc(need)) return false;
       ++graph_gen_;
@@ -673,6 +694,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
                               stream_),
               false);
     }
+    const bool mega = !profile && mega_usable();
     DecodeArgs a = dargs(forced ? dforced_.p : nullptr, logits ? dlogits_.p : nullptr);
     if (profile) {
       a.on_launch = [](void* ctx, int kind) {
@@ -688,7 +710,8 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     if (logits) logits->resize((size_t)max_steps * V);
     for (int i = 0; i < max_steps; ++i) {
       if (profile) a.on_launch(this, -1);
-      decode_step(a, stream_);
+      if (mega) enqueue_step(a);
+      else decode_step(a, stream_);
       if (logits)
         CUDA_OK(cudaMemcpyAsync(logits->data() + (size_t)i * V, dlogits_.p, (size_t)V * 4, cudaMemcpyDeviceToHost,
                                 stream_),
@@ -698,7 +721,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     CUDA_OK(cudaStreamSynchronize(stream_), false);
     CUDA_OK(cudaGetLastError(), false);
     out.assign(htokens_, htokens_ + max_steps);
-    launches += (long)max_steps * (5 * cfg_.dec_layers + 1);
+    launches += (long)max_steps * (mega ? 1 : decode_step_launches_1());
     for (size_t i = 1; i < prof_ev_.size(); ++i) {
       int k = prof_ev_[i].first;
       if (k < 0) continue;
@@ -747,7 +770,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
       if (checked >= max_steps) stop = true;
     }
     CUDA_OK(cudaStreamSynchronize(stream_), false);
-    launches += (long)launched * (5 * cfg_.dec_layers + 1);
+    launches += (long)launched * (persistent_decode_active() ? 1 : decode_step_launches_1());
     for (auto e : evs) cudaEventDestroy(e);
     CUDA_OK(cudaGetLastError(), false);
   }
@@ -756,6 +779,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     CUDA_OK(cudaMemcpy(&herr, derr_.p, sizeof(int), cudaMemcpyDeviceToHost), false);
     if (herr) {
       cudaMemset(derr_.p, 0, sizeof(int));
+      if (mega_) mega_reset(mega_, stream_);
       set_error("decode: a device-side wait timed out (code " + std::to_string(herr) + ")");
       return false;
     }
@@ -801,16 +825,29 @@ bool Engine::graph_for(int B) {
   if (built_gen_[B] == graph_gen_ && graph_exec_[B]) return true;
   if (graph_exec_[B]) cudaGraphExecDestroy(graph_exec_[B]);
   graph_exec_[B] = nullptr;
-  DecodeArgs a = dargs(nullptr, nullptr);
-  a.batch = std::max(B, 1);
-  cudaGraph_t g;
-  CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);
-  decode_step(a, stream_);
-  CUDA_OK(cudaStreamEndCapture(stream_, &g), false);
-  CUDA_OK(cudaGraphInstantiate(&graph_exec_[B], g, 0), false);
-  cudaGraphDestroy(g);
-  built_gen_[B] = graph_gen_;
-  return true;
+  if (B == 0) mega_usable();  // state creation allocates: not inside the capture
+  for (int attempt = 0; attempt < 2; ++attempt) {
+    DecodeArgs a = dargs(nullptr, nullptr);
+    a.batch = std::max(B, 1);
+    cudaGraph_t g = nullptr;
+    CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);
+    if (B == 0) enqueue_step(a);
+    else decode_step(a, stream_);
+    const cudaError_t e1 = cudaStreamEndCapture(stream_, &g);
+    cudaError_t e2 = cudaErrorUnknown;
+    if (e1 == cudaSuccess) e2 = cudaGraphInstantiate(&graph_exec_[B], g, 0);
+    if (g) cudaGraphDestroy(g);
+    if (e1 == cudaSuccess && e2 == cudaSuccess) {
+      built_gen_[B] = graph_gen_;
+      return true;
+    }
+    cudaGetLastError();
+    graph_exec_[B] = nullptr;
+    if (B != 0 || !persistent_decode_active()) break;
+    persistent_ = false;  // the persistent step could not be captured: use the kernel chain
+  }
+  set_error("decode: CUDA graph capture of the decode step failed");
+  return false;
 }
 
 int Engine::max_decode_batch() {
@@ -834,7 +871,7 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
   for (int b = 0; b < B; ++b) maxpos = std::max(maxpos, hstate_[b].pos);
   if (!ensure_kv(maxpos + max_steps + 1) || !ensure_tokens(max_steps, B)) return false;
   if (timeline_) {
-    size_t need = (size_t)max_steps * (cfg_.dec_layers * 5 + 1) * 4 + 64;
+    size_t need = (size_t)max_steps * (cfg_.dec_layers * 10 + 4) * 4 + 64;
     if (dtl_.n < need) {
       if (!dtl_.alloc(need)) return false;
       ++graph_gen_;

@@ -160,6 +160,15 @@ struct DecodeArgs {
 constexpr int kDecodeMaxBatch = 8;
 // Largest batch the decode kernels' shared memory admits for this model shape.
 int decode_max_batch(int hidden, int inter, int q_heads, bool int8);
+// Persistent one-launch decode step for a single sequence (decode_mega.cu). mega_create
+// returns nullptr when the device or the model shape is not supported; the state holds the
+// weight tensor maps of the decode mode of `a` (int8 or bf16).
+struct MegaState;
+MegaState* mega_create(const DecodeArgs& a);
+void mega_destroy(MegaState* m);
+bool mega_step(MegaState* m, const DecodeArgs& a, cudaStream_t s);
+// Clears the grid-barrier and ticket words after a step that reported an error.
+bool mega_reset(MegaState* m, cudaStream_t s);
 // Per-device kernel attributes (dynamic shared memory limits); call once per device.
 void decode_kernels_init();
 void enc_kernels_init();
