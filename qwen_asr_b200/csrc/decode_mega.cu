@@ -232,8 +232,10 @@ struct Smem {
   float* att;        // attention scratch (aliases xs / xq)
 };
 
-// Attention work items per kv head for this step: at least 48 positions per item, at most
-// as many items as CTAs allow (the last split of a head merges the others).
+// Attention work items per kv head for this step: at least 48 positions per item (one CTA
+// streams K/V at only ~20 GB/s through its ring while the machine prefetches weights, so a
+// head is spread over many CTAs), at most as many items as CTAs allow; the last split of a
+// head to finish merges the others.
 __device__ __forceinline__ int att_splits(const MegaArgs& a, int pos) {
   return max(1, min(a.p.splits, (pos + 1 + 47) / 48));
 }
@@ -503,6 +505,25 @@ __device__ void run_attention(const MegaArgs& a, const Smem& S, int layer, int p
         make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
   }
   cons_sync();
+  if (splits == 1) {  // the whole head in this CTA: finish here
+    for (int e = tid; e < G * kHdM; e += kCons) {
+      const int g = e / kHdM, d = e % kHdM;
+      float M = -3.0e38f;
+      for (int w = 0; w < kConsWarps; ++w)
+        if (wl[w * kMaxGq + g] > 0.f) M = fmaxf(M, wm[w * kMaxGq + g]);
+      float L = 0.f, O = 0.f;
+      for (int w = 0; w < kConsWarps; ++w) {
+        const float lw = wl[w * kMaxGq + g];
+        if (lw > 0.f) {
+          const float f = expf(__fsub_rn(wm[w * kMaxGq + g], M));
+          L = fmaf(lw, f, L);
+          O = fmaf(wo[(w * kMaxGq + g) * kHdM + d], f, O);
+        }
+      }
+      a.attn[(kvh * G + g) * kHdM + d] = __fdiv_rn(O, L);
+    }
+    return;
+  }
   float* mypart = a.apart + ((size_t)(kvh * splits + split) * kMaxGq) * kApart;
   for (int e = tid; e < G * kHdM; e += kCons) {
     const int g = e / kHdM, d = e % kHdM;
