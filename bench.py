@@ -34,7 +34,11 @@ CONFIGS = {
     "c3": ("1.7b", 960000, 2, 512, "bf16", 1),
     # C4: 20-minute clip split with -S 30, segments sharded over the ranks (strong scaling)
     "c4": ("0.6b", 19200000, 3, 200, "bf16", 0),
+    # C5: independent 120 s streams fed in 2 s chunks (<= 32 new tokens per chunk), streams
+    # sharded over the ranks; a step is one round in which every stream pushes one chunk
+    "c5": ("1.7b", 1920000, 5, 32, "int8", 1),
 }
+C5_STREAMS = 256
 PRESET_DIMS = {"0.6b": (1024, 3072), "1.7b": (2048, 6144)}  # dec hidden, intermediate
 N_LAYERS, KV_HEADS, HEAD_DIM, VOCAB, Q_DIM = 28, 8, 128, 151936, 2048
 
@@ -237,6 +241,84 @@ def config_dict(name, world):
             "parallelism": f"replicas x{world}"}
 
 
+def run_streams(args, world, rank, local):
+    """C5: every rank serves its share of the concurrent streams through the C ABI's
+    streaming calls (qwen_asr_stream_push, per-stream KV slots). The timed region is K rounds
+    of one 2 s chunk per stream (after W warm-up rounds) on a bounded sample of the streams."""
+    import numpy as np
+    import torch
+    import qwen_asr_b200 as Q
+    from qwen_asr_b200 import synth
+
+    preset, n, seed, tokens, mode, wseed = CONFIGS[args.config]
+    d = model_dir(preset, wseed, world, rank, local)
+    torch.cuda.set_device(local)
+    eng = Q.Engine(d, device=local)
+    eng.set_decode_mode(mode)
+    mine = list(range(rank, C5_STREAMS, world))
+    sample = mine[:max(1, args.streams)]
+    chunk = 32000
+    rounds = args.warmup + args.steps
+    audio = {i: synth.synth_audio(chunk * rounds, seed * 1000 + i) for i in sample}
+    streams = {i: Q.Stream() for i in sample}
+    stream = torch.cuda.ExternalStream(eng.cuda_stream(), device=f"cuda:{local}")
+    order = [streams[i] for i in sample]
+
+    def push_round(r):
+        return Q.stream_push_many(eng, order, [audio[i][r * chunk:(r + 1) * chunk] for i in sample])
+
+    for r in range(args.warmup):
+        push_round(r)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    l0 = eng.launch_count()
+    p0 = eng.perf()
+    lat = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for r in range(args.warmup, rounds):
+        t0 = time.perf_counter()
+        push_round(r)  # every stream's chunk is done when the batched round returns
+        lat += [1000.0 * (time.perf_counter() - t0)] * len(sample)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = eng.launch_count() - l0
+    p1 = eng.perf()
+    stage = {k: round((p1[k] - p0[k]) / args.steps, 2) for k in ("gpu_mel_ms", "gpu_enc_ms", "gpu_prefill_ms",
+                                                                  "gpu_decode_ms")}
+    ms = max_over_ranks(world, e0.elapsed_time(e1), local)
+    value = world * len(sample) * args.steps * 2.0 / (ms / 1000.0)
+    lat_all = lat
+    if world > 1:
+        import torch.distributed as dist
+        got = [None] * world
+        dist.all_gather_object(got, lat)
+        lat_all = [x for part in got for x in part]
+    if rank == 0:
+        p50, p99 = float(np.percentile(lat_all, 50)), float(np.percentile(lat_all, 99))
+        line = {
+            "metric": "audio-sec/sec", "value": round(value, 3), "unit": "audio-s/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8+f32",
+            "data": "synthetic",
+            "config": {"workload": f"C5: Qwen3-ASR-1.7B int8, {C5_STREAMS} independent 120 s streams in 2 s chunks "
+                                   f"(<= {tokens} new tokens per chunk), streams sharded over {world} GPU(s), each round's chunks decoded as "
+                                   f"one batch; timed "
+                                   f"sample: {len(sample)} streams per GPU x {args.steps} rounds after {args.warmup} "
+                                   f"warm-up rounds", "streams_per_gpu_sample": len(sample),
+                       "parallelism": f"stream shards x{world}", "l2": "no flush: every chunk streams >1.7 GB of weights"},
+            "latency_ms_per_chunk": {"p50": round(p50, 2), "p99": round(p99, 2)},
+            "stage_ms_per_round": stage,
+            "e2e": {"value": round(value, 3), "unit": "audio-s/s", "h2d_bytes_per_step": 4 * chunk * len(sample),
+                    "d2h_bytes_per_step": 0, "note": "streams run from host buffers through the C ABI"},
+            "gpu_launches": int(launches), "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    barrier(world)
+
+
 def run_segmented(args, world, rank, local):
     """C4: every rank transcribes its share of the -S 30 segments of one 20-minute clip
     (qwen_asr_b200.shard); rank 0 joins the texts. Total work is fixed: strong scaling."""
@@ -415,6 +497,7 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--tokens", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--streams", type=int, default=8, help="C5: streams per GPU in the timed sample")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     world, rank, local = dist_setup()
@@ -422,6 +505,8 @@ def main():
         run_reference(args, world, rank, local)
     elif args.config == "c4":
         run_segmented(args, world, rank, local)
+    elif args.config == "c5":
+        run_streams(args, world, rank, local)
     else:
         run_ours(args, world, rank, local)
     if world > 1:

@@ -10,11 +10,11 @@
  * Differences a caller can observe:
  *  - n_threads of qwen_asr_load_model() is accepted and ignored (the math runs on the GPU).
  *    The GPU is $QASR_DEVICE if set, else the calling thread's current CUDA device.
- *  - All streams of one engine share its decoder KV cache, as in the reference
- *    (context.rs:34), but the engine remembers which stream (or offline call) filled it:
- *    a stream whose push follows another stream's prefills from scratch instead of reusing
- *    a prefix that is no longer in the cache, so interleaved streams stay correct (the
- *    reference would reuse the other stream's KV rows).
+ *  - Each stream keeps its prompt rows in its own device KV slot (up to 32 streams per
+ *    engine; beyond that the least recently used stream's slot is reassigned and that
+ *    stream re-prefills on its next push). The reference shares one KV cache between all
+ *    streams and offline calls (context.rs:34), so interleaving streams there reuses another
+ *    stream's rows; here interleaved streams give the same deltas as streams run alone.
  * An engine is not thread-safe: serialise calls on one engine (as the reference's &mut does).
  */
 #ifndef QWEN_ASR_H

@@ -28,6 +28,14 @@ void qwen_asr_set_skip_silence(QwenAsrEngine* engine, int32_t on);
 int32_t qwen_asr_set_decode_mode(QwenAsrEngine* engine, int32_t mode);
 /* Benchmark mode: run exactly n decode steps per segment, ignoring EOS (0 = off). */
 void qwen_asr_set_force_n_tokens(QwenAsrEngine* engine, int32_t n);
+/* Pushes audio to `count` distinct streams at once: each stream runs exactly the chunks
+ * qwen_asr_stream_push would run for it, and the chunks of streams with adjacent KV slots
+ * decode as one batch (one weight read per step for all of them). deltas_out[i] receives
+ * stream i's delta (NULL when empty; free with qwen_asr_free_string). Returns 0, or -1
+ * on error (qwen_asr_last_error). */
+int32_t qwen_asr_stream_push_many(QwenAsrEngine* engine, QwenAsrStreamState* const* states,
+                                  const float* const* samples, const int32_t* n_samples, int32_t count,
+                                  int32_t finalize, char** deltas_out);
 /* 1 (default): a single sequence decodes through the persistent one-launch-per-step kernel
  * (one CTA per SM, a TMA producer warp streaming the step's weights, grid barriers between
  * the phases of a layer) when the device supports it; 0: the multi-kernel chain. */

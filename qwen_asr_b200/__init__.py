@@ -53,6 +53,8 @@ SIGNATURES = {
     "qwen_asr_set_use_graph": (None, [_VP, C.c_int32]),
     "qwen_asr_set_decode_batch": (C.c_int32, [_VP, C.c_int32]),
     "qwen_asr_set_persistent_decode": (None, [_VP, C.c_int32]),
+    "qwen_asr_stream_push_many": (C.c_int32, [_VP, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), _I32P, C.c_int32,
+                                              C.c_int32, C.POINTER(C.c_void_p)]),
     "qwen_asr_persistent_decode_active": (C.c_int32, [_VP]),
     "qwen_asr_transcribe_segments": (C.c_int32, [_VP, _F32P, C.c_int64, C.POINTER(C.c_int64), C.POINTER(C.c_int64),
                                                  C.c_int32, C.POINTER(C.c_void_p)]),
@@ -292,6 +294,20 @@ class Engine:
         if n < 0:
             raise RuntimeError(last_error())
         return ids[:n_steps], lg, hd
+
+
+def stream_push_many(engine, streams, chunks, finalize: bool = False) -> list:
+    """Pushes chunks[i] to streams[i] for every i in one call (batched decode across the
+    streams); returns the deltas (None when empty)."""
+    k = len(streams)
+    arrs = [np.ascontiguousarray(c, dtype=np.float32) for c in chunks]
+    st = (C.c_void_p * max(k, 1))(*[s._h for s in streams])
+    sp = (C.c_void_p * max(k, 1))(*[a.ctypes.data for a in arrs])
+    ns = (C.c_int32 * max(k, 1))(*[len(a) for a in arrs])
+    out = (C.c_void_p * max(k, 1))()
+    if lib().qwen_asr_stream_push_many(engine._h, st, sp, ns, k, int(finalize), out) != 0:
+        raise RuntimeError(last_error())
+    return [_take_string(out[i]) for i in range(k)]
 
 
 class Stream:

@@ -134,6 +134,37 @@ char* qwen_asr_stream_push(QwenAsrEngine* e, QwenAsrStreamState* s, const float*
   return to_c_string(txt);
 }
 
+int32_t qwen_asr_stream_push_many(QwenAsrEngine* e, QwenAsrStreamState* const* states, const float* const* samples,
+                                  const int32_t* n_samples, int32_t count, int32_t finalize, char** deltas_out) {
+  if (!e || count < 0 || (count > 0 && (!states || !deltas_out))) return -1;
+  std::vector<const std::vector<float>*> bufs;
+  std::vector<qasr::StreamState*> sts;
+  for (int32_t i = 0; i < count; ++i) {
+    if (!states[i]) return -1;
+    for (int32_t j = 0; j < i; ++j)
+      if (states[j] == states[i]) {
+        qasr::set_error("stream_push_many: a stream appears twice");
+        return -1;
+      }
+    if (samples && samples[i] && n_samples && n_samples[i] > 0)
+      states[i]->audio_buf.insert(states[i]->audio_buf.end(), samples[i], samples[i] + n_samples[i]);
+    bufs.push_back(&states[i]->audio_buf);
+    sts.push_back(&states[i]->state);
+  }
+  std::vector<std::string> deltas;
+  try {
+    if (!e->ctx.stream_push_many(bufs, sts, finalize != 0, deltas)) return -1;
+  } catch (const std::exception& ex) {
+    qasr::set_error(std::string("stream: ") + ex.what());
+    return -1;
+  }
+  for (int32_t i = 0; i < count; ++i) {
+    std::string txt = qasr::utf8_lossy(deltas[i]);
+    deltas_out[i] = txt.empty() ? nullptr : to_c_string(txt);
+  }
+  return 0;
+}
+
 char* qwen_asr_stream_get_result(QwenAsrStreamState* s) {
   if (!s) return nullptr;
   std::string txt = qasr::utf8_lossy(s->state.result_bytes);
@@ -328,7 +359,6 @@ int32_t qwen_asr_debug_decode(QwenAsrEngine* e, const float* rows, int32_t n_row
                               int32_t n_steps, int32_t* out_ids, float* out_logits, float* out_hidden) {
   if (!e || !rows || n_rows <= 0 || n_steps < 0) return -1;
   auto& eng = e->ctx.eng;
-  e->ctx.kv_owner = nullptr;
   if (!eng.prefill_rows(rows, n_rows, 0)) return -1;
   if (out_hidden) {
     std::vector<float> h;

@@ -11,6 +11,10 @@ Engine::~Engine() {
   if (device_ >= 0) cudaSetDevice(device_);
   for (auto& g : graph_exec_)
     if (g) cudaGraphExecDestroy(g);
+  for (auto& g : slot_graph_)
+    if (g) cudaGraphExecDestroy(g);
+  for (auto& kv : run_graphs_)
+    if (kv.second.first) cudaGraphExecDestroy(kv.second.first);
   if (mega_) mega_destroy(mega_);
   for (void* p : allocs_) cudaFree(p);
   if (hstate_) cudaFreeHost(hstate_);
@@ -281,12 +285,12 @@ bool Engine::load(const std::string& dir, int device, bool trunc_quant) {
 
   // ---- decode state
   if (!ensure_kv(4096)) return false;
-  CUDA_OK(cudaMallocHost(&hstate_, kDecodeMaxBatch * sizeof(StepState)), false);
+  CUDA_OK(cudaMallocHost(&hstate_, kMaxSlots * sizeof(StepState)), false);
   const int mb = kDecodeMaxBatch;
-  if (!dx_.alloc((size_t)mb * h) || !dqkv_.alloc(qd + 2 * kvd) || !dattn_.alloc((size_t)mb * qd) ||
+  if (!dx_.alloc((size_t)kMaxSlots * h) || !dqkv_.alloc(qd + 2 * kvd) || !dattn_.alloc((size_t)mb * qd) ||
       !dffn_.alloc((size_t)mb * inter) || !dpart_.alloc((size_t)c.dec_heads * 16 * 130) ||
       !dticket_.alloc(c.dec_kv_heads) || !dam_ticket_.alloc(1) || !dam_part_.alloc((size_t)mb * 1024) ||
-      !dstate_.alloc(mb) || !dlogits_.alloc(c.vocab_size) || !derr_.alloc(1))
+      !dstate_.alloc(kMaxSlots) || !dlogits_.alloc(c.vocab_size) || !derr_.alloc(1))
     return false;
   CUDA_OK(cudaMemset(dticket_.p, 0, c.dec_kv_heads * sizeof(int)), false);
   CUDA_OK(cudaMemset(dam_ticket_.p, 0, sizeof(int)), false);
@@ -533,12 +537,12 @@ bool Engine::prefill_ids(const std::vector<int>& ids, const float* d_enc, int st
   return run_prefill(n, start_pos, slot);
 }
 
-bool Engine::prefill_rows(const float* rows, int n, int start_pos) {
+bool Engine::prefill_rows(const float* rows, int n, int start_pos, int slot) {
   cudaSetDevice(device_);
   const int h = cfg_.dec_hidden;
   if (n < 1 || !px_.alloc((size_t)n * h)) return false;
   CUDA_OK(cudaMemcpyAsync(px_.p, rows, (size_t)n * h * 4, cudaMemcpyHostToDevice, stream_), false);
-  return run_prefill(n, start_pos);
+  return run_prefill(n, start_pos, slot);
 }
 
 // px_ holds all n prompt rows; rows [start_pos, n-1) are prefilled at positions
@@ -547,7 +551,7 @@ bool Engine::run_prefill(int n, int start_pos, int slot) {
   const Config& c = cfg_;
   const int h = c.dec_hidden, qd = c.dec_heads * 128, kvd = c.dec_kv_heads * 128, inter = c.dec_intermediate;
   const int S = n - 1 - start_pos;
-  if (S < 0 || slot < 0 || slot >= kDecodeMaxBatch) return false;
+  if (S < 0 || slot < 0 || slot >= kMaxSlots) return false;
   if (!ensure_slots(slot + 1) || !ensure_kv(n + 1024)) return false;
   if (!pxn_.alloc((size_t)std::max(S, 1) * h) || !pqkv_.alloc((size_t)std::max(S, 1) * (qd + 2 * kvd)) ||
       !patt_.alloc((size_t)std::max(S, 1) * qd) || !pmid_.alloc((size_t)std::max(S, 1) * inter))
@@ -613,7 +617,7 @@ bool Engine::copy_prefill_hidden(std::vector<float>& out, int rows) {
 }
 
 // ---------------------------------------------------------------------------- decode
-DecodeArgs Engine::dargs(const int* forced, float* logits) {
+DecodeArgs Engine::dargs(const int* forced, float* logits, int slot) {
   const Config& c = cfg_;
   bool i8 = mode_ == DECODE_INT8;
   pw_qkv_.clear(); pw_o_.clear(); pw_gu_.clear(); pw_down_.clear();
@@ -638,6 +642,13 @@ DecodeArgs Engine::dargs(const int* forced, float* logits) {
   a.x = dx_.p; a.qkv = dqkv_.p; a.attn = dattn_.p; a.ffn = dffn_.p; a.part = dpart_.p; a.ticket = dticket_.p;
   a.am_ticket = dam_ticket_.p; a.am_part = dam_part_.p; a.st = dstate_.p; a.tokens = dtokens_.p;
   a.kv_slot_stride = kv_slot_stride(); a.tokens_ld = tokens_ld_; a.batch = 1;
+  if (slot > 0) {  // one sequence in its own slot: offset the per-sequence buffers
+    a.k_cache += (size_t)slot * kv_slot_stride();
+    a.v_cache += (size_t)slot * kv_slot_stride();
+    a.x += (size_t)slot * c.dec_hidden;
+    a.st += slot;
+    a.tokens += (size_t)slot * tokens_ld_;
+  }
   a.forced = forced; a.logits = logits; a.err = derr_.p;
   if (timeline_) {
     a.tl = dtl_.p;
@@ -666,13 +677,18 @@ void Engine::enqueue_step(const DecodeArgs& a) {
 int Engine::decode_step_launches_1() const { return 5 * cfg_.dec_layers + 1; }
 
 bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, const std::vector<int>* forced,
-                    std::vector<float>* logits) {
+                    std::vector<float>* logits, int slot) {
   cudaSetDevice(device_);
   out.clear();
   if (max_steps <= 0) return true;
-  const int start_pos = hstate_->pos;
+  if (slot < 0 || slot >= kMaxSlots || slot >= slots_) {
+    set_error("decode: slot " + std::to_string(slot) + " holds no prefilled sequence");
+    return false;
+  }
+  StepState* hs = hstate_ + slot;
+  const int start_pos = hs->pos;
   if (!ensure_kv(start_pos + max_steps + 1)) return false;
-  if (!ensure_tokens(max_steps, 1)) return false;
+  if (!ensure_tokens(max_steps, slot + 1)) return false;
   if (timeline_) {
     size_t need = (size_t)max_steps * (cfg_.dec_layers * 10 + 4) * 4 + 64;
     if (dtl_.n < need) {
@@ -689,13 +705,13 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     if (forced) {
       if (!dforced_.alloc(std::max<size_t>(forced->size(), 1))) return false;
       CUDA_OK(cudaMemcpyAsync(dforced_.p, forced->data(), forced->size() * 4, cudaMemcpyHostToDevice, stream_), false);
-      hstate_->forced_mode = 1;
-      CUDA_OK(cudaMemcpyAsync(&dstate_.p->forced_mode, &hstate_->forced_mode, sizeof(int), cudaMemcpyHostToDevice,
+      hs->forced_mode = 1;
+      CUDA_OK(cudaMemcpyAsync(&dstate_.p[slot].forced_mode, &hs->forced_mode, sizeof(int), cudaMemcpyHostToDevice,
                               stream_),
               false);
     }
     const bool mega = !profile && mega_usable();
-    DecodeArgs a = dargs(forced ? dforced_.p : nullptr, logits ? dlogits_.p : nullptr);
+    DecodeArgs a = dargs(forced ? dforced_.p : nullptr, logits ? dlogits_.p : nullptr, slot);
     if (profile) {
       a.on_launch = [](void* ctx, int kind) {
         Engine* e = (Engine*)ctx;
@@ -717,7 +733,9 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
                                 stream_),
                 false);
     }
-    CUDA_OK(cudaMemcpyAsync(htokens_, dtokens_.p, max_steps * 4, cudaMemcpyDeviceToHost, stream_), false);
+    CUDA_OK(cudaMemcpyAsync(htokens_, dtokens_.p + (size_t)slot * tokens_ld_, max_steps * 4, cudaMemcpyDeviceToHost,
+                            stream_),
+            false);
     CUDA_OK(cudaStreamSynchronize(stream_), false);
     CUDA_OK(cudaGetLastError(), false);
     out.assign(htokens_, htokens_ + max_steps);
@@ -733,7 +751,8 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     for (auto& pe : prof_ev_) cudaEventDestroy(pe.second);
     prof_ev_.clear();
   } else {
-    if (!graph_for(0)) return false;
+    if (slot == 0 ? !graph_for(0) : !graph_for_slot(slot)) return false;
+    cudaGraphExec_t step_graph = slot == 0 ? graph_exec_[0] : slot_graph_[slot];
     // Launch in chunks; after each chunk copy its ids back and look for EOS while the
     // next chunk runs (transcribe.rs:194-226 stop rule).
     const int chunk = 16;
@@ -742,8 +761,9 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     std::vector<cudaEvent_t> evs;
     auto launch_chunk = [&]() -> bool {
       int c = std::min(chunk, max_steps - launched);
-      for (int i = 0; i < c; ++i) CUDA_OK(cudaGraphLaunch(graph_exec_[0], stream_), false);
-      CUDA_OK(cudaMemcpyAsync(htokens_ + launched, dtokens_.p + launched, c * 4, cudaMemcpyDeviceToHost, stream_),
+      for (int i = 0; i < c; ++i) CUDA_OK(cudaGraphLaunch(step_graph, stream_), false);
+      CUDA_OK(cudaMemcpyAsync(htokens_ + launched, dtokens_.p + (size_t)slot * tokens_ld_ + launched, c * 4,
+                              cudaMemcpyDeviceToHost, stream_),
               false);
       cudaEvent_t e;
       cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
@@ -792,9 +812,9 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     CUDA_OK(cudaMemcpy(last_timeline.data(), dtl_.p, last_timeline.size() * 8, cudaMemcpyDeviceToHost), false);
   }
   // KV length after the steps the caller consumes (extra speculative steps are ignored).
-  kv_len_ = start_pos + (int)out.size();
-  hstate_->pos = kv_len_;
-  hstate_->forced_mode = 0;
+  hs->pos = start_pos + (int)out.size();
+  hs->forced_mode = 0;
+  if (slot == 0) kv_len_ = hs->pos;
   cudaEventRecord(ev1_, stream_);
   cudaEventSynchronize(ev1_);
   float ms = 0;
@@ -850,6 +870,27 @@ bool Engine::graph_for(int B) {
   return false;
 }
 
+bool Engine::graph_for_slot(int slot) {
+  if ((int)slot_graph_.size() <= slot) {
+    slot_graph_.resize(slot + 1, nullptr);
+    slot_graph_gen_.resize(slot + 1, 0);
+  }
+  if (slot_graph_gen_[slot] == graph_gen_ && slot_graph_[slot]) return true;
+  if (slot_graph_[slot]) cudaGraphExecDestroy(slot_graph_[slot]);
+  slot_graph_[slot] = nullptr;
+  mega_usable();
+  DecodeArgs a = dargs(nullptr, nullptr, slot);
+  cudaGraph_t g = nullptr;
+  CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);
+  enqueue_step(a);
+  CUDA_OK(cudaStreamEndCapture(stream_, &g), false);
+  const cudaError_t e = cudaGraphInstantiate(&slot_graph_[slot], g, 0);
+  cudaGraphDestroy(g);
+  CUDA_OK(e, false);
+  slot_graph_gen_[slot] = graph_gen_;
+  return true;
+}
+
 int Engine::max_decode_batch() {
   if (max_batch_ == 0) {
     cudaSetDevice(device_);
@@ -859,17 +900,18 @@ int Engine::max_decode_batch() {
   return max_batch_;
 }
 
-bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<std::vector<int>>& out) {
+bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<std::vector<int>>& out,
+                          int first_slot) {
   cudaSetDevice(device_);
   out.assign(std::max(B, 0), {});
   if (B <= 0 || max_steps <= 0) return true;
-  if (B > max_decode_batch() || B > slots_) {
+  if (B > max_decode_batch() || first_slot < 0 || first_slot + B > slots_) {
     set_error("decode_batch: batch " + std::to_string(B) + " exceeds the prefilled slots or the kernel limit");
     return false;
   }
   int maxpos = 0;
-  for (int b = 0; b < B; ++b) maxpos = std::max(maxpos, hstate_[b].pos);
-  if (!ensure_kv(maxpos + max_steps + 1) || !ensure_tokens(max_steps, B)) return false;
+  for (int b = 0; b < B; ++b) maxpos = std::max(maxpos, hstate_[first_slot + b].pos);
+  if (!ensure_kv(maxpos + max_steps + 1) || !ensure_tokens(max_steps, first_slot + B)) return false;
   if (timeline_) {
     size_t need = (size_t)max_steps * (cfg_.dec_layers * 10 + 4) * 4 + 64;
     if (dtl_.n < need) {
@@ -879,8 +921,29 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
     if (!dtl_count_.alloc(1)) return false;
     CUDA_OK(cudaMemsetAsync(dtl_count_.p, 0, sizeof(int), stream_), false);
   }
-  if (use_graph && !graph_for(B)) return false;
-  DecodeArgs direct_args = dargs(nullptr, nullptr);
+  cudaGraphExec_t run_graph = nullptr;
+  if (use_graph && first_slot == 0) {
+    if (!graph_for(B)) return false;
+    run_graph = graph_exec_[B];
+  } else if (use_graph) {
+    auto& entry = run_graphs_[first_slot * 64 + B];
+    if (!entry.first || entry.second != graph_gen_) {
+      if (entry.first) cudaGraphExecDestroy(entry.first);
+      entry.first = nullptr;
+      DecodeArgs ga = dargs(nullptr, nullptr, first_slot);
+      ga.batch = B;
+      cudaGraph_t g = nullptr;
+      CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);
+      decode_step(ga, stream_);
+      CUDA_OK(cudaStreamEndCapture(stream_, &g), false);
+      const cudaError_t e = cudaGraphInstantiate(&entry.first, g, 0);
+      cudaGraphDestroy(g);
+      CUDA_OK(e, false);
+      entry.second = graph_gen_;
+    }
+    run_graph = entry.first;
+  }
+  DecodeArgs direct_args = dargs(nullptr, nullptr, first_slot);
   direct_args.batch = B;
   cudaEventRecord(ev0_, stream_);
   // Chunks of steps; after each chunk the ids of every sequence come back (one 2-D copy)
@@ -893,11 +956,11 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
   auto launch_chunk = [&]() -> bool {
     int c = std::min(chunk, max_steps - launched);
     for (int i = 0; i < c; ++i) {
-      if (use_graph) CUDA_OK(cudaGraphLaunch(graph_exec_[B], stream_), false);
+      if (run_graph) CUDA_OK(cudaGraphLaunch(run_graph, stream_), false);
       else decode_step(direct_args, stream_);
     }
-    CUDA_OK(cudaMemcpy2DAsync(htokens_ + launched, (size_t)ld * 4, dtokens_.p + launched, (size_t)ld * 4,
-                              (size_t)c * 4, B, cudaMemcpyDeviceToHost, stream_),
+    CUDA_OK(cudaMemcpy2DAsync(htokens_ + launched, (size_t)ld * 4, dtokens_.p + (size_t)first_slot * ld + launched,
+                              (size_t)ld * 4, (size_t)c * 4, B, cudaMemcpyDeviceToHost, stream_),
             false);
     cudaEvent_t e;
     cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
@@ -957,10 +1020,10 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
   }
   size_t longest = 0;
   for (int b = 0; b < B; ++b) {
-    hstate_[b].pos += (int)out[b].size();
+    hstate_[first_slot + b].pos += (int)out[b].size();
     longest = std::max(longest, out[b].size());
   }
-  kv_len_ = hstate_[0].pos;
+  if (first_slot == 0) kv_len_ = hstate_[0].pos;
   cudaEventRecord(ev1_, stream_);
   cudaEventSynchronize(ev1_);
   float ms = 0;

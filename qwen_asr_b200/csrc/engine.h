@@ -1,5 +1,6 @@
 // Device-resident Qwen3-ASR model and its forward stages on one GPU.
 #pragma once
+#include <map>
 #include <memory>
 #include <string>
 #include <vector>
@@ -66,17 +67,19 @@ class Engine {
   // (slot 0 is the one decode() continues).
   bool prefill_ids(const std::vector<int>& ids, const float* d_enc, int start_pos, int slot = 0);
   // Same with prompt embeddings already materialised on the host (streaming LCP path).
-  bool prefill_rows(const float* h_rows, int n_rows, int start_pos);
+  bool prefill_rows(const float* h_rows, int n_rows, int start_pos, int slot = 0);
   // Greedy decode: runs up to max_steps decoder_forward steps from the prepared state and
   // returns the produced ids. With stop_on_eos the loop stops after the first
   // 151643/151645 (inclusive). forced (teacher forcing) gives the input id of step i+1.
+  // `slot`: the KV cache / decode state of one sequence (0 = the offline path; batched
+  // segments use 0..kDecodeMaxBatch-1; streams own slots from kDecodeMaxBatch up).
   bool decode(int max_steps, bool stop_on_eos, std::vector<int>& out, const std::vector<int>* forced = nullptr,
-              std::vector<float>* logits = nullptr);
+              std::vector<float>* logits = nullptr, int slot = 0);
   // Batched greedy decode of the sequences prefilled into slots 0..B-1: every step reads
   // the weights once for all B sequences. Runs until every sequence has produced EOS (with
   // stop_on_eos) or max_steps; out[b] holds sequence b's ids exactly as decode() would
   // return them for that sequence alone.
-  bool decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<std::vector<int>>& out);
+  bool decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<std::vector<int>>& out, int first_slot = 0);
   // Largest B decode_batch accepts for this model (shared-memory bound, <= kDecodeMaxBatch).
   int max_decode_batch();
   // Single-sequence decode through the persistent one-launch kernel (decode_mega.cu) when the
@@ -181,7 +184,11 @@ class Engine {
   bool graph_for(int B);
   std::vector<const void*> pw_qkv_, pw_o_, pw_gu_, pw_down_;
   std::vector<const float*> ps_qkv_, ps_o_, ps_gu_, ps_down_, pn1_, pn2_, pqn_, pkn_;
-  DecodeArgs dargs(const int* forced, float* logits);
+  DecodeArgs dargs(const int* forced, float* logits, int slot = 0);
+  std::vector<cudaGraphExec_t> slot_graph_;  // single-sequence step graphs of slots >= 1
+  std::vector<unsigned> slot_graph_gen_;
+  bool graph_for_slot(int slot);
+  std::map<int, std::pair<cudaGraphExec_t, unsigned>> run_graphs_;  // batched steps of slot runs (first slot > 0)
   bool run_prefill(int n_rows, int start_pos, int slot = 0);  // rows already in px_
   cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
 };

@@ -158,6 +158,7 @@ struct DecodeArgs {
   int tokens_ld = 0;
 };
 constexpr int kDecodeMaxBatch = 8;
+constexpr int kMaxSlots = 64;  // KV slots / decode states an engine can hold
 // Largest batch the decode kernels' shared memory admits for this model shape.
 int decode_max_batch(int hidden, int inter, int q_heads, bool int8);
 // Persistent one-launch decode step for a single sequence (decode_mega.cu). mega_create

@@ -4,6 +4,7 @@
 #include "transcribe.h"
 
 #include <algorithm>
+#include <atomic>
 #include <chrono>
 #include <cstring>
 
@@ -21,10 +22,42 @@ static double now_ms() {
   return duration<double, std::milli>(steady_clock::now().time_since_epoch()).count();
 }
 
+uint64_t StreamState::next_uid() {
+  static std::atomic<uint64_t> counter{1};
+  return counter.fetch_add(1);
+}
+
 void StreamState::reset() {
   bool keep = prompt_prepared;
   *this = StreamState();
   prompt_prepared = keep;
+}
+
+int Ctx::stream_slot(StreamState& st, bool& owned) {
+  const int first = kDecodeMaxBatch, n = std::max(1, std::min(max_stream_slots, kMaxSlots - first));
+  if ((int)slot_uid.size() < first + n) {
+    slot_uid.resize(first + n, 0);
+    slot_used.resize(first + n, 0);
+  }
+  ++slot_tick;
+  if (st.slot >= first && st.slot < first + n && slot_uid[st.slot] == st.uid) {
+    owned = true;
+    slot_used[st.slot] = slot_tick;
+    return st.slot;
+  }
+  int pick = first;  // a free slot, else the least recently used one
+  for (int s = first; s < first + n; ++s) {
+    if (slot_uid[s] == 0) {
+      pick = s;
+      break;
+    }
+    if (slot_used[s] < slot_used[pick]) pick = s;
+  }
+  slot_uid[pick] = st.uid;
+  slot_used[pick] = slot_tick;
+  st.slot = pick;
+  owned = false;
+  return pick;
 }
 
 bool Ctx::load(const std::string& dir, int device) {
@@ -136,7 +169,6 @@ bool Ctx::transcribe_segment(const float* samples, size_t n, const std::vector<i
   if (!prepare_prompt_tokens()) return false;
   const bool has_past = past && !past->empty();
   if (!eng.prefill_ids(segment_ids(T, past), eng.enc_out(), 0)) return false;
-  kv_owner = nullptr;
   std::vector<int> gen;
   const int limit = force_n_tokens > 0 ? force_n_tokens : 2048;
   if (!eng.decode(limit, force_n_tokens <= 0, gen)) return false;
@@ -167,7 +199,6 @@ bool Ctx::transcribe_segments_batched(const std::vector<std::vector<float>>& seg
     if (!eng.prefill_ids(segment_ids(T, nullptr), eng.enc_out(), 0, B)) return false;
     slot_of[i] = B++;
   }
-  kv_owner = nullptr;
   std::vector<std::vector<int>> gen;
   const int limit = force_n_tokens > 0 ? force_n_tokens : 2048;
   if (B > 0 && !eng.decode_batch(B, limit, force_n_tokens <= 0, gen)) return false;
@@ -283,212 +314,283 @@ static std::pair<size_t, size_t> tail_repeat_blocks(const std::vector<int>& t, s
 }
 
 // stream_push_audio (transcribe.rs:902-1304). `samples` is the full audio so far.
-bool Ctx::stream_push_audio(const std::vector<float>& samples, StreamState& st, bool finalize, std::string& delta) {
-  delta.clear();
+// One chunk of stream_push_audio's loop (transcribe.rs:944-1304), split so that several
+// streams can share one batched decode: stream_chunk_prepare does the window encodes, the
+// prompt assembly, the LCP reuse and the prefill into the stream's KV slot; the caller
+// decodes max_new tokens in that slot; stream_chunk_finish turns them into the delta.
+bool Ctx::stream_chunk_prepare(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w) {
+  w = StreamChunk();
   const size_t chunk_samples = (size_t)(stream_chunk_sec * (float)kSampleRate);
   const int rollback = stream_rollback, unfixed = stream_unfixed_chunks;
-  const int max_new = stream_max_new_tokens > 0 ? stream_max_new_tokens : 32;
   const int dim = eng.cfg().dec_hidden;
   if (!st.prompt_prepared) {
     if (!prepare_prompt_tokens()) return false;
     st.prompt_prepared = true;
   }
-  size_t available = samples.size() > st.audio_cursor ? samples.size() - st.audio_cursor : 0;
-  if (available < chunk_samples && !finalize) return true;
-  if (available == 0) return true;
+  if (st.audio_cursor >= samples.size()) return true;
+  const size_t remaining = samples.size() - st.audio_cursor;
+  if (remaining < chunk_samples && !finalize) return true;
   const size_t enc_window_frames = (size_t)std::min(std::max(eng.cfg().enc_n_window_infer, 100), 800);
   const size_t enc_window_samples = enc_window_frames * kHop;
 
-  while (st.audio_cursor < samples.size()) {
-    size_t remaining = samples.size() - st.audio_cursor;
-    if (remaining < chunk_samples && !finalize) break;
-    double chunk_t0 = now_ms();
-    st.audio_cursor = std::min(st.audio_cursor + chunk_samples, samples.size());
-    bool is_final = finalize && st.audio_cursor >= samples.size();
-    StagePerf before = eng.perf;
+  w.t0 = now_ms();
+  st.audio_cursor = std::min(st.audio_cursor + chunk_samples, samples.size());
+  w.is_final = finalize && st.audio_cursor >= samples.size();
+  w.before = eng.perf;
 
-    size_t full_end = (st.audio_cursor / enc_window_samples) * enc_window_samples;
-    while ((st.enc_cache_base_windows + st.enc_cache.size()) * enc_window_samples < full_end) {
-      size_t ws = (st.enc_cache_base_windows + st.enc_cache.size()) * enc_window_samples;
-      StreamState::EncWindow w;
-      if (!encode_window(samples.data() + ws, enc_window_samples, w.enc, w.seq_len)) return false;
-      st.enc_cached_seq_total += w.seq_len;
-      st.enc_cache.push_back(std::move(w));
-    }
-    size_t enc_update_threshold = chunk_samples * 2;
-    size_t partial_age = st.audio_cursor > st.last_partial_cursor ? st.audio_cursor - st.last_partial_cursor : 0;
-    bool need_encode = st.last_partial_cursor == 0 || partial_age >= enc_update_threshold || is_final;
-    int partial_seq = 0;
-    const std::vector<float>* partial_enc = nullptr;
-    std::vector<float> fresh;
-    if (need_encode && full_end < st.audio_cursor) {
-      int seq = 0;
-      if (encode_window(samples.data() + full_end, st.audio_cursor - full_end, fresh, seq)) {
-        partial_seq = seq;
-        st.last_partial_cursor = st.audio_cursor;
-        st.last_partial_enc = fresh;
-        st.last_partial_seq = seq;
-        partial_enc = &st.last_partial_enc;
-      } else {
-        partial_seq = st.last_partial_seq;
-        partial_enc = &st.last_partial_enc;
-      }
-    } else if (full_end < st.audio_cursor) {
+  size_t full_end = (st.audio_cursor / enc_window_samples) * enc_window_samples;
+  while ((st.enc_cache_base_windows + st.enc_cache.size()) * enc_window_samples < full_end) {
+    size_t ws = (st.enc_cache_base_windows + st.enc_cache.size()) * enc_window_samples;
+    StreamState::EncWindow ew;
+    if (!encode_window(samples.data() + ws, enc_window_samples, ew.enc, ew.seq_len)) return false;
+    st.enc_cached_seq_total += ew.seq_len;
+    st.enc_cache.push_back(std::move(ew));
+  }
+  size_t enc_update_threshold = chunk_samples * 2;
+  size_t partial_age = st.audio_cursor > st.last_partial_cursor ? st.audio_cursor - st.last_partial_cursor : 0;
+  bool need_encode = st.last_partial_cursor == 0 || partial_age >= enc_update_threshold || w.is_final;
+  int partial_seq = 0;
+  const std::vector<float>* partial_enc = nullptr;
+  std::vector<float> fresh;
+  if (need_encode && full_end < st.audio_cursor) {
+    int seq = 0;
+    if (encode_window(samples.data() + full_end, st.audio_cursor - full_end, fresh, seq)) {
+      partial_seq = seq;
+      st.last_partial_cursor = st.audio_cursor;
+      st.last_partial_enc = fresh;
+      st.last_partial_seq = seq;
+      partial_enc = &st.last_partial_enc;
+    } else {
       partial_seq = st.last_partial_seq;
       partial_enc = &st.last_partial_enc;
     }
-    size_t enc_seq_len = st.enc_cached_seq_total + partial_seq;
-    if (enc_seq_len == 0) {
-      st.chunk_idx += 1;
-      delta.clear();  // the reference returns an empty delta here (transcribe.rs:1004-1007)
+  } else if (full_end < st.audio_cursor) {
+    partial_seq = st.last_partial_seq;
+    partial_enc = &st.last_partial_enc;
+  }
+  size_t enc_seq_len = st.enc_cached_seq_total + partial_seq;
+  if (enc_seq_len == 0) {  // the reference returns an empty delta here (transcribe.rs:1004-1007)
+    st.chunk_idx += 1;
+    w.empty_stop = true;
+    return true;
+  }
+  std::vector<float> enc_output(enc_seq_len * dim);
+  size_t off = 0;
+  for (auto& ew : st.enc_cache) {
+    memcpy(enc_output.data() + off * dim, ew.enc.data(), (size_t)ew.seq_len * dim * 4);
+    off += ew.seq_len;
+  }
+  if (partial_seq > 0) memcpy(enc_output.data() + off * dim, partial_enc->data(), (size_t)partial_seq * dim * 4);
+
+  w.n_prefix = 0;
+  if (past_text_conditioning && st.chunk_idx >= unfixed && !st.raw_tokens.empty())
+    w.n_prefix = (size_t)std::max((int)st.raw_tokens.size() - rollback, 0);
+
+  std::vector<int> ids;
+  ids.insert(ids.end(), std::begin(kPrefixHead), std::end(kPrefixHead));
+  if (has_prompt_tokens) ids.insert(ids.end(), prompt_tokens.begin(), prompt_tokens.end());
+  ids.insert(ids.end(), std::begin(kPrefixTail), std::end(kPrefixTail));
+  for (size_t i = 0; i < enc_seq_len; ++i) ids.push_back(-(int)(i + 1));
+  ids.insert(ids.end(), std::begin(kSuffixBase), std::end(kSuffixBase));
+  if (has_force_tokens) ids.insert(ids.end(), force_prompt_tokens.begin(), force_prompt_tokens.end());
+  for (size_t i = 0; i < w.n_prefix; ++i) ids.push_back(st.raw_tokens[i]);
+  const size_t total_seq = ids.size(), prefill_len = total_seq - 1;
+
+  // LCP reuse: rows equal as f32 vectors (transcribe.rs:1095-1106). Token rows compare
+  // by id; encoder rows compare element-wise; a token row never equals an encoder row.
+  size_t reused = 0;
+  bool owned = false;
+  w.slot = stream_slot(st, owned);
+  if (!owned) {  // the slot's rows belong to no earlier chunk of this stream
+    st.prev_ids.clear();
+    st.prev_prefill_len = 0;
+  }
+  if (!st.prev_ids.empty() && st.prev_prefill_len > 0) {
+    size_t cmp = std::min(prefill_len, st.prev_prefill_len);
+    while (reused < cmp) {
+      int a = st.prev_ids[reused], b = ids[reused];
+      bool eq;
+      if (a >= 0 || b >= 0) {
+        eq = a == b;
+      } else {
+        const float* ra = st.prev_enc.data() + (size_t)(-a - 1) * dim;
+        const float* rb = enc_output.data() + (size_t)(-b - 1) * dim;
+        eq = true;
+        for (int k = 0; k < dim; ++k)
+          if (!(ra[k] == rb[k])) {
+            eq = false;
+            break;
+          }
+      }
+      if (!eq) break;
+      ++reused;
+    }
+  }
+  // Device copy of the assembled encoder rows for the prompt gather.
+  DevBuf<float> denc;
+  if (!denc.alloc(enc_output.size())) return false;
+  if (cudaMemcpy(denc.p, enc_output.data(), enc_output.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    return false;
+  if (!eng.prefill_ids(ids, denc.p, (int)reused, w.slot)) return false;
+  st.prev_ids.assign(ids.begin(), ids.begin() + prefill_len);
+  st.prev_enc = std::move(enc_output);
+  st.prev_prefill_len = prefill_len;
+  w.active = true;
+  return true;
+}
+
+// Returns true when the stream's loop stops after this chunk (speech ended).
+bool Ctx::stream_chunk_finish(StreamState& st, StreamChunk& w, std::string& delta) {
+  const int rollback = stream_rollback, unfixed = stream_unfixed_chunks;
+  const int max_new = stream_max_new_tokens > 0 ? stream_max_new_tokens : 32;
+  const std::vector<int>& gen = w.gen;
+  const size_t n_prefix = w.n_prefix;
+  const bool is_final = w.is_final;
+  last_tokens.push_back(gen);
+  std::vector<int> chunk_tokens;
+  {
+    int token_i = 0, n_generated = 0;
+    while (n_generated < max_new && token_i < (int)gen.size()) {
+      ++n_generated;
+      int t = gen[token_i++];
+      if (t == kTokEndOfText || t == kTokImEnd) break;
+      chunk_tokens.push_back(t);
+    }
+  }
+
+  bool speech_ended = chunk_tokens.empty() && !st.raw_tokens.empty() && st.chunk_idx >= unfixed;
+  auto text_start_of = [&](const std::vector<int>& rt) -> size_t {
+    if (has_force_tokens) return 0;
+    auto it = std::find(rt.begin(), rt.end(), kTokAsrText);
+    return it == rt.end() ? 0 : (size_t)(it - rt.begin()) + 1;
+  };
+  auto emit = [&](const std::vector<int>& cand, size_t from, size_t to) {
+    for (size_t i = from; i < to; ++i) {
+      if (i < cand.size()) {
+        if (i >= st.stable_text_tokens.size()) st.stable_text_tokens.push_back(cand[i]);
+        const std::string& pb = tok.decode_bytes(cand[i]);
+        perf_text_tokens += 1;
+        st.result_bytes += pb;
+        delta += pb;
+      }
+    }
+  };
+  if (speech_ended) {
+    size_t ts = text_start_of(st.raw_tokens);
+    std::vector<int> cand(st.raw_tokens.begin() + ts, st.raw_tokens.end());
+    emit(cand, st.stable_text_tokens.size(), cand.size());
+  }
+  st.raw_tokens.resize(std::min(st.raw_tokens.size(), n_prefix));
+  st.raw_tokens.insert(st.raw_tokens.end(), chunk_tokens.begin(), chunk_tokens.end());
+
+  auto reset_context = [&]() {
+    size_t carry = std::min(st.stable_text_tokens.size(), kResetCarry);
+    size_t cs = st.stable_text_tokens.size() - carry;
+    st.raw_tokens.clear();
+    if (carry > 0) {
+      st.raw_tokens.push_back(kTokAsrText);
+      st.raw_tokens.insert(st.raw_tokens.end(), st.stable_text_tokens.begin() + cs, st.stable_text_tokens.end());
+    }
+    st.prev_ids.clear();
+    st.prev_enc.clear();
+    st.prev_prefill_len = 0;
+    st.stale_count = 0;
+    st.prev_tail_snapshot.clear();
+    if (st.enc_cache.size() >= kMaxEncWindows) {
+      st.enc_cache_base_windows += st.enc_cache.size();
+      st.enc_cache.clear();
+      st.enc_cached_seq_total = 0;
+    }
+  };
+  if (!speech_ended) {
+    if (st.raw_tokens == st.prev_tail_snapshot) {
+      st.stale_count += 1;
+    } else {
+      st.stale_count = 0;
+      st.prev_tail_snapshot = st.raw_tokens;
+    }
+    auto rep = tail_repeat_blocks(st.raw_tokens, kDegenMaxPeriod);
+    bool is_degen = st.stale_count >= kStaleChunks || rep.first >= (size_t)kDegenMinRepeats;
+    if (is_degen) reset_context();
+    if (st.chunk_idx > 0 && st.chunk_idx % kResetInterval == 0) reset_context();
+
+    size_t ts = text_start_of(st.raw_tokens);
+    size_t n_text_tokens = st.raw_tokens.size() > ts ? st.raw_tokens.size() - ts : 0;
+    size_t candidate_len;
+    if (is_final) candidate_len = n_text_tokens;
+    else if (st.chunk_idx >= unfixed) candidate_len = (size_t)std::max((int)n_text_tokens - rollback, 0);
+    else candidate_len = 0;
+    std::vector<int> cand(st.raw_tokens.begin() + std::min(ts, st.raw_tokens.size()), st.raw_tokens.end());
+    size_t from = st.stable_text_tokens.size();
+    emit(cand, from, std::max(candidate_len, from));
+  }
+  perf_encode_ms += (eng.perf.mel_ms - w.before.mel_ms) + (eng.perf.enc_ms - w.before.enc_ms);
+  perf_decode_ms += (eng.perf.prefill_ms - w.before.prefill_ms) + (eng.perf.decode_ms - w.before.decode_ms);
+  perf_total_ms += now_ms() - w.t0;
+  st.chunk_idx += 1;
+  return speech_ended;
+}
+
+bool Ctx::stream_push_audio(const std::vector<float>& samples, StreamState& st, bool finalize, std::string& delta) {
+  delta.clear();
+  const int max_new = stream_max_new_tokens > 0 ? stream_max_new_tokens : 32;
+  for (;;) {
+    StreamChunk w;
+    if (!stream_chunk_prepare(samples, st, finalize, w)) return false;
+    if (w.empty_stop) {
+      delta.clear();
       return true;
     }
-    std::vector<float> enc_output(enc_seq_len * dim);
-    size_t off = 0;
-    for (auto& w : st.enc_cache) {
-      memcpy(enc_output.data() + off * dim, w.enc.data(), (size_t)w.seq_len * dim * 4);
-      off += w.seq_len;
-    }
-    if (partial_seq > 0) memcpy(enc_output.data() + off * dim, partial_enc->data(), (size_t)partial_seq * dim * 4);
+    if (!w.active) return true;
+    if (!eng.decode(max_new, true, w.gen, nullptr, nullptr, w.slot)) return false;
+    if (stream_chunk_finish(st, w, delta)) break;
+  }
+  return true;
+}
 
-    size_t n_prefix = 0;
-    if (past_text_conditioning && st.chunk_idx >= unfixed && !st.raw_tokens.empty())
-      n_prefix = (size_t)std::max((int)st.raw_tokens.size() - rollback, 0);
-
-    std::vector<int> ids;
-    ids.insert(ids.end(), std::begin(kPrefixHead), std::end(kPrefixHead));
-    if (has_prompt_tokens) ids.insert(ids.end(), prompt_tokens.begin(), prompt_tokens.end());
-    ids.insert(ids.end(), std::begin(kPrefixTail), std::end(kPrefixTail));
-    for (size_t i = 0; i < enc_seq_len; ++i) ids.push_back(-(int)(i + 1));
-    ids.insert(ids.end(), std::begin(kSuffixBase), std::end(kSuffixBase));
-    if (has_force_tokens) ids.insert(ids.end(), force_prompt_tokens.begin(), force_prompt_tokens.end());
-    for (size_t i = 0; i < n_prefix; ++i) ids.push_back(st.raw_tokens[i]);
-    const size_t total_seq = ids.size(), prefill_len = total_seq - 1;
-
-    // LCP reuse: rows equal as f32 vectors (transcribe.rs:1095-1106). Token rows compare
-    // by id; encoder rows compare element-wise; a token row never equals an encoder row.
-    size_t reused = 0;
-    if (kv_owner != &st) {  // another stream or an offline call overwrote the KV cache
-      st.prev_ids.clear();
-      st.prev_prefill_len = 0;
-    }
-    if (!st.prev_ids.empty() && st.prev_prefill_len > 0) {
-      size_t cmp = std::min(prefill_len, st.prev_prefill_len);
-      while (reused < cmp) {
-        int a = st.prev_ids[reused], b = ids[reused];
-        bool eq;
-        if (a >= 0 || b >= 0) {
-          eq = a == b;
-        } else {
-          const float* ra = st.prev_enc.data() + (size_t)(-a - 1) * dim;
-          const float* rb = enc_output.data() + (size_t)(-b - 1) * dim;
-          eq = true;
-          for (int k = 0; k < dim; ++k)
-            if (!(ra[k] == rb[k])) {
-              eq = false;
-              break;
-            }
-        }
-        if (!eq) break;
-        ++reused;
-      }
-    }
-    // Device copy of the assembled encoder rows for the prompt gather.
-    DevBuf<float> denc;
-    if (!denc.alloc(enc_output.size())) return false;
-    if (cudaMemcpy(denc.p, enc_output.data(), enc_output.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
-      return false;
-    if (!eng.prefill_ids(ids, denc.p, (int)reused)) return false;
-    kv_owner = &st;
-    st.prev_ids.assign(ids.begin(), ids.begin() + prefill_len);
-    st.prev_enc = enc_output;
-    st.prev_prefill_len = prefill_len;
-
-    std::vector<int> gen;
-    if (!eng.decode(max_new, true, gen)) return false;
-    last_tokens.push_back(gen);
-    std::vector<int> chunk_tokens;
-    {
-      int token_i = 0, n_generated = 0;
-      while (n_generated < max_new && token_i < (int)gen.size()) {
-        ++n_generated;
-        int t = gen[token_i++];
-        if (t == kTokEndOfText || t == kTokImEnd) break;
-        chunk_tokens.push_back(t);
-      }
-    }
-
-    bool speech_ended = chunk_tokens.empty() && !st.raw_tokens.empty() && st.chunk_idx >= unfixed;
-    auto text_start_of = [&](const std::vector<int>& rt) -> size_t {
-      if (has_force_tokens) return 0;
-      auto it = std::find(rt.begin(), rt.end(), kTokAsrText);
-      return it == rt.end() ? 0 : (size_t)(it - rt.begin()) + 1;
-    };
-    auto emit = [&](const std::vector<int>& cand, size_t from, size_t to) {
-      for (size_t i = from; i < to; ++i) {
-        if (i < cand.size()) {
-          if (i >= st.stable_text_tokens.size()) st.stable_text_tokens.push_back(cand[i]);
-          const std::string& pb = tok.decode_bytes(cand[i]);
-          perf_text_tokens += 1;
-          st.result_bytes += pb;
-          delta += pb;
-        }
-      }
-    };
-    if (speech_ended) {
-      size_t ts = text_start_of(st.raw_tokens);
-      std::vector<int> cand(st.raw_tokens.begin() + ts, st.raw_tokens.end());
-      emit(cand, st.stable_text_tokens.size(), cand.size());
-    }
-    st.raw_tokens.resize(std::min(st.raw_tokens.size(), n_prefix));
-    st.raw_tokens.insert(st.raw_tokens.end(), chunk_tokens.begin(), chunk_tokens.end());
-
-    auto reset_context = [&]() {
-      size_t carry = std::min(st.stable_text_tokens.size(), kResetCarry);
-      size_t cs = st.stable_text_tokens.size() - carry;
-      st.raw_tokens.clear();
-      if (carry > 0) {
-        st.raw_tokens.push_back(kTokAsrText);
-        st.raw_tokens.insert(st.raw_tokens.end(), st.stable_text_tokens.begin() + cs, st.stable_text_tokens.end());
-      }
-      st.prev_ids.clear();
-      st.prev_enc.clear();
-      st.prev_prefill_len = 0;
-      st.stale_count = 0;
-      st.prev_tail_snapshot.clear();
-      if (st.enc_cache.size() >= kMaxEncWindows) {
-        st.enc_cache_base_windows += st.enc_cache.size();
-        st.enc_cache.clear();
-        st.enc_cached_seq_total = 0;
-      }
-    };
-    if (!speech_ended) {
-      if (st.raw_tokens == st.prev_tail_snapshot) {
-        st.stale_count += 1;
+// Several streams advance together: every round, each stream with a pending chunk runs
+// its prepare step, the chunks whose KV slots are contiguous decode as one batch (weights
+// read once per step for all of them), then each finishes its delta. A stream's deltas
+// are the ones stream_push_audio gives it alone (same prompts, same per-sequence decode).
+bool Ctx::stream_push_many(const std::vector<const std::vector<float>*>& samples, const std::vector<StreamState*>& sts,
+                           bool finalize, std::vector<std::string>& deltas) {
+  const size_t n = sts.size();
+  deltas.assign(n, std::string());
+  const int max_new = stream_max_new_tokens > 0 ? stream_max_new_tokens : 32;
+  std::vector<char> done(n, 0);
+  const int max_b = std::max(1, std::min(decode_batch > 0 ? decode_batch : kDecodeMaxBatch, eng.max_decode_batch()));
+  for (;;) {
+    std::vector<StreamChunk> work(n);
+    std::vector<size_t> act;
+    for (size_t i = 0; i < n; ++i) {
+      if (done[i]) continue;
+      if (!stream_chunk_prepare(*samples[i], *sts[i], finalize, work[i])) return false;
+      if (work[i].empty_stop) {
+        deltas[i].clear();
+        done[i] = 1;
+      } else if (!work[i].active) {
+        done[i] = 1;
       } else {
-        st.stale_count = 0;
-        st.prev_tail_snapshot = st.raw_tokens;
+        act.push_back(i);
       }
-      auto rep = tail_repeat_blocks(st.raw_tokens, kDegenMaxPeriod);
-      bool is_degen = st.stale_count >= kStaleChunks || rep.first >= (size_t)kDegenMinRepeats;
-      if (is_degen) reset_context();
-      if (st.chunk_idx > 0 && st.chunk_idx % kResetInterval == 0) reset_context();
-
-      size_t ts = text_start_of(st.raw_tokens);
-      size_t n_text_tokens = st.raw_tokens.size() > ts ? st.raw_tokens.size() - ts : 0;
-      size_t candidate_len;
-      if (is_final) candidate_len = n_text_tokens;
-      else if (st.chunk_idx >= unfixed) candidate_len = (size_t)std::max((int)n_text_tokens - rollback, 0);
-      else candidate_len = 0;
-      std::vector<int> cand(st.raw_tokens.begin() + std::min(ts, st.raw_tokens.size()), st.raw_tokens.end());
-      size_t from = st.stable_text_tokens.size();
-      emit(cand, from, std::max(candidate_len, from));
     }
-    perf_encode_ms += (eng.perf.mel_ms - before.mel_ms) + (eng.perf.enc_ms - before.enc_ms);
-    perf_decode_ms += (eng.perf.prefill_ms - before.prefill_ms) + (eng.perf.decode_ms - before.decode_ms);
-    perf_total_ms += now_ms() - chunk_t0;
-    st.chunk_idx += 1;
-    if (speech_ended) break;
+    if (act.empty()) break;
+    std::sort(act.begin(), act.end(), [&](size_t a, size_t b) { return work[a].slot < work[b].slot; });
+    for (size_t k = 0; k < act.size();) {
+      size_t e = k + 1;  // a run of contiguous slots, at most max_b long
+      while (e < act.size() && (int)(e - k) < max_b && work[act[e]].slot == work[act[e - 1]].slot + 1) ++e;
+      const int B = (int)(e - k);
+      if (B == 1) {
+        if (!eng.decode(max_new, true, work[act[k]].gen, nullptr, nullptr, work[act[k]].slot)) return false;
+      } else {
+        std::vector<std::vector<int>> gen;
+        if (!eng.decode_batch(B, max_new, true, gen, work[act[k]].slot)) return false;
+        for (int b = 0; b < B; ++b) work[act[k + b]].gen = std::move(gen[b]);
+      }
+      k = e;
+    }
+    for (size_t i : act)
+      if (stream_chunk_finish(*sts[i], work[i], deltas[i])) done[i] = 1;
   }
   return true;
 }

@@ -32,7 +32,24 @@ struct StreamState {  // transcribe.rs:801-893
   size_t audio_cursor = 0;
   int chunk_idx = 0;
   bool prompt_prepared = false;
+  // Device KV slot of this stream (assigned by the engine context on first use) and a
+  // process-unique id that proves ownership of it: a reset or a new stream gets a new id.
+  int slot = -1;
+  uint64_t uid = next_uid();
   void reset();
+  static uint64_t next_uid();
+};
+
+// One chunk of a stream in flight between its prepare and finish steps.
+struct StreamChunk {
+  bool active = false;      // prefilled, waiting for its decode
+  bool empty_stop = false;  // nothing encoded yet: the push ends with an empty delta
+  bool is_final = false;
+  int slot = -1;
+  size_t n_prefix = 0;
+  double t0 = 0;
+  StagePerf before;
+  std::vector<int> gen;
 };
 
 class Ctx {
@@ -51,7 +68,14 @@ class Ctx {
   // all of them); 0 = the engine's largest batch, 1 = one segment at a time. Only used
   // when past-text conditioning is off (the segments are then independent).
   int decode_batch = 0;
-  const void* kv_owner = nullptr;  // stream whose prompt rows the KV cache currently holds
+  // Streams keep their prompt rows in their own KV slots (kDecodeMaxBatch..): slot_uid[s]
+  // is the id of the stream whose rows slot s holds, slot_used[s] its last-use tick (LRU).
+  int max_stream_slots = 32;
+  std::vector<uint64_t> slot_uid, slot_used;
+  uint64_t slot_tick = 0;
+  // Returns the stream's slot; `owned` is false when the slot was (re)assigned, so its KV
+  // rows are not the stream's and the prefill starts from scratch.
+  int stream_slot(StreamState& st, bool& owned);
   // prompt tokens
   std::vector<int> prompt_tokens, force_prompt_tokens;
   bool has_prompt_tokens = false, has_force_tokens = false, prompt_tokens_ready = false;
@@ -73,6 +97,10 @@ class Ctx {
   bool transcribe_segment(const float* samples, size_t n, const std::vector<int>* past, std::string& text,
                           int& n_text, bool on_device = false);
   bool stream_push_audio(const std::vector<float>& samples, StreamState& st, bool finalize, std::string& delta);
+  bool stream_push_many(const std::vector<const std::vector<float>*>& samples, const std::vector<StreamState*>& sts,
+                        bool finalize, std::vector<std::string>& deltas);
+  bool stream_chunk_prepare(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w);
+  bool stream_chunk_finish(StreamState& st, StreamChunk& w, std::string& delta);
   void reset_perf();
   // Transcribes the independent segments [starts[i], ends[i]) of `samples` (each padded to
   // 0.5 s as transcribe.rs:374-384 does), batching their decodes; texts[i] per segment.

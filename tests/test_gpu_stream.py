@@ -85,3 +85,36 @@ def test_stream_reset_and_empty(tiny_dir):
     assert s.result() is None
     s.reset()
     assert s.push(eng, np.zeros(0, np.float32), finalize=True) is None
+
+
+@pytest.mark.parametrize("mode", ["int8", "bf16"])
+def test_stream_push_many_matches_single_streams(tiny_dir, mode):
+    """Streams advanced together (batched decode across their KV slots) produce exactly the
+    deltas each produces when pushed alone."""
+    import qwen_asr_b200 as Q
+    n_streams, n_chunks, chunk = 3, 4, 32000
+    audio = [synth.synth_audio(chunk * n_chunks, seed=300 + i) for i in range(n_streams)]
+
+    def make():
+        eng = Q.Engine(tiny_dir)
+        eng.set_decode_mode(mode)
+        eng.set_language("English")
+        return eng
+
+    eng_a = make()
+    many = [Q.Stream() for _ in range(n_streams)]
+    got = []
+    for c in range(n_chunks):
+        fin = c == n_chunks - 1
+        got.append(Q.stream_push_many(eng_a, many, [a[c * chunk:(c + 1) * chunk] for a in audio], finalize=fin))
+    eng_b = make()
+    want = []
+    singles = [Q.Stream() for _ in range(n_streams)]
+    for c in range(n_chunks):
+        fin = c == n_chunks - 1
+        want.append([s.push(eng_b, a[c * chunk:(c + 1) * chunk], finalize=fin) for s, a in zip(singles, audio)])
+    assert got == want
+    assert [s.result() for s in many] == [s.result() for s in singles]
+    # generated ids of every chunk of every stream, accumulated round by round in both engines
+    ids_a, ids_b = eng_a.last_tokens(), eng_b.last_tokens()
+    assert ids_a == ids_b and len(ids_a) == n_chunks * n_streams and sum(len(g) for g in ids_a) > 0
