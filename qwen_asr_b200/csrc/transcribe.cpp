@@ -4,6 +4,8 @@
 #include "transcribe.h"
 
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include <atomic>
 #include <chrono>
 #include <cstring>
@@ -334,6 +336,8 @@ bool Ctx::stream_chunk_prepare(const std::vector<float>& samples, StreamState& s
   const size_t enc_window_samples = enc_window_frames * kHop;
 
   w.t0 = now_ms();
+  static const bool timing = getenv("QASR_STREAM_TIMING") != nullptr;  // debugging aid
+  double tm[5] = {w.t0, 0, 0, 0, 0};
   st.audio_cursor = std::min(st.audio_cursor + chunk_samples, samples.size());
   w.is_final = finalize && st.audio_cursor >= samples.size();
   w.before = eng.perf;
@@ -369,6 +373,7 @@ bool Ctx::stream_chunk_prepare(const std::vector<float>& samples, StreamState& s
     partial_enc = &st.last_partial_enc;
   }
   size_t enc_seq_len = st.enc_cached_seq_total + partial_seq;
+  tm[1] = now_ms();
   if (enc_seq_len == 0) {  // the reference returns an empty delta here (transcribe.rs:1004-1007)
     st.chunk_idx += 1;
     w.empty_stop = true;
@@ -426,15 +431,23 @@ bool Ctx::stream_chunk_prepare(const std::vector<float>& samples, StreamState& s
       ++reused;
     }
   }
-  // Device copy of the assembled encoder rows for the prompt gather.
-  DevBuf<float> denc;
-  if (!denc.alloc(enc_output.size())) return false;
-  if (cudaMemcpy(denc.p, enc_output.data(), enc_output.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+  tm[2] = now_ms();
+  // Device copy of the assembled encoder rows for the prompt gather (grow-only buffer: a
+  // free per chunk would synchronise the device).
+  if (!stream_enc_dev.alloc(enc_output.size())) return false;
+  if (cudaMemcpyAsync(stream_enc_dev.p, enc_output.data(), enc_output.size() * 4, cudaMemcpyHostToDevice,
+                      eng.stream()) != cudaSuccess)
     return false;
-  if (!eng.prefill_ids(ids, denc.p, (int)reused, w.slot)) return false;
+  if (!eng.prefill_ids(ids, stream_enc_dev.p, (int)reused, w.slot)) return false;
+  tm[3] = now_ms();
   st.prev_ids.assign(ids.begin(), ids.begin() + prefill_len);
   st.prev_enc = std::move(enc_output);
   st.prev_prefill_len = prefill_len;
+  tm[4] = now_ms();
+  if (timing)
+    fprintf(stderr, "stream chunk %d: encode %.2f ms, assemble+lcp %.2f ms, upload+prefill %.2f ms (%zu rows, %zu reused), "
+            "keep %.2f ms\n", st.chunk_idx, tm[1] - tm[0], tm[2] - tm[1], tm[3] - tm[2], prefill_len, reused,
+            tm[4] - tm[3]);
   w.active = true;
   return true;
 }

@@ -71,6 +71,7 @@ class Ctx {
   // Streams keep their prompt rows in their own KV slots (kDecodeMaxBatch..): slot_uid[s]
   // is the id of the stream whose rows slot s holds, slot_used[s] its last-use tick (LRU).
   int max_stream_slots = 32;
+  DevBuf<float> stream_enc_dev;  // encoder rows of the chunk being prefilled
   std::vector<uint64_t> slot_uid, slot_used;
   uint64_t slot_tick = 0;
   // Returns the stream's slot; `owned` is false when the slot was (re)assigned, so its KV
