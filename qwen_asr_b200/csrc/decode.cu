@@ -968,13 +968,22 @@ size_t small_smem(int N, int K, bool int8, int B, int num_sms, int* rpc_out, int
   return 1024 + (size_t)nkc * rpc * kChunk + xbytes + (size_t)rpc * 4 + (size_t)K * 4 + (size_t)B * rpc * nkc * 4 + 64;
 }
 
+// The single-stage kernel takes a matrix when each CTA's slab is at most 48 rows and at most
+// 100 KB (larger slabs arrive as one batch with nothing to overlap: the streaming ring
+// kernel is faster there) and its shared memory fits.
+bool small_ok(int N, int K, bool int8, int B, int num_sms) {
+  int rpc = 0, nkc = 0;
+  const size_t smem = small_smem(N, K, int8, B, num_sms, &rpc, &nkc);
+  const int raw = (N + num_sms - 1) / num_sms;
+  return raw <= 48 && (size_t)nkc * rpc * kChunk <= 100 * 1024 && smem <= kSmallSmemMax;
+}
+
 template <int EPI>
 void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pdl = true) {
   const int row_bytes = m.K * (int8 ? 1 : 2);
-  const int raw = (m.N + num_sms - 1) / num_sms;
   int rpc = 0, nkc = 0;
   const size_t smem_small = small_smem(m.N, m.K, int8, m.B, num_sms, &rpc, &nkc);
-  if (EPI != MV_ARGMAX && raw <= 48 && smem_small <= kSmallSmemMax) {
+  if (EPI != MV_ARGMAX && small_ok(m.N, m.K, int8, m.B, num_sms)) {
     // small matrix: one stage per CTA holding the whole slab, K split across warps
     m.rows_per_cta = rpc;
     m.nkc = nkc;
@@ -1053,7 +1062,8 @@ int decode_max_batch(int hidden, int inter, int q_heads, bool int8) {
       const int N = shapes[i][0], K = shapes[i][1];
       const int raw = (N + nsm - 1) / nsm;
       auto small_at = [&](int b) {
-        return i < 3 && raw <= 48 && small_smem(N, K, int8, b, nsm, nullptr, nullptr) <= kSmallSmemMax;
+        (void)raw;
+        return i < 3 && small_ok(N, K, int8, b, nsm);
       };
       // the kernel (and so the summation order) must be the one a single sequence gets
       if (small_at(1) != small_at(B)) ok = false;
