@@ -25,6 +25,11 @@ constexpr int kWarps = 16;  // decode matvec CTA: 512 threads
 constexpr int kThreads = kWarps * 32;
 constexpr int kSplits = 16;  // attention split-K CTAs per kv head
 constexpr int kMaxG = 4;     // q heads per kv head
+// qkv_attn_kernel threads: 8 warps with int8 weights; 4 with bf16, whose larger register
+// and shared-memory footprint would otherwise keep the next kernel's CTAs (launched early
+// under programmatic dependent launch) off the SM.
+template <bool INT8>
+constexpr int qa_threads() { return INT8 ? 256 : 128; }
 
 enum MvEpi { MV_STORE = 0, MV_RESID = 1, MV_SWIGLU = 2, MV_ARGMAX = 3 };
 
@@ -542,7 +547,8 @@ struct QkvAttnArgs {
 };
 
 template <bool INT8>
-__global__ void __launch_bounds__(128, 1) qkv_attn_kernel(QkvAttnArgs a) {
+__global__ void __launch_bounds__(qa_threads<INT8>(), 1) qkv_attn_kernel(QkvAttnArgs a) {
+  constexpr int kQA = qa_threads<INT8>(), kQAW = kQA / 32;
   namespace cg = cooperative_groups;
   {  // sequence blockIdx.z of a batched step: its own residual row, state and KV slot
     const int b = blockIdx.z;
@@ -561,8 +567,8 @@ __global__ void __launch_bounds__(128, 1) qkv_attn_kernel(QkvAttnArgs a) {
   __shared__ float vals[64];                          // this CTA's projected rows
   __shared__ __align__(16) float hv[kMaxG + 2][kHd];  // normalised q heads, k, v of `pos`
   __shared__ float red[4][kMaxG + 1];
-  __shared__ float wm[4][kMaxG], wl[4][kMaxG];
-  __shared__ __align__(16) float wo[4][kMaxG][kHd];
+  __shared__ float wm[kQAW][kMaxG], wl[kQAW][kMaxG];
+  __shared__ __align__(16) float wo[kQAW][kMaxG][kHd];
   __shared__ float pm[kMaxG], pl[kMaxG];
   __shared__ __align__(16) float po[kMaxG][kHd];
   cg::cluster_group cluster = cg::this_cluster();
@@ -619,9 +625,10 @@ __global__ void __launch_bounds__(128, 1) qkv_attn_kernel(QkvAttnArgs a) {
     }
   }
   if (INT8 && d < rpc) sws[d] = a.ws[wrow(g0 + d)];
-  for (int i = d; i < K; i += 128) snw[i] = a.norm_w[i];
-  const float qn = a.qn[d], kn = a.kn[d];
-  const float c = a.rc[(size_t)pos * (kHd / 2) + (d & 63)], sn = a.rs[(size_t)pos * (kHd / 2) + (d & 63)];
+  for (int i = d; i < K; i += kQA) snw[i] = a.norm_w[i];
+  const int dd = d & (kHd - 1);  // head dimension of threads 0..127 (the rest help in loops)
+  const float qn = a.qn[dd], kn = a.kn[dd];
+  const float c = a.rc[(size_t)pos * (kHd / 2) + (dd & 63)], sn = a.rs[(size_t)pos * (kHd / 2) + (dd & 63)];
   pdl_launch_dependents();
   pdl_wait();
   tline.mark(2);
@@ -633,7 +640,7 @@ __global__ void __launch_bounds__(128, 1) qkv_attn_kernel(QkvAttnArgs a) {
     if (tok >= 0) erow = reinterpret_cast<const uint16_t*>(a.embed) + (size_t)tok * K;
   }
   float ss = 0.f;
-  for (int i = d * 4; i < K; i += 128 * 4) {
+  for (int i = d * 4; i < K; i += kQA * 4) {
     float4 v;
     if (erow) {
       uint2 b = *reinterpret_cast<const uint2*>(erow + i);
@@ -653,23 +660,23 @@ __global__ void __launch_bounds__(128, 1) qkv_attn_kernel(QkvAttnArgs a) {
   {
     float tot = block_sum(ss, red32);
     float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
-    for (int i = d; i < K; i += 128) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), snw[i]);
+    for (int i = d; i < K; i += kQA) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), snw[i]);
   }
   float xscale = 1.0f;
   if (INT8) {
     float mx = 0.f;
-    for (int i = d; i < K; i += 128) mx = fmaxf(mx, fabsf(xs[i]));
+    for (int i = d; i < K; i += kQA) mx = fmaxf(mx, fabsf(xs[i]));
     mx = block_max(mx, red32);
     xscale = mx > 0.f ? __fdiv_rn(mx, 127.0f) : 1.0f;
     float inv = __fdiv_rn(127.0f, fmaxf(mx, 1e-10f));
-    for (int i = d; i < K; i += 128) {
+    for (int i = d; i < K; i += kQA) {
       float r = roundf(__fmul_rn(xs[i], inv));
       xq[i] = (int8_t)fminf(fmaxf(r, -127.f), 127.f);
     }
   }
   __syncthreads();
   mbar_wait(&wbar, 0, a.err, 4);
-  for (int rr = warp * 2; rr < rpc; rr += 8) {
+  for (int rr = warp * 2; rr < rpc; rr += 2 * kQAW) {
     const bool two = rr + 1 < rpc;
     float v0, v1 = 0.f;
     if (INT8) {
@@ -729,23 +736,27 @@ __global__ void __launch_bounds__(128, 1) qkv_attn_kernel(QkvAttnArgs a) {
   cluster.sync();  // every CTA's rows are ready
 
   // ---- phase 2: gather this head group's raw q/k/v from the cluster
+  // (per-dimension work: threads 0..127, warps 0..3; the other warps wait at the barriers)
+  const bool hd = d < kHd;
   float raw[kMaxG + 2];
 #pragma unroll
   for (int g = 0; g < kMaxG + 2; ++g) {
     int gi = g < G ? g * kHd + d : (g == kMaxG ? G * kHd + d : (g == kMaxG + 1 ? (G + 1) * kHd + d : -1));
-    raw[g] = gi >= 0 ? *cluster.map_shared_rank(&vals[gi % rpc], gi / rpc) : 0.f;
+    raw[g] = hd && gi >= 0 ? *cluster.map_shared_rank(&vals[gi % rpc], gi / rpc) : 0.f;
   }
+  if (hd) {
 #pragma unroll
-  for (int g = 0; g <= kMaxG; ++g) {
-    float v = raw[g];
-    float s2 = warp_sum(v * v);
-    if (lane == 0 && (g < G || g == kMaxG)) red[warp][g < G ? g : G] = s2;
+    for (int g = 0; g <= kMaxG; ++g) {
+      float v = raw[g];
+      float s2 = warp_sum(v * v);
+      if (lane == 0 && (g < G || g == kMaxG)) red[warp][g < G ? g : G] = s2;
+    }
   }
   __syncthreads();
   float nv[kMaxG + 1];
 #pragma unroll
   for (int g = 0; g <= kMaxG; ++g) {
-    if (g < G || g == kMaxG) {
+    if (hd && (g < G || g == kMaxG)) {
       int r = g < G ? g : G;
       float tot = red[0][r] + red[1][r] + red[2][r] + red[3][r];
       float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)kHd), a.eps)));
@@ -758,18 +769,20 @@ __global__ void __launch_bounds__(128, 1) qkv_attn_kernel(QkvAttnArgs a) {
   float rot[kMaxG + 1];
 #pragma unroll
   for (int g = 0; g <= kMaxG; ++g) {
-    if (g < G || g == kMaxG) {
+    if (hd && (g < G || g == kMaxG)) {
       int h = g < G ? g : kMaxG;
       if (d < kHd / 2) rot[g] = __fadd_rn(__fmul_rn(nv[g], c), __fmul_rn(-hv[h][d + kHd / 2], sn));
       else rot[g] = __fadd_rn(__fmul_rn(nv[g], c), __fmul_rn(hv[h][d - kHd / 2], sn));
     }
   }
   __syncthreads();
+  if (hd) {
 #pragma unroll
-  for (int g = 0; g <= kMaxG; ++g)
-    if (g < G || g == kMaxG) hv[g < G ? g : kMaxG][d] = rot[g];
-  hv[kMaxG + 1][d] = raw[kMaxG + 1];
-  if (rank == 0) {
+    for (int g = 0; g <= kMaxG; ++g)
+      if (g < G || g == kMaxG) hv[g < G ? g : kMaxG][d] = rot[g];
+    hv[kMaxG + 1][d] = raw[kMaxG + 1];
+  }
+  if (hd && rank == 0) {
     kb[(size_t)pos * kHd + d] = rot[kMaxG];
     vb[(size_t)pos * kHd + d] = raw[kMaxG + 1];
   }
@@ -784,7 +797,7 @@ __global__ void __launch_bounds__(128, 1) qkv_attn_kernel(QkvAttnArgs a) {
     l[g] = 0.f;
     o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
   }
-  for (int jb = j0 + warp * 4; jb < j1; jb += 16) {
+  for (int jb = j0 + warp * 4; jb < j1; jb += 4 * kQAW) {
     float4 kv[4], vv[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -836,11 +849,13 @@ __global__ void __launch_bounds__(128, 1) qkv_attn_kernel(QkvAttnArgs a) {
     *reinterpret_cast<float4*>(&wo[warp][g][lane * 4]) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
   }
   __syncthreads();
-  for (int g = 0; g < G; ++g) {
-    float M = fmaxf(fmaxf(wm[0][g], wm[1][g]), fmaxf(wm[2][g], wm[3][g]));
+  for (int g = 0; g < G && hd; ++g) {
+    float M = wm[0][g];
+#pragma unroll
+    for (int w = 1; w < kQAW; ++w) M = fmaxf(M, wm[w][g]);
     float L = 0.f, O = 0.f;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
+    for (int w = 0; w < kQAW; ++w) {
       float f = wl[w][g] > 0.f ? expf(__fsub_rn(wm[w][g], M)) : 0.f;
       L = fmaf(wl[w][g], f, L);
       O = fmaf(wo[w][g][d], f, O);
@@ -1045,7 +1060,8 @@ void decode_kernels_init() {
   mv_attr<false, MV_SWIGLU>(kMax);
   mv_attr<false, MV_ARGMAX>(kMax);
   for (auto k : {qkv_attn_kernel<true>, qkv_attn_kernel<false>}) {
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
+    // its static shared memory (~22 KB) plus this stays within the 227 KB per block
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   }
 }
@@ -1133,8 +1149,8 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
       q.kv_rows = (int)std::max<long>(0, std::min<long>(24, ((long)budget - (long)(wbytes + tail)) / (2 * kHd * 4)));
       const size_t smem = wbytes + (size_t)q.kv_rows * kHd * 8 + tail;
       const dim3 grid(a.kv_heads, kSplits, B);
-      if (a.int8) launch_ex(qkv_attn_kernel<true>, grid, dim3(128), smem, s, l != 0, kSplits, q);
-      else launch_ex(qkv_attn_kernel<false>, grid, dim3(128), smem, s, l != 0, kSplits, q);
+      if (a.int8) launch_ex(qkv_attn_kernel<true>, grid, dim3(qa_threads<true>()), smem, s, l != 0, kSplits, q);
+      else launch_ex(qkv_attn_kernel<false>, grid, dim3(qa_threads<false>()), smem, s, l != 0, kSplits, q);
       if (a.on_launch) a.on_launch(a.hook_ctx, 1);
       check("qkv_attn", l);
     }
