@@ -547,7 +547,7 @@ struct QkvAttnArgs {
 };
 
 template <bool INT8>
-__global__ void __launch_bounds__(qa_threads<INT8>(), 1) qkv_attn_kernel(QkvAttnArgs a) {
+__global__ void __launch_bounds__(qa_threads<INT8>(), INT8 ? 3 : 1) qkv_attn_kernel(QkvAttnArgs a) {
   constexpr int kQA = qa_threads<INT8>(), kQAW = kQA / 32;
   namespace cg = cooperative_groups;
   {  // sequence blockIdx.z of a batched step: its own residual row, state and KV slot
