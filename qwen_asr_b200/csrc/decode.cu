@@ -121,6 +121,29 @@ __device__ __forceinline__ T warp_reduce_rows(const T* v, int lane) {
     return s;
   }
 }
+// Reduces v[0..8) over the warp with the lane pairing of warp_sum (xor 16, 8, 4, 2, 1), so
+// each result is bit-identical to warp_sum of that value; afterwards lane l holds value
+// ((l >> 4) & 1) * 4 + ((l >> 3) & 1) * 2 + ((l >> 2) & 1).
+template <typename T>
+__device__ __forceinline__ T warp_reduce8(const T (&v)[kMaxB], int lane) {
+  T s[4], t[2];
+  const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const T keep = h16 ? v[i + 4] : v[i], send = h16 ? v[i] : v[i + 4];
+    s[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const T keep = h8 ? s[i + 2] : s[i], send = h8 ? s[i] : s[i + 2];
+    t[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  T u = (h4 ? t[1] : t[0]) + __shfl_xor_sync(0xffffffffu, h4 ? t[0] : t[1], 4);
+  u += __shfl_xor_sync(0xffffffffu, u, 2);
+  u += __shfl_xor_sync(0xffffffffu, u, 1);
+  return u;
+}
+
 template <int RPW>
 __device__ __forceinline__ int lane_row(int lane) {
   return RPW == 4 ? ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1) : (RPW == 2 ? (lane >> 4) : 0);
@@ -130,7 +153,8 @@ __device__ __forceinline__ bool row_lane(int lane) {
   return RPW == 4 ? (lane & 7) == 0 : (RPW == 2 ? (lane & 15) == 0 : lane == 0);
 }
 
-// Stages sequence b's input vector in shared memory: gathered from the embedding (layer 0)
+// Single-sequence staging (B = 1; stage_all below gives the same bits for B > 1): stages
+// sequence b's input vector in shared memory: gathered from the embedding (layer 0)
 // or read from x, RMS-normalised when norm_w is set, and for int8 weights quantised per
 // vector (kernels/mod.rs:1795-1802) into xq_b; returns the activation scale (1 for bf16).
 template <bool INT8>
@@ -183,6 +207,136 @@ __device__ float stage_x(const MvArgs& a, int b, float* xs_b, int8_t* xq_b, cons
   }
   __syncthreads();
   return xscale;
+}
+
+// Stages the input vectors of all B (> 1) sequences at once: read from x, RMS-normalised
+// when norm_w is set, and for int8 weights quantised per vector (kernels/mod.rs:1795-1802)
+// into xq[b] with scale xscale[b] (bf16: the f32 vector goes to xs[b], xscale[b] = 1). The
+// decode matvecs never gather the embedding (the fused QKV kernel does). Thread t owns the
+// 4-element chunks c = t + 512 j of every sequence and accumulates them in the order
+// stage_x does, so a batched step is bit-identical to single-sequence steps. Every load
+// is unconditional (a row past B re-reads row B - 1 and is discarded) so the B loads are
+// in flight together; the block-wide reductions are shared by all sequences. The int8
+// path keeps chunk j = 0 in registers and needs no f32 staging buffer.
+template <bool INT8>
+__device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* snw, float* red /* [kMaxB][kWarps] */,
+                          float* sinv /* [2 * kMaxB] */, float* xscale, int kpad) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, K = a.K, B = a.B;
+  const int nc = K >> 2;
+  auto ldx = [&](int b, int c) -> float4 {
+    return *reinterpret_cast<const float4*>(a.x + (size_t)min(b, B - 1) * a.ldx + 4 * c);
+  };
+  auto normed = [&](float4 v, float inv, int c) -> float4 {
+    const float4 w = *reinterpret_cast<const float4*>(snw + 4 * c);
+    return make_float4(__fmul_rn(__fmul_rn(v.x, inv), w.x), __fmul_rn(__fmul_rn(v.y, inv), w.y),
+                       __fmul_rn(__fmul_rn(v.z, inv), w.z), __fmul_rn(__fmul_rn(v.w, inv), w.w));
+  };
+  auto sumsq = [](float s, float4 v) {
+    s = fmaf(v.x, v.x, s);
+    s = fmaf(v.y, v.y, s);
+    s = fmaf(v.z, v.z, s);
+    return fmaf(v.w, v.w, s);
+  };
+  auto absmax = [](float m, float4 v) {
+    return fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  };
+  for (int i = K + tid; i < kpad; i += kThreads)  // padding past K multiplies zero weights
+    for (int b = 0; b < B; ++b) {
+      if (INT8) xq[(size_t)b * kpad + i] = 0;
+      else xs[(size_t)b * kpad + i] = 0.f;
+    }
+  const bool has0 = tid < nc;
+  const int c0 = has0 ? tid : 0;
+  float4 hold[kMaxB];
+  float acc[kMaxB];  // sum of squares (norm) or max |x| (int8 without norm)
+#pragma unroll
+  for (int b = 0; b < kMaxB; ++b) hold[b] = ldx(b, c0);
+#pragma unroll
+  for (int b = 0; b < kMaxB; ++b) {
+    acc[b] = 0.f;
+    if (!has0) continue;
+    if (!INT8 && b < B) *reinterpret_cast<float4*>(xs + (size_t)b * kpad + 4 * c0) = hold[b];
+    acc[b] = a.norm_w ? sumsq(0.f, hold[b]) : absmax(0.f, hold[b]);
+  }
+  for (int c = tid + kThreads; c < nc; c += kThreads) {  // chunks j >= 1 (K > 2048)
+    float4 t[kMaxB];
+#pragma unroll
+    for (int b = 0; b < kMaxB; ++b) t[b] = ldx(b, c);
+#pragma unroll
+    for (int b = 0; b < kMaxB; ++b) {
+      if (!INT8 && b < B) *reinterpret_cast<float4*>(xs + (size_t)b * kpad + 4 * c) = t[b];
+      acc[b] = a.norm_w ? sumsq(acc[b], t[b]) : absmax(acc[b], t[b]);
+    }
+  }
+  // per-sequence block reduction: warp butterflies, then warp b combines the 16 warp values
+  auto reduce = [&](bool is_sum) {
+#pragma unroll
+    for (int b = 0; b < kMaxB; ++b) {
+      const float v = is_sum ? warp_sum(acc[b]) : warp_max(acc[b]);
+      if (lane == 0 && b < B) red[b * kWarps + warp] = v;
+    }
+    __syncthreads();
+    if (warp < B) {
+      const float t = lane < kWarps ? red[warp * kWarps + lane] : (is_sum ? 0.f : -3.0e38f);
+      const float r = is_sum ? warp_sum(t) : warp_max(t);
+      if (lane == 0) {
+        if (is_sum) {
+          sinv[warp] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(r, (float)K), a.eps)));  // norm
+        } else {
+          xscale[warp] = r > 0.f ? __fdiv_rn(r, 127.0f) : 1.0f;
+          sinv[kMaxB + warp] = __fdiv_rn(127.0f, fmaxf(r, 1e-10f));  // quantisation
+        }
+      }
+    }
+    __syncthreads();
+  };
+  if (!INT8 && tid < B) xscale[tid] = 1.0f;
+  if (a.norm_w) {
+    reduce(true);
+    if (INT8) {
+#pragma unroll
+      for (int b = 0; b < kMaxB; ++b) {
+        hold[b] = normed(hold[b], sinv[min(b, B - 1)], c0);
+        acc[b] = has0 ? absmax(0.f, hold[b]) : 0.f;
+      }
+      for (int c = tid + kThreads; c < nc; c += kThreads) {
+        float4 t[kMaxB];
+#pragma unroll
+        for (int b = 0; b < kMaxB; ++b) t[b] = ldx(b, c);
+#pragma unroll
+        for (int b = 0; b < kMaxB; ++b) acc[b] = absmax(acc[b], normed(t[b], sinv[min(b, B - 1)], c));
+      }
+    } else {
+      for (int i = tid; i < B * nc; i += kThreads) {
+        const int b = i / nc, c = i - b * nc;
+        float4* p = reinterpret_cast<float4*>(xs + (size_t)b * kpad + 4 * c);
+        *p = normed(*p, sinv[b], c);
+      }
+    }
+  }
+  if (INT8) {
+    reduce(false);
+    auto quant = [&](int b, int c, float4 v) {
+      const float inv = sinv[kMaxB + b];
+      auto q = [&](float f) -> int {
+        const float r = roundf(__fmul_rn(f, inv));
+        return (int)fminf(fmaxf(r, -127.f), 127.f) & 0xFF;
+      };
+      *reinterpret_cast<int*>(xq + (size_t)b * kpad + 4 * c) = q(v.x) | (q(v.y) << 8) | (q(v.z) << 16) | (q(v.w) << 24);
+    };
+#pragma unroll
+    for (int b = 0; b < kMaxB; ++b)
+      if (has0 && b < B) quant(b, c0, hold[b]);
+    for (int c = tid + kThreads; c < nc; c += kThreads) {
+      float4 t[kMaxB];
+#pragma unroll
+      for (int b = 0; b < kMaxB; ++b) t[b] = ldx(b, c);
+#pragma unroll
+      for (int b = 0; b < kMaxB; ++b)
+        if (b < B) quant(b, c, a.norm_w ? normed(t[b], sinv[b], c) : t[b]);
+    }
+  }
+  __syncthreads();
 }
 
 // Greedy-token bookkeeping of sequence b after its argmax (decoder.rs:550-645 returns the
@@ -247,22 +401,24 @@ __device__ __forceinline__ void argmax_finish(const MvArgs& a, const unsigned lo
 // x 512 bytes each (2-D TMA boxes; the first ones issued before the dependency wait).
 // Every warp owns R/16 rows of a stage and accumulates them for every sequence across the
 // row's 512-byte chunks, so all 16 warps work on every stage.
-template <bool INT8, int EPI, int RPW>
+template <bool INT8, int EPI, int RPW, bool BATCH>
 __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__ CUtensorMap wmap, MvArgs a) {
   Timeline tline;
   tline.begin(a.tl, a.tl_count, a.kind);
   extern __shared__ unsigned char sm_raw[];
-  __shared__ float red[32];
+  __shared__ float red_raw[BATCH ? kMaxB * kWarps : 32];
+  __shared__ float sinv[BATCH ? 2 * kMaxB : 1];
+  float* red = red_raw;
   __shared__ unsigned long long am_warp[kWarps][kMaxB];
   __shared__ float xscale[kMaxB];
   __shared__ int is_last;
   unsigned char* sm = (unsigned char*)(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int K = a.K, R = a.block_rows, nkc = a.nkc, B = a.B;
+  const int K = a.K, R = a.block_rows, nkc = a.nkc, B = BATCH ? a.B : 1;
   const int kpad = nkc * kChunk / (INT8 ? 1 : 2);  // padded vector length in elements
   const int stage_bytes = R * kChunk;
   unsigned char* wst = sm;
-  float* xs = reinterpret_cast<float*>(sm + (size_t)a.stages * stage_bytes);  // int8: [kpad]; bf16: [B][kpad]
+  float* xs = reinterpret_cast<float*>(sm + (size_t)a.stages * stage_bytes);  // int8: [kpad] (B = 1 staging); bf16: [B][kpad]
   int8_t* xq = reinterpret_cast<int8_t*>(xs + (INT8 ? kpad : B * kpad));    // int8: [B][kpad]
   uint64_t* full = reinterpret_cast<uint64_t*>(xq + (INT8 ? ((B * kpad + 15) & ~15) : 0));
   uint64_t* empty = full + a.stages;
@@ -293,11 +449,13 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__
   pdl_launch_dependents();
   pdl_wait();
   tline.mark(2);
-  for (int b = 0; b < B; ++b) {
-    float sc = stage_x<INT8>(a, b, INT8 ? xs : xs + (size_t)b * kpad, xq + (size_t)b * kpad, snw, red, kpad);
-    if (tid == 0) xscale[b] = sc;
+  if constexpr (!BATCH) {
+    const float sc = stage_x<INT8>(a, 0, xs, xq, snw, red, kpad);
+    if (tid == 0) xscale[0] = sc;
+    __syncthreads();
+  } else {
+    stage_all<INT8>(a, xs, xq, snw, red, sinv, xscale, kpad);
   }
-  __syncthreads();
 
   unsigned long long best[kMaxB];
   int iacc[4][kMaxB];
@@ -409,12 +567,14 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__
 // whole weight slab arrives in ONE stage (one TMA box per 512-byte column chunk) issued
 // before the dependency wait; the 16 warps split the (sequence, row, chunk) dot products,
 // and each row's chunk partials are summed in a fixed order (deterministic for f32 too).
-template <bool INT8, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) mv_small_kernel(const __grid_constant__ CUtensorMap wmap, MvArgs a) {
+template <bool INT8, int EPI, bool BATCH>
+__device__ __forceinline__ void mv_small_body(const CUtensorMap& wmap, const MvArgs& a) {
   Timeline tline;
   tline.begin(a.tl, a.tl_count, a.kind);
   extern __shared__ unsigned char sm_raw[];
-  __shared__ float red[32];
+  __shared__ float red_raw[BATCH ? kMaxB * kWarps : 32];
+  __shared__ float sinv[BATCH ? 2 * kMaxB : 1];
+  float* red = red_raw;
   __shared__ float xscale[kMaxB];
   __shared__ __align__(8) uint64_t bar;
   unsigned char* sm = (unsigned char*)(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
@@ -422,10 +582,10 @@ __global__ void __launch_bounds__(kThreads, 1) mv_small_kernel(const __grid_cons
   const int K = a.K, nkc = a.nkc, R = a.rows_per_cta, B = a.B;
   const int kpad = nkc * kChunk / (INT8 ? 1 : 2);
   unsigned char* wst = sm;  // [kc][R rows][512 B]
-  float* xs = reinterpret_cast<float*>(sm + (size_t)nkc * R * kChunk);  // int8: [kpad]; bf16: [B][kpad]
+  float* xs = reinterpret_cast<float*>(sm + (size_t)nkc * R * kChunk);  // int8: [kpad] (B = 1 staging); bf16: [B][kpad]
   int8_t* xq = reinterpret_cast<int8_t*>(xs + (INT8 ? kpad : B * kpad));
   float* sws = reinterpret_cast<float*>(xq + (INT8 ? ((B * kpad + 15) & ~15) : 0));
-  float* snw = sws + R;
+  float* snw = sws + ((R + 3) & ~3);  // 16-byte aligned: read as float4
   float* part = snw + K;  // [B][R][nkc] chunk partials (int32 bit patterns for int8)
   const int r0 = blockIdx.x * R;
   const int nrows = max(0, min(a.N, r0 + R) - r0);
@@ -442,12 +602,53 @@ __global__ void __launch_bounds__(kThreads, 1) mv_small_kernel(const __grid_cons
   pdl_launch_dependents();
   pdl_wait();
   tline.mark(2);
-  for (int b = 0; b < B; ++b) {
-    float sc = stage_x<INT8>(a, b, INT8 ? xs : xs + (size_t)b * kpad, xq + (size_t)b * kpad, snw, red, kpad);
-    if (tid == 0) xscale[b] = sc;
+  if constexpr (!BATCH) {
+    for (int b = 0; b < B; ++b) {
+      const float sc = stage_x<INT8>(a, b, INT8 ? xs : xs + (size_t)b * kpad, xq + (size_t)b * kpad, snw, red, kpad);
+      if (tid == 0) xscale[b] = sc;
+    }
+  } else {
+    stage_all<INT8>(a, xs, xq, snw, red, sinv, xscale, kpad);
   }
   mbar_wait(&bar, 0, a.err, 5);
-  const int items = B * R * nkc;
+  if (BATCH) {
+    // one (row, chunk) weight item per warp pass, dotted with every sequence's vector
+    const int sel = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+    for (int it = warp; it < R * nkc; it += kWarps) {
+      const int r = it / nkc, kc = it % nkc;
+      const uint4 wv = *reinterpret_cast<const uint4*>(wst + ((size_t)kc * R + r) * kChunk + lane * 16);
+      if (INT8) {
+        int acc[kMaxB];
+#pragma unroll
+        for (int b = 0; b < kMaxB; ++b) {  // rows past B repeat row B - 1 and are dropped
+          const int4 xv = *reinterpret_cast<const int4*>(xq + (size_t)min(b, B - 1) * kpad + kc * kChunk + lane * 16);
+          acc[b] = __dp4a((int)wv.x, xv.x, 0);
+          acc[b] = __dp4a((int)wv.y, xv.y, acc[b]);
+          acc[b] = __dp4a((int)wv.z, xv.z, acc[b]);
+          acc[b] = __dp4a((int)wv.w, xv.w, acc[b]);
+        }
+        const int u = warp_reduce8(acc, lane);
+        if ((lane & 3) == 0 && sel < B) part[((size_t)sel * R + r) * nkc + kc] = __int_as_float(u);
+      } else {
+        float f[8], acc[kMaxB];
+        bf16x8_to_f32(wv, f);
+#pragma unroll
+        for (int b = 0; b < kMaxB; ++b) {
+          const float* xb = xs + (size_t)min(b, B - 1) * kpad + kc * (kChunk / 2) + lane * 8;
+          const float4 x0 = *reinterpret_cast<const float4*>(xb);
+          const float4 x1 = *reinterpret_cast<const float4*>(xb + 4);
+          float s = f[0] * x0.x;
+          s = fmaf(f[1], x0.y, s); s = fmaf(f[2], x0.z, s); s = fmaf(f[3], x0.w, s);
+          s = fmaf(f[4], x1.x, s); s = fmaf(f[5], x1.y, s); s = fmaf(f[6], x1.z, s);
+          s = fmaf(f[7], x1.w, s);
+          acc[b] = s;
+        }
+        const float u = warp_reduce8(acc, lane);
+        if ((lane & 3) == 0 && sel < B) part[((size_t)sel * R + r) * nkc + kc] = u;
+      }
+    }
+  }
+  const int items = BATCH ? 0 : B * R * nkc;
   for (int it = warp; it < items; it += kWarps) {
     const int b = it / (R * nkc), r = (it / nkc) % R, kc = it % nkc;
     const unsigned char* w = wst + ((size_t)kc * R + r) * kChunk + lane * 16;
@@ -503,6 +704,17 @@ __global__ void __launch_bounds__(kThreads, 1) mv_small_kernel(const __grid_cons
     }
   }
   tline.mark(3);
+}
+
+// B = 1 instantiation, and the batched one (capped at 96 registers so a successor kernel's
+// CTAs still fit beside it under programmatic dependent launch).
+template <bool INT8, int EPI>
+__global__ void __launch_bounds__(kThreads, 1) mv_small_kernel(const __grid_constant__ CUtensorMap wmap, MvArgs a) {
+  mv_small_body<INT8, EPI, false>(wmap, a);
+}
+template <bool INT8, int EPI>
+__global__ void __maxnreg__(96) mv_small_batch_kernel(const __grid_constant__ CUtensorMap wmap, MvArgs a) {
+  mv_small_body<INT8, EPI, true>(wmap, a);
 }
 
 // ------------------------------------------------------------------ QKV + attention
@@ -965,9 +1177,16 @@ void launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
 template <bool INT8, int EPI>
 void mv_launch(const CUtensorMap& map, const MvArgs& m, const MvPlan& p, cudaStream_t s, bool pdl) {
   const int rpw = p.block_rows / kWarps;
-  if (rpw == 4) launch_ex(mv_kernel<INT8, EPI, 4>, dim3(p.grid), dim3(kThreads), p.smem, s, pdl, 1, map, m);
-  else if (rpw == 2) launch_ex(mv_kernel<INT8, EPI, 2>, dim3(p.grid), dim3(kThreads), p.smem, s, pdl, 1, map, m);
-  else launch_ex(mv_kernel<INT8, EPI, 1>, dim3(p.grid), dim3(kThreads), p.smem, s, pdl, 1, map, m);
+  const dim3 g(p.grid), t(kThreads);
+  if (m.B > 1) {
+    if (rpw == 4) launch_ex(mv_kernel<INT8, EPI, 4, true>, g, t, p.smem, s, pdl, 1, map, m);
+    else if (rpw == 2) launch_ex(mv_kernel<INT8, EPI, 2, true>, g, t, p.smem, s, pdl, 1, map, m);
+    else launch_ex(mv_kernel<INT8, EPI, 1, true>, g, t, p.smem, s, pdl, 1, map, m);
+  } else {
+    if (rpw == 4) launch_ex(mv_kernel<INT8, EPI, 4, false>, g, t, p.smem, s, pdl, 1, map, m);
+    else if (rpw == 2) launch_ex(mv_kernel<INT8, EPI, 2, false>, g, t, p.smem, s, pdl, 1, map, m);
+    else launch_ex(mv_kernel<INT8, EPI, 1, false>, g, t, p.smem, s, pdl, 1, map, m);
+  }
 }
 
 // Shared memory of the single-stage small matvec for B sequences (0 when it does not apply).
@@ -980,7 +1199,7 @@ size_t small_smem(int N, int K, bool int8, int B, int num_sms, int* rpc_out, int
   const size_t xbytes = int8 ? (size_t)kpad * 4 + (((size_t)B * kpad + 15) & ~(size_t)15) : (size_t)B * kpad * 4;
   if (rpc_out) *rpc_out = rpc;
   if (nkc_out) *nkc_out = nkc;
-  return 1024 + (size_t)nkc * rpc * kChunk + xbytes + (size_t)rpc * 4 + (size_t)K * 4 + (size_t)B * rpc * nkc * 4 + 64;
+  return 1024 + (size_t)nkc * rpc * kChunk + xbytes + (size_t)((rpc + 3) & ~3) * 4 + (size_t)K * 4 + (size_t)B * rpc * nkc * 4 + 64;
 }
 
 // The single-stage kernel takes a matrix when each CTA's slab is at most 48 rows and at most
@@ -1008,8 +1227,14 @@ void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pd
       return;
     }
     dim3 grid((m.N + rpc - 1) / rpc);
-    if (int8) launch_ex(mv_small_kernel<true, EPI>, grid, dim3(kThreads), smem_small, s, pdl, 1, map, m);
-    else launch_ex(mv_small_kernel<false, EPI>, grid, dim3(kThreads), smem_small, s, pdl, 1, map, m);
+    const dim3 t(kThreads);
+    if (m.B > 1) {
+      if (int8) launch_ex(mv_small_batch_kernel<true, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
+      else launch_ex(mv_small_batch_kernel<false, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
+    } else {
+      if (int8) launch_ex(mv_small_kernel<true, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
+      else launch_ex(mv_small_kernel<false, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
+    }
     return;
   }
   MvPlan p = plan_mv(m.N, m.K, int8, m.B, num_sms, EPI == MV_SWIGLU, EPI == MV_ARGMAX);
@@ -1032,9 +1257,9 @@ void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pd
 
 template <bool INT8, int EPI>
 void mv_attr(int bytes) {
-  cudaFuncSetAttribute(mv_kernel<INT8, EPI, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  cudaFuncSetAttribute(mv_kernel<INT8, EPI, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  cudaFuncSetAttribute(mv_kernel<INT8, EPI, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  for (auto k : {mv_kernel<INT8, EPI, 1, false>, mv_kernel<INT8, EPI, 2, false>, mv_kernel<INT8, EPI, 4, false>,
+                 mv_kernel<INT8, EPI, 1, true>, mv_kernel<INT8, EPI, 2, true>, mv_kernel<INT8, EPI, 4, true>})
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 int sm_count() {
@@ -1049,7 +1274,10 @@ void decode_kernels_init() {
   const int kMax = 210 * 1024;
   for (auto k : {mv_small_kernel<true, MV_RESID>, mv_small_kernel<false, MV_RESID>, mv_small_kernel<true, MV_STORE>,
                  mv_small_kernel<false, MV_STORE>, mv_small_kernel<true, MV_SWIGLU>,
-                 mv_small_kernel<false, MV_SWIGLU>})
+                 mv_small_kernel<false, MV_SWIGLU>, mv_small_batch_kernel<true, MV_RESID>,
+                 mv_small_batch_kernel<false, MV_RESID>, mv_small_batch_kernel<true, MV_STORE>,
+                 mv_small_batch_kernel<false, MV_STORE>, mv_small_batch_kernel<true, MV_SWIGLU>,
+                 mv_small_batch_kernel<false, MV_SWIGLU>})
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMax);
   mv_attr<true, MV_STORE>(kMax);
   mv_attr<true, MV_RESID>(kMax);
