@@ -30,6 +30,10 @@ constexpr int kMaxG = 4;     // q heads per kv head
 // under programmatic dependent launch) off the SM.
 template <bool INT8>
 constexpr int qa_threads() { return INT8 ? 256 : 128; }
+// The attention-only variant (batched steps, q/k/v projected by a batched matvec) needs
+// one thread per head dimension.
+template <bool INT8, bool PROJ>
+constexpr int qa_block() { return PROJ ? qa_threads<INT8>() : 128; }
 
 enum MvEpi { MV_STORE = 0, MV_RESID = 1, MV_SWIGLU = 2, MV_ARGMAX = 3 };
 
@@ -61,6 +65,7 @@ struct MvArgs {
   unsigned long long* tl;
   int* tl_count;
   int kind;
+  int sum_threads;             // batched staging: threads owning sum-of-squares chunks (0: all)
 };
 
 __device__ __forceinline__ unsigned long long am_key(float v, int idx) {
@@ -209,12 +214,13 @@ __device__ float stage_x(const MvArgs& a, int b, float* xs_b, int8_t* xq_b, cons
   return xscale;
 }
 
-// Stages the input vectors of all B (> 1) sequences at once: read from x, RMS-normalised
-// when norm_w is set, and for int8 weights quantised per vector (kernels/mod.rs:1795-1802)
-// into xq[b] with scale xscale[b] (bf16: the f32 vector goes to xs[b], xscale[b] = 1). The
-// decode matvecs never gather the embedding (the fused QKV kernel does). Thread t owns the
-// 4-element chunks c = t + 512 j of every sequence and accumulates them in the order
-// stage_x does, so a batched step is bit-identical to single-sequence steps. Every load
+// Stages the input vectors of all B (> 1) sequences at once: read from x (layer 0: gathered
+// from the embedding, the rows also written to x_out by CTA 0), RMS-normalised when norm_w
+// is set, and for int8 weights quantised per vector (kernels/mod.rs:1795-1802) into xq[b]
+// with scale xscale[b] (bf16: the f32 vector goes to xs[b], xscale[b] = 1). Thread t < P
+// owns the 4-element chunks c = t + P j of every sequence and accumulates them in order:
+// with P = 512 that is the order of stage_x, with P = the fused QKV kernel's block size
+// that kernel's order, so a batched step is bit-identical to single-sequence steps. Every load
 // is unconditional (a row past B re-reads row B - 1 and is discarded) so the B loads are
 // in flight together; the block-wide reductions are shared by all sequences. The int8
 // path keeps chunk j = 0 in registers and needs no f32 staging buffer.
@@ -222,9 +228,23 @@ template <bool INT8>
 __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* snw, float* red /* [kMaxB][kWarps] */,
                           float* sinv /* [2 * kMaxB] */, float* xscale, int kpad) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, K = a.K, B = a.B;
-  const int nc = K >> 2;
+  const int nc = K >> 2, P = a.sum_threads ? a.sum_threads : kThreads;
+  __shared__ int stok[kMaxB];
+  if (a.embed) {
+    if (tid < kMaxB) stok[tid] = tid < B ? a.st[tid].cur_token : -1;
+    __syncthreads();
+  }
   auto ldx = [&](int b, int c) -> float4 {
-    return *reinterpret_cast<const float4*>(a.x + (size_t)min(b, B - 1) * a.ldx + 4 * c);
+    const int bb = min(b, B - 1);
+    const float4 xv = *reinterpret_cast<const float4*>(a.x + (size_t)bb * a.ldx + 4 * c);
+    if (!a.embed) return xv;
+    // layer 0: the row of the sequence's current token (both loads issued, one kept)
+    const int tok = stok[bb];
+    const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(a.embed) +
+                                                    (size_t)max(tok, 0) * K + 4 * c);
+    const float4 ev = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                                  __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+    return tok >= 0 ? ev : xv;
   };
   auto normed = [&](float4 v, float inv, int c) -> float4 {
     const float4 w = *reinterpret_cast<const float4*>(snw + 4 * c);
@@ -245,7 +265,7 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
       if (INT8) xq[(size_t)b * kpad + i] = 0;
       else xs[(size_t)b * kpad + i] = 0.f;
     }
-  const bool has0 = tid < nc;
+  const bool has0 = tid < min(P, nc);
   const int c0 = has0 ? tid : 0;
   float4 hold[kMaxB];
   float acc[kMaxB];  // sum of squares (norm) or max |x| (int8 without norm)
@@ -256,15 +276,19 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
     acc[b] = 0.f;
     if (!has0) continue;
     if (!INT8 && b < B) *reinterpret_cast<float4*>(xs + (size_t)b * kpad + 4 * c0) = hold[b];
+    if (a.embed && blockIdx.x == 0 && b < B && stok[b] >= 0)
+      *reinterpret_cast<float4*>(a.x_out + (size_t)b * a.ldx + 4 * c0) = hold[b];
     acc[b] = a.norm_w ? sumsq(0.f, hold[b]) : absmax(0.f, hold[b]);
   }
-  for (int c = tid + kThreads; c < nc; c += kThreads) {  // chunks j >= 1 (K > 2048)
+  for (int c = tid + P; c < nc && tid < P; c += P) {  // chunks j >= 1
     float4 t[kMaxB];
 #pragma unroll
     for (int b = 0; b < kMaxB; ++b) t[b] = ldx(b, c);
 #pragma unroll
     for (int b = 0; b < kMaxB; ++b) {
       if (!INT8 && b < B) *reinterpret_cast<float4*>(xs + (size_t)b * kpad + 4 * c) = t[b];
+      if (a.embed && blockIdx.x == 0 && b < B && stok[b] >= 0)
+        *reinterpret_cast<float4*>(a.x_out + (size_t)b * a.ldx + 4 * c) = t[b];
       acc[b] = a.norm_w ? sumsq(acc[b], t[b]) : absmax(acc[b], t[b]);
     }
   }
@@ -299,7 +323,7 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
         hold[b] = normed(hold[b], sinv[min(b, B - 1)], c0);
         acc[b] = has0 ? absmax(0.f, hold[b]) : 0.f;
       }
-      for (int c = tid + kThreads; c < nc; c += kThreads) {
+      for (int c = tid + P; c < nc && tid < P; c += P) {
         float4 t[kMaxB];
 #pragma unroll
         for (int b = 0; b < kMaxB; ++b) t[b] = ldx(b, c);
@@ -327,7 +351,7 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
 #pragma unroll
     for (int b = 0; b < kMaxB; ++b)
       if (has0 && b < B) quant(b, c0, hold[b]);
-    for (int c = tid + kThreads; c < nc; c += kThreads) {
+    for (int c = tid + P; c < nc && tid < P; c += P) {
       float4 t[kMaxB];
 #pragma unroll
       for (int b = 0; b < kMaxB; ++b) t[b] = ldx(b, c);
@@ -756,11 +780,13 @@ struct QkvAttnArgs {
   int* err;
   unsigned long long* tl;
   int* tl_count;
+  const float* qkv;            // attention-only variant: projected rows [B][ldq]
+  int ldq;
 };
 
-template <bool INT8>
-__global__ void __launch_bounds__(qa_threads<INT8>(), INT8 ? 3 : 1) qkv_attn_kernel(QkvAttnArgs a) {
-  constexpr int kQA = qa_threads<INT8>(), kQAW = kQA / 32;
+template <bool INT8, bool PROJ>
+__global__ void __launch_bounds__(qa_block<INT8, PROJ>(), PROJ ? (INT8 ? 3 : 1) : 4) qkv_attn_kernel(QkvAttnArgs a) {
+  constexpr int kQA = qa_block<INT8, PROJ>(), kQAW = kQA / 32;
   namespace cg = cooperative_groups;
   {  // sequence blockIdx.z of a batched step: its own residual row, state and KV slot
     const int b = blockIdx.z;
@@ -770,6 +796,7 @@ __global__ void __launch_bounds__(qa_threads<INT8>(), INT8 ? 3 : 1) qkv_attn_ker
     a.st += b;
     a.kc += (size_t)b * a.kv_slot_stride;
     a.vc += (size_t)b * a.kv_slot_stride;
+    if (!PROJ) a.qkv += (size_t)b * a.ldq;
   }
   Timeline tline;
   tline.begin(a.tl, a.tl_count, 1);
@@ -818,10 +845,10 @@ __global__ void __launch_bounds__(qa_threads<INT8>(), INT8 ? 3 : 1) qkv_attn_ker
     mbar_init(&wbar, 1);
     mbar_init(&kvbar, 1);
     fence_mbar_init();
-    mbar_expect_tx(&wbar, (uint32_t)(rpc * row_bytes));
+    if (PROJ) mbar_expect_tx(&wbar, (uint32_t)(rpc * row_bytes));
     // the CTA's rows form at most two runs (a q/k/v segment boundary may fall inside)
     int i = 0;
-    while (i < rpc) {
+    while (PROJ && i < rpc) {
       int gi = g0 + i;
       int seg_end = (gi / kHd + 1) * kHd;
       int n = min(rpc - i, seg_end - gi);
@@ -836,8 +863,10 @@ __global__ void __launch_bounds__(qa_threads<INT8>(), INT8 ? 3 : 1) qkv_attn_ker
       bulk_g2s(vsm, vb + (size_t)j0 * kHd, bytes, &kvbar);
     }
   }
-  if (INT8 && d < rpc) sws[d] = a.ws[wrow(g0 + d)];
-  for (int i = d; i < K; i += kQA) snw[i] = a.norm_w[i];
+  if (PROJ) {
+    if (INT8 && d < rpc) sws[d] = a.ws[wrow(g0 + d)];
+    for (int i = d; i < K; i += kQA) snw[i] = a.norm_w[i];
+  }
   const int dd = d & (kHd - 1);  // head dimension of threads 0..127 (the rest help in loops)
   const float qn = a.qn[dd], kn = a.kn[dd];
   const float c = a.rc[(size_t)pos * (kHd / 2) + (dd & 63)], sn = a.rs[(size_t)pos * (kHd / 2) + (dd & 63)];
@@ -845,6 +874,7 @@ __global__ void __launch_bounds__(qa_threads<INT8>(), INT8 ? 3 : 1) qkv_attn_ker
   pdl_wait();
   tline.mark(2);
 
+  if constexpr (PROJ) {
   // ---- phase 1: x -> RMSNorm -> (int8) -> this CTA's rows of q/k/v
   const uint16_t* erow = nullptr;
   if (a.embed) {
@@ -946,6 +976,7 @@ __global__ void __launch_bounds__(qa_threads<INT8>(), INT8 ? 3 : 1) qkv_attn_ker
     }
   }
   cluster.sync();  // every CTA's rows are ready
+  }
 
   // ---- phase 2: gather this head group's raw q/k/v from the cluster
   // (per-dimension work: threads 0..127, warps 0..3; the other warps wait at the barriers)
@@ -954,7 +985,12 @@ __global__ void __launch_bounds__(qa_threads<INT8>(), INT8 ? 3 : 1) qkv_attn_ker
 #pragma unroll
   for (int g = 0; g < kMaxG + 2; ++g) {
     int gi = g < G ? g * kHd + d : (g == kMaxG ? G * kHd + d : (g == kMaxG + 1 ? (G + 1) * kHd + d : -1));
-    raw[g] = hd && gi >= 0 ? *cluster.map_shared_rank(&vals[gi % rpc], gi / rpc) : 0.f;
+    if (PROJ) {
+      raw[g] = hd && gi >= 0 ? *cluster.map_shared_rank(&vals[gi % rpc], gi / rpc) : 0.f;
+    } else {  // rows of the batched projection: q heads, then k, then v
+      const int row = g < G ? (kvh * G + g) * kHd : g == kMaxG ? (a.n_heads + kvh) * kHd : (a.n_heads + a.n_kv + kvh) * kHd;
+      raw[g] = hd && gi >= 0 ? a.qkv[row + d] : 0.f;
+    }
   }
   if (hd) {
 #pragma unroll
@@ -1113,6 +1149,7 @@ __global__ void __launch_bounds__(qa_threads<INT8>(), INT8 ? 3 : 1) qkv_attn_ker
 namespace {
 constexpr int kSmemBudget = 112 * 1024;  // two decode kernels co-reside on one SM
 constexpr size_t kSmallSmemMax = 200 * 1024;
+constexpr int kAttnKvRows = 16;  // K/V rows per CTA staged before the wait (attention-only kernel)
 
 struct MvPlan {
   int grid, rows_per_cta, block_rows, nkc, stages;
@@ -1212,12 +1249,14 @@ bool small_ok(int N, int K, bool int8, int B, int num_sms) {
   return raw <= 48 && (size_t)nkc * rpc * kChunk <= 100 * 1024 && smem <= kSmallSmemMax;
 }
 
+// allow_small = false keeps the streaming kernel, whose f32 dot products accumulate each
+// lane's chunks in order before one warp reduction (the fused QKV kernel's order).
 template <int EPI>
-void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pdl = true) {
+void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pdl = true, bool allow_small = true) {
   const int row_bytes = m.K * (int8 ? 1 : 2);
   int rpc = 0, nkc = 0;
   const size_t smem_small = small_smem(m.N, m.K, int8, m.B, num_sms, &rpc, &nkc);
-  if (EPI != MV_ARGMAX && small_ok(m.N, m.K, int8, m.B, num_sms)) {
+  if (EPI != MV_ARGMAX && allow_small && small_ok(m.N, m.K, int8, m.B, num_sms)) {
     // small matrix: one stage per CTA holding the whole slab, K split across warps
     m.rows_per_cta = rpc;
     m.nkc = nkc;
@@ -1287,14 +1326,15 @@ void decode_kernels_init() {
   mv_attr<false, MV_RESID>(kMax);
   mv_attr<false, MV_SWIGLU>(kMax);
   mv_attr<false, MV_ARGMAX>(kMax);
-  for (auto k : {qkv_attn_kernel<true>, qkv_attn_kernel<false>}) {
+  for (auto k : {qkv_attn_kernel<true, true>, qkv_attn_kernel<false, true>, qkv_attn_kernel<true, false>,
+                 qkv_attn_kernel<false, false>}) {
     // its static shared memory (~22 KB) plus this stays within the 227 KB per block
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   }
 }
 
-int decode_max_batch(int hidden, int inter, int q_heads, bool int8) {
+int decode_max_batch(int hidden, int inter, int q_heads, int kv_heads, bool int8) {
   const int nsm = sm_count();
   const int qd = q_heads * kHd;
   int best = 1;
@@ -1302,6 +1342,10 @@ int decode_max_batch(int hidden, int inter, int q_heads, bool int8) {
     bool ok = true;
     // every matvec must fit either the small kernel or a streaming ring of >= 2 stages
     const int shapes[4][2] = {{hidden, qd}, {2 * inter, hidden}, {hidden, inter}, {1 << 17, hidden}};
+    // the batched q/k/v projection (int8: either kernel; bf16: the streaming kernel)
+    const int nqkv = qd + 2 * kv_heads * kHd;
+    if (!(int8 && small_ok(nqkv, hidden, true, B, nsm)) && plan_mv(nqkv, hidden, int8, B, nsm, false, false).stages == 0)
+      ok = false;
     for (int i = 0; i < 4 && ok; ++i) {
       const int N = shapes[i][0], K = shapes[i][1];
       const int raw = (N + nsm - 1) / nsm;
@@ -1355,6 +1399,22 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
     // step is a plain launch: it starts only after the previous step (which advanced
     // StepState and wrote the last KV row) has completed, so every kernel of the step may
     // read StepState and earlier KV rows before its dependency wait.
+    const int nqkv = (a.q_heads + 2 * a.kv_heads) * kHd;
+    if (B > 1) {
+      // batched steps: one matvec projects q/k/v of every sequence (input RMSNorm fused,
+      // staged in the fused kernel's summation order), then the attention-only kernel
+      MvArgs m = base(0);
+      m.x = a.x; m.ldx = a.hidden; m.st = a.st;
+      if (l == 0) {
+        m.embed = a.embed;
+        m.x_out = a.x;
+      }
+      m.norm_w = a.n1[l]; m.K = a.hidden; m.N = nqkv; m.ws = a.s_qkv[l]; m.out = a.qkv; m.ldo = nqkv;
+      m.sum_threads = a.int8 ? qa_threads<true>() : qa_threads<false>();
+      mv<MV_STORE>(a.int8, a.w_qkv[l], m, nsm, s, l != 0, a.int8);
+      if (a.on_launch) a.on_launch(a.hook_ctx, 0);
+      check("qkv_proj", l);
+    }
     {
       QkvAttnArgs q{};
       q.x = a.x;
@@ -1371,14 +1431,26 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
       q.rows_per_cta = (a.q_heads / a.kv_heads + 2) * kHd / kSplits;
       q.st = a.st; q.out = a.attn; q.err = a.err; q.tl = a.tl; q.tl_count = a.tl_count;
       q.ldx = a.hidden; q.ldo = qd; q.kv_slot_stride = a.kv_slot_stride;
-      const size_t wbytes = ((size_t)q.rows_per_cta * a.hidden * (a.int8 ? 1 : 2) + 127) & ~(size_t)127;
-      const size_t tail = (size_t)a.hidden * 5 + 16 + 64 * 4 + (size_t)a.hidden * 4;
-      const size_t budget = 200 * 1024;
-      q.kv_rows = (int)std::max<long>(0, std::min<long>(24, ((long)budget - (long)(wbytes + tail)) / (2 * kHd * 4)));
-      const size_t smem = wbytes + (size_t)q.kv_rows * kHd * 8 + tail;
       const dim3 grid(a.kv_heads, kSplits, B);
-      if (a.int8) launch_ex(qkv_attn_kernel<true>, grid, dim3(qa_threads<true>()), smem, s, l != 0, kSplits, q);
-      else launch_ex(qkv_attn_kernel<false>, grid, dim3(qa_threads<false>()), smem, s, l != 0, kSplits, q);
+      if (B > 1) {
+        q.embed = nullptr;
+        q.x_out = nullptr;
+        q.qkv = a.qkv;
+        q.ldq = nqkv;
+        q.rows_per_cta = 0;
+        q.kv_rows = kAttnKvRows;
+        const size_t smem = (size_t)q.kv_rows * kHd * 8;
+        if (a.int8) launch_ex(qkv_attn_kernel<true, false>, grid, dim3(qa_block<true, false>()), smem, s, true, kSplits, q);
+        else launch_ex(qkv_attn_kernel<false, false>, grid, dim3(qa_block<false, false>()), smem, s, true, kSplits, q);
+      } else {
+        const size_t wbytes = ((size_t)q.rows_per_cta * a.hidden * (a.int8 ? 1 : 2) + 127) & ~(size_t)127;
+        const size_t tail = (size_t)a.hidden * 5 + 16 + 64 * 4 + (size_t)a.hidden * 4;
+        const size_t budget = 200 * 1024;
+        q.kv_rows = (int)std::max<long>(0, std::min<long>(24, ((long)budget - (long)(wbytes + tail)) / (2 * kHd * 4)));
+        const size_t smem = wbytes + (size_t)q.kv_rows * kHd * 8 + tail;
+        if (a.int8) launch_ex(qkv_attn_kernel<true, true>, grid, dim3(qa_threads<true>()), smem, s, l != 0, kSplits, q);
+        else launch_ex(qkv_attn_kernel<false, true>, grid, dim3(qa_threads<false>()), smem, s, l != 0, kSplits, q);
+      }
       if (a.on_launch) a.on_launch(a.hook_ctx, 1);
       check("qkv_attn", l);
     }

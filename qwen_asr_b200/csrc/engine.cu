@@ -287,7 +287,7 @@ bool Engine::load(const std::string& dir, int device, bool trunc_quant) {
   if (!ensure_kv(4096)) return false;
   CUDA_OK(cudaMallocHost(&hstate_, kMaxSlots * sizeof(StepState)), false);
   const int mb = kDecodeMaxBatch;
-  if (!dx_.alloc((size_t)kMaxSlots * h) || !dqkv_.alloc(qd + 2 * kvd) || !dattn_.alloc((size_t)mb * qd) ||
+  if (!dx_.alloc((size_t)kMaxSlots * h) || !dqkv_.alloc((size_t)mb * (qd + 2 * kvd)) || !dattn_.alloc((size_t)mb * qd) ||
       !dffn_.alloc((size_t)mb * inter) || !dpart_.alloc((size_t)c.dec_heads * 16 * 130) ||
       !dticket_.alloc(c.dec_kv_heads) || !dam_ticket_.alloc(1) || !dam_part_.alloc((size_t)mb * 1024) ||
       !dstate_.alloc(kMaxSlots) || !dlogits_.alloc(c.vocab_size) || !derr_.alloc(1))
@@ -895,7 +895,7 @@ int Engine::max_decode_batch() {
   if (max_batch_ == 0) {
     cudaSetDevice(device_);
     const Config& c = cfg_;
-    max_batch_ = decode_max_batch(c.dec_hidden, c.dec_intermediate, c.dec_heads, mode_ == DECODE_INT8);
+    max_batch_ = decode_max_batch(c.dec_hidden, c.dec_intermediate, c.dec_heads, c.dec_kv_heads, mode_ == DECODE_INT8);
   }
   return max_batch_;
 }

@@ -129,7 +129,7 @@ struct DecodeArgs {
   int layers;
   // scratch
   float* x;        // [hidden] residual stream
-  float* qkv;      // [q_dim + 2 kv_dim]
+  float* qkv;      // [batch][q_dim + 2 kv_dim] projected q/k/v (batched steps, persistent kernel)
   float* attn;     // [q_dim]
   float* ffn;      // [inter]
   float* part;     // attention split partials
@@ -160,7 +160,7 @@ struct DecodeArgs {
 constexpr int kDecodeMaxBatch = 8;
 constexpr int kMaxSlots = 64;  // KV slots / decode states an engine can hold
 // Largest batch the decode kernels' shared memory admits for this model shape.
-int decode_max_batch(int hidden, int inter, int q_heads, bool int8);
+int decode_max_batch(int hidden, int inter, int q_heads, int kv_heads, bool int8);
 // Persistent one-launch decode step for a single sequence (decode_mega.cu). mega_create
 // returns nullptr when the device or the model shape is not supported; the state holds the
 // weight tensor maps of the decode mode of `a` (int8 or bf16).
