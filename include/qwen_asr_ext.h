@@ -55,6 +55,12 @@ int32_t qwen_asr_transcribe_segments(QwenAsrEngine* engine, const float* samples
 int32_t qwen_asr_set_decode_batch(QwenAsrEngine* engine, int32_t n);
 /* 1 (default): decode steps replay a CUDA graph; 0: plain launches. */
 void qwen_asr_set_use_graph(QwenAsrEngine* engine, int32_t on);
+/* Debug: when on, every decode keeps each sequence's f32 logits of its final step (decode
+ * runs as plain launches); switching it on or off clears what was kept. */
+void qwen_asr_set_record_logits(QwenAsrEngine* engine, int32_t on);
+/* Copies up to cap floats of the kept logits (rows of vocab_size, in decode order); returns
+ * the number kept. */
+int64_t qwen_asr_recorded_logits(QwenAsrEngine* engine, float* out, int64_t cap);
 /* Per-op decode profiler (the reference's --profile counters, kernels/mod.rs:78-168): when
  * on, decode steps run as plain launches with CUDA events around each kernel. */
 void qwen_asr_set_profile(QwenAsrEngine* engine, int32_t on);

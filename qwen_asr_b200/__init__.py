@@ -60,6 +60,8 @@ SIGNATURES = {
                                                  C.c_int32, C.POINTER(C.c_void_p)]),
     "qwen_asr_last_tokens": (C.c_int32, [_VP, C.c_int32, _I32P, C.c_int32]),
     "qwen_asr_set_profile": (None, [_VP, C.c_int32]),
+    "qwen_asr_set_record_logits": (None, [_VP, C.c_int32]),
+    "qwen_asr_recorded_logits": (C.c_int64, [_VP, C.POINTER(C.c_float), C.c_int64]),
     "qwen_asr_set_timeline": (None, [_VP, C.c_int32]),
     "qwen_asr_transcribe_device": (_VP, [_VP, C.c_void_p, C.c_int32]),
     "qwen_asr_cuda_stream": (C.c_void_p, [_VP]),
@@ -202,6 +204,18 @@ class Engine:
 
     def set_use_graph(self, on: bool):
         lib().qwen_asr_set_use_graph(self._h, int(on))
+
+    def set_record_logits(self, on: bool):
+        """Debug: keep each decoded sequence's logits of its final step (clears the store)."""
+        lib().qwen_asr_set_record_logits(self._h, int(on))
+
+    def recorded_logits(self) -> np.ndarray:
+        """The kept logits, one row of vocab_size per decoded sequence, in decode order."""
+        n = lib().qwen_asr_recorded_logits(self._h, None, 0)
+        out = np.zeros(max(n, 0), np.float32)
+        if n > 0:
+            lib().qwen_asr_recorded_logits(self._h, out.ctypes.data_as(C.POINTER(C.c_float)), n)
+        return out
 
     def set_profile(self, on: bool):
         lib().qwen_asr_set_profile(self._h, int(on))

@@ -2,6 +2,7 @@
 // names, argument meaning and error convention (NULL / -1, never an exception), plus
 // the clearly separated extensions declared in include/qwen_asr_ext.h.
 #include <cstdlib>
+#include <algorithm>
 #include <cstring>
 #include <fstream>
 #include <mutex>
@@ -251,6 +252,19 @@ int32_t qwen_asr_set_decode_batch(QwenAsrEngine* e, int32_t n) {
 }
 void qwen_asr_set_use_graph(QwenAsrEngine* e, int32_t on) {
   if (e) e->ctx.eng.use_graph = on != 0;
+}
+
+void qwen_asr_set_record_logits(QwenAsrEngine* e, int32_t on) {
+  if (!e) return;
+  e->ctx.eng.record_logits = on != 0;
+  e->ctx.eng.recorded_logits.clear();
+}
+
+int64_t qwen_asr_recorded_logits(QwenAsrEngine* e, float* out, int64_t cap) {
+  if (!e) return -1;
+  const auto& r = e->ctx.eng.recorded_logits;
+  if (out) memcpy(out, r.data(), std::min<size_t>(r.size(), cap > 0 ? (size_t)cap : 0) * 4);
+  return (int64_t)r.size();
 }
 
 void qwen_asr_set_profile(QwenAsrEngine* e, int32_t on) {

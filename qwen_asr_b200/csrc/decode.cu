@@ -30,10 +30,6 @@ constexpr int kMaxG = 4;     // q heads per kv head
 // under programmatic dependent launch) off the SM.
 template <bool INT8>
 constexpr int qa_threads() { return INT8 ? 256 : 128; }
-// The attention-only variant (batched steps, q/k/v projected by a batched matvec) needs
-// one thread per head dimension.
-template <bool INT8, bool PROJ>
-constexpr int qa_block() { return PROJ ? qa_threads<INT8>() : 128; }
 
 enum MvEpi { MV_STORE = 0, MV_RESID = 1, MV_SWIGLU = 2, MV_ARGMAX = 3 };
 
@@ -785,8 +781,12 @@ struct QkvAttnArgs {
 };
 
 template <bool INT8, bool PROJ>
-__global__ void __launch_bounds__(qa_block<INT8, PROJ>(), PROJ ? (INT8 ? 3 : 1) : 4) qkv_attn_kernel(QkvAttnArgs a) {
-  constexpr int kQA = qa_block<INT8, PROJ>(), kQAW = kQA / 32;
+__global__ void __launch_bounds__(PROJ ? qa_threads<INT8>() : 128, PROJ ? (INT8 ? 3 : 1) : 4)
+qkv_attn_kernel(QkvAttnArgs a) {
+  // The attention loop splits a CTA's positions over kVW virtual warps (the fused kernel's
+  // warp count, which fixes the summation order); the attention-only variant runs them on
+  // 4 warps, virtual warps w and w + 4 one after the other.
+  constexpr int kQA = PROJ ? qa_threads<INT8>() : 128, kQAW = kQA / 32, kVW = qa_threads<INT8>() / 32;
   namespace cg = cooperative_groups;
   {  // sequence blockIdx.z of a batched step: its own residual row, state and KV slot
     const int b = blockIdx.z;
@@ -806,8 +806,8 @@ __global__ void __launch_bounds__(qa_block<INT8, PROJ>(), PROJ ? (INT8 ? 3 : 1) 
   __shared__ float vals[64];                          // this CTA's projected rows
   __shared__ __align__(16) float hv[kMaxG + 2][kHd];  // normalised q heads, k, v of `pos`
   __shared__ float red[4][kMaxG + 1];
-  __shared__ float wm[kQAW][kMaxG], wl[kQAW][kMaxG];
-  __shared__ __align__(16) float wo[kQAW][kMaxG][kHd];
+  __shared__ float wm[kVW][kMaxG], wl[kVW][kMaxG];
+  __shared__ __align__(16) float wo[kVW][kMaxG][kHd];
   __shared__ float pm[kMaxG], pl[kMaxG];
   __shared__ __align__(16) float po[kMaxG][kHd];
   cg::cluster_group cluster = cg::this_cluster();
@@ -1038,72 +1038,74 @@ __global__ void __launch_bounds__(qa_block<INT8, PROJ>(), PROJ ? (INT8 ? 3 : 1) 
   if (npre > 0) mbar_wait(&kvbar, 0, a.err, 3);
   const float* ks = hv[kMaxG];
   const float* vs = hv[kMaxG + 1];
-  float m[kMaxG], l[kMaxG], o[kMaxG][4];
+  for (int vw = warp; vw < kVW; vw += kQAW) {
+    float m[kMaxG], l[kMaxG], o[kMaxG][4];
 #pragma unroll
-  for (int g = 0; g < kMaxG; ++g) {
-    m[g] = -3.0e38f;
-    l[g] = 0.f;
-    o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
-  }
-  for (int jb = j0 + warp * 4; jb < j1; jb += 4 * kQAW) {
-    float4 kv[4], vv[4];
+    for (int g = 0; g < kMaxG; ++g) {
+      m[g] = -3.0e38f;
+      l[g] = 0.f;
+      o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+    }
+    for (int jb = j0 + vw * 4; jb < j1; jb += 4 * kVW) {
+      float4 kv[4], vv[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int j = jb + u;
-      if (j < j1 && j != pos) {
-        if (j - j0 < npre) {
-          kv[u] = reinterpret_cast<const float4*>(ksm + (size_t)(j - j0) * kHd)[lane];
-          vv[u] = reinterpret_cast<const float4*>(vsm + (size_t)(j - j0) * kHd)[lane];
+      for (int u = 0; u < 4; ++u) {
+        const int j = jb + u;
+        if (j < j1 && j != pos) {
+          if (j - j0 < npre) {
+            kv[u] = reinterpret_cast<const float4*>(ksm + (size_t)(j - j0) * kHd)[lane];
+            vv[u] = reinterpret_cast<const float4*>(vsm + (size_t)(j - j0) * kHd)[lane];
+          } else {
+            kv[u] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)j * kHd) + lane);
+            vv[u] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)j * kHd) + lane);
+          }
         } else {
-          kv[u] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)j * kHd) + lane);
-          vv[u] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)j * kHd) + lane);
+          kv[u] = *reinterpret_cast<const float4*>(&ks[lane * 4]);
+          vv[u] = *reinterpret_cast<const float4*>(&vs[lane * 4]);
         }
-      } else {
-        kv[u] = *reinterpret_cast<const float4*>(&ks[lane * 4]);
-        vv[u] = *reinterpret_cast<const float4*>(&vs[lane * 4]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (jb + u >= j1) break;
+#pragma unroll
+        for (int g = 0; g < kMaxG; ++g) {
+          if (g >= G) break;
+          float4 q = *reinterpret_cast<const float4*>(&hv[g][lane * 4]);
+          float p = q.x * kv[u].x;
+          p = fmaf(q.y, kv[u].y, p);
+          p = fmaf(q.z, kv[u].z, p);
+          p = fmaf(q.w, kv[u].w, p);
+          float sc = __fmul_rn(warp_sum(p), a.scale);
+          float mn = fmaxf(m[g], sc);
+          float corr = expf(__fsub_rn(m[g], mn));
+          float e = expf(__fsub_rn(sc, mn));
+          l[g] = fmaf(l[g], corr, e);
+          o[g][0] = fmaf(o[g][0], corr, e * vv[u].x);
+          o[g][1] = fmaf(o[g][1], corr, e * vv[u].y);
+          o[g][2] = fmaf(o[g][2], corr, e * vv[u].z);
+          o[g][3] = fmaf(o[g][3], corr, e * vv[u].w);
+          m[g] = mn;
+        }
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (jb + u >= j1) break;
-#pragma unroll
-      for (int g = 0; g < kMaxG; ++g) {
-        if (g >= G) break;
-        float4 q = *reinterpret_cast<const float4*>(&hv[g][lane * 4]);
-        float p = q.x * kv[u].x;
-        p = fmaf(q.y, kv[u].y, p);
-        p = fmaf(q.z, kv[u].z, p);
-        p = fmaf(q.w, kv[u].w, p);
-        float sc = __fmul_rn(warp_sum(p), a.scale);
-        float mn = fmaxf(m[g], sc);
-        float corr = expf(__fsub_rn(m[g], mn));
-        float e = expf(__fsub_rn(sc, mn));
-        l[g] = fmaf(l[g], corr, e);
-        o[g][0] = fmaf(o[g][0], corr, e * vv[u].x);
-        o[g][1] = fmaf(o[g][1], corr, e * vv[u].y);
-        o[g][2] = fmaf(o[g][2], corr, e * vv[u].z);
-        o[g][3] = fmaf(o[g][3], corr, e * vv[u].w);
-        m[g] = mn;
+    for (int g = 0; g < kMaxG; ++g) {
+      if (g >= G) break;
+      if (lane == 0) {
+        wm[vw][g] = m[g];
+        wl[vw][g] = l[g];
       }
+      *reinterpret_cast<float4*>(&wo[vw][g][lane * 4]) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
     }
-  }
-#pragma unroll
-  for (int g = 0; g < kMaxG; ++g) {
-    if (g >= G) break;
-    if (lane == 0) {
-      wm[warp][g] = m[g];
-      wl[warp][g] = l[g];
-    }
-    *reinterpret_cast<float4*>(&wo[warp][g][lane * 4]) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
   }
   __syncthreads();
   for (int g = 0; g < G && hd; ++g) {
     float M = wm[0][g];
 #pragma unroll
-    for (int w = 1; w < kQAW; ++w) M = fmaxf(M, wm[w][g]);
+    for (int w = 1; w < kVW; ++w) M = fmaxf(M, wm[w][g]);
     float L = 0.f, O = 0.f;
 #pragma unroll
-    for (int w = 0; w < kQAW; ++w) {
+    for (int w = 0; w < kVW; ++w) {
       float f = wl[w][g] > 0.f ? expf(__fsub_rn(wm[w][g], M)) : 0.f;
       L = fmaf(wl[w][g], f, L);
       O = fmaf(wo[w][g][d], f, O);
@@ -1440,8 +1442,8 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
         q.rows_per_cta = 0;
         q.kv_rows = kAttnKvRows;
         const size_t smem = (size_t)q.kv_rows * kHd * 8;
-        if (a.int8) launch_ex(qkv_attn_kernel<true, false>, grid, dim3(qa_block<true, false>()), smem, s, true, kSplits, q);
-        else launch_ex(qkv_attn_kernel<false, false>, grid, dim3(qa_block<false, false>()), smem, s, true, kSplits, q);
+        if (a.int8) launch_ex(qkv_attn_kernel<true, false>, grid, dim3(128), smem, s, true, kSplits, q);
+        else launch_ex(qkv_attn_kernel<false, false>, grid, dim3(128), smem, s, true, kSplits, q);
       } else {
         const size_t wbytes = ((size_t)q.rows_per_cta * a.hidden * (a.int8 ? 1 : 2) + 127) & ~(size_t)127;
         const size_t tail = (size_t)a.hidden * 5 + 16 + 64 * 4 + (size_t)a.hidden * 4;

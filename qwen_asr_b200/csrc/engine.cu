@@ -674,7 +674,8 @@ void Engine::enqueue_step(const DecodeArgs& a) {
   decode_step(a, stream_);
 }
 
-int Engine::decode_step_launches_1() const { return 5 * cfg_.dec_layers + 1; }
+// qkv+attention, o, gate/up, down per layer, then lm_head (batched steps add a q/k/v matvec)
+int Engine::decode_step_launches_1() const { return 4 * cfg_.dec_layers + 1; }
 
 bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, const std::vector<int>* forced,
                     std::vector<float>* logits, int slot) {
@@ -698,6 +699,8 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     if (!dtl_count_.alloc(1)) return false;
     CUDA_OK(cudaMemsetAsync(dtl_count_.p, 0, sizeof(int), stream_), false);
   }
+  std::vector<float> rec;
+  if (record_logits && !logits) logits = &rec;
   cudaEventRecord(ev0_, stream_);
   const bool direct = forced || logits || !use_graph || profile;
   if (direct) {
@@ -739,6 +742,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     CUDA_OK(cudaStreamSynchronize(stream_), false);
     CUDA_OK(cudaGetLastError(), false);
     out.assign(htokens_, htokens_ + max_steps);
+    if (record_logits) recorded_logits.insert(recorded_logits.end(), logits->end() - V, logits->end());
     launches += (long)max_steps * (mega ? 1 : decode_step_launches_1());
     for (size_t i = 1; i < prof_ev_.size(); ++i) {
       int k = prof_ev_[i].first;
@@ -922,7 +926,10 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
     CUDA_OK(cudaMemsetAsync(dtl_count_.p, 0, sizeof(int), stream_), false);
   }
   cudaGraphExec_t run_graph = nullptr;
-  if (use_graph && first_slot == 0) {
+  if (record_logits) {
+    // plain launches writing every sequence's logits at each step; the last step's are kept
+    if (!drec_.alloc((size_t)B * cfg_.vocab_size)) return false;
+  } else if (use_graph && first_slot == 0) {
     if (!graph_for(B)) return false;
     run_graph = graph_exec_[B];
   } else if (use_graph) {
@@ -943,7 +950,7 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
     }
     run_graph = entry.first;
   }
-  DecodeArgs direct_args = dargs(nullptr, nullptr, first_slot);
+  DecodeArgs direct_args = dargs(nullptr, record_logits ? drec_.p : nullptr, first_slot);
   direct_args.batch = B;
   cudaEventRecord(ev0_, stream_);
   // Chunks of steps; after each chunk the ids of every sequence come back (one 2-D copy)
@@ -1003,7 +1010,7 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
     return false;
   }
   CUDA_OK(cudaGetLastError(), false);
-  launches += (long)launched * (5 * cfg_.dec_layers + 1);
+  launches += (long)launched * (decode_step_launches_1() + (B > 1 ? cfg_.dec_layers : 0));
   int herr = 0;
   CUDA_OK(cudaMemcpy(&herr, derr_.p, sizeof(int), cudaMemcpyDeviceToHost), false);
   if (herr) {
@@ -1024,6 +1031,12 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
     longest = std::max(longest, out[b].size());
   }
   if (first_slot == 0) kv_len_ = hstate_[0].pos;
+  if (record_logits) {
+    const size_t n = (size_t)B * cfg_.vocab_size;
+    recorded_logits.resize(recorded_logits.size() + n);
+    CUDA_OK(cudaMemcpy(recorded_logits.data() + recorded_logits.size() - n, drec_.p, n * 4, cudaMemcpyDeviceToHost),
+            false);
+  }
   cudaEventRecord(ev1_, stream_);
   cudaEventSynchronize(ev1_);
   float ms = 0;

@@ -104,6 +104,10 @@ class Engine {
   long launches = 0;  // kernels enqueued by this engine (graph replays count their nodes)
   // Per-op decode profiler (CUDA events around every launch; disables the graph).
   bool profile = false;
+  // Debug: every decode keeps each sequence's f32 logits of its last step here (plain
+  // launches instead of graphs), so batched and single-sequence decodes can be compared.
+  bool record_logits = false;
+  std::vector<float> recorded_logits;
   double prof_ms[6] = {0, 0, 0, 0, 0, 0};
   long prof_n[6] = {0, 0, 0, 0, 0, 0};
   std::vector<std::pair<int, cudaEvent_t>> prof_ev_;
@@ -159,7 +163,7 @@ class Engine {
   bool ensure_slots(int n);
   size_t kv_slot_stride() const { return (size_t)cfg_.dec_layers * cfg_.dec_kv_heads * max_seq_ * 128; }
   // decode scratch
-  DevBuf<float> dx_, dqkv_, dattn_, dffn_, dpart_, dlogits_;
+  DevBuf<float> dx_, dqkv_, dattn_, dffn_, dpart_, dlogits_, drec_;
   DevBuf<int> dticket_, dam_ticket_, dtokens_, dforced_, derr_;
   DevBuf<unsigned long long> dam_part_;
   DevBuf<StepState> dstate_;

@@ -44,6 +44,32 @@ def test_batched_segments_match_sequential_06b(Q, m06_dir, mode):
     assert tb == t1
 
 
+@pytest.mark.parametrize("preset", ["tiny", "06b"])
+@pytest.mark.parametrize("mode", ["int8", "bf16"])
+def test_batched_logits_bit_identical(Q, tiny_dir, m06_dir, preset, mode):
+    """The final-step logits of every segment are bit-equal between one-at-a-time decoding
+    and batched decoding (token equality alone would hide a changed summation order). The
+    segments are long enough (> 256 positions) that every warp of every attention split
+    holds positions."""
+    d = tiny_dir if preset == "tiny" else m06_dir
+    x = synth.synth_audio(16000 * 80, seed=73)
+    kept = []
+    for batch in (1, 0):
+        eng = Q.Engine(d)
+        eng.set_decode_mode(mode)
+        eng.set_language("English")
+        eng.set_segment_sec(26.0)
+        eng.set_force_n_tokens(12)
+        used = eng.set_decode_batch(batch)
+        eng.set_record_logits(True)
+        eng.transcribe_pcm(x)
+        kept.append((eng.recorded_logits(), used))
+    (a, _), (b, ub) = kept
+    assert ub >= 2
+    assert a.size > 0 and a.shape == b.shape
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
 @pytest.fixture(scope="module")
 def Q():
     import qwen_asr_b200 as Q
