@@ -780,8 +780,8 @@ struct QkvAttnArgs {
   int ldq;
 };
 
-template <bool INT8, bool PROJ>
-__global__ void __launch_bounds__(PROJ ? qa_threads<INT8>() : 128, PROJ ? (INT8 ? 3 : 1) : 4)
+template <bool INT8, bool PROJ, int MG>
+__global__ void __launch_bounds__(PROJ ? qa_threads<INT8>() : 128, PROJ ? (INT8 ? 3 : 1) : 6)
 qkv_attn_kernel(QkvAttnArgs a) {
   // The attention loop splits a CTA's positions over kVW virtual warps (the fused kernel's
   // warp count, which fixes the summation order); the attention-only variant runs them on
@@ -804,12 +804,12 @@ qkv_attn_kernel(QkvAttnArgs a) {
   __shared__ __align__(8) uint64_t wbar, kvbar;
   __shared__ float red32[32];
   __shared__ float vals[64];                          // this CTA's projected rows
-  __shared__ __align__(16) float hv[kMaxG + 2][kHd];  // normalised q heads, k, v of `pos`
-  __shared__ float red[4][kMaxG + 1];
-  __shared__ float wm[kVW][kMaxG], wl[kVW][kMaxG];
-  __shared__ __align__(16) float wo[kVW][kMaxG][kHd];
-  __shared__ float pm[kMaxG], pl[kMaxG];
-  __shared__ __align__(16) float po[kMaxG][kHd];
+  __shared__ __align__(16) float hv[MG + 2][kHd];  // normalised q heads, k, v of `pos`
+  __shared__ float red[4][MG + 1];
+  __shared__ float wm[kVW][MG], wl[kVW][MG];
+  __shared__ __align__(16) float wo[kVW][MG][kHd];
+  __shared__ float pm[MG], pl[MG];
+  __shared__ __align__(16) float po[MG][kHd];
   cg::cluster_group cluster = cg::this_cluster();
   const int kvh = blockIdx.x, rank = blockIdx.y, d = threadIdx.x;
   const int warp = d >> 5, lane = d & 31;
@@ -981,44 +981,44 @@ qkv_attn_kernel(QkvAttnArgs a) {
   // ---- phase 2: gather this head group's raw q/k/v from the cluster
   // (per-dimension work: threads 0..127, warps 0..3; the other warps wait at the barriers)
   const bool hd = d < kHd;
-  float raw[kMaxG + 2];
+  float raw[MG + 2];
 #pragma unroll
-  for (int g = 0; g < kMaxG + 2; ++g) {
-    int gi = g < G ? g * kHd + d : (g == kMaxG ? G * kHd + d : (g == kMaxG + 1 ? (G + 1) * kHd + d : -1));
+  for (int g = 0; g < MG + 2; ++g) {
+    int gi = g < G ? g * kHd + d : (g == MG ? G * kHd + d : (g == MG + 1 ? (G + 1) * kHd + d : -1));
     if (PROJ) {
       raw[g] = hd && gi >= 0 ? *cluster.map_shared_rank(&vals[gi % rpc], gi / rpc) : 0.f;
     } else {  // rows of the batched projection: q heads, then k, then v
-      const int row = g < G ? (kvh * G + g) * kHd : g == kMaxG ? (a.n_heads + kvh) * kHd : (a.n_heads + a.n_kv + kvh) * kHd;
+      const int row = g < G ? (kvh * G + g) * kHd : g == MG ? (a.n_heads + kvh) * kHd : (a.n_heads + a.n_kv + kvh) * kHd;
       raw[g] = hd && gi >= 0 ? a.qkv[row + d] : 0.f;
     }
   }
   if (hd) {
 #pragma unroll
-    for (int g = 0; g <= kMaxG; ++g) {
+    for (int g = 0; g <= MG; ++g) {
       float v = raw[g];
       float s2 = warp_sum(v * v);
-      if (lane == 0 && (g < G || g == kMaxG)) red[warp][g < G ? g : G] = s2;
+      if (lane == 0 && (g < G || g == MG)) red[warp][g < G ? g : G] = s2;
     }
   }
   __syncthreads();
-  float nv[kMaxG + 1];
+  float nv[MG + 1];
 #pragma unroll
-  for (int g = 0; g <= kMaxG; ++g) {
-    if (hd && (g < G || g == kMaxG)) {
+  for (int g = 0; g <= MG; ++g) {
+    if (hd && (g < G || g == MG)) {
       int r = g < G ? g : G;
       float tot = red[0][r] + red[1][r] + red[2][r] + red[3][r];
       float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)kHd), a.eps)));
       nv[g] = __fmul_rn(__fmul_rn(raw[g], inv), g < G ? qn : kn);
-      hv[g < G ? g : kMaxG][d] = nv[g];
+      hv[g < G ? g : MG][d] = nv[g];
     }
   }
   __syncthreads();
   // NeoX rotation (generic path, kernels/mod.rs:1780-1788): pairs (d, d + 64).
-  float rot[kMaxG + 1];
+  float rot[MG + 1];
 #pragma unroll
-  for (int g = 0; g <= kMaxG; ++g) {
-    if (hd && (g < G || g == kMaxG)) {
-      int h = g < G ? g : kMaxG;
+  for (int g = 0; g <= MG; ++g) {
+    if (hd && (g < G || g == MG)) {
+      int h = g < G ? g : MG;
       if (d < kHd / 2) rot[g] = __fadd_rn(__fmul_rn(nv[g], c), __fmul_rn(-hv[h][d + kHd / 2], sn));
       else rot[g] = __fadd_rn(__fmul_rn(nv[g], c), __fmul_rn(hv[h][d - kHd / 2], sn));
     }
@@ -1026,22 +1026,22 @@ qkv_attn_kernel(QkvAttnArgs a) {
   __syncthreads();
   if (hd) {
 #pragma unroll
-    for (int g = 0; g <= kMaxG; ++g)
-      if (g < G || g == kMaxG) hv[g < G ? g : kMaxG][d] = rot[g];
-    hv[kMaxG + 1][d] = raw[kMaxG + 1];
+    for (int g = 0; g <= MG; ++g)
+      if (g < G || g == MG) hv[g < G ? g : MG][d] = rot[g];
+    hv[MG + 1][d] = raw[MG + 1];
   }
   if (hd && rank == 0) {
-    kb[(size_t)pos * kHd + d] = rot[kMaxG];
-    vb[(size_t)pos * kHd + d] = raw[kMaxG + 1];
+    kb[(size_t)pos * kHd + d] = rot[MG];
+    vb[(size_t)pos * kHd + d] = raw[MG + 1];
   }
   __syncthreads();
   if (npre > 0) mbar_wait(&kvbar, 0, a.err, 3);
-  const float* ks = hv[kMaxG];
-  const float* vs = hv[kMaxG + 1];
+  const float* ks = hv[MG];
+  const float* vs = hv[MG + 1];
   for (int vw = warp; vw < kVW; vw += kQAW) {
-    float m[kMaxG], l[kMaxG], o[kMaxG][4];
+    float m[MG], l[MG], o[MG][4];
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g) {
+    for (int g = 0; g < MG; ++g) {
       m[g] = -3.0e38f;
       l[g] = 0.f;
       o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
@@ -1068,7 +1068,7 @@ qkv_attn_kernel(QkvAttnArgs a) {
       for (int u = 0; u < 4; ++u) {
         if (jb + u >= j1) break;
 #pragma unroll
-        for (int g = 0; g < kMaxG; ++g) {
+        for (int g = 0; g < MG; ++g) {
           if (g >= G) break;
           float4 q = *reinterpret_cast<const float4*>(&hv[g][lane * 4]);
           float p = q.x * kv[u].x;
@@ -1089,7 +1089,7 @@ qkv_attn_kernel(QkvAttnArgs a) {
       }
     }
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g) {
+    for (int g = 0; g < MG; ++g) {
       if (g >= G) break;
       if (lane == 0) {
         wm[vw][g] = m[g];
@@ -1328,8 +1328,10 @@ void decode_kernels_init() {
   mv_attr<false, MV_RESID>(kMax);
   mv_attr<false, MV_SWIGLU>(kMax);
   mv_attr<false, MV_ARGMAX>(kMax);
-  for (auto k : {qkv_attn_kernel<true, true>, qkv_attn_kernel<false, true>, qkv_attn_kernel<true, false>,
-                 qkv_attn_kernel<false, false>}) {
+  for (auto k : {qkv_attn_kernel<true, true, 2>, qkv_attn_kernel<false, true, 2>, qkv_attn_kernel<true, false, 2>,
+                 qkv_attn_kernel<false, false, 2>, qkv_attn_kernel<true, true, kMaxG>,
+                 qkv_attn_kernel<false, true, kMaxG>, qkv_attn_kernel<true, false, kMaxG>,
+                 qkv_attn_kernel<false, false, kMaxG>}) {
     // its static shared memory (~22 KB) plus this stays within the 227 KB per block
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -1434,6 +1436,7 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
       q.st = a.st; q.out = a.attn; q.err = a.err; q.tl = a.tl; q.tl_count = a.tl_count;
       q.ldx = a.hidden; q.ldo = qd; q.kv_slot_stride = a.kv_slot_stride;
       const dim3 grid(a.kv_heads, kSplits, B);
+      const bool g2 = a.q_heads <= 2 * a.kv_heads;  // group arrays sized for 2 q heads
       if (B > 1) {
         q.embed = nullptr;
         q.x_out = nullptr;
@@ -1442,16 +1445,28 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
         q.rows_per_cta = 0;
         q.kv_rows = kAttnKvRows;
         const size_t smem = (size_t)q.kv_rows * kHd * 8;
-        if (a.int8) launch_ex(qkv_attn_kernel<true, false>, grid, dim3(128), smem, s, true, kSplits, q);
-        else launch_ex(qkv_attn_kernel<false, false>, grid, dim3(128), smem, s, true, kSplits, q);
+        const dim3 t(128);
+        if (g2) {
+          if (a.int8) launch_ex(qkv_attn_kernel<true, false, 2>, grid, t, smem, s, true, kSplits, q);
+          else launch_ex(qkv_attn_kernel<false, false, 2>, grid, t, smem, s, true, kSplits, q);
+        } else {
+          if (a.int8) launch_ex(qkv_attn_kernel<true, false, kMaxG>, grid, t, smem, s, true, kSplits, q);
+          else launch_ex(qkv_attn_kernel<false, false, kMaxG>, grid, t, smem, s, true, kSplits, q);
+        }
       } else {
         const size_t wbytes = ((size_t)q.rows_per_cta * a.hidden * (a.int8 ? 1 : 2) + 127) & ~(size_t)127;
         const size_t tail = (size_t)a.hidden * 5 + 16 + 64 * 4 + (size_t)a.hidden * 4;
         const size_t budget = 200 * 1024;
         q.kv_rows = (int)std::max<long>(0, std::min<long>(24, ((long)budget - (long)(wbytes + tail)) / (2 * kHd * 4)));
         const size_t smem = wbytes + (size_t)q.kv_rows * kHd * 8 + tail;
-        if (a.int8) launch_ex(qkv_attn_kernel<true, true>, grid, dim3(qa_threads<true>()), smem, s, l != 0, kSplits, q);
-        else launch_ex(qkv_attn_kernel<false, true>, grid, dim3(qa_threads<false>()), smem, s, l != 0, kSplits, q);
+        const bool p = l != 0;
+        if (g2) {
+          if (a.int8) launch_ex(qkv_attn_kernel<true, true, 2>, grid, dim3(qa_threads<true>()), smem, s, p, kSplits, q);
+          else launch_ex(qkv_attn_kernel<false, true, 2>, grid, dim3(qa_threads<false>()), smem, s, p, kSplits, q);
+        } else {
+          if (a.int8) launch_ex(qkv_attn_kernel<true, true, kMaxG>, grid, dim3(qa_threads<true>()), smem, s, p, kSplits, q);
+          else launch_ex(qkv_attn_kernel<false, true, kMaxG>, grid, dim3(qa_threads<false>()), smem, s, p, kSplits, q);
+        }
       }
       if (a.on_launch) a.on_launch(a.hook_ctx, 1);
       check("qkv_attn", l);
