@@ -537,6 +537,101 @@ bool Engine::prefill_ids(const std::vector<int>& ids, const float* d_enc, int st
   return run_prefill(n, start_pos, slot);
 }
 
+bool Engine::prefill_many(const std::vector<PrefillJob>& jobs, const float* d_enc) {
+  cudaSetDevice(device_);
+  const Config& c = cfg_;
+  const int h = c.dec_hidden, qd = c.dec_heads * 128, kvd = c.dec_kv_heads * 128, inter = c.dec_intermediate;
+  const int J = (int)jobs.size();
+  if (J == 0) return true;
+  // packed rows: every job's rows [start_pos, n - 1), then every job's last row
+  std::vector<int> packed, off(J + 1, 0);
+  int max_n = 0, max_slot = 0;
+  for (int j = 0; j < J; ++j) {
+    const auto& ids = *jobs[j].ids;
+    const int n = (int)ids.size(), s0 = jobs[j].start_pos;
+    if (n < 1 || s0 < 0 || s0 > n - 1 || jobs[j].slot < 0 || jobs[j].slot >= kMaxSlots) {
+      set_error("prefill_many: job " + std::to_string(j) + " has no rows to prefill or a bad slot");
+      return false;
+    }
+    packed.insert(packed.end(), ids.begin() + s0, ids.end() - 1);
+    off[j + 1] = (int)packed.size();
+    max_n = std::max(max_n, n);
+    max_slot = std::max(max_slot, jobs[j].slot);
+  }
+  const int R = (int)packed.size();
+  for (int j = 0; j < J; ++j) packed.push_back(jobs[j].ids->back());
+  if (!ensure_slots(max_slot + 1) || !ensure_kv(max_n + 1024)) return false;
+  if (!ids_.alloc(packed.size()) || !px_.alloc(packed.size() * h) || !pxn_.alloc((size_t)std::max(R, 1) * h) ||
+      !pqkv_.alloc((size_t)std::max(R, 1) * (qd + 2 * kvd)) || !patt_.alloc((size_t)std::max(R, 1) * qd) ||
+      !pmid_.alloc((size_t)std::max(R, 1) * inter))
+    return false;
+  CUDA_OK(cudaMemcpyAsync(ids_.p, packed.data(), packed.size() * 4, cudaMemcpyHostToDevice, stream_), false);
+  cudaEventRecord(ev0_, stream_);
+  gather_embeds(ids_.p, (int)packed.size(), embed_, d_enc, h, px_.p, stream_);
+  launches += 1;
+  float* x = px_.p;
+  const float scale = 1.0f / sqrtf(128.f);
+  const int ldq = qd + 2 * kvd;
+  for (int l = 0; l < c.dec_layers && R > 0; ++l) {
+    const DecLayerW& L = dec_layers_[l];
+    rms_norm_rows(x, pxn_.p, R, h, L.n1, c.dec_rms_norm_eps, stream_);
+    GemmArgs a;
+    a.M = R; a.N = ldq; a.K = h; a.A = pxn_.p; a.lda = h; a.B = L.wqkv; a.ldb = h;
+    a.C = pqkv_.p; a.ldc = ldq;
+    gemm(a, stream_);
+    for (int j = 0; j < J; ++j) {
+      const int S = off[j + 1] - off[j];
+      if (S == 0) continue;
+      const size_t slot_off = (size_t)jobs[j].slot * kv_slot_stride() + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
+      float* qkv = pqkv_.p + (size_t)off[j] * ldq;
+      prefill_qk_rope_kv(qkv, S, jobs[j].start_pos, c.dec_heads, c.dec_kv_heads, L.qn, L.kn, c.dec_rms_norm_eps,
+                         rope_cos_, rope_sin_, kc_.p + slot_off, vc_.p + slot_off, max_seq_, stream_);
+      prefill_attention(qkv, S, jobs[j].start_pos, c.dec_heads, c.dec_kv_heads, kc_.p + slot_off, vc_.p + slot_off,
+                        max_seq_, scale, patt_.p + (size_t)off[j] * qd, stream_);
+      launches += 2;
+    }
+    GemmArgs o;
+    o.M = R; o.N = h; o.K = qd; o.A = patt_.p; o.lda = qd; o.B = L.wo; o.ldb = qd;
+    o.C = x; o.ldc = h; o.epi = EPI_RESID; o.resid = x; o.ldr = h;
+    gemm(o, stream_);
+    rms_norm_rows(x, pxn_.p, R, h, L.n2, c.dec_rms_norm_eps, stream_);
+    GemmArgs g;
+    g.M = R; g.N = 2 * inter; g.K = h; g.A = pxn_.p; g.lda = h; g.B = L.wgu; g.ldb = h;
+    g.C = pmid_.p; g.ldc = inter; g.epi = EPI_SWIGLU;
+    gemm(g, stream_);
+    GemmArgs dn;
+    dn.M = R; dn.N = h; dn.K = inter; dn.A = pmid_.p; dn.lda = inter; dn.B = L.wdown; dn.ldb = inter;
+    dn.C = x; dn.ldc = h; dn.epi = EPI_RESID; dn.resid = x; dn.ldr = h;
+    gemm(dn, stream_);
+    launches += 6;
+  }
+  // each job's first decode input is its last prompt row (transcribe.rs:171-185)
+  for (int j = 0; j < J; ++j) {
+    const int slot = jobs[j].slot, n = (int)jobs[j].ids->size();
+    CUDA_OK(cudaMemcpyAsync(dx_.p + (size_t)slot * h, px_.p + (size_t)(R + j) * h, (size_t)h * 4,
+                            cudaMemcpyDeviceToDevice, stream_),
+            false);
+    StepState* hs = hstate_ + slot;
+    hs->pos = n - 1;
+    hs->step = 0;
+    hs->cur_token = -1;
+    hs->forced_mode = 0;
+    CUDA_OK(cudaMemcpyAsync(dstate_.p + slot, hs, sizeof(StepState), cudaMemcpyHostToDevice, stream_), false);
+    if (slot == 0) kv_len_ = n - 1;
+  }
+  cudaEventRecord(ev1_, stream_);
+  CUDA_OK(cudaEventSynchronize(ev1_), false);
+  float ms = 0;
+  cudaEventElapsedTime(&ms, ev0_, ev1_);
+  perf.prefill_ms += ms;
+  if (int e = gemm_tc_error()) {
+    set_error("tensor-core GEMM: a device-side wait timed out (code " + std::to_string(e) + ")");
+    return false;
+  }
+  CUDA_OK(cudaGetLastError(), false);
+  return true;
+}
+
 bool Engine::prefill_rows(const float* rows, int n, int start_pos, int slot) {
   cudaSetDevice(device_);
   const int h = cfg_.dec_hidden;

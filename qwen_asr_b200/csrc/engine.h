@@ -68,6 +68,17 @@ class Engine {
   bool prefill_ids(const std::vector<int>& ids, const float* d_enc, int start_pos, int slot = 0);
   // Same with prompt embeddings already materialised on the host (streaming LCP path).
   bool prefill_rows(const float* h_rows, int n_rows, int start_pos, int slot = 0);
+  // Several sequences' prefills in one pass: the rows every job recomputes are packed into
+  // one matrix, so each GEMM reads the weights once for all of them; RoPE, the KV append and
+  // attention run per job on its rows and slot. Each job is prefill_ids(ids, d_enc,
+  // start_pos, slot) with its encoder rows inside the shared `d_enc`; per-row results equal
+  // the single-job call's bit for bit (the GEMM tiles do not depend on the row count).
+  struct PrefillJob {
+    const std::vector<int>* ids;
+    int start_pos;
+    int slot;
+  };
+  bool prefill_many(const std::vector<PrefillJob>& jobs, const float* d_enc);
   // Greedy decode: runs up to max_steps decoder_forward steps from the prepared state and
   // returns the produced ids. With stop_on_eos the loop stops after the first
   // 151643/151645 (inclusive). forced (teacher forcing) gives the input id of step i+1.

@@ -318,9 +318,11 @@ static std::pair<size_t, size_t> tail_repeat_blocks(const std::vector<int>& t, s
 // stream_push_audio (transcribe.rs:902-1304). `samples` is the full audio so far.
 // One chunk of stream_push_audio's loop (transcribe.rs:944-1304), split so that several
 // streams can share one batched decode: stream_chunk_prepare does the window encodes, the
-// prompt assembly, the LCP reuse and the prefill into the stream's KV slot; the caller
-// decodes max_new tokens in that slot; stream_chunk_finish turns them into the delta.
-bool Ctx::stream_chunk_prepare(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w) {
+// prompt assembly, the LCP reuse and the prefill into the stream's KV slot (or, with
+// defer_prefill, leaves the prefill job in `w`); the caller decodes max_new tokens in that
+// slot; stream_chunk_finish turns them into the delta.
+bool Ctx::stream_chunk_prepare(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w,
+                               bool defer_prefill) {
   w = StreamChunk();
   const size_t chunk_samples = (size_t)(stream_chunk_sec * (float)kSampleRate);
   const int rollback = stream_rollback, unfixed = stream_unfixed_chunks;
@@ -432,17 +434,23 @@ bool Ctx::stream_chunk_prepare(const std::vector<float>& samples, StreamState& s
     }
   }
   tm[2] = now_ms();
-  // Device copy of the assembled encoder rows for the prompt gather (grow-only buffer: a
-  // free per chunk would synchronise the device).
-  if (!stream_enc_dev.alloc(enc_output.size())) return false;
-  if (cudaMemcpyAsync(stream_enc_dev.p, enc_output.data(), enc_output.size() * 4, cudaMemcpyHostToDevice,
-                      eng.stream()) != cudaSuccess)
-    return false;
-  if (!eng.prefill_ids(ids, stream_enc_dev.p, (int)reused, w.slot)) return false;
+  if (defer_prefill) {
+    w.ids = ids;
+    w.reused = (int)reused;
+  } else {
+    // Device copy of the assembled encoder rows for the prompt gather (grow-only buffer: a
+    // free per chunk would synchronise the device).
+    if (!stream_enc_dev.alloc(enc_output.size())) return false;
+    if (cudaMemcpyAsync(stream_enc_dev.p, enc_output.data(), enc_output.size() * 4, cudaMemcpyHostToDevice,
+                        eng.stream()) != cudaSuccess)
+      return false;
+    if (!eng.prefill_ids(ids, stream_enc_dev.p, (int)reused, w.slot)) return false;
+  }
   tm[3] = now_ms();
   st.prev_ids.assign(ids.begin(), ids.begin() + prefill_len);
   st.prev_enc = std::move(enc_output);
   st.prev_prefill_len = prefill_len;
+  w.enc = &st.prev_enc;
   tm[4] = now_ms();
   if (timing)
     fprintf(stderr, "stream chunk %d: encode %.2f ms, assemble+lcp %.2f ms, upload+prefill %.2f ms (%zu rows, %zu reused), "
@@ -577,7 +585,7 @@ bool Ctx::stream_push_many(const std::vector<const std::vector<float>*>& samples
     std::vector<size_t> act;
     for (size_t i = 0; i < n; ++i) {
       if (done[i]) continue;
-      if (!stream_chunk_prepare(*samples[i], *sts[i], finalize, work[i])) return false;
+      if (!stream_chunk_prepare(*samples[i], *sts[i], finalize, work[i], true)) return false;
       if (work[i].empty_stop) {
         deltas[i].clear();
         done[i] = 1;
@@ -588,6 +596,28 @@ bool Ctx::stream_push_many(const std::vector<const std::vector<float>*>& samples
       }
     }
     if (act.empty()) break;
+    // one prefill pass for every active chunk: their encoder rows go up as one buffer and
+    // each chunk's encoder ids are offset into it
+    {
+      size_t rows = 0;
+      const int dim = eng.cfg().dec_hidden;
+      for (size_t i : act) rows += work[i].enc->size() / dim;
+      if (!stream_enc_dev.alloc(std::max<size_t>(rows, 1) * dim)) return false;
+      std::vector<Engine::PrefillJob> jobs;
+      size_t base = 0;
+      for (size_t i : act) {
+        StreamChunk& w = work[i];
+        const size_t r = w.enc->size() / dim;
+        if (r > 0 && cudaMemcpyAsync(stream_enc_dev.p + base * dim, w.enc->data(), w.enc->size() * 4,
+                                     cudaMemcpyHostToDevice, eng.stream()) != cudaSuccess)
+          return false;
+        for (int& id : w.ids)
+          if (id < 0) id -= (int)base;
+        jobs.push_back({&w.ids, w.reused, w.slot});
+        base += r;
+      }
+      if (!eng.prefill_many(jobs, stream_enc_dev.p)) return false;
+    }
     std::sort(act.begin(), act.end(), [&](size_t a, size_t b) { return work[a].slot < work[b].slot; });
     for (size_t k = 0; k < act.size();) {
       size_t e = k + 1;  // a run of contiguous slots, at most max_b long

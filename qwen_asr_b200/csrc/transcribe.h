@@ -50,6 +50,11 @@ struct StreamChunk {
   double t0 = 0;
   StagePerf before;
   std::vector<int> gen;
+  // deferred prefill (stream_push_many prefills all streams' chunks in one pass): the
+  // prompt ids (encoder rows as -(r+1) into *enc), the reused LCP length
+  std::vector<int> ids;
+  int reused = 0;
+  const std::vector<float>* enc = nullptr;
 };
 
 class Ctx {
@@ -100,7 +105,8 @@ class Ctx {
   bool stream_push_audio(const std::vector<float>& samples, StreamState& st, bool finalize, std::string& delta);
   bool stream_push_many(const std::vector<const std::vector<float>*>& samples, const std::vector<StreamState*>& sts,
                         bool finalize, std::vector<std::string>& deltas);
-  bool stream_chunk_prepare(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w);
+  bool stream_chunk_prepare(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w,
+                            bool defer_prefill = false);
   bool stream_chunk_finish(StreamState& st, StreamChunk& w, std::string& delta);
   void reset_perf();
   // Transcribes the independent segments [starts[i], ends[i]) of `samples` (each padded to

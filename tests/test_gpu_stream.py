@@ -89,8 +89,9 @@ def test_stream_reset_and_empty(tiny_dir):
 
 @pytest.mark.parametrize("mode", ["int8", "bf16"])
 def test_stream_push_many_matches_single_streams(tiny_dir, mode):
-    """Streams advanced together (batched decode across their KV slots) produce exactly the
-    deltas each produces when pushed alone."""
+    """Streams advanced together (one prefill pass and a batched decode across their KV
+    slots) produce exactly the deltas, ids and final-step logits (bit for bit) that each
+    produces when pushed alone."""
     import qwen_asr_b200 as Q
     n_streams, n_chunks, chunk = 3, 4, 32000
     audio = [synth.synth_audio(chunk * n_chunks, seed=300 + i) for i in range(n_streams)]
@@ -99,6 +100,7 @@ def test_stream_push_many_matches_single_streams(tiny_dir, mode):
         eng = Q.Engine(tiny_dir)
         eng.set_decode_mode(mode)
         eng.set_language("English")
+        eng.set_record_logits(True)
         return eng
 
     eng_a = make()
@@ -118,3 +120,6 @@ def test_stream_push_many_matches_single_streams(tiny_dir, mode):
     # generated ids of every chunk of every stream, accumulated round by round in both engines
     ids_a, ids_b = eng_a.last_tokens(), eng_b.last_tokens()
     assert ids_a == ids_b and len(ids_a) == n_chunks * n_streams and sum(len(g) for g in ids_a) > 0
+    la, lb = eng_a.recorded_logits(), eng_b.recorded_logits()
+    assert la.size > 0 and la.shape == lb.shape
+    assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
