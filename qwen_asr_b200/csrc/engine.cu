@@ -421,25 +421,45 @@ int Engine::mel(const float* samples, int n, bool on_device) {
 }
 
 // ---------------------------------------------------------------------------- encoder
+float* Engine::mel_scratch(size_t floats) { return mel_keep_.alloc(floats) ? mel_keep_.p : nullptr; }
+
 int Engine::encode(const float* d_mel, int F) {
+  std::vector<int> seq;
+  return encode_many({{d_mel, F}}, seq);
+}
+
+// Several inputs (mel matrices) through the encoder in one pass: each input's conv front
+// end fills its rows of x_enc, the attention windows restart at every input's first row,
+// and every transformer layer runs once over all rows. Rows depend only on their own
+// input, so each equals the single-input encode bit for bit.
+int Engine::encode_many(const std::vector<EncInput>& in, std::vector<int>& seq) {
   cudaSetDevice(device_);
   const Config& c = cfg_;
   const int d = c.enc_d_model, cs = c.enc_chunk_size, H = kConvHidden;
   auto cw = [](int w) { return (w + 2 - 3) / 2 + 1; };
-  const int n_chunks = (F + cs - 1) / cs, full = F / cs;
-  struct Grp { int c0, nc, w; };
+  struct Grp { int input, c0, nc, w; };
   std::vector<Grp> groups;
-  if (full > 0) groups.push_back({0, full, cs});
-  if (full < n_chunks) groups.push_back({full, 1, F - full * cs});
+  seq.assign(in.size(), 0);
+  for (size_t i = 0; i < in.size(); ++i) {
+    const int F = in[i].F;
+    const int n_chunks = (F + cs - 1) / cs, full = F / cs;
+    if (full > 0) groups.push_back({(int)i, 0, full, cs});
+    if (full < n_chunks) groups.push_back({(int)i, full, 1, F - full * cs});
+  }
   int T = 0;
   size_t max_cols = 0, max_a1 = 0, max_a2 = 0, max_a3 = 0;
   for (auto& g : groups) {
     int w1 = cw(g.w), w2 = cw(w1), w3 = cw(w2);
     T += g.nc * w3;
+    seq[g.input] += g.nc * w3;
     max_a1 = std::max(max_a1, (size_t)g.nc * 64 * w1 * H);
     max_a2 = std::max(max_a2, (size_t)g.nc * 32 * w2 * H);
     max_a3 = std::max(max_a3, (size_t)g.nc * 16 * w3 * H);
     max_cols = std::max(max_cols, (size_t)g.nc * 32 * w2 * 9 * H);
+  }
+  if (T == 0) {
+    set_error("encode: no input frames");
+    return 0;
   }
   if (!act1_.alloc(max_a1) || !act2_.alloc(max_a2) || !act3_.alloc(max_a3) || !cols_.alloc(max_cols) ||
       !x_enc_.alloc((size_t)T * d) || !xn_enc_.alloc((size_t)T * d) || !qkv_enc_.alloc((size_t)T * 3 * d) ||
@@ -451,7 +471,7 @@ int Engine::encode(const float* d_mel, int F) {
   int tok = 0;
   for (auto& g : groups) {
     int w1 = cw(g.w), w2 = cw(w1), w3 = cw(w2);
-    conv1_gelu(d_mel, F, g.c0 * cs, cs, g.nc, g.w, conv1_w, conv1_b, act1_.p, stream_);
+    conv1_gelu(in[g.input].mel, in[g.input].F, g.c0 * cs, cs, g.nc, g.w, conv1_w, conv1_b, act1_.p, stream_);
     im2col_s2(act1_.p, g.nc, 64, w1, cols_.p, false, stream_);
     GemmArgs a;
     a.M = g.nc * 32 * w2; a.N = H; a.K = 9 * H;
@@ -472,10 +492,11 @@ int Engine::encode(const float* d_mel, int F) {
   // attention windows (encoder.rs:292-298)
   int tpc = cw(cw(cw(cs)));
   int wts = tpc * (c.enc_n_window_infer / cs);
-  int n_win = (T + wts - 1) / wts;
-  std::vector<int> ws(n_win + 1);
-  for (int w = 0; w < n_win; ++w) ws[w] = w * wts;
-  ws[n_win] = T;
+  std::vector<int> ws;
+  for (size_t i = 0, t0 = 0; i < in.size(); t0 += seq[i], ++i)
+    for (int s = 0; s < seq[i]; s += wts) ws.push_back((int)t0 + s);
+  const int n_win = (int)ws.size();
+  ws.push_back(T);
   int max_win = 0;
   for (int w = 0; w < n_win; ++w) max_win = std::max(max_win, ws[w + 1] - ws[w]);
   if (!win_starts_.alloc(n_win + 1)) return 0;

@@ -51,6 +51,14 @@ class Engine {
   int mel(const float* samples, int n, bool samples_on_device);
   // Stage 2: mel (device, [F][128]) -> encoder output rows [T][dec_hidden] in enc_out(). Returns T.
   int encode(const float* d_mel, int n_frames);
+  // Several mel inputs through the encoder in one pass (rows of input i follow those of
+  // inputs < i in enc_out; seq[i] = its row count); returns the total rows (0 on error).
+  struct EncInput {
+    const float* mel;
+    int F;
+  };
+  int encode_many(const std::vector<EncInput>& in, std::vector<int>& seq);
+  float* mel_scratch(size_t floats);  // grow-only device buffer for mels kept across calls
   float* mel_buf() { return mel_.p; }
   // Read-only device tables of the mel front end (Hann window, DFT matrix [408][400],
   // mel filterbank [128][208]).
@@ -165,6 +173,7 @@ class Engine {
   DevBuf<int> win_starts_;
   DevBuf<float> px_, pxn_, pqkv_, patt_, pmid_;
   DevBuf<int> ids_;
+  DevBuf<float> mel_keep_;
   // KV cache [slot][layers][kv][max_seq][128] f32
   DevBuf<float> kc_, vc_;
   int max_seq_ = 0;

@@ -323,10 +323,62 @@ static std::pair<size_t, size_t> tail_repeat_blocks(const std::vector<int>& t, s
 // slot; stream_chunk_finish turns them into the delta.
 bool Ctx::stream_chunk_prepare(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w,
                                bool defer_prefill) {
+  if (!stream_chunk_begin(samples, st, finalize, w)) return false;
+  if (!w.pending) return true;
+  std::vector<EncJob*> jobs;
+  for (auto& j : w.enc_jobs) jobs.push_back(&j);
+  if (!run_enc_jobs(jobs)) return false;
+  return stream_chunk_assemble(samples, st, w, defer_prefill);
+}
+
+// Encodes the jobs' audio windows in one encoder pass (mel per window, then encode_many);
+// a window too short for one mel frame is marked failed, as encode_window fails on it.
+bool Ctx::run_enc_jobs(const std::vector<EncJob*>& jobs) {
+  if (jobs.empty()) return true;
+  const int dim = eng.cfg().dec_hidden;
+  size_t frames = 0;
+  for (EncJob* j : jobs) frames += j->n / kHop;
+  float* keep = eng.mel_scratch(std::max<size_t>(frames, 1) * kMelBins);
+  if (!keep) return false;
+  std::vector<Engine::EncInput> in;
+  std::vector<EncJob*> run;
+  size_t off = 0;
+  for (EncJob* j : jobs) {
+    j->ok = false;
+    j->seq = 0;
+    if (j->n / kHop == 0) continue;
+    const int F = eng.mel(j->samples, (int)j->n, false);
+    if (F <= 0) continue;
+    if (cudaMemcpyAsync(keep + off, eng.mel_buf(), (size_t)F * kMelBins * 4, cudaMemcpyDeviceToDevice,
+                        eng.stream()) != cudaSuccess)
+      return false;
+    in.push_back({keep + off, F});
+    run.push_back(j);
+    off += (size_t)F * kMelBins;
+  }
+  if (in.empty()) return true;
+  std::vector<int> seq;
+  const int T = eng.encode_many(in, seq);
+  if (T <= 0) return true;  // as a failed encode_window: every job falls back
+  std::vector<float> all((size_t)T * dim);
+  if (cudaMemcpy(all.data(), eng.enc_out(), all.size() * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return false;
+  size_t row = 0;
+  for (size_t i = 0; i < run.size(); ++i) {
+    EncJob* j = run[i];
+    j->seq = seq[i];
+    j->ok = seq[i] > 0;
+    j->enc.assign(all.begin() + row * dim, all.begin() + (row + seq[i]) * dim);
+    row += seq[i];
+  }
+  return true;
+}
+
+// The part of a chunk before its window encodes: advances the audio cursor and lists the
+// windows to encode (full windows the cursor crossed, then the partial window when it is
+// due) in w.enc_jobs; w.pending is false when the stream has no chunk to run.
+bool Ctx::stream_chunk_begin(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w) {
   w = StreamChunk();
   const size_t chunk_samples = (size_t)(stream_chunk_sec * (float)kSampleRate);
-  const int rollback = stream_rollback, unfixed = stream_unfixed_chunks;
-  const int dim = eng.cfg().dec_hidden;
   if (!st.prompt_prepared) {
     if (!prepare_prompt_tokens()) return false;
     st.prompt_prepared = true;
@@ -337,40 +389,67 @@ bool Ctx::stream_chunk_prepare(const std::vector<float>& samples, StreamState& s
   const size_t enc_window_frames = (size_t)std::min(std::max(eng.cfg().enc_n_window_infer, 100), 800);
   const size_t enc_window_samples = enc_window_frames * kHop;
 
+  w.pending = true;
   w.t0 = now_ms();
-  static const bool timing = getenv("QASR_STREAM_TIMING") != nullptr;  // debugging aid
-  double tm[5] = {w.t0, 0, 0, 0, 0};
   st.audio_cursor = std::min(st.audio_cursor + chunk_samples, samples.size());
   w.is_final = finalize && st.audio_cursor >= samples.size();
   w.before = eng.perf;
 
-  size_t full_end = (st.audio_cursor / enc_window_samples) * enc_window_samples;
-  while ((st.enc_cache_base_windows + st.enc_cache.size()) * enc_window_samples < full_end) {
-    size_t ws = (st.enc_cache_base_windows + st.enc_cache.size()) * enc_window_samples;
+  w.full_end = (st.audio_cursor / enc_window_samples) * enc_window_samples;
+  for (size_t k = st.enc_cache_base_windows + st.enc_cache.size(); k * enc_window_samples < w.full_end; ++k) {
+    EncJob j;
+    j.samples = samples.data() + k * enc_window_samples;
+    j.n = enc_window_samples;
+    w.enc_jobs.push_back(std::move(j));
+  }
+  const size_t enc_update_threshold = chunk_samples * 2;
+  const size_t partial_age = st.audio_cursor > st.last_partial_cursor ? st.audio_cursor - st.last_partial_cursor : 0;
+  const bool need_encode = st.last_partial_cursor == 0 || partial_age >= enc_update_threshold || w.is_final;
+  w.need_partial = need_encode && w.full_end < st.audio_cursor;
+  if (w.need_partial) {
+    EncJob j;
+    j.samples = samples.data() + w.full_end;
+    j.n = st.audio_cursor - w.full_end;
+    w.enc_jobs.push_back(std::move(j));
+  }
+  return true;
+}
+
+// The rest of a chunk once its windows are encoded: caches the window outputs, assembles
+// the prompt, finds the reusable prefix and prefills (or leaves the prefill job in `w`).
+bool Ctx::stream_chunk_assemble(const std::vector<float>& samples, StreamState& st, StreamChunk& w,
+                                bool defer_prefill) {
+  const int rollback = stream_rollback, unfixed = stream_unfixed_chunks;
+  const int dim = eng.cfg().dec_hidden;
+  static const bool timing = getenv("QASR_STREAM_TIMING") != nullptr;  // debugging aid
+  double tm[5] = {w.t0, 0, 0, 0, 0};
+  (void)samples;
+  size_t k = 0;
+  const size_t n_full = w.enc_jobs.size() - (w.need_partial ? 1 : 0);
+  for (; k < n_full; ++k) {
+    EncJob& j = w.enc_jobs[k];
+    if (!j.ok) {
+      set_error("stream: encoding a full window failed");
+      return false;
+    }
     StreamState::EncWindow ew;
-    if (!encode_window(samples.data() + ws, enc_window_samples, ew.enc, ew.seq_len)) return false;
+    ew.enc = std::move(j.enc);
+    ew.seq_len = j.seq;
     st.enc_cached_seq_total += ew.seq_len;
     st.enc_cache.push_back(std::move(ew));
   }
-  size_t enc_update_threshold = chunk_samples * 2;
-  size_t partial_age = st.audio_cursor > st.last_partial_cursor ? st.audio_cursor - st.last_partial_cursor : 0;
-  bool need_encode = st.last_partial_cursor == 0 || partial_age >= enc_update_threshold || w.is_final;
   int partial_seq = 0;
   const std::vector<float>* partial_enc = nullptr;
-  std::vector<float> fresh;
-  if (need_encode && full_end < st.audio_cursor) {
-    int seq = 0;
-    if (encode_window(samples.data() + full_end, st.audio_cursor - full_end, fresh, seq)) {
-      partial_seq = seq;
+  if (w.need_partial) {
+    EncJob& j = w.enc_jobs[k];
+    if (j.ok) {
       st.last_partial_cursor = st.audio_cursor;
-      st.last_partial_enc = fresh;
-      st.last_partial_seq = seq;
-      partial_enc = &st.last_partial_enc;
-    } else {
-      partial_seq = st.last_partial_seq;
-      partial_enc = &st.last_partial_enc;
+      st.last_partial_enc = std::move(j.enc);
+      st.last_partial_seq = j.seq;
     }
-  } else if (full_end < st.audio_cursor) {
+    partial_seq = st.last_partial_seq;
+    partial_enc = &st.last_partial_enc;
+  } else if (w.full_end < st.audio_cursor) {
     partial_seq = st.last_partial_seq;
     partial_enc = &st.last_partial_enc;
   }
@@ -583,9 +662,17 @@ bool Ctx::stream_push_many(const std::vector<const std::vector<float>*>& samples
   for (;;) {
     std::vector<StreamChunk> work(n);
     std::vector<size_t> act;
+    // every stream's window encodes of this round in one encoder pass
+    std::vector<EncJob*> jobs;
     for (size_t i = 0; i < n; ++i) {
       if (done[i]) continue;
-      if (!stream_chunk_prepare(*samples[i], *sts[i], finalize, work[i], true)) return false;
+      if (!stream_chunk_begin(*samples[i], *sts[i], finalize, work[i])) return false;
+      for (auto& j : work[i].enc_jobs) jobs.push_back(&j);
+    }
+    if (!run_enc_jobs(jobs)) return false;
+    for (size_t i = 0; i < n; ++i) {
+      if (done[i]) continue;
+      if (work[i].pending && !stream_chunk_assemble(*samples[i], *sts[i], work[i], true)) return false;
       if (work[i].empty_stop) {
         deltas[i].clear();
         done[i] = 1;

@@ -41,6 +41,15 @@ struct StreamState {  // transcribe.rs:801-893
 };
 
 // One chunk of a stream in flight between its prepare and finish steps.
+// One audio window of a stream chunk to encode (host samples), and its encoder output.
+struct EncJob {
+  const float* samples = nullptr;
+  size_t n = 0;
+  bool ok = false;
+  int seq = 0;
+  std::vector<float> enc;
+};
+
 struct StreamChunk {
   bool active = false;      // prefilled, waiting for its decode
   bool empty_stop = false;  // nothing encoded yet: the push ends with an empty delta
@@ -54,7 +63,11 @@ struct StreamChunk {
   // prompt ids (encoder rows as -(r+1) into *enc), the reused LCP length
   std::vector<int> ids;
   int reused = 0;
-  const std::vector<float>* enc = nullptr;
+  const std::vector<float>* enc = nullptr;  // window encodes of the chunk (full windows, then the partial window when due)
+  bool pending = false;
+  bool need_partial = false;
+  size_t full_end = 0;
+  std::vector<EncJob> enc_jobs;
 };
 
 class Ctx {
@@ -107,6 +120,9 @@ class Ctx {
                         bool finalize, std::vector<std::string>& deltas);
   bool stream_chunk_prepare(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w,
                             bool defer_prefill = false);
+  bool stream_chunk_begin(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w);
+  bool run_enc_jobs(const std::vector<EncJob*>& jobs);
+  bool stream_chunk_assemble(const std::vector<float>& samples, StreamState& st, StreamChunk& w, bool defer_prefill);
   bool stream_chunk_finish(StreamState& st, StreamChunk& w, std::string& delta);
   void reset_perf();
   // Transcribes the independent segments [starts[i], ends[i]) of `samples` (each padded to
