@@ -192,15 +192,29 @@ bool Ctx::transcribe_segments_batched(const std::vector<std::vector<float>>& seg
   StagePerf before = eng.perf;
   texts.assign(segs.size(), std::string());
   std::vector<int> slot_of(segs.size(), -1);
-  int B = 0;
+  // one encoder pass and one prefill pass for the whole group
+  std::vector<const float*> smp;
+  std::vector<size_t> n;
+  for (auto& s : segs) {
+    smp.push_back(s.data());
+    n.push_back(s.size());
+  }
+  std::vector<int> seq;
+  if (!encode_inputs(smp, n, seq)) return false;
+  std::vector<std::vector<int>> ids;
+  ids.reserve(segs.size());
+  std::vector<Engine::PrefillJob> jobs;
+  int B = 0, base = 0;
   for (size_t i = 0; i < segs.size(); ++i) {
-    int F = eng.mel(segs[i].data(), (int)segs[i].size(), false);
-    if (F <= 0) continue;
-    int T = eng.encode(eng.mel_buf(), F);
-    if (T <= 0) continue;
-    if (!eng.prefill_ids(segment_ids(T, nullptr), eng.enc_out(), 0, B)) return false;
+    if (seq[i] <= 0) continue;
+    ids.push_back(segment_ids(seq[i], nullptr));
+    for (int& id : ids.back())
+      if (id < 0) id -= base;
+    base += seq[i];
+    jobs.push_back({&ids.back(), 0, B});
     slot_of[i] = B++;
   }
+  if (!jobs.empty() && !eng.prefill_many(jobs, eng.enc_out())) return false;
   std::vector<std::vector<int>> gen;
   const int limit = force_n_tokens > 0 ? force_n_tokens : 2048;
   if (B > 0 && !eng.decode_batch(B, limit, force_n_tokens <= 0, gen)) return false;
@@ -331,40 +345,59 @@ bool Ctx::stream_chunk_prepare(const std::vector<float>& samples, StreamState& s
   return stream_chunk_assemble(samples, st, w, defer_prefill);
 }
 
-// Encodes the jobs' audio windows in one encoder pass (mel per window, then encode_many);
-// a window too short for one mel frame is marked failed, as encode_window fails on it.
-bool Ctx::run_enc_jobs(const std::vector<EncJob*>& jobs) {
-  if (jobs.empty()) return true;
-  const int dim = eng.cfg().dec_hidden;
+// Host audio inputs through the encoder in one pass (mel per input, then encode_many):
+// seq[i] = the encoder rows of input i (0 when it is too short for one mel frame or the
+// encode failed); the rows of the inputs with seq > 0 follow each other in eng.enc_out().
+bool Ctx::encode_inputs(const std::vector<const float*>& samples, const std::vector<size_t>& n,
+                        std::vector<int>& seq) {
+  seq.assign(samples.size(), 0);
   size_t frames = 0;
-  for (EncJob* j : jobs) frames += j->n / kHop;
-  float* keep = eng.mel_scratch(std::max<size_t>(frames, 1) * kMelBins);
+  for (size_t x : n) frames += x / kHop;
+  if (frames == 0) return true;
+  float* keep = eng.mel_scratch(frames * kMelBins);
   if (!keep) return false;
   std::vector<Engine::EncInput> in;
-  std::vector<EncJob*> run;
+  std::vector<size_t> which;
   size_t off = 0;
-  for (EncJob* j : jobs) {
-    j->ok = false;
-    j->seq = 0;
-    if (j->n / kHop == 0) continue;
-    const int F = eng.mel(j->samples, (int)j->n, false);
+  for (size_t i = 0; i < samples.size(); ++i) {
+    if (n[i] / kHop == 0) continue;
+    const int F = eng.mel(samples[i], (int)n[i], false);
     if (F <= 0) continue;
     if (cudaMemcpyAsync(keep + off, eng.mel_buf(), (size_t)F * kMelBins * 4, cudaMemcpyDeviceToDevice,
                         eng.stream()) != cudaSuccess)
       return false;
     in.push_back({keep + off, F});
-    run.push_back(j);
+    which.push_back(i);
     off += (size_t)F * kMelBins;
   }
   if (in.empty()) return true;
+  std::vector<int> s;
+  if (eng.encode_many(in, s) <= 0) return true;  // as failed encodes: every input falls back
+  for (size_t k = 0; k < which.size(); ++k) seq[which[k]] = s[k];
+  return true;
+}
+
+// Encodes the jobs' audio windows in one encoder pass; a window too short for one mel
+// frame is marked failed, as encode_window fails on it.
+bool Ctx::run_enc_jobs(const std::vector<EncJob*>& jobs) {
+  if (jobs.empty()) return true;
+  const int dim = eng.cfg().dec_hidden;
+  std::vector<const float*> smp;
+  std::vector<size_t> n;
+  for (EncJob* j : jobs) {
+    smp.push_back(j->samples);
+    n.push_back(j->n);
+  }
   std::vector<int> seq;
-  const int T = eng.encode_many(in, seq);
-  if (T <= 0) return true;  // as a failed encode_window: every job falls back
-  std::vector<float> all((size_t)T * dim);
-  if (cudaMemcpy(all.data(), eng.enc_out(), all.size() * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return false;
+  if (!encode_inputs(smp, n, seq)) return false;
+  size_t T = 0;
+  for (int s : seq) T += s;
+  std::vector<float> all(T * dim);
+  if (T > 0 && cudaMemcpy(all.data(), eng.enc_out(), all.size() * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return false;
   size_t row = 0;
-  for (size_t i = 0; i < run.size(); ++i) {
-    EncJob* j = run[i];
+  for (size_t i = 0; i < jobs.size(); ++i) {
+    EncJob* j = jobs[i];
     j->seq = seq[i];
     j->ok = seq[i] > 0;
     j->enc.assign(all.begin() + row * dim, all.begin() + (row + seq[i]) * dim);

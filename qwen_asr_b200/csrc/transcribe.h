@@ -121,6 +121,7 @@ class Ctx {
   bool stream_chunk_prepare(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w,
                             bool defer_prefill = false);
   bool stream_chunk_begin(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w);
+  bool encode_inputs(const std::vector<const float*>& samples, const std::vector<size_t>& n, std::vector<int>& seq);
   bool run_enc_jobs(const std::vector<EncJob*>& jobs);
   bool stream_chunk_assemble(const std::vector<float>& samples, StreamState& st, StreamChunk& w, bool defer_prefill);
   bool stream_chunk_finish(StreamState& st, StreamChunk& w, std::string& delta);
