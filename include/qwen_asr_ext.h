@@ -55,6 +55,18 @@ int32_t qwen_asr_transcribe_segments(QwenAsrEngine* engine, const float* samples
 int32_t qwen_asr_set_decode_batch(QwenAsrEngine* engine, int32_t n);
 /* 1 (default): decode steps replay a CUDA graph; 0: plain launches. */
 void qwen_asr_set_use_graph(QwenAsrEngine* engine, int32_t on);
+/* Forced alignment (the reference's align::forced_align, align.rs:207-351; an aligner
+ * model directory, classify_num > 0): word (CJK languages: character) timestamps of `text`
+ * in `samples` (16 kHz mono). `language` is normalised as the CLI does (main.rs:355). Returns a
+ * JSON array [{"text": "...", "start_ms": s, "end_ms": e}, ...] to release with
+ * qwen_asr_free_string(), or NULL (qwen_asr_last_error()). */
+char* qwen_asr_forced_align(QwenAsrEngine* engine, const float* samples, int64_t n_samples, const char* text,
+                            const char* language);
+/* Debug: the aligner's units of `text` joined by '\n' (align.rs:44-61); returns the count,
+ * -1 on invalid UTF-8 or a short buffer. */
+int32_t qwen_asr_debug_align_words(const char* text, const char* language, char* out, int32_t cap);
+/* Debug: the aligner's timestamp repair in place (align.rs:140-189). */
+void qwen_asr_debug_fix_timestamps(float* ts, int32_t n);
 /* Debug: when on, every decode keeps each sequence's f32 logits of its final step (decode
  * runs as plain launches); switching it on or off clears what was kept. */
 void qwen_asr_set_record_logits(QwenAsrEngine* engine, int32_t on);

@@ -1261,3 +1261,125 @@ def stream_push_audio(ctx: "Ctx", samples, st: StreamState, finalize: bool) -> b
         if speech_ended:
             break
     return delta
+
+
+# ---------------------------------------------------------------------------- forced aligner
+TOKEN_TIMESTAMP = 151705  # config.rs:20
+_CJK = ("Chinese", "Japanese", "Korean", "Cantonese")
+
+
+def align_split_words(text: str, language: str):
+    """align.rs:44-61: CJK languages -> every non-white-space character, otherwise
+    white-space separated words (Rust char::is_whitespace)."""
+    if language in _CJK:
+        return [ch for ch in text if ord(ch) not in _RUST_WS]
+    words, cur = [], ""
+    for ch in text:
+        if ord(ch) in _RUST_WS:
+            if cur:
+                words.append(cur)
+            cur = ""
+        else:
+            cur += ch
+    if cur:
+        words.append(cur)
+    return words
+
+
+def longest_increasing_subsequence(vals):
+    """align.rs:97-137 (non-decreasing; the first longest end; traced back)."""
+    n = len(vals)
+    if n == 0:
+        return []
+    dp, prev = [1] * n, [None] * n
+    for i in range(1, n):
+        for j in range(i):
+            if vals[j] <= vals[i] and dp[j] + 1 > dp[i]:
+                dp[i] = dp[j] + 1
+                prev[i] = j
+    best_len, best_end = 0, 0
+    for i in range(n):
+        if dp[i] > best_len:
+            best_len, best_end = dp[i], i
+    out, idx = [], best_end
+    while True:
+        out.append(idx)
+        if prev[idx] is None:
+            break
+        idx = prev[idx]
+    return out[::-1]
+
+
+def fix_timestamps(ts):
+    """align.rs:140-189 in f32: blocks off the LIS of <= 2 take the nearest normal value,
+    longer blocks are interpolated linearly."""
+    ts = [F32(t) for t in ts]
+    n = len(ts)
+    if n <= 1:
+        return ts
+    lis = longest_increasing_subsequence(ts)
+    if len(lis) == n:
+        return ts
+    normal = [False] * n
+    for i in lis:
+        normal[i] = True
+    i = 0
+    while i < n:
+        if normal[i]:
+            i += 1
+            continue
+        bs = i
+        while i < n and not normal[i]:
+            i += 1
+        be, bl = i, i - bs
+        left = ts[bs - 1] if bs > 0 else F32(0.0)
+        right = ts[be] if be < n else F32(left + F32(F32(bl) * F32(80.0)))
+        if bl <= 2:
+            fill = left if bs > 0 else right
+            for k in range(bs, be):
+                ts[k] = fill
+        else:
+            for j in range(bl):
+                t = F32(F32(j + 1) / F32(bl + 1))
+                ts[bs + j] = F32(left + F32(t * F32(right - left)))
+    return ts
+
+
+def forced_align(ctx, samples: np.ndarray, text: str, language: str):
+    """align.rs:207-351: [(word, start_ms, end_ms)], or None. Also returns the raw argmax
+    classes of the <timestamp> rows (for parity tests)."""
+    m, c = ctx.model, ctx.model.cfg
+    words = align_split_words(text, language)
+    if not words:
+        return None
+    text_tokens = []
+    for i, w in enumerate(words):  # encode_timestamp, align.rs:66-93
+        wt = ctx.tok.encode(w)
+        if wt is None:
+            return None
+        text_tokens += list(wt) + [TOKEN_TIMESTAMP, TOKEN_TIMESTAMP]
+        if i == 0 and not wt:
+            return None
+    mel = mel_spectrogram(samples)
+    if mel is None:
+        return None
+    enc = m.encode(mel)
+    ids = PREFIX_HEAD + PREFIX_TAIL
+    rows = [m.embed(t) for t in ids] + [enc[i] for i in range(enc.shape[0])]
+    rows += [m.embed(t) for t in SUFFIX_BASE]
+    text_off = len(rows)
+    rows += [m.embed(t) for t in text_tokens]
+    ctx.dec.kv.len = 0
+    x = ctx.dec.prefill(np.stack(rows).astype(F32))
+    ts_rows = [text_off + i for i, t in enumerate(text_tokens) if t == TOKEN_TIMESTAMP]
+    xn = rms_norm(x[ts_rows], m.norm, c.eps)
+    logits = (xn @ bf16_to_f32(m.lm_bits).T).astype(F32)
+    cls = [int(np.argmax(r)) for r in logits]  # first maximum, as the strictly-greater scan
+    ts = fix_timestamps([F32(k) * F32(80.0) for k in cls])
+    out = []
+    for i, w in enumerate(words):
+        s = ts[2 * i] if 2 * i < len(ts) else F32(0.0)
+        e = ts[2 * i + 1] if 2 * i + 1 < len(ts) else s
+        out.append((w, float(s), float(e)))
+    return out, cls
+

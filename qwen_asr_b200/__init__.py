@@ -84,6 +84,9 @@ SIGNATURES = {
     "qwen_asr_debug_compact_silence": (C.c_int64, [_F32P, C.c_int64, _F32P, C.c_int64]),
     "qwen_asr_debug_lossy_trim": (C.c_int32, [C.c_char_p, C.c_int32, C.c_char_p, C.c_int32]),
     "qwen_asr_debug_normalize_language": (C.c_int32, [C.c_char_p, C.c_char_p, C.c_int32]),
+    "qwen_asr_forced_align": (_VP, [_VP, _F32P, C.c_int64, C.c_char_p, C.c_char_p]),
+    "qwen_asr_debug_align_words": (C.c_int32, [C.c_char_p, C.c_char_p, C.c_char_p, C.c_int32]),
+    "qwen_asr_debug_fix_timestamps": (None, [C.POINTER(C.c_float), C.c_int32]),
 }
 
 
@@ -139,6 +142,14 @@ class Engine:
     def transcribe_pcm(self, samples) -> str | None:
         a, p = _f32(samples)
         return _take_string(lib().qwen_asr_transcribe_pcm(self._h, p, len(a)))
+
+    def forced_align(self, samples, text: str, language: str = "English") -> list | None:
+        """Word (CJK: character) timestamps of `text` in `samples` with an aligner model:
+        [{"text", "start_ms", "end_ms"}, ...], or None (see last_error())."""
+        import json
+        a, p = _f32(samples)
+        s = _take_string(lib().qwen_asr_forced_align(self._h, p, len(a), text.encode(), language.encode()))
+        return None if s is None else json.loads(s)
 
     def transcribe_file(self, path: str) -> str | None:
         return _take_string(lib().qwen_asr_transcribe_file(self._h, path.encode()))
@@ -347,3 +358,19 @@ class Stream:
 
     def __del__(self):
         self.close()
+
+
+def debug_align_words(text: str, language: str) -> list | None:
+    """The forced aligner's units of `text` (align.rs:44-61)."""
+    buf = C.create_string_buffer(4 * len(text.encode()) + 16)
+    n = lib().qwen_asr_debug_align_words(text.encode(), language.encode(), buf, len(buf))
+    if n < 0:
+        return None
+    return buf.value.decode().split("\n") if n > 0 else []
+
+
+def debug_fix_timestamps(ts) -> np.ndarray:
+    """The forced aligner's timestamp repair (align.rs:140-189)."""
+    a = np.ascontiguousarray(ts, dtype=np.float32).copy()
+    lib().qwen_asr_debug_fix_timestamps(a.ctypes.data_as(C.POINTER(C.c_float)), len(a))
+    return a

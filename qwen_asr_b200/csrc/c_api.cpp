@@ -482,6 +482,68 @@ int32_t qwen_asr_debug_lossy_trim(const char* bytes, int32_t n, char* out, int32
   return (int32_t)r.size();
 }
 
+char* qwen_asr_forced_align(QwenAsrEngine* e, const float* samples, int64_t n_samples, const char* text,
+                            const char* language) {
+  if (!e || !samples || n_samples <= 0 || !text) {
+    qasr::set_error("forced_align: invalid arguments");
+    return nullptr;
+  }
+  std::string lang = language ? language : "";
+  if (!lang.empty()) {
+    const std::string norm = qasr::normalize_language(lang);
+    if (!norm.empty()) lang = norm;
+  }
+  std::vector<qasr::Ctx::AlignItem> items;
+  try {
+    if (!e->ctx.forced_align(samples, (size_t)n_samples, text, lang, items)) return nullptr;
+  } catch (const std::exception& ex) {
+    qasr::set_error(std::string("forced_align: ") + ex.what());
+    return nullptr;
+  }
+  auto esc = [](const std::string& s) {
+    std::string o;
+    for (unsigned char ch : s) {
+      if (ch == '"' || ch == '\\') {
+        o += '\\';
+        o += (char)ch;
+      } else if (ch < 0x20) {
+        char b[8];
+        snprintf(b, sizeof b, "\\u%04x", ch);
+        o += b;
+      } else {
+        o += (char)ch;
+      }
+    }
+    return o;
+  };
+  std::string js = "[";
+  for (size_t i = 0; i < items.size(); ++i) {
+    char b[96];
+    snprintf(b, sizeof b, "\",\"start_ms\":%.9g,\"end_ms\":%.9g}", items[i].start_ms, items[i].end_ms);
+    js += (i ? ",{\"text\":\"" : "{\"text\":\"") + esc(items[i].text) + b;
+  }
+  js += "]";
+  return to_c_string(js);
+}
+
+int32_t qwen_asr_debug_align_words(const char* text, const char* language, char* out, int32_t cap) {
+  if (!text || !language) return -1;
+  std::vector<std::string> words;
+  if (!qasr::align_split_words(text, language, words)) return -1;
+  std::string r;
+  for (size_t i = 0; i < words.size(); ++i) r += (i ? "\n" : "") + words[i];
+  if ((int)r.size() + 1 > cap) return -1;
+  memcpy(out, r.c_str(), r.size() + 1);
+  return (int32_t)words.size();
+}
+
+void qwen_asr_debug_fix_timestamps(float* ts, int32_t n) {
+  if (!ts || n <= 0) return;
+  std::vector<float> v(ts, ts + n);
+  qasr::fix_timestamps(v);
+  memcpy(ts, v.data(), (size_t)n * 4);
+}
+
 int32_t qwen_asr_debug_normalize_language(const char* lang, char* out, int32_t cap) {
   if (!lang) return -1;
   std::string r = qasr::normalize_language(lang);

@@ -24,6 +24,7 @@ constexpr int kTokEndOfText = 151643;
 constexpr int kTokAudioStart = 151669;
 constexpr int kTokAudioEnd = 151670;
 constexpr int kTokAsrText = 151704;
+constexpr int kTokTimestamp = 151705;  // config.rs:20 (forced aligner)
 
 // Verbosity shared by all engines (the reference keeps it global too, kernels/mod.rs:69).
 extern int g_verbose;

@@ -653,6 +653,55 @@ bool Engine::prefill_many(const std::vector<PrefillJob>& jobs, const float* d_en
   return true;
 }
 
+bool Engine::prefill_classify(const std::vector<int>& ids, const float* d_enc, const std::vector<int>& rows,
+                              std::vector<int>& cls) {
+  cudaSetDevice(device_);
+  const Config& c = cfg_;
+  const int h = c.dec_hidden, N = c.classify_num, m = (int)rows.size();
+  if (N <= 0) {
+    set_error("align: model is not a forced aligner (classify_num=0)");
+    return false;
+  }
+  if (ids.empty()) {
+    set_error("align: empty prompt");
+    return false;
+  }
+  for (int r : rows)
+    if (r < 0 || r >= (int)ids.size()) {
+      set_error("align: classify row out of range");
+      return false;
+    }
+  // prefill_many prefills rows [0, n - 1) of a job: one extra row makes every prompt row
+  // part of the prefill (its own hidden state stays unused)
+  std::vector<int> ext(ids);
+  ext.push_back(ids.back());
+  if (!prefill_many({{&ext, 0, 0}}, d_enc)) return false;
+  cls.assign(m, 0);
+  if (m == 0) return true;
+  std::vector<int> g(m);
+  for (int k = 0; k < m; ++k) g[k] = -(rows[k] + 1);  // rows of px_ through the encoder-row path
+  if (!cls_ids_.alloc(m) || !cls_out_.alloc(m) || !cls_x_.alloc((size_t)m * h) || !cls_xn_.alloc((size_t)m * h) ||
+      !cls_logits_.alloc((size_t)m * N))
+    return false;
+  CUDA_OK(cudaMemcpyAsync(cls_ids_.p, g.data(), m * 4, cudaMemcpyHostToDevice, stream_), false);
+  gather_embeds(cls_ids_.p, m, embed_, px_.p, h, cls_x_.p, stream_);
+  rms_norm_rows(cls_x_.p, cls_xn_.p, m, h, final_norm_, c.dec_rms_norm_eps, stream_);
+  GemmArgs a;
+  a.M = m; a.N = N; a.K = h; a.A = cls_xn_.p; a.lda = h; a.B = lm_bf16_; a.ldb = h;
+  a.C = cls_logits_.p; a.ldc = N;
+  gemm(a, stream_);
+  rows_argmax(cls_logits_.p, m, N, cls_out_.p, stream_);
+  launches += 4;
+  CUDA_OK(cudaMemcpyAsync(cls.data(), cls_out_.p, m * 4, cudaMemcpyDeviceToHost, stream_), false);
+  CUDA_OK(cudaStreamSynchronize(stream_), false);
+  if (int e = gemm_tc_error()) {
+    set_error("tensor-core GEMM: a device-side wait timed out (code " + std::to_string(e) + ")");
+    return false;
+  }
+  CUDA_OK(cudaGetLastError(), false);
+  return true;
+}
+
 bool Engine::prefill_rows(const float* rows, int n, int start_pos, int slot) {
   cudaSetDevice(device_);
   const int h = cfg_.dec_hidden;

@@ -87,6 +87,12 @@ class Engine {
     int slot;
   };
   bool prefill_many(const std::vector<PrefillJob>& jobs, const float* d_enc);
+  // Forced aligner (decoder.rs:649-681, align.rs:275-301): prefill of every prompt row from
+  // position 0 (the last row included) into slot 0, then the final RMSNorm and the classify
+  // head (classify_num classes) at `rows`; cls[k] = the argmax class of row rows[k] (first
+  // maximum).
+  bool prefill_classify(const std::vector<int>& ids, const float* d_enc, const std::vector<int>& rows,
+                        std::vector<int>& cls);
   // Greedy decode: runs up to max_steps decoder_forward steps from the prepared state and
   // returns the produced ids. With stop_on_eos the loop stops after the first
   // 151643/151645 (inclusive). forced (teacher forcing) gives the input id of step i+1.
@@ -173,7 +179,8 @@ class Engine {
   DevBuf<int> win_starts_;
   DevBuf<float> px_, pxn_, pqkv_, patt_, pmid_;
   DevBuf<int> ids_;
-  DevBuf<float> mel_keep_;
+  DevBuf<float> mel_keep_, cls_x_, cls_xn_, cls_logits_;
+  DevBuf<int> cls_ids_, cls_out_;
   // KV cache [slot][layers][kv][max_seq][128] f32
   DevBuf<float> kc_, vc_;
   int max_seq_ = 0;

@@ -770,6 +770,95 @@ std::string rust_trim(const std::string& s) {
 }
 
 // =====================================================================================
+// Forced aligner host steps (align.rs).
+// =====================================================================================
+bool align_split_words(const std::string& text, const std::string& language, std::vector<std::string>& words) {
+  words.clear();
+  const bool cjk = language == "Chinese" || language == "Japanese" || language == "Korean" || language == "Cantonese";
+  std::string cur;
+  size_t i = 0;
+  while (i < text.size()) {
+    const unsigned char c = (unsigned char)text[i];
+    const size_t len = c < 0x80 ? 1 : (c & 0xE0) == 0xC0 ? 2 : (c & 0xF0) == 0xE0 ? 3 : (c & 0xF8) == 0xF0 ? 4 : 0;
+    if (len == 0 || i + len > text.size()) return false;
+    const std::string ch = text.substr(i, len);
+    const auto cps = utf8_cps(ch);
+    if (cps.size() != 1) return false;
+    const bool ws = is_white_space_cp(cps[0]);
+    if (cjk) {
+      if (!ws) words.push_back(ch);  // text.chars().filter(!whitespace) (align.rs:51-55)
+    } else if (ws) {  // split_whitespace (align.rs:57-60)
+      if (!cur.empty()) words.push_back(cur);
+      cur.clear();
+    } else {
+      cur += ch;
+    }
+    i += len;
+  }
+  if (!cur.empty()) words.push_back(cur);
+  return true;
+}
+
+// align.rs:97-137: O(n^2) DP over "vals[j] <= vals[i]", the first longest end, traced back.
+std::vector<size_t> longest_increasing_subsequence(const std::vector<float>& v) {
+  const size_t n = v.size();
+  if (n == 0) return {};
+  const size_t none = (size_t)-1;
+  std::vector<size_t> dp(n, 1), prev(n, none);
+  for (size_t i = 1; i < n; ++i)
+    for (size_t j = 0; j < i; ++j)
+      if (v[j] <= v[i] && dp[j] + 1 > dp[i]) {
+        dp[i] = dp[j] + 1;
+        prev[i] = j;
+      }
+  size_t best_len = 0, best_end = 0;
+  for (size_t i = 0; i < n; ++i)
+    if (dp[i] > best_len) {
+      best_len = dp[i];
+      best_end = i;
+    }
+  std::vector<size_t> out;
+  for (size_t idx = best_end;; idx = prev[idx]) {
+    out.push_back(idx);
+    if (prev[idx] == none) break;
+  }
+  std::reverse(out.begin(), out.end());
+  return out;
+}
+
+// align.rs:140-189: entries off the longest non-decreasing subsequence are repaired, blocks
+// of <= 2 with the nearest normal value, longer blocks by linear interpolation.
+void fix_timestamps(std::vector<float>& ts) {
+  const size_t n = ts.size();
+  if (n <= 1) return;
+  const auto lis = longest_increasing_subsequence(ts);
+  if (lis.size() == n) return;
+  std::vector<char> normal(n, 0);
+  for (size_t i : lis) normal[i] = 1;
+  size_t i = 0;
+  while (i < n) {
+    if (normal[i]) {
+      ++i;
+      continue;
+    }
+    const size_t bs = i;
+    while (i < n && !normal[i]) ++i;
+    const size_t be = i, bl = be - bs;
+    const float left = bs > 0 ? ts[bs - 1] : 0.0f;
+    const float right = be < n ? ts[be] : left + (float)bl * 80.0f;
+    if (bl <= 2) {
+      const float fill = bs > 0 ? left : right;
+      for (size_t k = bs; k < be; ++k) ts[k] = fill;
+    } else {
+      for (size_t j = 0; j < bl; ++j) {
+        const float t = (float)(j + 1) / (float)(bl + 1);
+        ts[bs + j] = left + t * (right - left);
+      }
+    }
+  }
+}
+
+// =====================================================================================
 // Tables shared with the device, computed with the reference's f32 formulas.
 // =====================================================================================
 static float hz_to_mel(float f) {

@@ -88,6 +88,12 @@ bool should_insert_boundary_space(uint8_t prev, uint8_t next);
 // Rust str::trim (Unicode White_Space) and String::from_utf8_lossy.
 std::string utf8_lossy(const std::string& bytes);
 std::string rust_trim(const std::string& s);
+// Forced-aligner host steps (align.rs:44-61, 96-189): the units of `text` (CJK languages:
+// every non-white-space character; others: white-space separated words; false on invalid
+// UTF-8), the longest non-decreasing subsequence, and the timestamp repair.
+bool align_split_words(const std::string& text, const std::string& language, std::vector<std::string>& words);
+std::vector<size_t> longest_increasing_subsequence(const std::vector<float>& v);
+void fix_timestamps(std::vector<float>& ts);
 
 // Host tables shared with the device (built with the reference's f32 formulas).
 void build_mel_filters(std::vector<float>& filt);           // [128][201]  audio.rs:202-262

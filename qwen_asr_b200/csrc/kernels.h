@@ -88,6 +88,9 @@ void prefill_attention(const float* qkv, int S, int start, int n_heads, int n_kv
 // Gathers prompt rows: row r = ids[r] >= 0 ? embed[ids[r]] : enc[-ids[r]-1].
 void gather_embeds(const int* ids, int rows, const __nv_bfloat16* embed, const float* enc, int d, float* out,
                    cudaStream_t s);
+// Per-row argmax of f32 [rows][n] (the first index of the maximum, as align.rs:290-301's
+// strictly-greater scan picks it).
+void rows_argmax(const float* x, int rows, int n, int* out, cudaStream_t s);
 // Per-row symmetric int8 quantisation of a bf16 [rows][cols] matrix (load time).
 void quantize_rows_int8(const __nv_bfloat16* w, int rows, int cols, bool truncate, int8_t* q, float* scale,
                         cudaStream_t s);

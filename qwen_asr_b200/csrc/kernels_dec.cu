@@ -210,4 +210,55 @@ void quantize_rows_int8(const __nv_bfloat16* w, int rows, int cols, bool truncat
   if (rows > 0) quantize_rows_kernel<<<rows, 256, 0, s>>>(w, cols, truncate, q, scale);
 }
 
+// ------------------------------------------------------------------ row argmax
+// One block per row: each thread keeps its strided first maximum, then the block keeps the
+// larger value, or the smaller index between equal values (the first maximum overall).
+__global__ void rows_argmax_kernel(const float* __restrict__ x, int n, int* __restrict__ out) {
+  const float* r = x + (size_t)blockIdx.x * n;
+  float bv = -INFINITY;
+  int bi = 0x7FFFFFFF;  // no element seen
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = r[i];
+    if (bi == 0x7FFFFFFF || v > bv) {
+      bv = v;
+      bi = i;
+    }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    sv[w] = bv;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (w == 0) {
+    bv = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7FFFFFFF;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) out[blockIdx.x] = bi == 0x7FFFFFFF ? 0 : bi;
+  }
+}
+
+void rows_argmax(const float* x, int rows, int n, int* out, cudaStream_t s) {
+  if (rows > 0 && n > 0) rows_argmax_kernel<<<rows, 256, 0, s>>>(x, n, out);
+}
+
 }  // namespace qasr

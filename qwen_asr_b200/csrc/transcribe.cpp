@@ -758,4 +758,70 @@ bool Ctx::stream_push_many(const std::vector<const std::vector<float>*>& samples
   return true;
 }
 
+// align.rs:207-351. The prompt is the transcription prompt without prompt or language
+// tokens, followed by every word's tokens and two <timestamp> tokens after each word; one
+// prefill gives the classify-head argmax at every <timestamp> row (align.rs:275-301).
+bool Ctx::forced_align(const float* samples, size_t n, const std::string& text, const std::string& language,
+                       std::vector<AlignItem>& out) {
+  out.clear();
+  const Config& c = eng.cfg();
+  if (c.classify_num <= 0) {
+    set_error("align: model is not a forced aligner (classify_num=0)");
+    return false;
+  }
+  reset_perf();
+  perf_audio_ms = 1000.0 * (double)n / kSampleRate;
+  const double t0 = now_ms();
+  std::vector<std::string> words;
+  if (!align_split_words(text, language, words) || words.empty()) {
+    set_error("align: the text has no words");
+    return false;
+  }
+  std::vector<int> text_tokens;  // encode_timestamp (align.rs:66-93)
+  for (size_t i = 0; i < words.size(); ++i) {
+    std::vector<int> wt;
+    if (!tok.encode(words[i], wt)) {
+      set_error("align: cannot tokenize \"" + words[i] + "\"");
+      return false;
+    }
+    text_tokens.insert(text_tokens.end(), wt.begin(), wt.end());
+    text_tokens.push_back(kTokTimestamp);
+    text_tokens.push_back(kTokTimestamp);
+    if (i == 0 && wt.empty()) {
+      set_error("align: the first word yields no tokens");
+      return false;
+    }
+  }
+  StagePerf before = eng.perf;
+  const int F = eng.mel(samples, (int)n, false);
+  if (F <= 0) return false;
+  const int T = eng.encode(eng.mel_buf(), F);
+  if (T <= 0) return false;
+  std::vector<int> ids;
+  ids.insert(ids.end(), std::begin(kPrefixHead), std::end(kPrefixHead));
+  ids.insert(ids.end(), std::begin(kPrefixTail), std::end(kPrefixTail));
+  for (int i = 0; i < T; ++i) ids.push_back(-(i + 1));
+  ids.insert(ids.end(), std::begin(kSuffixBase), std::end(kSuffixBase));
+  const int text_off = (int)ids.size();
+  ids.insert(ids.end(), text_tokens.begin(), text_tokens.end());
+  std::vector<int> rows;
+  for (size_t i = 0; i < text_tokens.size(); ++i)
+    if (text_tokens[i] == kTokTimestamp) rows.push_back(text_off + (int)i);
+  std::vector<int> cls;
+  if (!eng.prefill_classify(ids, eng.enc_out(), rows, cls)) return false;
+  const float seg_time = 80.0f;  // timestamp_segment_time (config.rs:150)
+  std::vector<float> ts(cls.size());
+  for (size_t i = 0; i < cls.size(); ++i) ts[i] = (float)cls[i] * seg_time;
+  fix_timestamps(ts);
+  for (size_t i = 0; i < words.size(); ++i) {
+    const float s = 2 * i < ts.size() ? ts[2 * i] : 0.0f;
+    const float e = 2 * i + 1 < ts.size() ? ts[2 * i + 1] : s;
+    out.push_back({words[i], s, e});
+  }
+  perf_total_ms += now_ms() - t0;
+  perf_encode_ms += (eng.perf.mel_ms - before.mel_ms) + (eng.perf.enc_ms - before.enc_ms);
+  perf_decode_ms += eng.perf.prefill_ms - before.prefill_ms;
+  return true;
+}
+
 }  // namespace qasr

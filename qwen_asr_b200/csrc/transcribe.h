@@ -126,6 +126,15 @@ class Ctx {
   bool stream_chunk_assemble(const std::vector<float>& samples, StreamState& st, StreamChunk& w, bool defer_prefill);
   bool stream_chunk_finish(StreamState& st, StreamChunk& w, std::string& delta);
   void reset_perf();
+  // Forced alignment (align.rs:207-351): one unit (word, or character for CJK languages) per
+  // entry with its start/end in ms; false (with the error set) when the model is not an
+  // aligner, the text has no unit or encoding fails.
+  struct AlignItem {
+    std::string text;
+    float start_ms, end_ms;
+  };
+  bool forced_align(const float* samples, size_t n, const std::string& text, const std::string& language,
+                    std::vector<AlignItem>& out);
   // Transcribes the independent segments [starts[i], ends[i]) of `samples` (each padded to
   // 0.5 s as transcribe.rs:374-384 does), batching their decodes; texts[i] per segment.
   bool transcribe_segment_list(const float* samples, size_t n, const std::vector<std::pair<size_t, size_t>>& bounds,

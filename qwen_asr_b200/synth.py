@@ -31,7 +31,12 @@ PRESETS = {
     "1.7b": (1024, 24, 4096, 2048, 28, 6144, 16, 8),
     # Small shapes for CPU tests (loaded through the shape-inferring config path).
     "tiny": (128, 2, 256, 256, 2, 512, 4, 2),
+    # Forced aligner: the large (1.7B) encoder with the 0.6B decoder (config.rs:109-110) and
+    # an untied lm_head of classify classes (config.rs:145-151).
+    "aligner": (1024, 24, 4096, 1024, 28, 3072, 16, 8),
+    "tiny-aligner": (128, 2, 256, 256, 2, 512, 4, 2),
 }
+ALIGNER_CLASSES = {"aligner": 5000, "tiny-aligner": 300}
 
 
 def tensor_specs(preset: str):
@@ -80,6 +85,8 @@ def tensor_specs(preset: str):
                   (lp + "mlp.up_proj.weight", (inter, hid), "normal"),
                   (lp + "mlp.down_proj.weight", (hid, inter), "normal")]
     specs.append((m + "norm.weight", (hid,), "one"))
+    if preset in ALIGNER_CLASSES:
+        specs.append(("thinker.lm_head.weight", (ALIGNER_CLASSES[preset], hid), "normal"))
     return specs
 
 
