@@ -749,6 +749,12 @@ __global__ void __maxnreg__(96) mv_small_batch_kernel(const __grid_constant__ CU
 // rows of earlier positions (written by earlier steps; StepState is constant within a
 // step) are also pulled into shared memory before the wait. Split partials are merged
 // through distributed shared memory (no global atomics).
+// Split cluster barrier (arrive early, wait later). arrive.release / wait.acquire order the
+// distributed-shared-memory stores before the barrier with the local loads after it.
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
 struct QkvAttnArgs {
   const float* x;              // residual stream [K]
   const __nv_bfloat16* embed;  // layer 0: take x from embed[st->cur_token] when >= 0
@@ -810,7 +816,12 @@ qkv_attn_kernel(QkvAttnArgs a) {
   __shared__ __align__(16) float wo[kVW][MG][kHd];
   __shared__ float pm[MG], pl[MG];
   __shared__ __align__(16) float po[MG][kHd];
+  // receive buffers written by the cluster's CTAs (distributed shared memory pushes)
+  constexpr int kDimsPerCta = kHd / kSplits;
+  __shared__ float allv[PROJ ? (MG + 2) * kHd : 1];                // the group's projected rows
+  __shared__ float rcv_o[kSplits][MG][kDimsPerCta], rcv_m[kSplits][MG], rcv_l[kSplits][MG];
   cg::cluster_group cluster = cg::this_cluster();
+  cluster_arrive_relaxed();  // "started": peers may push into this CTA once they wait on it
   const int kvh = blockIdx.x, rank = blockIdx.y, d = threadIdx.x;
   const int warp = d >> 5, lane = d & 31;
   const int G = a.n_heads / a.n_kv;
@@ -975,7 +986,14 @@ qkv_attn_kernel(QkvAttnArgs a) {
       if (two) vals[rr + 1] = v1;
     }
   }
-  cluster.sync();  // every CTA's rows are ready
+  __syncthreads();
+  cluster_wait();  // every CTA of the cluster has started
+  for (int t = d; t < rpc * kSplits; t += kQA) {  // this CTA's rows into every CTA's allv
+    const int q = t / rpc, rr = t - q * rpc;
+    *cluster.map_shared_rank(&allv[g0 + rr], q) = vals[rr];
+  }
+  cluster_arrive();
+  cluster_wait();  // every CTA's rows have arrived
   }
 
   // ---- phase 2: gather this head group's raw q/k/v from the cluster
@@ -986,7 +1004,7 @@ qkv_attn_kernel(QkvAttnArgs a) {
   for (int g = 0; g < MG + 2; ++g) {
     int gi = g < G ? g * kHd + d : (g == MG ? G * kHd + d : (g == MG + 1 ? (G + 1) * kHd + d : -1));
     if (PROJ) {
-      raw[g] = hd && gi >= 0 ? *cluster.map_shared_rank(&vals[gi % rpc], gi / rpc) : 0.f;
+      raw[g] = hd && gi >= 0 ? allv[gi] : 0.f;
     } else {  // rows of the batched projection: q heads, then k, then v
       const int row = g < G ? (kvh * G + g) * kHd : g == MG ? (a.n_heads + kvh) * kHd : (a.n_heads + a.n_kv + kvh) * kHd;
       raw[g] = hd && gi >= 0 ? a.qkv[row + d] : 0.f;
@@ -1116,18 +1134,30 @@ qkv_attn_kernel(QkvAttnArgs a) {
       pl[g] = L;
     }
   }
-  cluster.sync();
+  // Push this split's partial of the dims each CTA finalises (CTA q: dims [q*8, q*8 + 8) of
+  // every head of the group), then one cluster barrier; nothing reads a peer afterwards.
+  __syncthreads();
+  if (!PROJ) cluster_wait();  // every CTA of the cluster has started
+  for (int i = d; i < G * kHd; i += kQA) {
+    const int g = i / kHd, dim = i - g * kHd, q = dim / kDimsPerCta;
+    *cluster.map_shared_rank(&rcv_o[rank][g][dim - q * kDimsPerCta], q) = po[g][dim];
+  }
+  if (d < G * kSplits) {
+    const int g = d / kSplits, q = d - g * kSplits;
+    *cluster.map_shared_rank(&rcv_m[rank][g], q) = pm[g];
+    *cluster.map_shared_rank(&rcv_l[rank][g], q) = pl[g];
+  }
+  cluster_arrive();
+  cluster_wait();
   tline.mark(3);
-  // CTA `rank` finalises dims [rank*8, rank*8 + 8) of every head of the group.
-  constexpr int kDimsPerCta = kHd / kSplits;
   if (d < G * kDimsPerCta) {
-    const int g = d / kDimsPerCta, dim = rank * kDimsPerCta + d % kDimsPerCta;
+    const int g = d / kDimsPerCta, dd = d % kDimsPerCta, dim = rank * kDimsPerCta + dd;
     float Ms[kSplits], Ls[kSplits], Os[kSplits];
 #pragma unroll
     for (int r = 0; r < kSplits; ++r) {
-      Ms[r] = *cluster.map_shared_rank(&pm[g], r);
-      Ls[r] = *cluster.map_shared_rank(&pl[g], r);
-      Os[r] = *cluster.map_shared_rank(&po[g][dim], r);
+      Ms[r] = rcv_m[r][g];
+      Ls[r] = rcv_l[r][g];
+      Os[r] = rcv_o[r][g][dd];
     }
     float M = -3.0e38f;
 #pragma unroll
@@ -1144,7 +1174,6 @@ qkv_attn_kernel(QkvAttnArgs a) {
     }
     a.out[(kvh * G + g) * kHd + dim] = __fdiv_rn(O, L);
   }
-  cluster.sync();  // peers may still be reading this CTA's shared memory
 }
 
 // ------------------------------------------------------------------ host side
