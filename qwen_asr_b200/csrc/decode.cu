@@ -145,6 +145,23 @@ __device__ __forceinline__ T warp_reduce8(const T (&v)[kMaxB], int lane) {
   return u;
 }
 
+// warp_reduce8 for four values: afterwards lane l holds value ((l >> 4) & 1) * 2 + ((l >> 3) & 1).
+template <typename T>
+__device__ __forceinline__ T warp_reduce4(const T (&v)[4], int lane) {
+  T s[2];
+  const bool h16 = lane & 16, h8 = lane & 8;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const T keep = h16 ? v[i + 2] : v[i], send = h16 ? v[i] : v[i + 2];
+    s[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+  T u = (h8 ? s[1] : s[0]) + __shfl_xor_sync(0xffffffffu, h8 ? s[0] : s[1], 8);
+  u += __shfl_xor_sync(0xffffffffu, u, 4);
+  u += __shfl_xor_sync(0xffffffffu, u, 2);
+  u += __shfl_xor_sync(0xffffffffu, u, 1);
+  return u;
+}
+
 template <int RPW>
 __device__ __forceinline__ int lane_row(int lane) {
   return RPW == 4 ? ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1) : (RPW == 2 ? (lane >> 4) : 0);
@@ -210,6 +227,12 @@ __device__ float stage_x(const MvArgs& a, int b, float* xs_b, int8_t* xq_b, cons
   return xscale;
 }
 
+// Batched bf16 staging keeps each 256-float chunk (one 512-byte weight chunk's inputs) so
+// that lane L's 8 floats sit in two halves at L*4 and 128 + L*4: the two 16-byte loads of a
+// warp each read 512 contiguous bytes (no bank conflicts). Float offset of the 4 elements
+// 4c..4c+3 within a sequence's vector:
+__device__ __forceinline__ int xperm4(int c) { return (c >> 6) * 256 + (c & 1) * 128 + ((c & 63) >> 1) * 4; }
+
 // Stages the input vectors of all B (> 1) sequences at once: read from x (layer 0: gathered
 // from the embedding, the rows also written to x_out by CTA 0), RMS-normalised when norm_w
 // is set, and for int8 weights quantised per vector (kernels/mod.rs:1795-1802) into xq[b]
@@ -232,15 +255,15 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
   }
   auto ldx = [&](int b, int c) -> float4 {
     const int bb = min(b, B - 1);
-    const float4 xv = *reinterpret_cast<const float4*>(a.x + (size_t)bb * a.ldx + 4 * c);
-    if (!a.embed) return xv;
-    // layer 0: the row of the sequence's current token (both loads issued, one kept)
-    const int tok = stok[bb];
-    const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(a.embed) +
-                                                    (size_t)max(tok, 0) * K + 4 * c);
-    const float4 ev = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
-                                  __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
-    return tok >= 0 ? ev : xv;
+    if (a.embed) {  // layer 0 (the q/k/v projection only): the row of the current token
+      const int tok = stok[bb];
+      if (tok >= 0) {
+        const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(a.embed) + (size_t)tok * K + 4 * c);
+        return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                           __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+      }
+    }
+    return *reinterpret_cast<const float4*>(a.x + (size_t)bb * a.ldx + 4 * c);
   };
   auto normed = [&](float4 v, float inv, int c) -> float4 {
     const float4 w = *reinterpret_cast<const float4*>(snw + 4 * c);
@@ -259,7 +282,7 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
   for (int i = K + tid; i < kpad; i += kThreads)  // padding past K multiplies zero weights
     for (int b = 0; b < B; ++b) {
       if (INT8) xq[(size_t)b * kpad + i] = 0;
-      else xs[(size_t)b * kpad + i] = 0.f;
+      else xs[(size_t)b * kpad + xperm4(i >> 2) + (i & 3)] = 0.f;
     }
   const bool has0 = tid < min(P, nc);
   const int c0 = has0 ? tid : 0;
@@ -271,21 +294,25 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
   for (int b = 0; b < kMaxB; ++b) {
     acc[b] = 0.f;
     if (!has0) continue;
-    if (!INT8 && b < B) *reinterpret_cast<float4*>(xs + (size_t)b * kpad + 4 * c0) = hold[b];
+    if (!INT8 && b < B) *reinterpret_cast<float4*>(xs + (size_t)b * kpad + xperm4(c0)) = hold[b];
     if (a.embed && blockIdx.x == 0 && b < B && stok[b] >= 0)
       *reinterpret_cast<float4*>(a.x_out + (size_t)b * a.ldx + 4 * c0) = hold[b];
     acc[b] = a.norm_w ? sumsq(0.f, hold[b]) : absmax(0.f, hold[b]);
   }
   for (int c = tid + P; c < nc && tid < P; c += P) {  // chunks j >= 1
-    float4 t[kMaxB];
 #pragma unroll
-    for (int b = 0; b < kMaxB; ++b) t[b] = ldx(b, c);
+    for (int h = 0; h < kMaxB; h += 4) {  // four sequences' loads in flight (registers)
+      float4 t[4];
 #pragma unroll
-    for (int b = 0; b < kMaxB; ++b) {
-      if (!INT8 && b < B) *reinterpret_cast<float4*>(xs + (size_t)b * kpad + 4 * c) = t[b];
-      if (a.embed && blockIdx.x == 0 && b < B && stok[b] >= 0)
-        *reinterpret_cast<float4*>(a.x_out + (size_t)b * a.ldx + 4 * c) = t[b];
-      acc[b] = a.norm_w ? sumsq(acc[b], t[b]) : absmax(acc[b], t[b]);
+      for (int i = 0; i < 4; ++i) t[i] = ldx(h + i, c);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int b = h + i;
+        if (!INT8 && b < B) *reinterpret_cast<float4*>(xs + (size_t)b * kpad + xperm4(c)) = t[i];
+        if (a.embed && blockIdx.x == 0 && b < B && stok[b] >= 0)
+          *reinterpret_cast<float4*>(a.x_out + (size_t)b * a.ldx + 4 * c) = t[i];
+        acc[b] = a.norm_w ? sumsq(acc[b], t[i]) : absmax(acc[b], t[i]);
+      }
     }
   }
   // per-sequence block reduction: warp butterflies, then warp b combines the 16 warp values
@@ -320,16 +347,19 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
         acc[b] = has0 ? absmax(0.f, hold[b]) : 0.f;
       }
       for (int c = tid + P; c < nc && tid < P; c += P) {
-        float4 t[kMaxB];
 #pragma unroll
-        for (int b = 0; b < kMaxB; ++b) t[b] = ldx(b, c);
+        for (int h = 0; h < kMaxB; h += 4) {
+          float4 t[4];
 #pragma unroll
-        for (int b = 0; b < kMaxB; ++b) acc[b] = absmax(acc[b], normed(t[b], sinv[min(b, B - 1)], c));
+          for (int i = 0; i < 4; ++i) t[i] = ldx(h + i, c);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[h + i] = absmax(acc[h + i], normed(t[i], sinv[min(h + i, B - 1)], c));
+        }
       }
     } else {
       for (int i = tid; i < B * nc; i += kThreads) {
         const int b = i / nc, c = i - b * nc;
-        float4* p = reinterpret_cast<float4*>(xs + (size_t)b * kpad + 4 * c);
+        float4* p = reinterpret_cast<float4*>(xs + (size_t)b * kpad + xperm4(c));
         *p = normed(*p, sinv[b], c);
       }
     }
@@ -348,12 +378,15 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
     for (int b = 0; b < kMaxB; ++b)
       if (has0 && b < B) quant(b, c0, hold[b]);
     for (int c = tid + P; c < nc && tid < P; c += P) {
-      float4 t[kMaxB];
 #pragma unroll
-      for (int b = 0; b < kMaxB; ++b) t[b] = ldx(b, c);
+      for (int h = 0; h < kMaxB; h += 4) {
+        float4 t[4];
 #pragma unroll
-      for (int b = 0; b < kMaxB; ++b)
-        if (b < B) quant(b, c, a.norm_w ? normed(t[b], sinv[b], c) : t[b]);
+        for (int i = 0; i < 4; ++i) t[i] = ldx(h + i, c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (h + i < B) quant(h + i, c, a.norm_w ? normed(t[i], sinv[h + i], c) : t[i]);
+      }
     }
   }
   __syncthreads();
@@ -516,9 +549,9 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__
 #pragma unroll
       for (int b = 0; b < kMaxB; ++b) {
         if (b >= B) break;
-        const float* xb = xs + (size_t)b * kpad + kc * (kChunk / 2) + lane * 8;
+        const float* xb = xs + (size_t)b * kpad + kc * (kChunk / 2) + lane * (BATCH ? 4 : 8);
         const float4 x0 = *reinterpret_cast<const float4*>(xb);
-        const float4 x1 = *reinterpret_cast<const float4*>(xb + 4);
+        const float4 x1 = *reinterpret_cast<const float4*>(xb + (BATCH ? 128 : 4));
 #pragma unroll
         for (int r = 0; r < RPW; ++r) {
           float acc = facc[r][b];
@@ -632,39 +665,66 @@ __device__ __forceinline__ void mv_small_body(const CUtensorMap& wmap, const MvA
   }
   mbar_wait(&bar, 0, a.err, 5);
   if (BATCH) {
-    // one (row, chunk) weight item per warp pass, dotted with every sequence's vector
-    const int sel = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
-    for (int it = warp; it < R * nkc; it += kWarps) {
-      const int r = it / nkc, kc = it % nkc;
-      const uint4 wv = *reinterpret_cast<const uint4*>(wst + ((size_t)kc * R + r) * kChunk + lane * 16);
-      if (INT8) {
-        int acc[kMaxB];
+    // items of kRG rows x one 512-byte chunk: each sequence's input chunk is read once and
+    // dotted with the kRG rows (rows past R repeat row R - 1 and are dropped; sequences past
+    // B repeat sequence B - 1 and are dropped); every (row, sequence) dot product keeps the
+    // single-sequence kernel's arithmetic
+    constexpr int kRG = 4;
+    const int sel = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);  // warp_reduce4's value index
+    const int ngroups = (R + kRG - 1) / kRG;
+    for (int it = warp; it < ngroups * nkc; it += kWarps) {
+      const int rg = it / nkc, kc = it - rg * nkc, rb = rg * kRG;
+      uint4 wv[kRG];
 #pragma unroll
-        for (int b = 0; b < kMaxB; ++b) {  // rows past B repeat row B - 1 and are dropped
-          const int4 xv = *reinterpret_cast<const int4*>(xq + (size_t)min(b, B - 1) * kpad + kc * kChunk + lane * 16);
-          acc[b] = __dp4a((int)wv.x, xv.x, 0);
-          acc[b] = __dp4a((int)wv.y, xv.y, acc[b]);
-          acc[b] = __dp4a((int)wv.z, xv.z, acc[b]);
-          acc[b] = __dp4a((int)wv.w, xv.w, acc[b]);
-        }
-        const int u = warp_reduce8(acc, lane);
-        if ((lane & 3) == 0 && sel < B) part[((size_t)sel * R + r) * nkc + kc] = __int_as_float(u);
-      } else {
-        float f[8], acc[kMaxB];
-        bf16x8_to_f32(wv, f);
+      for (int j = 0; j < kRG; ++j)
+        wv[j] = *reinterpret_cast<const uint4*>(wst + ((size_t)kc * R + min(rb + j, R - 1)) * kChunk + lane * 16);
+      for (int bh = 0; bh < kMaxB / 4 && bh * 4 < B; ++bh) {  // sequences in groups of four
+        if (INT8) {
+          int acc[kRG][4];
 #pragma unroll
-        for (int b = 0; b < kMaxB; ++b) {
-          const float* xb = xs + (size_t)min(b, B - 1) * kpad + kc * (kChunk / 2) + lane * 8;
-          const float4 x0 = *reinterpret_cast<const float4*>(xb);
-          const float4 x1 = *reinterpret_cast<const float4*>(xb + 4);
-          float s = f[0] * x0.x;
-          s = fmaf(f[1], x0.y, s); s = fmaf(f[2], x0.z, s); s = fmaf(f[3], x0.w, s);
-          s = fmaf(f[4], x1.x, s); s = fmaf(f[5], x1.y, s); s = fmaf(f[6], x1.z, s);
-          s = fmaf(f[7], x1.w, s);
-          acc[b] = s;
+          for (int i = 0; i < 4; ++i) {
+            const int b = min(bh * 4 + i, B - 1);
+            const int4 xv = *reinterpret_cast<const int4*>(xq + (size_t)b * kpad + kc * kChunk + lane * 16);
+#pragma unroll
+            for (int j = 0; j < kRG; ++j) {
+              acc[j][i] = __dp4a((int)wv[j].x, xv.x, 0);
+              acc[j][i] = __dp4a((int)wv[j].y, xv.y, acc[j][i]);
+              acc[j][i] = __dp4a((int)wv[j].z, xv.z, acc[j][i]);
+              acc[j][i] = __dp4a((int)wv[j].w, xv.w, acc[j][i]);
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < kRG; ++j) {
+            const int u = warp_reduce4(acc[j], lane);
+            const int b = bh * 4 + sel;
+            if ((lane & 7) == 0 && b < B && rb + j < R) part[((size_t)b * R + rb + j) * nkc + kc] = __int_as_float(u);
+          }
+        } else {
+          float acc[kRG][4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int b = min(bh * 4 + i, B - 1);
+            const float* xb = xs + (size_t)b * kpad + kc * (kChunk / 2) + lane * 4;
+            const float4 x0 = *reinterpret_cast<const float4*>(xb);
+            const float4 x1 = *reinterpret_cast<const float4*>(xb + 128);
+#pragma unroll
+            for (int j = 0; j < kRG; ++j) {
+              float f[8];
+              bf16x8_to_f32(wv[j], f);
+              float s = f[0] * x0.x;
+              s = fmaf(f[1], x0.y, s); s = fmaf(f[2], x0.z, s); s = fmaf(f[3], x0.w, s);
+              s = fmaf(f[4], x1.x, s); s = fmaf(f[5], x1.y, s); s = fmaf(f[6], x1.z, s);
+              s = fmaf(f[7], x1.w, s);
+              acc[j][i] = s;
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < kRG; ++j) {
+            const float u = warp_reduce4(acc[j], lane);
+            const int b = bh * 4 + sel;
+            if ((lane & 7) == 0 && b < B && rb + j < R) part[((size_t)b * R + rb + j) * nkc + kc] = u;
+          }
         }
-        const float u = warp_reduce8(acc, lane);
-        if ((lane & 3) == 0 && sel < B) part[((size_t)sel * R + r) * nkc + kc] = u;
       }
     }
   }
