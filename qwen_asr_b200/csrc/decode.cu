@@ -669,6 +669,37 @@ __device__ __forceinline__ void mv_small_body(const CUtensorMap& wmap, const MvA
     // dotted with the kRG rows (rows past R repeat row R - 1 and are dropped; sequences past
     // B repeat sequence B - 1 and are dropped); every (row, sequence) dot product keeps the
     // single-sequence kernel's arithmetic
+    if constexpr (INT8) {
+    // int8: items of 2 rows x one chunk, all sequences at once (16-byte conflict-free input
+    // loads make the input cheap; the 8-value reduction keeps the shuffle count low)
+    constexpr int kRG = 2;
+    const int sel = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+    const int ngroups = (R + kRG - 1) / kRG;
+    for (int it = warp; it < ngroups * nkc; it += kWarps) {
+      const int rg = it / nkc, kc = it - rg * nkc, rb = rg * kRG;
+      uint4 wv[kRG];
+#pragma unroll
+      for (int j = 0; j < kRG; ++j)
+        wv[j] = *reinterpret_cast<const uint4*>(wst + ((size_t)kc * R + min(rb + j, R - 1)) * kChunk + lane * 16);
+      int acc[kRG][kMaxB];
+#pragma unroll
+      for (int b = 0; b < kMaxB; ++b) {
+        const int4 xv = *reinterpret_cast<const int4*>(xq + (size_t)min(b, B - 1) * kpad + kc * kChunk + lane * 16);
+#pragma unroll
+        for (int j = 0; j < kRG; ++j) {
+          acc[j][b] = __dp4a((int)wv[j].x, xv.x, 0);
+          acc[j][b] = __dp4a((int)wv[j].y, xv.y, acc[j][b]);
+          acc[j][b] = __dp4a((int)wv[j].z, xv.z, acc[j][b]);
+          acc[j][b] = __dp4a((int)wv[j].w, xv.w, acc[j][b]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kRG; ++j) {
+        const int u = warp_reduce8(acc[j], lane);
+        if ((lane & 3) == 0 && sel < B && rb + j < R) part[((size_t)sel * R + rb + j) * nkc + kc] = __int_as_float(u);
+      }
+    }
+    } else {
     constexpr int kRG = 4;
     const int sel = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);  // warp_reduce4's value index
     const int ngroups = (R + kRG - 1) / kRG;
@@ -679,7 +710,7 @@ __device__ __forceinline__ void mv_small_body(const CUtensorMap& wmap, const MvA
       for (int j = 0; j < kRG; ++j)
         wv[j] = *reinterpret_cast<const uint4*>(wst + ((size_t)kc * R + min(rb + j, R - 1)) * kChunk + lane * 16);
       for (int bh = 0; bh < kMaxB / 4 && bh * 4 < B; ++bh) {  // sequences in groups of four
-        if (INT8) {
+        if (false) {
           int acc[kRG][4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -728,6 +759,7 @@ __device__ __forceinline__ void mv_small_body(const CUtensorMap& wmap, const MvA
       }
     }
   }
+    }
   const int items = BATCH ? 0 : B * R * nkc;
   for (int it = warp; it < items; it += kWarps) {
     const int b = it / (R * nkc), r = (it / nkc) % R, kc = it % nkc;
@@ -1241,6 +1273,7 @@ namespace {
 constexpr int kSmemBudget = 112 * 1024;  // two decode kernels co-reside on one SM
 constexpr size_t kSmallSmemMax = 200 * 1024;
 constexpr int kAttnKvRows = 16;  // K/V rows per CTA staged before the wait (attention-only kernel)
+constexpr size_t kSplitSlabBytes = 64 * 1024;  // single-sequence split above this slab (1.7B bf16)
 
 struct MvPlan {
   int grid, rows_per_cta, block_rows, nkc, stages;
@@ -1303,10 +1336,10 @@ void launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
 }
 
 template <bool INT8, int EPI>
-void mv_launch(const CUtensorMap& map, const MvArgs& m, const MvPlan& p, cudaStream_t s, bool pdl) {
+void mv_launch(const CUtensorMap& map, const MvArgs& m, const MvPlan& p, cudaStream_t s, bool pdl, bool batch) {
   const int rpw = p.block_rows / kWarps;
   const dim3 g(p.grid), t(kThreads);
-  if (m.B > 1) {
+  if (batch) {
     if (rpw == 4) launch_ex(mv_kernel<INT8, EPI, 4, true>, g, t, p.smem, s, pdl, 1, map, m);
     else if (rpw == 2) launch_ex(mv_kernel<INT8, EPI, 2, true>, g, t, p.smem, s, pdl, 1, map, m);
     else launch_ex(mv_kernel<INT8, EPI, 1, true>, g, t, p.smem, s, pdl, 1, map, m);
@@ -1343,7 +1376,11 @@ bool small_ok(int N, int K, bool int8, int B, int num_sms) {
 // allow_small = false keeps the streaming kernel, whose f32 dot products accumulate each
 // lane's chunks in order before one warp reduction (the fused QKV kernel's order).
 template <int EPI>
-void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pdl = true, bool allow_small = true) {
+// batch_kernels selects the batched instantiations also for B = 1 (their staging order is
+// the one sum_threads names).
+void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pdl = true, bool allow_small = true,
+        bool batch_kernels = false) {
+  const bool batch = m.B > 1 || batch_kernels;
   const int row_bytes = m.K * (int8 ? 1 : 2);
   int rpc = 0, nkc = 0;
   const size_t smem_small = small_smem(m.N, m.K, int8, m.B, num_sms, &rpc, &nkc);
@@ -1358,7 +1395,7 @@ void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pd
     }
     dim3 grid((m.N + rpc - 1) / rpc);
     const dim3 t(kThreads);
-    if (m.B > 1) {
+    if (batch) {
       if (int8) launch_ex(mv_small_batch_kernel<true, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
       else launch_ex(mv_small_batch_kernel<false, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
     } else {
@@ -1381,8 +1418,8 @@ void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pd
     set_error("decode: cannot encode the weight tensor map");
     return;
   }
-  if (int8) mv_launch<true, EPI>(map, m, p, s, pdl);
-  else mv_launch<false, EPI>(map, m, p, s, pdl);
+  if (int8) mv_launch<true, EPI>(map, m, p, s, pdl, batch);
+  else mv_launch<false, EPI>(map, m, p, s, pdl, batch);
 }
 
 template <bool INT8, int EPI>
@@ -1425,6 +1462,20 @@ void decode_kernels_init() {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   }
+}
+
+// A single sequence also takes the split q/k/v path (batched matvec + attention-only
+// kernel) when the fused kernel's per-CTA weight slab is large: each CTA of the fused kernel
+// fetches (G + 2) * 128 / kSplits rows, which for 1.7B bf16 is 128 KB and arrives too late to
+// overlap. Both paths give the same bits.
+bool decode_split_qkv(int hidden, int q_heads, int kv_heads, bool int8) {
+  static const int env = [] {
+    const char* e = getenv("QASR_SPLIT_QKV");
+    return e ? atoi(e) : -1;
+  }();
+  if (env >= 0) return env != 0;
+  const size_t slab = (size_t)(q_heads / kv_heads + 2) * kHd / kSplits * hidden * (int8 ? 1 : 2);
+  return slab > kSplitSlabBytes;
 }
 
 int decode_max_batch(int hidden, int inter, int q_heads, int kv_heads, bool int8) {
@@ -1487,13 +1538,14 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
     m.B = B;
     return m;
   };
+  const bool split = B > 1 || decode_split_qkv(a.hidden, a.q_heads, a.kv_heads, a.int8);
   for (int l = 0; l < a.layers; ++l) {
     // QKV projection + attention, one cluster per (kv head, sequence). The first kernel of a
     // step is a plain launch: it starts only after the previous step (which advanced
     // StepState and wrote the last KV row) has completed, so every kernel of the step may
     // read StepState and earlier KV rows before its dependency wait.
     const int nqkv = (a.q_heads + 2 * a.kv_heads) * kHd;
-    if (B > 1) {
+    if (split) {
       // batched steps: one matvec projects q/k/v of every sequence (input RMSNorm fused,
       // staged in the fused kernel's summation order), then the attention-only kernel
       MvArgs m = base(0);
@@ -1504,7 +1556,7 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
       }
       m.norm_w = a.n1[l]; m.K = a.hidden; m.N = nqkv; m.ws = a.s_qkv[l]; m.out = a.qkv; m.ldo = nqkv;
       m.sum_threads = a.int8 ? qa_threads<true>() : qa_threads<false>();
-      mv<MV_STORE>(a.int8, a.w_qkv[l], m, nsm, s, l != 0, a.int8);
+      mv<MV_STORE>(a.int8, a.w_qkv[l], m, nsm, s, l != 0, a.int8, true);
       if (a.on_launch) a.on_launch(a.hook_ctx, 0);
       check("qkv_proj", l);
     }
@@ -1526,7 +1578,7 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
       q.ldx = a.hidden; q.ldo = qd; q.kv_slot_stride = a.kv_slot_stride;
       const dim3 grid(a.kv_heads, kSplits, B);
       const bool g2 = a.q_heads <= 2 * a.kv_heads;  // group arrays sized for 2 q heads
-      if (B > 1) {
+      if (split) {
         q.embed = nullptr;
         q.x_out = nullptr;
         q.qkv = a.qkv;

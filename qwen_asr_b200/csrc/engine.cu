@@ -840,7 +840,10 @@ void Engine::enqueue_step(const DecodeArgs& a) {
 }
 
 // qkv+attention, o, gate/up, down per layer, then lm_head (batched steps add a q/k/v matvec)
-int Engine::decode_step_launches_1() const { return 4 * cfg_.dec_layers + 1; }
+int Engine::decode_step_launches_1() const {
+  const bool split = decode_split_qkv(cfg_.dec_hidden, cfg_.dec_heads, cfg_.dec_kv_heads, mode_ == DECODE_INT8);
+  return (split ? 5 : 4) * cfg_.dec_layers + 1;
+}
 
 bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, const std::vector<int>* forced,
                     std::vector<float>* logits, int slot) {
@@ -1175,7 +1178,7 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
     return false;
   }
   CUDA_OK(cudaGetLastError(), false);
-  launches += (long)launched * (decode_step_launches_1() + (B > 1 ? cfg_.dec_layers : 0));
+  launches += (long)launched * (B > 1 ? 5 * cfg_.dec_layers + 1 : decode_step_launches_1());
   int herr = 0;
   CUDA_OK(cudaMemcpy(&herr, derr_.p, sizeof(int), cudaMemcpyDeviceToHost), false);
   if (herr) {

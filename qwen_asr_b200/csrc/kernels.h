@@ -164,6 +164,8 @@ constexpr int kDecodeMaxBatch = 8;
 constexpr int kMaxSlots = 64;  // KV slots / decode states an engine can hold
 // Largest batch the decode kernels' shared memory admits for this model shape.
 int decode_max_batch(int hidden, int inter, int q_heads, int kv_heads, bool int8);
+// Whether a single-sequence step projects q/k/v with a separate matvec (5 kernels per layer).
+bool decode_split_qkv(int hidden, int q_heads, int kv_heads, bool int8);
 // Persistent one-launch decode step for a single sequence (decode_mega.cu). mega_create
 // returns nullptr when the device or the model shape is not supported; the state holds the
 // weight tensor maps of the decode mode of `a` (int8 or bf16).

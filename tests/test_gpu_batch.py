@@ -108,3 +108,34 @@ def test_persistent_decode_transcript_matches_chain(Q, tiny_dir):
     # the two paths sum in different orders: ids agree except at near-ties
     a, b = np.asarray(out[0][1][0]), np.asarray(out[1][1][0])
     assert a.shape == b.shape and float(np.mean(a == b)) >= 0.9
+
+
+_SPLIT_SCRIPT = r"""
+import sys, numpy as np
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/tests")
+import qwen_asr_b200 as Q
+from qwen_asr_b200 import synth
+eng = Q.Engine(sys.argv[2]); eng.set_decode_mode(sys.argv[3]); eng.set_force_n_tokens(12)
+eng.set_record_logits(True)
+eng.transcribe_pcm(synth.synth_audio(16000 * 25, seed=74))
+np.save(sys.argv[4], eng.recorded_logits())
+"""
+
+
+@pytest.mark.parametrize("mode", ["int8", "bf16"])
+def test_split_qkv_path_is_bit_identical(tiny_dir, mode, tmp_path):
+    """A single sequence may decode through the fused q/k/v+attention kernel or through the
+    split path (batched matvec + attention-only kernel, chosen for large weight slabs); both
+    give the same final-step logits bit for bit."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = []
+    for split in ("0", "1"):
+        f = str(tmp_path / f"l{split}.npy")
+        env = dict(os.environ, QASR_SPLIT_QKV=split)
+        subprocess.run([sys.executable, "-c", _SPLIT_SCRIPT, root, tiny_dir, mode, f], env=env, check=True)
+        out.append(np.load(f))
+    assert out[0].size > 0 and out[0].shape == out[1].shape
+    assert np.array_equal(out[0].view(np.uint32), out[1].view(np.uint32))
