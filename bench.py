@@ -155,15 +155,19 @@ def model_dir(preset, seed, world, rank, local):
 
 
 # ------------------------------------------------------------------------ CPU baseline
-def cpu_sample(preset, n_samples, seed, tokens, mode, wseed, model_path, n_decode=2, model=None):
-    """One bounded sample of the workload on the host with the oracle (the numpy
-    restatement of the reference's CPU path): mel + encoder + prefill of the full clip,
-    then `n_decode` greedy decode steps; decode time is extrapolated to `tokens`.
-    Returns (audio-sec/sec, seconds measured, model)."""
+def cpu_sample(preset, n_samples, seed, tokens, mode, wseed, model_path, model=None, prep=None):
+    """One full transcription of the workload on the host, measured end to end (nothing
+    extrapolated): mel + encoder + prefill of the whole clip with the numpy restatement of the
+    reference's CPU path (oracle/qwen_oracle.py, float32 sgemm on every core), then all
+    `tokens` greedy decode steps with the C restatement of decoder_forward
+    (oracle/decode_ref.c, OpenMP over every core). Returns (audio-sec/sec, seconds, model, prep)."""
+    import numpy as np
     from oracle import qwen_oracle as O
+    from oracle import ref_decode as R
     from qwen_asr_b200 import synth
     if model is None:
         model = O.Model(model_path, decode_mode=mode)
+        prep = R.Prepared(model)
     x = synth.synth_audio(n_samples, seed)
     t0 = time.perf_counter()
     mel = O.mel_spectrogram(x)
@@ -173,28 +177,40 @@ def cpu_sample(preset, n_samples, seed, tokens, mode, wseed, model_path, n_decod
     rows = O.prompt_rows(ctx, enc)
     dec = O.Decoder(model)
     dec.prefill(rows[:-1])
+    ids, _ = R.decode(prep, dec, rows[-1], tokens)
     t1 = time.perf_counter()
-    tok = dec.forward(rows[-1])
-    for _ in range(n_decode - 1):
-        tok = dec.forward(model.embed(tok))
-    t2 = time.perf_counter()
-    per_tok = (t2 - t1) / n_decode
-    total = (t1 - t0) + tokens * per_tok
-    return (n_samples / 16000.0) / total, t2 - t0, model
+    assert len(ids) == tokens and np.all(ids >= 0)
+    return (n_samples / 16000.0) / (t1 - t0), t1 - t0, model, prep
 
 
-def all_host_threads():
-    """BLAS thread pool sized to every host core (torchrun sets OMP_NUM_THREADS=1)."""
-    from threadpoolctl import threadpool_limits
-    return threadpool_limits(limits=os.cpu_count())
-
-
-def cpu_threads():
+def host_cpu():
+    """CPU model, logical and physical core counts of this host."""
+    model, phys = None, set()
     try:
-        from threadpoolctl import threadpool_info
-        return max(int(i.get("num_threads", 1)) for i in threadpool_info()) or os.cpu_count()
-    except Exception:
-        return os.cpu_count()
+        cur = {}
+        for line in open("/proc/cpuinfo"):
+            k, _, v = line.partition(":")
+            k, v = k.strip(), v.strip()
+            if k == "model name" and model is None:
+                model = v
+            if k in ("physical id", "core id"):
+                cur[k] = v
+            if not line.strip():
+                if cur:
+                    phys.add((cur.get("physical id"), cur.get("core id")))
+                cur = {}
+    except OSError:
+        pass
+    return {"model": model, "logical": os.cpu_count(), "physical": len(phys) or None}
+
+
+def set_host_threads(n):
+    """BLAS pool (numpy sgemm) and OpenMP pool (C decode) sized to n threads (torchrun sets
+    OMP_NUM_THREADS=1, so both are set explicitly)."""
+    from threadpoolctl import threadpool_limits
+    from oracle import ref_decode as R
+    R.set_threads(n)
+    return threadpool_limits(limits=n)
 
 
 # ------------------------------------------------------------------------ main arms
@@ -202,32 +218,41 @@ def run_reference(args, world, rank, local):
     if rank != 0:
         return
     preset, n, seed, tokens, mode, wseed = CONFIGS[args.config]
+    if args.tokens:
+        tokens = args.tokens
     from qwen_asr_b200 import synth
     d = os.path.join(os.environ.get("QASR_BENCH_DIR", "/tmp/qasr_bench"), f"{preset}-s{wseed}")
     synth.write_model(d, preset, wseed, device="cpu")  # same file as the GPU arm writes
-    all_host_threads()
-    model = None
+    cpu = host_cpu()
+    threads = cpu["logical"]
+    set_host_threads(threads)
+    model = prep = None
     for _ in range(args.warmup):
-        _, _, model = cpu_sample(preset, n, seed, tokens, mode, wseed, d, model=model)
-    vals, secs = [], []
+        _, _, model, prep = cpu_sample(preset, n, seed, tokens, mode, wseed, d, model, prep)
+    secs = []
     for _ in range(args.steps):
-        v, s, model = cpu_sample(preset, n, seed, tokens, mode, wseed, d, model=model)
-        vals.append(v)
+        _, s, model, prep = cpu_sample(preset, n, seed, tokens, mode, wseed, d, model, prep)
         secs.append(s)
-    value = statistics.mean(vals)
-    sample = (f"per step: mel+encoder+prefill of the full {n / 16000:.1f} s clip + 2 decode steps, decode "
-              f"extrapolated to {tokens} tokens")
+    total = sum(secs)
+    value = args.steps * (n / 16000.0) / total
+    t16 = min(16, threads)
+    set_host_threads(t16)
+    v16, s16, _, _ = cpu_sample(preset, n, seed, tokens, mode, wseed, d, model, prep)
+    sample = (f"every step one full transcription of the {n / 16000:.1f} s clip: numpy mel+encoder+prefill and "
+              f"all {tokens} decode steps in C, measured")
     line = {
         "impl": "reference", "metric": "audio-sec/sec", "value": round(value, 4), "unit": "audio-s/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1000 * (n / 16000.0) / value, 2), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(1000 * total / args.steps, 2), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8+f32" if mode == "int8" else "bf16+f32", "data": "synthetic",
         "config": config_dict(args.config, world),
-        "cpu_baseline": {"value": round(value, 4), "unit": "audio-s/s", "cores": cpu_threads(), "kind": "port",
-                         "sample": sample},
+        "cpu_baseline": {"value": round(value, 4), "unit": "audio-s/s", "cores": threads, "kind": "port",
+                         "sample": sample, "cpu": cpu,
+                         f"at_{t16}_threads": {"value": round(v16, 4), "seconds": round(s16, 2)}},
         "e2e": {"value": round(value, 4), "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "reference = numpy restatement of the reference CPU path (oracle/); the Rust reference cannot be "
-                "built here (no cargo) and its int8 decode is unimplemented on x86_64",
+        "note": "reference = restatement of the reference CPU path (oracle/qwen_oracle.py numpy + oracle/decode_ref.c "
+                "OpenMP decode); the Rust reference cannot be built here (no cargo) and its int8 decode is "
+                "unimplemented on x86_64",
     }
     print(json.dumps(line), flush=True)
 
@@ -459,14 +484,15 @@ def run_ours(args, world, rank, local):
     if rank == 0:
         cb = None
         if not args.no_cpu_baseline:
+            cpu = host_cpu()
             try:
-                all_host_threads()
-                v1, s1, model = cpu_sample(preset, n, seed, tokens, mode, wseed, d)
-                cb = {"value": round(v1, 4), "unit": "audio-s/s", "cores": cpu_threads(), "kind": "port",
-                      "sample": f"mel+encoder+prefill of the full {n / 16000:.1f} s clip + 2 decode steps on the host "
-                                f"({s1:.1f} s), decode extrapolated to {tokens} tokens"}
+                set_host_threads(cpu["logical"])
+                v1, s1, _, _ = cpu_sample(preset, n, seed, tokens, mode, wseed, d)
+                cb = {"value": round(v1, 4), "unit": "audio-s/s", "cores": cpu["logical"], "kind": "port",
+                      "sample": f"one full transcription of the {n / 16000:.1f} s clip on the host ({s1:.1f} s): numpy "
+                                f"mel+encoder+prefill and all {tokens} decode steps in C, measured", "cpu": cpu}
             except Exception as ex:  # the baseline must not break the GPU line
-                cb = {"value": None, "unit": "audio-s/s", "cores": cpu_threads(), "kind": "port",
+                cb = {"value": None, "unit": "audio-s/s", "cores": cpu["logical"], "kind": "port",
                       "sample": f"failed: {ex}"}
         line = {
             "metric": "audio-sec/sec", "value": round(value, 3), "unit": "audio-s/s", "n_gpus": world,

@@ -122,6 +122,23 @@ int32_t qwen_asr_debug_decode(QwenAsrEngine* engine, const float* rows, int32_t 
  * Host buffers. Returns 0, or < 0 on error. (Parity hook for the contraction kernels.) */
 int32_t qwen_asr_debug_gemm(int32_t M, int32_t N, int32_t K, const float* A, const uint16_t* B, const float* bias,
                             const float* resid, int32_t epi, int32_t impl, float* C);
+/* Bf16-weight GEMMs that could not run on the tensor cores since the library loaded (each
+ * one also failed its stage with an error); 0 in a healthy process. */
+int64_t qwen_asr_gemm_fallbacks(void);
+/* KV cache (decoder.rs:185-253) of one slot and layer: k, v [kv_heads][n_pos][128] f32 for
+ * positions 0..n_pos-1 (slot 0 = the offline path). Returns 0 or -1. */
+int32_t qwen_asr_debug_kv(QwenAsrEngine* engine, int32_t slot, int32_t layer, int32_t n_pos, float* k, float* v);
+/* Current KV capacity in positions (KvCache::max_seq). */
+int32_t qwen_asr_debug_kv_capacity(QwenAsrEngine* engine);
+/* Grows the KV cache to hold `needed` positions by doubling, keeping the rows already
+ * written (KvCache::grow, decoder.rs:199-231). Returns the new capacity or -1. */
+int32_t qwen_asr_debug_grow_kv(QwenAsrEngine* engine, int32_t needed);
+/* Device int8 weights of one decoder matrix (which: 0 q/k/v rows [q | k | v], 1 o, 2 gate/up
+ * rows interleaved gate0, up0, ..., 3 down, 4 lm_head) as quantised at load
+ * (kernels/mod.rs:1805-1829 / kernels/neon.rs:636-694): q [rows][cols], s [rows]. Returns
+ * the row count (nothing copied when it exceeds cap_rows) or -1. */
+int64_t qwen_asr_debug_quant(QwenAsrEngine* engine, int32_t layer, int32_t which, int8_t* q, float* s,
+                             int64_t cap_rows);
 
 /* ---- allocation-free mel front end (no counterpart in the reference) ----
  * For callers that must not allocate device memory during a call: processes holding a
@@ -157,6 +174,9 @@ int64_t qwen_asr_debug_compact_silence(const float* samples, int64_t n, float* o
 /* String::from_utf8_lossy + str::trim as used on transcripts (transcribe.rs:237-238). */
 int32_t qwen_asr_debug_lossy_trim(const char* bytes, int32_t n, char* out, int32_t cap);
 /* normalize_language (config.rs:167-182); "" when unsupported. */
+/* 1 when the NUL-terminated bytes are strict UTF-8 as CStr::to_str accepts them (the check
+ * qwen_asr_load_model, qwen_asr_transcribe_file and qwen_asr_set_language apply), else 0. */
+int32_t qwen_asr_debug_valid_utf8(const char* s);
 int32_t qwen_asr_debug_normalize_language(const char* lang, char* out, int32_t cap);
 
 #ifdef __cplusplus

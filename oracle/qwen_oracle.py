@@ -461,10 +461,28 @@ def layer_norm(x, w, b, eps=F32(1e-5)):
     return (d * inv * w + b).astype(F32)
 
 
+# Noise-floor switch for parity statistics: True accumulates the RMSNorm sums of squares and
+# the decoder-prefill products in f64 and rounds the results to f32 - equally valid f32
+# implementations of kernels/mod.rs:1191-1212 and of the prefill sgemm calls that differ from
+# the default only in the last bits. Comparing the oracle with itself under this switch
+# measures how often int8 decode ids flip from rounding order alone.
+RMS_SUM_F64 = False
+
+
+def _mm(a, w):
+    """a @ w^T rounded to f32 (f64 accumulation under RMS_SUM_F64)."""
+    if RMS_SUM_F64:
+        return (a.astype(np.float64) @ w.T.astype(np.float64)).astype(F32)
+    return (a @ w.T).astype(F32)
+
+
 def rms_norm(x, w, eps):
     """kernels/mod.rs:1191-1212."""
     h = x.shape[-1]
-    ss = (x * x).sum(axis=-1, keepdims=True, dtype=F32)
+    if RMS_SUM_F64:
+        ss = (x.astype(np.float64) ** 2).sum(axis=-1, keepdims=True).astype(F32)
+    else:
+        ss = (x * x).sum(axis=-1, keepdims=True, dtype=F32)
     inv = (F32(1.0) / np.sqrt(ss / F32(h) + eps)).astype(F32)
     return (x * inv * w).astype(F32)
 
@@ -612,6 +630,7 @@ class Model:
                     q, s = quantize_weights(bits, weight_quant)
                     L[key + "_q"] = int8_chunks(q)
                     L[key + "_s"] = s
+                    L[key + "_i8"] = q
             self.dec_layers.append(L)
         self.norm = st.f32(m + "norm.weight")
         lm_name = "thinker.lm_head.weight"
@@ -620,6 +639,7 @@ class Model:
             q, s = quantize_weights(self.lm_bits, weight_quant)
             self.lm_q = int8_chunks(q)
             self.lm_s = s
+            self.lm_i8 = q
         else:
             self.lm_f32 = bf16_to_f32(self.lm_bits)
         # RoPE inverse frequencies, decoder.rs:302-309 (f32 powf)
@@ -766,19 +786,19 @@ class Decoder:
         cos, sin = self._rope(start, seq)
         for li, L in enumerate(m.dec_layers):
             xn = rms_norm(x, L["n1"], c.eps)
-            q = (xn @ L["wq"].T).astype(F32).reshape(seq, c.dec_heads, 128)
-            k = (xn @ L["wk"].T).astype(F32).reshape(seq, c.dec_kv_heads, 128)
-            v = (xn @ L["wv"].T).astype(F32).reshape(seq, c.dec_kv_heads, 128)
+            q = _mm(xn, L["wq"]).reshape(seq, c.dec_heads, 128)
+            k = _mm(xn, L["wk"]).reshape(seq, c.dec_kv_heads, 128)
+            v = _mm(xn, L["wv"]).reshape(seq, c.dec_kv_heads, 128)
             q = self._apply_rope(rms_norm(q, L["qn"], c.eps), cos, sin)
             k = self._apply_rope(rms_norm(k, L["kn"], c.eps), cos, sin)
             self.kv.k[li, :, start:start + seq] = k.transpose(1, 0, 2)
             self.kv.v[li, :, start:start + seq] = v.transpose(1, 0, 2)
             att = self._attend(q, li, start, seq).reshape(seq, -1)
-            x = (x + (att @ L["wo"].T).astype(F32)).astype(F32)
+            x = (x + _mm(att, L["wo"])).astype(F32)
             xn = rms_norm(x, L["n2"], c.eps)
-            gu = (xn @ L["gu"].T).astype(F32)
+            gu = _mm(xn, L["gu"])
             mid = silu_mul(gu[:, 0::2], gu[:, 1::2])
-            x = (x + (mid @ L["down"].T).astype(F32)).astype(F32)
+            x = (x + _mm(mid, L["down"])).astype(F32)
         self.kv.len = start + seq
         return x
 

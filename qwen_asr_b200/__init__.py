@@ -68,6 +68,12 @@ SIGNATURES = {
     "qwen_asr_launch_count": (C.c_int64, [_VP]),
     "qwen_asr_debug_gemm": (C.c_int32, [C.c_int32, C.c_int32, C.c_int32, _F32P, C.POINTER(C.c_uint16), _F32P,
                                          _F32P, C.c_int32, C.c_int32, _F32P]),
+    "qwen_asr_gemm_fallbacks": (C.c_int64, []),
+    "qwen_asr_debug_valid_utf8": (C.c_int32, [C.c_char_p]),
+    "qwen_asr_debug_kv": (C.c_int32, [_VP, C.c_int32, C.c_int32, C.c_int32, _F32P, _F32P]),
+    "qwen_asr_debug_kv_capacity": (C.c_int32, [_VP]),
+    "qwen_asr_debug_grow_kv": (C.c_int32, [_VP, C.c_int32]),
+    "qwen_asr_debug_quant": (C.c_int64, [_VP, C.c_int32, C.c_int32, C.POINTER(C.c_int8), _F32P, C.c_int64]),
     "qwen_asr_mel_noalloc": (C.c_int32, [_VP, C.c_void_p, C.c_int32, C.c_void_p, C.c_int64]),
     "qwen_asr_get_timeline": (C.c_int64, [_VP, C.POINTER(C.c_uint64), C.c_int64]),
     "qwen_asr_profile_report": (C.c_int32, [_VP, C.POINTER(C.c_double), _I64P, C.c_int32]),
@@ -303,6 +309,40 @@ class Engine:
             raise RuntimeError(last_error())
         return out[:T * hid].reshape(T, hid).copy()
 
+    def debug_kv(self, layer: int, n_pos: int, slot: int = 0):
+        """(k, v) f32 [kv_heads][n_pos][128] of one layer of a KV slot."""
+        kvh = self.model_info()["dec_kv_heads"]
+        k = np.zeros((kvh, n_pos, 128), dtype=np.float32)
+        v = np.zeros_like(k)
+        if lib().qwen_asr_debug_kv(self._h, slot, layer, n_pos, k.ctypes.data_as(_F32P), v.ctypes.data_as(_F32P)) != 0:
+            raise RuntimeError(last_error())
+        return k, v
+
+    def kv_capacity(self) -> int:
+        return lib().qwen_asr_debug_kv_capacity(self._h)
+
+    def grow_kv(self, needed: int) -> int:
+        n = lib().qwen_asr_debug_grow_kv(self._h, needed)
+        if n < 0:
+            raise RuntimeError(last_error())
+        return n
+
+    def debug_quant(self, layer: int, which: int):
+        """Device int8 rows and f32 scales of a decoder matrix (0 qkv, 1 o, 2 gate/up, 3 down, 4 lm_head)."""
+        n = lib().qwen_asr_debug_quant(self._h, layer, which, C.cast(None, C.POINTER(C.c_int8)),
+                                       C.cast(None, _F32P), 0)
+        if n < 0:
+            raise RuntimeError(last_error())
+        info = self.model_info()
+        h, inter, qd = info["dec_hidden"], info["dec_intermediate"], info["dec_heads"] * 128
+        cols = {0: h, 1: qd, 2: h, 3: inter, 4: h}[which]
+        q = np.zeros((n, cols), dtype=np.int8)
+        s = np.zeros(n, dtype=np.float32)
+        if lib().qwen_asr_debug_quant(self._h, layer, which, q.ctypes.data_as(C.POINTER(C.c_int8)),
+                                      s.ctypes.data_as(_F32P), n) != n:
+            raise RuntimeError(last_error())
+        return q, s
+
     def debug_decode(self, rows: np.ndarray, n_steps: int, forced=None, want_logits=False, want_hidden=False):
         r, p = _f32(rows)
         info = self.model_info()
@@ -319,6 +359,11 @@ class Engine:
         if n < 0:
             raise RuntimeError(last_error())
         return ids[:n_steps], lg, hd
+
+
+def gemm_fallbacks() -> int:
+    """Bf16-weight GEMMs that could not run on the tensor cores in this process."""
+    return int(lib().qwen_asr_gemm_fallbacks())
 
 
 def stream_push_many(engine, streams, chunks, finalize: bool = False) -> list:

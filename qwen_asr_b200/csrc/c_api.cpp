@@ -25,6 +25,44 @@ char* to_c_string(const std::string& s) {
   return out;
 }
 
+// Strict UTF-8 as Rust's CStr::to_str accepts it (no overlong forms, no surrogates, at most
+// U+10FFFF): the reference returns NULL / -1 for paths and languages that fail it
+// (c_api.rs:28-31, 59-62, 141-144).
+bool valid_utf8(const char* z) {
+  const unsigned char* s = (const unsigned char*)z;
+  while (*s) {
+    const unsigned c = *s;
+    int n;
+    unsigned cp;
+    if (c < 0x80) {
+      ++s;
+      continue;
+    } else if (c >= 0xC2 && c <= 0xDF) {
+      n = 1; cp = c & 0x1F;
+    } else if (c >= 0xE0 && c <= 0xEF) {
+      n = 2; cp = c & 0x0F;
+    } else if (c >= 0xF0 && c <= 0xF4) {
+      n = 3; cp = c & 0x07;
+    } else {
+      return false;
+    }
+    for (int i = 1; i <= n; ++i) {
+      if ((s[i] & 0xC0) != 0x80) return false;
+      cp = (cp << 6) | (s[i] & 0x3F);
+    }
+    if ((n == 2 && (cp < 0x800 || (cp >= 0xD800 && cp <= 0xDFFF))) || (n == 3 && (cp < 0x10000 || cp > 0x10FFFF)))
+      return false;
+    s += n + 1;
+  }
+  return true;
+}
+
+bool utf8_arg(const char* z, const char* what) {
+  if (valid_utf8(z)) return true;
+  qasr::set_error(std::string(what) + " is not valid UTF-8");
+  return false;
+}
+
 int pick_device() {
   if (const char* d = getenv("QASR_DEVICE")) return atoi(d);
   int dev = 0;
@@ -52,7 +90,7 @@ QwenAsrEngine* qwen_asr_load_model(const char* model_dir, int32_t n_threads, int
 }
 
 QwenAsrEngine* qwen_asr_load_model_on_device(const char* model_dir, int32_t device, int32_t verbosity) {
-  if (!model_dir) return nullptr;
+  if (!model_dir || !utf8_arg(model_dir, "model_dir")) return nullptr;
   qasr::g_verbose = verbosity;
   QwenAsrEngine* e = new (std::nothrow) QwenAsrEngine();
   if (!e) return nullptr;
@@ -70,7 +108,7 @@ QwenAsrEngine* qwen_asr_load_model_on_device(const char* model_dir, int32_t devi
 }
 
 char* qwen_asr_transcribe_file(QwenAsrEngine* e, const char* wav_path) {
-  if (!e || !wav_path) return nullptr;
+  if (!e || !wav_path || !utf8_arg(wav_path, "wav_path")) return nullptr;
   std::ifstream f(wav_path, std::ios::binary);
   if (!f) {
     qasr::set_error(std::string("cannot read ") + wav_path);
@@ -101,7 +139,7 @@ void qwen_asr_set_segment_sec(QwenAsrEngine* e, float sec) {
 }
 
 int32_t qwen_asr_set_language(QwenAsrEngine* e, const char* language) {
-  if (!e || !language) return -1;
+  if (!e || !language || !utf8_arg(language, "language")) return -1;
   return e->ctx.set_force_language(language) ? 0 : -1;
 }
 
@@ -140,13 +178,19 @@ int32_t qwen_asr_stream_push_many(QwenAsrEngine* e, QwenAsrStreamState* const* s
   if (!e || count < 0 || (count > 0 && (!states || !deltas_out))) return -1;
   std::vector<const std::vector<float>*> bufs;
   std::vector<qasr::StreamState*> sts;
+  // validate the whole list before any stream takes new audio, so a rejected call changes nothing
   for (int32_t i = 0; i < count; ++i) {
-    if (!states[i]) return -1;
+    if (!states[i]) {
+      qasr::set_error("stream_push_many: a null stream");
+      return -1;
+    }
     for (int32_t j = 0; j < i; ++j)
       if (states[j] == states[i]) {
         qasr::set_error("stream_push_many: a stream appears twice");
         return -1;
       }
+  }
+  for (int32_t i = 0; i < count; ++i) {
     if (samples && samples[i] && n_samples && n_samples[i] > 0)
       states[i]->audio_buf.insert(states[i]->audio_buf.end(), samples[i], samples[i] + n_samples[i]);
     bufs.push_back(&states[i]->audio_buf);
@@ -387,6 +431,27 @@ int32_t qwen_asr_debug_decode(QwenAsrEngine* e, const float* rows, int32_t n_row
     for (int i = 0; i < (int)ids.size(); ++i) out_ids[i] = ids[i];
   if (out_logits) memcpy(out_logits, lg.data(), lg.size() * 4);
   return (int32_t)ids.size();
+}
+
+int32_t qwen_asr_debug_valid_utf8(const char* s) { return s && valid_utf8(s) ? 1 : 0; }
+
+int64_t qwen_asr_gemm_fallbacks(void) { return qasr::gemm_tc_fallbacks(); }
+
+int32_t qwen_asr_debug_kv(QwenAsrEngine* e, int32_t slot, int32_t layer, int32_t n_pos, float* k, float* v) {
+  if (!e || !k || !v) return -1;
+  return e->ctx.eng.copy_kv(slot, layer, n_pos, k, v) ? 0 : -1;
+}
+
+int32_t qwen_asr_debug_kv_capacity(QwenAsrEngine* e) { return e ? e->ctx.eng.kv_capacity() : -1; }
+
+int32_t qwen_asr_debug_grow_kv(QwenAsrEngine* e, int32_t needed) {
+  if (!e || needed <= 0) return -1;
+  return e->ctx.eng.grow_kv(needed) ? e->ctx.eng.kv_capacity() : -1;
+}
+
+int64_t qwen_asr_debug_quant(QwenAsrEngine* e, int32_t layer, int32_t which, int8_t* q, float* s, int64_t cap_rows) {
+  if (!e || (cap_rows > 0 && (!q || !s))) return -1;
+  return e->ctx.eng.copy_quant(layer, which, q, s, cap_rows);
 }
 
 int32_t qwen_asr_debug_gemm(int32_t M, int32_t N, int32_t K, const float* A, const uint16_t* B, const float* bias,

@@ -31,6 +31,16 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
 }
 
+// f32 -> three bf16 planes with v = hi + mid + lo: each plane is the bf16 rounding of what
+// the planes before it left over (both subtractions are exact), so together they hold all 24
+// significand bits of v. The tensor-core GEMM multiplies each plane by bf16 weights.
+__device__ __forceinline__ void split3_bf16(float v, __nv_bfloat16& hi, __nv_bfloat16& mid, __nv_bfloat16& lo) {
+  hi = __float2bfloat16_rn(v);
+  const float r = __fsub_rn(v, __bfloat162float(hi));
+  mid = __float2bfloat16_rn(r);
+  lo = __float2bfloat16_rn(__fsub_rn(r, __bfloat162float(mid)));
+}
+
 // Monotonic float <-> int mapping for atomicMax on floats.
 __device__ __forceinline__ int float_to_ordered(float f) {
   int i = __float_as_int(f);

@@ -464,8 +464,10 @@ int Engine::encode_many(const std::vector<EncInput>& in, std::vector<int>& seq) 
   if (!act1_.alloc(max_a1) || !act2_.alloc(max_a2) || !act3_.alloc(max_a3) || !cols_.alloc(max_cols) ||
       !x_enc_.alloc((size_t)T * d) || !xn_enc_.alloc((size_t)T * d) || !qkv_enc_.alloc((size_t)T * 3 * d) ||
       !att_enc_.alloc((size_t)T * d) || !mid_enc_.alloc((size_t)T * std::max(c.enc_ffn_dim, d)) ||
-      !enc_.alloc((size_t)T * c.enc_output_dim))
+      !enc_.alloc((size_t)T * c.enc_output_dim) || !pl_a_.alloc(split_planes_elems(T, d)) ||
+      !pl_b_.alloc(split_planes_elems(T, std::max(c.enc_ffn_dim, d))))
     return 0;
+  const long fb0 = gemm_tc_fallbacks();
   cudaEventRecord(ev0_, stream_);
   launches += 7 * (long)groups.size() + 7 * (long)enc_layers_.size() + 3;
   int tok = 0;
@@ -476,7 +478,7 @@ int Engine::encode_many(const std::vector<EncInput>& in, std::vector<int>& seq) 
     GemmArgs a;
     a.M = g.nc * 32 * w2; a.N = H; a.K = 9 * H;
     a.A = cols_.p; a.lda = 9 * H; a.B = conv2_w; a.ldb = 9 * H;
-    a.C = act2_.p; a.ldc = H; a.epi = EPI_BIAS_GELU; a.bias = conv2_b;
+    a.C = act2_.p; a.ldc = H; a.epi = EPI_BIAS_GELU; a.bias = conv2_b; a.split_k = -1;
     gemm(a, stream_);
     im2col_s2(act2_.p, g.nc, 32, w2, cols_.p, true, stream_);
     a.M = g.nc * w3 * 16; a.A = cols_.p; a.B = conv3_w; a.C = act3_.p; a.bias = conv3_b;
@@ -502,51 +504,165 @@ int Engine::encode_many(const std::vector<EncInput>& in, std::vector<int>& seq) 
   if (!win_starts_.alloc(n_win + 1)) return 0;
   CUDA_OK(cudaMemcpyAsync(win_starts_.p, ws.data(), ws.size() * 4, cudaMemcpyHostToDevice, stream_), 0);
   const float scale = 1.0f / sqrtf((float)c.enc_head_dim);
+  const long long plT = (long long)T * d, plF = (long long)T * c.enc_ffn_dim;
   for (auto& L : enc_layers_) {
-    layer_norm_rows(x_enc_.p, xn_enc_.p, T, d, L.ln1w, L.ln1b, 1e-5f, stream_);
+    layer_norm_rows(x_enc_.p, xn_enc_.p, T, d, L.ln1w, L.ln1b, 1e-5f, stream_, pl_a_.p, plT);
     GemmArgs a;
     a.M = T; a.N = 3 * d; a.K = d; a.A = xn_enc_.p; a.lda = d; a.B = L.wqkv; a.ldb = d;
     a.C = qkv_enc_.p; a.ldc = 3 * d; a.epi = EPI_BIAS; a.bias = L.bqkv;
+    a.a_split = pl_a_.p; a.a_split_ld = d; a.a_split_plane = plT;
     gemm(a, stream_);
-    window_attention(qkv_enc_.p, att_enc_.p, T, d, c.enc_heads, win_starts_.p, n_win, max_win, scale, stream_);
+    // tensor-core windows (att planes feed the o projection); the SIMT kernel only for
+    // windows above 128 rows or under QASR_ATTN=simt
+    const bool tc_att = !simt_attention() && window_attention_tc(qkv_enc_.p, att_enc_.p, pl_a_.p, plT, d, c.enc_heads,
+                                                                 c.enc_head_dim, win_starts_.p, n_win, max_win,
+                                                                 scale, stream_);
+    if (!tc_att)
+      window_attention(qkv_enc_.p, att_enc_.p, T, d, c.enc_heads, win_starts_.p, n_win, max_win, scale, stream_);
     GemmArgs o;
     o.M = T; o.N = d; o.K = d; o.A = att_enc_.p; o.lda = d; o.B = L.wo; o.ldb = d;
     o.C = x_enc_.p; o.ldc = d; o.epi = EPI_RESID; o.resid = x_enc_.p; o.ldr = d; o.bias = L.bo;
+    if (tc_att) {
+      o.a_split = pl_a_.p; o.a_split_ld = d; o.a_split_plane = plT;
+    }
     gemm(o, stream_);
-    layer_norm_rows(x_enc_.p, xn_enc_.p, T, d, L.ln2w, L.ln2b, 1e-5f, stream_);
+    layer_norm_rows(x_enc_.p, xn_enc_.p, T, d, L.ln2w, L.ln2b, 1e-5f, stream_, pl_a_.p, plT);
     GemmArgs f1;
     f1.M = T; f1.N = c.enc_ffn_dim; f1.K = d; f1.A = xn_enc_.p; f1.lda = d; f1.B = L.w1; f1.ldb = d;
     f1.C = mid_enc_.p; f1.ldc = c.enc_ffn_dim; f1.epi = EPI_BIAS_GELU; f1.bias = L.b1;
+    f1.a_split = pl_a_.p; f1.a_split_ld = d; f1.a_split_plane = plT;
+    f1.c_split = pl_b_.p; f1.c_split_ld = c.enc_ffn_dim; f1.c_split_plane = plF;
     gemm(f1, stream_);
     GemmArgs f2;
     f2.M = T; f2.N = d; f2.K = c.enc_ffn_dim; f2.A = mid_enc_.p; f2.lda = c.enc_ffn_dim; f2.B = L.w2;
     f2.ldb = c.enc_ffn_dim; f2.C = x_enc_.p; f2.ldc = d; f2.epi = EPI_RESID; f2.resid = x_enc_.p; f2.ldr = d;
     f2.bias = L.b2;
+    f2.a_split = pl_b_.p; f2.a_split_ld = c.enc_ffn_dim; f2.a_split_plane = plF;
     gemm(f2, stream_);
   }
-  layer_norm_rows(x_enc_.p, xn_enc_.p, T, d, ln_post_w, ln_post_b, 1e-5f, stream_);
+  layer_norm_rows(x_enc_.p, xn_enc_.p, T, d, ln_post_w, ln_post_b, 1e-5f, stream_, pl_a_.p, plT);
   GemmArgs p1;
   p1.M = T; p1.N = d; p1.K = d; p1.A = xn_enc_.p; p1.lda = d; p1.B = proj1_w; p1.ldb = d;
   p1.C = mid_enc_.p; p1.ldc = d; p1.epi = EPI_BIAS_GELU; p1.bias = proj1_b;
+  p1.a_split = pl_a_.p; p1.a_split_ld = d; p1.a_split_plane = plT;
+  p1.c_split = pl_b_.p; p1.c_split_ld = d; p1.c_split_plane = plT;
   gemm(p1, stream_);
   GemmArgs p2;
   p2.M = T; p2.N = c.enc_output_dim; p2.K = d; p2.A = mid_enc_.p; p2.lda = d; p2.B = proj2_w; p2.ldb = d;
   p2.C = enc_.p; p2.ldc = c.enc_output_dim; p2.epi = EPI_BIAS; p2.bias = proj2_b;
+  p2.a_split = pl_b_.p; p2.a_split_ld = d; p2.a_split_plane = plT;
   gemm(p2, stream_);
   cudaEventRecord(ev1_, stream_);
   CUDA_OK(cudaEventSynchronize(ev1_), 0);
   float ms = 0;
   cudaEventElapsedTime(&ms, ev0_, ev1_);
   perf.enc_ms += ms;
-  if (int e = gemm_tc_error()) {
-    set_error("tensor-core GEMM: a device-side wait timed out (code " + std::to_string(e) + ")");
-    return 0;
-  }
+  if (!gemm_stage_ok(fb0)) return 0;
   CUDA_OK(cudaGetLastError(), 0);
   return T;
 }
 
 // ---------------------------------------------------------------------------- prefill
+// Tensor-core GEMM health after a stage: a bounded device wait that gave up or a GEMM that
+// left the tensor cores fails the stage with a recorded error.
+bool Engine::simt_attention() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QASR_ATTN");
+    v = (e && strcmp(e, "simt") == 0) ? 1 : 0;
+  }
+  return v == 1;
+}
+
+bool Engine::gemm_stage_ok(long fallbacks_before) {
+  if (int e = attn_tc_error()) {
+    set_error("tensor-core attention: a device-side wait timed out (code " + std::to_string(e) + ")");
+    return false;
+  }
+  if (int e = gemm_tc_error()) {
+    set_error("tensor-core GEMM: a device-side wait timed out (code " + std::to_string(e) + ")");
+    return false;
+  }
+  if (gemm_tc_fallbacks() != fallbacks_before) {
+    set_error("a bf16-weight GEMM left the tensor cores: " + last_error());
+    return false;
+  }
+  return true;
+}
+
+// decoder_prefill's layer loop (decoder.rs:455-547) over R packed rows x: block b is
+// rows [off, off + S) of one sequence at KV positions start.. in KV slot `slot`. The
+// GEMMs run once over all rows; q/k norm + RoPE + KV append and attention per block.
+bool Engine::prefill_layers(float* x, int R, const std::vector<RowBlock>& blocks) {
+  const Config& c = cfg_;
+  const int h = c.dec_hidden, qd = c.dec_heads * 128, kvd = c.dec_kv_heads * 128, inter = c.dec_intermediate;
+  const int ldq = qd + 2 * kvd;
+  const float scale = 1.0f / sqrtf(128.f);
+  if (R <= 0) return true;
+  if (!pl_a_.alloc(split_planes_elems(R, h)) || !pl_b_.alloc(split_planes_elems(R, inter)) ||
+      !pl_c_.alloc(split_planes_elems(R, qd)))
+    return false;
+  const long long plH = (long long)R * h, plI = (long long)R * inter, plQ = (long long)R * qd;
+  const bool simt_att = simt_attention();
+  for (int l = 0; l < c.dec_layers; ++l) {
+    const DecLayerW& L = dec_layers_[l];
+    rms_norm_rows(x, pxn_.p, R, h, L.n1, c.dec_rms_norm_eps, stream_, pl_a_.p, plH);
+    GemmArgs a;
+    a.M = R; a.N = ldq; a.K = h; a.A = pxn_.p; a.lda = h; a.B = L.wqkv; a.ldb = h;
+    a.C = pqkv_.p; a.ldc = ldq;
+    a.a_split = pl_a_.p; a.a_split_ld = h; a.a_split_plane = plH;
+    gemm(a, stream_);
+    bool tc_att = !simt_att;
+    for (const RowBlock& bk : blocks) {
+      if (bk.S == 0) continue;
+      if (simt_att) {
+        const size_t so = (size_t)bk.slot * kv_slot_stride() + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
+        float* qk = pqkv_.p + (size_t)bk.off * ldq;
+        prefill_qk_rope_kv(qk, bk.S, bk.start, c.dec_heads, c.dec_kv_heads, L.qn, L.kn, c.dec_rms_norm_eps,
+                           rope_cos_, rope_sin_, kc_.p + so, vc_.p + so, max_seq_, stream_);
+        prefill_attention(qk, bk.S, bk.start, c.dec_heads, c.dec_kv_heads, kc_.p + so, vc_.p + so, max_seq_, scale,
+                          patt_.p + (size_t)bk.off * qd, stream_);
+        launches += 2;
+        continue;
+      }
+      const size_t slot_off = (size_t)bk.slot * kv_slot_stride() + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
+      float* qkv = pqkv_.p + (size_t)bk.off * ldq;
+      prefill_qk_rope_kv(qkv, bk.S, bk.start, c.dec_heads, c.dec_kv_heads, L.qn, L.kn, c.dec_rms_norm_eps,
+                         rope_cos_, rope_sin_, kc_.p + slot_off, vc_.p + slot_off, max_seq_, stream_);
+      if (tc_att)
+        tc_att = prefill_attention_tc(qkv, bk.S, bk.start, c.dec_heads, c.dec_kv_heads, kc_.p + slot_off,
+                                      vc_.p + slot_off, max_seq_, scale, patt_.p + (size_t)bk.off * qd,
+                                      pl_c_.p + (size_t)bk.off * qd, plQ, stream_);
+      if (!tc_att) {
+        set_error("prefill: the tensor-core attention kernel could not run");
+        return false;
+      }
+      launches += 2;
+    }
+    GemmArgs o;
+    o.M = R; o.N = h; o.K = qd; o.A = patt_.p; o.lda = qd; o.B = L.wo; o.ldb = qd;
+    o.C = x; o.ldc = h; o.epi = EPI_RESID; o.resid = x; o.ldr = h;
+    if (!simt_att) {
+      o.a_split = pl_c_.p; o.a_split_ld = qd; o.a_split_plane = plQ;
+    }
+    gemm(o, stream_);
+    rms_norm_rows(x, pxn_.p, R, h, L.n2, c.dec_rms_norm_eps, stream_, pl_a_.p, plH);
+    GemmArgs g;
+    g.M = R; g.N = 2 * inter; g.K = h; g.A = pxn_.p; g.lda = h; g.B = L.wgu; g.ldb = h;
+    g.C = pmid_.p; g.ldc = inter; g.epi = EPI_SWIGLU;
+    g.a_split = pl_a_.p; g.a_split_ld = h; g.a_split_plane = plH;
+    g.c_split = pl_b_.p; g.c_split_ld = inter; g.c_split_plane = plI;
+    gemm(g, stream_);
+    GemmArgs dn;
+    dn.M = R; dn.N = h; dn.K = inter; dn.A = pmid_.p; dn.lda = inter; dn.B = L.wdown; dn.ldb = inter;
+    dn.C = x; dn.ldc = h; dn.epi = EPI_RESID; dn.resid = x; dn.ldr = h;
+    dn.a_split = pl_b_.p; dn.a_split_ld = inter; dn.a_split_plane = plI;
+    gemm(dn, stream_);
+    launches += 6;
+  }
+  return true;
+}
+
 bool Engine::prefill_ids(const std::vector<int>& ids, const float* d_enc, int start_pos, int slot) {
   cudaSetDevice(device_);
   const int h = cfg_.dec_hidden, n = (int)ids.size();
@@ -586,46 +702,14 @@ bool Engine::prefill_many(const std::vector<PrefillJob>& jobs, const float* d_en
       !pqkv_.alloc((size_t)std::max(R, 1) * (qd + 2 * kvd)) || !patt_.alloc((size_t)std::max(R, 1) * qd) ||
       !pmid_.alloc((size_t)std::max(R, 1) * inter))
     return false;
+  const long fb0 = gemm_tc_fallbacks();
   CUDA_OK(cudaMemcpyAsync(ids_.p, packed.data(), packed.size() * 4, cudaMemcpyHostToDevice, stream_), false);
   cudaEventRecord(ev0_, stream_);
   gather_embeds(ids_.p, (int)packed.size(), embed_, d_enc, h, px_.p, stream_);
   launches += 1;
-  float* x = px_.p;
-  const float scale = 1.0f / sqrtf(128.f);
-  const int ldq = qd + 2 * kvd;
-  for (int l = 0; l < c.dec_layers && R > 0; ++l) {
-    const DecLayerW& L = dec_layers_[l];
-    rms_norm_rows(x, pxn_.p, R, h, L.n1, c.dec_rms_norm_eps, stream_);
-    GemmArgs a;
-    a.M = R; a.N = ldq; a.K = h; a.A = pxn_.p; a.lda = h; a.B = L.wqkv; a.ldb = h;
-    a.C = pqkv_.p; a.ldc = ldq;
-    gemm(a, stream_);
-    for (int j = 0; j < J; ++j) {
-      const int S = off[j + 1] - off[j];
-      if (S == 0) continue;
-      const size_t slot_off = (size_t)jobs[j].slot * kv_slot_stride() + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
-      float* qkv = pqkv_.p + (size_t)off[j] * ldq;
-      prefill_qk_rope_kv(qkv, S, jobs[j].start_pos, c.dec_heads, c.dec_kv_heads, L.qn, L.kn, c.dec_rms_norm_eps,
-                         rope_cos_, rope_sin_, kc_.p + slot_off, vc_.p + slot_off, max_seq_, stream_);
-      prefill_attention(qkv, S, jobs[j].start_pos, c.dec_heads, c.dec_kv_heads, kc_.p + slot_off, vc_.p + slot_off,
-                        max_seq_, scale, patt_.p + (size_t)off[j] * qd, stream_);
-      launches += 2;
-    }
-    GemmArgs o;
-    o.M = R; o.N = h; o.K = qd; o.A = patt_.p; o.lda = qd; o.B = L.wo; o.ldb = qd;
-    o.C = x; o.ldc = h; o.epi = EPI_RESID; o.resid = x; o.ldr = h;
-    gemm(o, stream_);
-    rms_norm_rows(x, pxn_.p, R, h, L.n2, c.dec_rms_norm_eps, stream_);
-    GemmArgs g;
-    g.M = R; g.N = 2 * inter; g.K = h; g.A = pxn_.p; g.lda = h; g.B = L.wgu; g.ldb = h;
-    g.C = pmid_.p; g.ldc = inter; g.epi = EPI_SWIGLU;
-    gemm(g, stream_);
-    GemmArgs dn;
-    dn.M = R; dn.N = h; dn.K = inter; dn.A = pmid_.p; dn.lda = inter; dn.B = L.wdown; dn.ldb = inter;
-    dn.C = x; dn.ldc = h; dn.epi = EPI_RESID; dn.resid = x; dn.ldr = h;
-    gemm(dn, stream_);
-    launches += 6;
-  }
+  std::vector<RowBlock> blocks;
+  for (int j = 0; j < J; ++j) blocks.push_back({off[j], off[j + 1] - off[j], jobs[j].start_pos, jobs[j].slot});
+  if (!prefill_layers(px_.p, R, blocks)) return false;
   // each job's first decode input is its last prompt row (transcribe.rs:171-185)
   for (int j = 0; j < J; ++j) {
     const int slot = jobs[j].slot, n = (int)jobs[j].ids->size();
@@ -645,10 +729,7 @@ bool Engine::prefill_many(const std::vector<PrefillJob>& jobs, const float* d_en
   float ms = 0;
   cudaEventElapsedTime(&ms, ev0_, ev1_);
   perf.prefill_ms += ms;
-  if (int e = gemm_tc_error()) {
-    set_error("tensor-core GEMM: a device-side wait timed out (code " + std::to_string(e) + ")");
-    return false;
-  }
+  if (!gemm_stage_ok(fb0)) return false;
   CUDA_OK(cudaGetLastError(), false);
   return true;
 }
@@ -683,6 +764,7 @@ bool Engine::prefill_classify(const std::vector<int>& ids, const float* d_enc, c
   if (!cls_ids_.alloc(m) || !cls_out_.alloc(m) || !cls_x_.alloc((size_t)m * h) || !cls_xn_.alloc((size_t)m * h) ||
       !cls_logits_.alloc((size_t)m * N))
     return false;
+  const long fb0 = gemm_tc_fallbacks();
   CUDA_OK(cudaMemcpyAsync(cls_ids_.p, g.data(), m * 4, cudaMemcpyHostToDevice, stream_), false);
   gather_embeds(cls_ids_.p, m, embed_, px_.p, h, cls_x_.p, stream_);
   rms_norm_rows(cls_x_.p, cls_xn_.p, m, h, final_norm_, c.dec_rms_norm_eps, stream_);
@@ -694,10 +776,7 @@ bool Engine::prefill_classify(const std::vector<int>& ids, const float* d_enc, c
   launches += 4;
   CUDA_OK(cudaMemcpyAsync(cls.data(), cls_out_.p, m * 4, cudaMemcpyDeviceToHost, stream_), false);
   CUDA_OK(cudaStreamSynchronize(stream_), false);
-  if (int e = gemm_tc_error()) {
-    set_error("tensor-core GEMM: a device-side wait timed out (code " + std::to_string(e) + ")");
-    return false;
-  }
+  if (!gemm_stage_ok(fb0)) return false;
   CUDA_OK(cudaGetLastError(), false);
   return true;
 }
@@ -722,35 +801,8 @@ bool Engine::run_prefill(int n, int start_pos, int slot) {
       !patt_.alloc((size_t)std::max(S, 1) * qd) || !pmid_.alloc((size_t)std::max(S, 1) * inter))
     return false;
   cudaEventRecord(ev0_, stream_);
-  if (S > 0) launches += 8 * (long)c.dec_layers;
-  float* x = px_.p + (size_t)start_pos * h;
-  const float scale = 1.0f / sqrtf(128.f);
-  for (int l = 0; l < c.dec_layers && S > 0; ++l) {
-    const DecLayerW& L = dec_layers_[l];
-    float* kc = kc_.p + slot * kv_slot_stride() + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
-    float* vc = vc_.p + slot * kv_slot_stride() + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
-    rms_norm_rows(x, pxn_.p, S, h, L.n1, c.dec_rms_norm_eps, stream_);
-    GemmArgs a;
-    a.M = S; a.N = qd + 2 * kvd; a.K = h; a.A = pxn_.p; a.lda = h; a.B = L.wqkv; a.ldb = h;
-    a.C = pqkv_.p; a.ldc = qd + 2 * kvd;
-    gemm(a, stream_);
-    prefill_qk_rope_kv(pqkv_.p, S, start_pos, c.dec_heads, c.dec_kv_heads, L.qn, L.kn, c.dec_rms_norm_eps, rope_cos_,
-                       rope_sin_, kc, vc, max_seq_, stream_);
-    prefill_attention(pqkv_.p, S, start_pos, c.dec_heads, c.dec_kv_heads, kc, vc, max_seq_, scale, patt_.p, stream_);
-    GemmArgs o;
-    o.M = S; o.N = h; o.K = qd; o.A = patt_.p; o.lda = qd; o.B = L.wo; o.ldb = qd;
-    o.C = x; o.ldc = h; o.epi = EPI_RESID; o.resid = x; o.ldr = h;
-    gemm(o, stream_);
-    rms_norm_rows(x, pxn_.p, S, h, L.n2, c.dec_rms_norm_eps, stream_);
-    GemmArgs g;
-    g.M = S; g.N = 2 * inter; g.K = h; g.A = pxn_.p; g.lda = h; g.B = L.wgu; g.ldb = h;
-    g.C = pmid_.p; g.ldc = inter; g.epi = EPI_SWIGLU;
-    gemm(g, stream_);
-    GemmArgs dn;
-    dn.M = S; dn.N = h; dn.K = inter; dn.A = pmid_.p; dn.lda = inter; dn.B = L.wdown; dn.ldb = inter;
-    dn.C = x; dn.ldc = h; dn.epi = EPI_RESID; dn.resid = x; dn.ldr = h;
-    gemm(dn, stream_);
-  }
+  const long fb0 = gemm_tc_fallbacks();
+  if (S > 0 && !prefill_layers(px_.p + (size_t)start_pos * h, S, {{0, S, start_pos, slot}})) return false;
   if (slot == 0) kv_len_ = n - 1;
   // first decode input: the last prompt row
   CUDA_OK(cudaMemcpyAsync(dx_.p + (size_t)slot * h, px_.p + (size_t)(n - 1) * h, (size_t)h * 4,
@@ -767,12 +819,58 @@ bool Engine::run_prefill(int n, int start_pos, int slot) {
   float ms = 0;
   cudaEventElapsedTime(&ms, ev0_, ev1_);
   perf.prefill_ms += ms;
-  if (int e = gemm_tc_error()) {
-    set_error("tensor-core GEMM: a device-side wait timed out (code " + std::to_string(e) + ")");
-    return false;
-  }
+  if (!gemm_stage_ok(fb0)) return false;
   CUDA_OK(cudaGetLastError(), false);
   return true;
+}
+
+bool Engine::copy_kv(int slot, int layer, int n_pos, float* k, float* v) {
+  cudaSetDevice(device_);
+  const Config& c = cfg_;
+  if (slot < 0 || slot >= slots_ || layer < 0 || layer >= c.dec_layers || n_pos < 0 || n_pos > max_seq_) {
+    set_error("copy_kv: slot, layer or position count out of range");
+    return false;
+  }
+  CUDA_OK(cudaStreamSynchronize(stream_), false);
+  for (int hh = 0; hh < c.dec_kv_heads; ++hh) {
+    const size_t off = (size_t)slot * kv_slot_stride() + ((size_t)layer * c.dec_kv_heads + hh) * max_seq_ * 128;
+    CUDA_OK(cudaMemcpy(k + (size_t)hh * n_pos * 128, kc_.p + off, (size_t)n_pos * 128 * 4, cudaMemcpyDeviceToHost),
+            false);
+    CUDA_OK(cudaMemcpy(v + (size_t)hh * n_pos * 128, vc_.p + off, (size_t)n_pos * 128 * 4, cudaMemcpyDeviceToHost),
+            false);
+  }
+  return true;
+}
+
+long Engine::copy_quant(int layer, int which, int8_t* q, float* s, long cap_rows) {
+  cudaSetDevice(device_);
+  const Config& c = cfg_;
+  const int h = c.dec_hidden, qd = c.dec_heads * 128, kvd = c.dec_kv_heads * 128, inter = c.dec_intermediate;
+  const int8_t* dq = nullptr;
+  const float* ds = nullptr;
+  long rows = 0, cols = 0;
+  if (which == 4) {
+    dq = lm_q_; ds = lm_s_; rows = c.vocab_size; cols = h;
+  } else {
+    if (layer < 0 || layer >= c.dec_layers) return -1;
+    const DecLayerW& L = dec_layers_[layer];
+    switch (which) {
+      case 0: dq = L.qqkv; ds = L.sqkv; rows = qd + 2 * kvd; cols = h; break;
+      case 1: dq = L.qo; ds = L.so; rows = h; cols = qd; break;
+      case 2: dq = L.qgu; ds = L.sgu; rows = 2 * inter; cols = h; break;
+      case 3: dq = L.qdown; ds = L.sdown; rows = h; cols = inter; break;
+      default: return -1;
+    }
+  }
+  if (!dq || !ds) {
+    set_error("copy_quant: the int8 weights are not resident");
+    return -1;
+  }
+  if (rows > cap_rows) return rows;
+  CUDA_OK(cudaStreamSynchronize(stream_), -1);
+  CUDA_OK(cudaMemcpy(q, dq, (size_t)rows * cols, cudaMemcpyDeviceToHost), -1);
+  CUDA_OK(cudaMemcpy(s, ds, (size_t)rows * 4, cudaMemcpyDeviceToHost), -1);
+  return rows;
 }
 
 bool Engine::copy_prefill_hidden(std::vector<float>& out, int rows) {

@@ -142,6 +142,17 @@ class Engine {
 
   // Debug: final hidden of prefill rows (after the last layer, before final norm).
   bool copy_prefill_hidden(std::vector<float>& out, int rows);
+  // Debug: K and V rows [kv_heads][n_pos][128] of positions 0..n_pos-1 of one slot and layer.
+  bool copy_kv(int slot, int layer, int n_pos, float* k, float* v);
+  int kv_capacity() const { return max_seq_; }
+  // Debug: grow the KV cache to hold `needed` positions (the doubling path of KvCache::grow).
+  bool grow_kv(int needed) {
+    cudaSetDevice(device_);
+    return ensure_kv(needed);
+  }
+  // Debug: the int8 rows and f32 row scales of one quantised decoder matrix (which: 0 q/k/v,
+  // 1 o, 2 gate/up interleaved, 3 down, 4 lm_head; layer ignored for 4). Returns the row count.
+  long copy_quant(int layer, int which, int8_t* q, float* s, long cap_rows);
 
  private:
   Config cfg_;
@@ -221,6 +232,14 @@ class Engine {
   bool graph_for_slot(int slot);
   std::map<int, std::pair<cudaGraphExec_t, unsigned>> run_graphs_;  // batched steps of slot runs (first slot > 0)
   bool run_prefill(int n_rows, int start_pos, int slot = 0);  // rows already in px_
+  struct RowBlock {
+    int off, S, start, slot;
+  };
+  bool prefill_layers(float* x, int R, const std::vector<RowBlock>& blocks);
+  bool gemm_stage_ok(long fallbacks_before);
+  static bool simt_attention();  // QASR_ATTN=simt: the SIMT attention kernels (A/B checks)
+  // bf16 planes (hi/mid/lo) of GEMM inputs written by their producers
+  DevBuf<__nv_bfloat16> pl_a_, pl_b_, pl_c_;
   cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
 };
 

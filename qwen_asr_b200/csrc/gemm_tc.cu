@@ -1,16 +1,32 @@
 // Tensor-core GEMM for sm_100a: C = epi(A[M][K] * B[N][K]^T) on tcgen05 with the
-// accumulator in TMEM, operands moved by TMA (cp.async.bulk.tensor, no multicast).
+// accumulators in TMEM and every operand moved by TMA (cp.async.bulk.tensor, no multicast).
 //
-// Precision: B holds bf16 weights (exact: the reference upcasts the same bf16 values to
-// f32). A holds f32 activations; it is split into bf16 hi + lo parts (a = hi + lo up to
-// 2^-16 relative) and both are multiplied against B into the same f32 accumulator, which
-// keeps the contraction at f32-level accuracy, as the reference's sgemm is.
+// Precision. B holds bf16 weights, exact (the reference upcasts the same bf16 values to
+// f32 before its sgemm). A holds f32 activations and enters as three bf16 planes,
+// a = hi + mid + lo, each plane the bf16 rounding of what the planes before it left over,
+// so the three carry all 24 significand bits of an f32 (exact except for rare
+// sub-2^-126 remainders). Every product of a bf16 plane with a bf16 weight is exact in the
+// f32 accumulator, so the contraction has the f32 accumulation error of an sgemm, not the
+// 2^-9 or 2^-17 representation error of one or two bf16 terms. The planes come either from
+// the producing kernel (LayerNorm/RMSNorm, GEMM epilogues, attention) or from split3_kernel.
 //
-// Tile 128 x 128 x 64 per CTA, 4-stage smem ring. 128 threads: thread 0 issues TMA,
-// thread 32 issues MMAs, then all four warps drain TMEM (warp w owns rows 32w..32w+31).
+// Schedule. A persistent grid (one CTA per SM) walks work units (m tile, n tile, k split)
+// in a fixed order. Warp 0 issues TMA into a 3-stage ring (per stage the three A planes and
+// the B tile, 64 KB), warp 1 issues 12 MMAs (128x128x16) per stage into one of two TMEM
+// accumulators, and warps 2-5 drain the other accumulator: tcgen05.ld, a transpose through
+// shared memory, then the fused epilogue with coalesced row-wise stores. So the epilogue of
+// one unit overlaps the mainloop of the next.
+//
+// Split K. A GEMM with few output tiles splits K into S parts so that about 148 CTAs work.
+// S depends only on the call's (N, K) and its split policy, never on M, so a row's result
+// never depends on how many other rows share the call (batched segments and streams equal
+// single ones bit for bit). Each split stores its f32 partial tile to a workspace; the last
+// split of a tile to arrive (ticket) sums the S partials in split order and applies the
+// epilogue, so the sum order is fixed too.
 #include <cuda.h>
 
 #include <mutex>
+#include <unordered_map>
 
 #include "bulk.cuh"
 #include "common.h"
@@ -20,11 +36,30 @@
 namespace qasr {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4;
-constexpr int kTileA = BM * BK * 2;  // 16 KB (bf16)
-constexpr int kTileB = BN * BK * 2;  // 16 KB
-constexpr int kStage = 2 * kTileA + kTileB;
-constexpr int kSmem = STAGES * kStage + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3, NPART = 3;
+constexpr int kTile = BM * BK * 2;           // 16 KB: one bf16 operand tile (an A plane or B)
+constexpr int kStage = (NPART + 1) * kTile;  // 64 KB
+constexpr int kEpiPitch = 33;                // floats per staged row (bank-conflict padding)
+constexpr int kEpiBytes = 4 * 32 * kEpiPitch * 4;
+constexpr int kSmem = 1024 /*align*/ + STAGES * kStage + kEpiBytes + 256 /*barriers*/;
+constexpr int kThreads = 192;
+constexpr int kSms = 148;
+
+struct TcParams {
+  int M, N, K, MT, NT, S, nk, units;
+  int epi;
+  float* C;
+  int ldc;
+  const float* bias;
+  const float* resid;
+  int ldr;
+  __nv_bfloat16* cs;  // optional split-plane output [3][plane] of rows of cs_ld
+  int cs_ld;
+  long long cs_plane;
+  float* ws;     // split-K partial tiles [tile][S][BM][BN]
+  int* tickets;  // [tile], zero at rest
+  int* err;
+};
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SBO), descriptor version 1 (sm_100).
@@ -38,7 +73,7 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor, kind::f16: f32 accumulator, bf16 A and B, both K-major.
+// Instruction descriptor, kind::f16: f32 accumulator, bf16 A and B, both K-major, M=128, N=128.
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                             ((uint32_t)(BM >> 4) << 24);
 
@@ -47,6 +82,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
           smem_u32(dst)),
       "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -62,6 +104,8 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
 #define TMEM_LD32(taddr, r)                                                                                       \
   asm volatile(                                                                                                   \
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18," \
@@ -72,31 +116,95 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])    \
       : "r"(taddr))
 
-__global__ void __launch_bounds__(128, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap map_ahi,
-                                                         const __grid_constant__ CUtensorMap map_alo,
-                                                         const __grid_constant__ CUtensorMap map_b, GemmArgs a,
-                                                         int* err) {
+__device__ __forceinline__ void unit_coords(const TcParams& p, int u, int& mt, int& nt, int& s) {
+  mt = u % p.MT;
+  const int t = u / p.MT;
+  s = t % p.S;
+  nt = t / p.S;
+}
+__device__ __forceinline__ void split_range(const TcParams& p, int s, int& k0, int& k1) {
+  k0 = (int)((long)s * p.nk / p.S);
+  k1 = (int)((long)(s + 1) * p.nk / p.S);
+}
+
+// Final value of one output element (or SwiGLU pair) to C and/or the split planes.
+__device__ __forceinline__ void store_out(const TcParams& p, int m, int n, float v) {
+  if (p.C) p.C[(size_t)m * p.ldc + n] = v;
+  if (p.cs) {
+    __nv_bfloat16 h, md, l;
+    split3_bf16(v, h, md, l);
+    __nv_bfloat16* q = p.cs + (size_t)m * p.cs_ld + n;
+    q[0] = h;
+    q[p.cs_plane] = md;
+    q[2 * p.cs_plane] = l;
+  }
+}
+__device__ __forceinline__ float epi_value(const TcParams& p, int m, int n, float v) {
+  switch (p.epi) {
+    case EPI_BIAS:
+      return __fadd_rn(v, p.bias[n]);
+    case EPI_BIAS_GELU:
+      return gelu_tanh(__fadd_rn(v, p.bias[n]));
+    case EPI_RESID: {
+      float r = p.resid[(size_t)m * p.ldr + n];
+      if (p.bias) r = __fadd_rn(r, p.bias[n]);
+      return __fadd_rn(v, r);
+    }
+    default:
+      return v;
+  }
+}
+
+// One 32x32 block (rows m0.., columns n0..) staged in st[32][kEpiPitch]: epilogue + stores,
+// lane = column, so every store instruction writes consecutive addresses of one row.
+__device__ __forceinline__ void epilogue_block(const TcParams& p, const float* st, int m0, int n0, int lane) {
+  if (p.epi == EPI_SWIGLU) {
+    // columns (2j, 2j+1) = (gate, up) -> output column n/2 + j; two rows per pass
+#pragma unroll 4
+    for (int rr = 0; rr < 32; rr += 2) {
+      const int r = rr + (lane >> 4), j = lane & 15, m = m0 + r, n = n0 + 2 * j;
+      if (m < p.M && n + 1 < p.N) store_out(p, m, n >> 1, silu_mul(st[r * kEpiPitch + 2 * j], st[r * kEpiPitch + 2 * j + 1]));
+    }
+    return;
+  }
+  const int n = n0 + lane;
+#pragma unroll 4
+  for (int r = 0; r < 32; ++r) {
+    const int m = m0 + r;
+    if (m < p.M && n < p.N) store_out(p, m, n, epi_value(p, m, n, st[r * kEpiPitch + lane]));
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
+                                                              const __grid_constant__ CUtensorMap map_b,
+                                                              const TcParams p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStage);
+  float* epi_st = reinterpret_cast<float*>(smem + STAGES * kStage);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStage + kEpiBytes);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum_bar = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  volatile int* abort_flag = last_flag + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  const int nk = (a.K + BK - 1) / BK;
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0) {  // TMEM: 128 f32 columns = the 128 x 128 accumulator
+  if (warp == 0) {  // TMEM: two 128 x 128 f32 accumulators = 256 columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(BN));
+                 "r"(2 * BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
@@ -104,81 +212,156 @@ __global__ void __launch_bounds__(128, 1) gemm_tc_kernel(const __grid_constant__
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = *tmem_slot;
 
-  if (tid == 0) {
+  if (warp == 0) {
     // ---- TMA producer
-    for (int kt = 0; kt < nk; ++kt) {
-      const int s = kt % STAGES;
-      if (kt >= STAGES) mbar_wait(&empty[s], (uint32_t)((kt / STAGES) - 1) & 1u, err, 11);
-      unsigned char* st = smem + s * kStage;
-      mbar_expect_tx(&full[s], kStage);
-      tma_load_2d(st, &map_ahi, kt * BK, m0, &full[s]);
-      tma_load_2d(st + kTileA, &map_alo, kt * BK, m0, &full[s]);
-      tma_load_2d(st + 2 * kTileA, &map_b, kt * BK, n0, &full[s]);
-    }
-  } else if (tid == 32) {
-    // ---- MMA issuer
-    for (int kt = 0; kt < nk; ++kt) {
-      const int s = kt % STAGES;
-      mbar_wait(&full[s], (uint32_t)(kt / STAGES) & 1u, err, 12);
-      asm volatile("tcgen05.fence::after_thread_sync;");
-      const uint32_t sa = smem_u32(smem + s * kStage);
-      const uint32_t sal = sa + kTileA, sb = sa + 2 * kTileA;
+    if (lane == 0) {
+      int it = 0;
+      for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
+        int mt, nt, s, k0, k1;
+        unit_coords(p, u, mt, nt, s);
+        split_range(p, s, k0, k1);
+        for (int kt = k0; kt < k1; ++kt, ++it) {
+          const int st = it % STAGES;
+          if (it >= STAGES && !mbar_wait(&empty[st], (uint32_t)((it / STAGES) - 1) & 1u, p.err, 11)) {
+            *abort_flag = 1;
+            break;
+          }
+          unsigned char* sp = smem + st * kStage;
+          mbar_expect_tx(&full[st], kStage);
 #pragma unroll
-      for (int kk = 0; kk < BK / 16; ++kk) {  // K = 16 per instruction = 32 bytes along the row
-        const uint64_t bd = sw128_desc(sb + kk * 32);
-        mma_bf16(tmem, sw128_desc(sa + kk * 32), bd, (kt > 0 || kk > 0) ? 1u : 0u);
-        mma_bf16(tmem, sw128_desc(sal + kk * 32), bd, 1u);
+          for (int q = 0; q < NPART; ++q) tma_load_3d(sp + q * kTile, &map_a, kt * BK, mt * BM, q, &full[st]);
+          tma_load_2d(sp + NPART * kTile, &map_b, kt * BK, nt * BN, &full[st]);
+        }
       }
-      mma_commit(&empty[s]);  // stage reusable once these MMAs have read it
     }
-    mma_commit(accum_bar);
-  }
-  __syncwarp();
-
-  // ---- epilogue: TMEM -> registers -> fused epilogue -> global
-  mbar_wait(accum_bar, 0, err, 13);
-  asm volatile("tcgen05.fence::after_thread_sync;");
-  const int m = m0 + warp * 32 + lane;
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  } else if (warp == 1) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      int it = 0, lt = 0;
+      for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x, ++lt) {
+        int mt, nt, s, k0, k1;
+        unit_coords(p, u, mt, nt, s);
+        split_range(p, s, k0, k1);
+        const int ab = lt & 1;
+        if (lt >= 2 && !mbar_wait(&acc_empty[ab], (uint32_t)((lt >> 1) - 1) & 1u, p.err, 12)) {
+          *abort_flag = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        const uint32_t acc = tmem + (uint32_t)(ab * BN);
+        bool ok = true;
+        for (int kt = k0; kt < k1; ++kt, ++it) {
+          const int st = it % STAGES;
+          if (!mbar_wait(&full[st], (uint32_t)(it / STAGES) & 1u, p.err, 13)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;");
+          const uint32_t sa = smem_u32(smem + st * kStage), sb = sa + NPART * kTile;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {  // K = 16 per instruction = 32 bytes along the row
+            const uint64_t bd = sw128_desc(sb + kk * 32);
+#pragma unroll
+            for (int q = 0; q < NPART; ++q)
+              mma_bf16(acc, sw128_desc(sa + q * kTile + kk * 32), bd, (kt > k0 || kk > 0 || q > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[st]);  // stage reusable once these MMAs have read it
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+        mma_commit(&acc_full[ab]);
+      }
+    }
+  } else {
+    // ---- epilogue warps 2..5: TMEM lane quarter q = warp % 4 -> tile rows 32q..32q+31
+    const int q = warp & 3;
+    float* st = epi_st + (warp - 2) * 32 * kEpiPitch;
+    int lt = 0;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++lt) {
+      int mt, nt, s;
+      unit_coords(p, u, mt, nt, s);
+      const int ab = lt & 1;
+      if (!mbar_wait(&acc_full[ab], (uint32_t)(lt >> 1) & 1u, p.err, 14)) {
+        *abort_flag = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      const int m0 = mt * BM + q * 32, nb = nt * BN;
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
+      const int tile = nt * p.MT + mt;
+      float* wsp = p.S > 1 ? p.ws + ((size_t)tile * p.S + s) * (BM * BN) : nullptr;
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 32) {
-    uint32_t r[32];
-    TMEM_LD32(trow + c0, r);
-    asm volatile("tcgen05.wait::ld.sync.aligned;");
-    if (m >= a.M) continue;
-    const int nb = n0 + c0;
-    if (a.epi == EPI_SWIGLU) {
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        TMEM_LD32(trow + c0, r);
+        asm volatile("tcgen05.wait::ld.sync.aligned;");
 #pragma unroll
-      for (int j = 0; j < 32; j += 2)
-        if (nb + j + 1 < a.N)
-          a.C[(size_t)m * a.ldc + (nb + j) / 2] = silu_mul(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (nb + j < a.N) a.C[(size_t)m * a.ldc + nb + j] = apply_epi(a, m, nb + j, __uint_as_float(r[j]));
+        for (int j = 0; j < 32; ++j) st[lane * kEpiPitch + j] = __uint_as_float(r[j]);
+        __syncwarp();
+        if (wsp) {
+          // raw partial, rows 32q.. of the tile, columns c0..c0+31
+#pragma unroll 4
+          for (int rr = 0; rr < 32; ++rr) wsp[(size_t)(q * 32 + rr) * BN + c0 + lane] = st[rr * kEpiPitch + lane];
+        } else {
+          epilogue_block(p, st, m0, nb + c0, lane);
+        }
+        __syncwarp();
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+      if (wsp) {
+        __threadfence();
+        epi_bar();
+        if (tid == 64) {
+          const int t = atomicAdd(p.tickets + tile, 1);
+          *last_flag = (t == p.S - 1);
+        }
+        epi_bar();
+        if (*last_flag) {
+          __threadfence();
+          const float* w0 = p.ws + (size_t)tile * p.S * (BM * BN);
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 32) {
+#pragma unroll 2
+            for (int rr = 0; rr < 32; ++rr) {
+              const size_t off = (size_t)(q * 32 + rr) * BN + c0 + lane;
+              float v = __ldcg(w0 + off);
+              for (int k = 1; k < p.S; ++k) v = __fadd_rn(v, __ldcg(w0 + (size_t)k * (BM * BN) + off));
+              st[rr * kEpiPitch + lane] = v;
+            }
+            __syncwarp();
+            epilogue_block(p, st, m0, nb + c0, lane);
+            __syncwarp();
+          }
+          epi_bar();
+          if (tid == 64) p.tickets[tile] = 0;  // ready for the next call
+        }
+        epi_bar();
+      }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
 }
 
-// a -> (hi, lo) bf16 with a = hi + lo to 2^-16 relative; rows [M][K] packed (ld = K).
-__global__ void split_bf16_kernel(const float* __restrict__ A, int lda, int M, int K, __nv_bfloat16* __restrict__ hi,
-                                  __nv_bfloat16* __restrict__ lo) {
+// f32 rows [M][lda] -> bf16 planes hi/mid/lo [3][plane] of rows [M][K] (ld = K).
+__global__ void split3_kernel(const float* __restrict__ A, int lda, int M, int K, __nv_bfloat16* __restrict__ out,
+                              long long plane) {
   const long total = (long)M * (K / 4);
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
     const int r = (int)(i / (K / 4)), c = (int)(i % (K / 4)) * 4;
-    float4 v = *reinterpret_cast<const float4*>(A + (size_t)r * lda + c);
-    float f[4] = {v.x, v.y, v.z, v.w};
-    __nv_bfloat16 h[4], l[4];
+    const float4 v = *reinterpret_cast<const float4*>(A + (size_t)r * lda + c);
+    const float f[4] = {v.x, v.y, v.z, v.w};
+    __nv_bfloat16 h[4], m[4], l[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      h[j] = __float2bfloat16_rn(f[j]);
-      l[j] = __float2bfloat16_rn(__fsub_rn(f[j], __bfloat162float(h[j])));
-    }
-    *reinterpret_cast<uint2*>(hi + (size_t)r * K + c) = *reinterpret_cast<uint2*>(h);
-    *reinterpret_cast<uint2*>(lo + (size_t)r * K + c) = *reinterpret_cast<uint2*>(l);
+    for (int j = 0; j < 4; ++j) split3_bf16(f[j], h[j], m[j], l[j]);
+    __nv_bfloat16* o = out + (size_t)r * K + c;
+    *reinterpret_cast<uint2*>(o) = *reinterpret_cast<uint2*>(h);
+    *reinterpret_cast<uint2*>(o + plane) = *reinterpret_cast<uint2*>(m);
+    *reinterpret_cast<uint2*>(o + 2 * plane) = *reinterpret_cast<uint2*>(l);
   }
 }
 
@@ -200,31 +383,106 @@ EncodeTiledFn get_encode() {
   return fn;
 }
 
-// Row-major bf16 [rows][cols] (ld elements), box = box_rows x 64, 128-byte swizzle.
-bool make_map(CUtensorMap* map, const void* base, int rows, int cols, int ld, int box_rows) {
+// Tensor maps are encoded once per (base, shape) and reused: weights never move and the
+// engine's activation buffers only change address when they grow.
+struct MapKey {
+  const void* base;
+  long long rows, cols, ld, planes, plane;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && rows == o.rows && cols == o.cols && ld == o.ld && planes == o.planes && plane == o.plane;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = std::hash<const void*>()(k.base);
+    for (long long v : {k.rows, k.cols, k.ld, k.planes, k.plane}) h = h * 1000003u ^ std::hash<long long>()(v);
+    return h;
+  }
+};
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+// bf16 operand [planes][rows][cols] (row pitch ld, plane pitch `plane` elements), box =
+// 64 columns x 128 rows x 1 plane, 128-byte swizzle; out-of-range boxes read zeros.
+bool operand_map(CUtensorMap* out, const void* base, int rows, int cols, int ld, int planes, long long plane) {
+  MapKey key{base, rows, cols, ld, planes, plane};
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  auto itm = g_maps.find(key);
+  if (itm != g_maps.end()) {
+    *out = itm->second;
+    return true;
+  }
   EncodeTiledFn enc = get_encode();
   if (!enc) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)planes};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)plane * 2};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)BM, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUtensorMap m;
+  if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, planes > 1 ? 3 : 2, const_cast<void*>(base), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  if (g_maps.size() > 4096) g_maps.clear();
+  g_maps.emplace(key, m);
+  *out = m;
+  return true;
 }
 
 struct TcScratch {
-  __nv_bfloat16* hi = nullptr;
-  __nv_bfloat16* lo = nullptr;
-  size_t cap = 0;
+  __nv_bfloat16* planes = nullptr;  // split3 output
+  size_t planes_cap = 0;
+  float* ws = nullptr;
+  size_t ws_cap = 0;
+  int* tickets = nullptr;
+  size_t tickets_cap = 0;
   int* err = nullptr;
+  bool init = false;
 };
 TcScratch g_tc[16];
 std::mutex g_tc_mu;
+long g_fallbacks = 0;
+
+// Grow-only device buffer (the engine calls gemm outside stream capture).
+template <typename T>
+bool grow(T*& p, size_t& cap, size_t need, cudaStream_t s, bool zero) {
+  if (cap >= need && p) return true;
+  cudaStreamSynchronize(s);
+  if (p) cudaFree(p);
+  p = nullptr;
+  cap = 0;
+  need = std::max(need, (size_t)4096);
+  if (cudaMalloc(&p, need * sizeof(T)) != cudaSuccess) {
+    p = nullptr;
+    return false;
+  }
+  if (zero && cudaMemset(p, 0, need * sizeof(T)) != cudaSuccess) return false;
+  cap = need;
+  return true;
+}
 
 }  // namespace
 
 bool gemm_tc_available() { return get_encode() != nullptr; }
+
+long gemm_tc_fallbacks() {
+  std::lock_guard<std::mutex> lk(g_tc_mu);
+  return g_fallbacks;
+}
+void gemm_tc_note_fallback() {
+  std::lock_guard<std::mutex> lk(g_tc_mu);
+  ++g_fallbacks;
+}
+
+int gemm_split_k(int N, int K, int policy) {
+  if (policy > 0) return policy;
+  const int nk = (K + BK - 1) / BK, nt = (N + BN - 1) / BN;
+  if (policy < 0) return 1;
+  // about one wave of 148 CTAs for a ~384-row call (3 row tiles), >= 4 k-steps per split
+  int s = (kSms + 3 * nt - 1) / (3 * nt);
+  s = std::min(s, std::max(1, nk / 4));
+  return std::max(1, std::min(s, 16));
+}
 
 bool make_tma_2d_u16(void* map, const void* base, int rows, int cols, int box_cols, int box_rows, bool swizzle128) {
   EncodeTiledFn enc = get_encode();
@@ -238,43 +496,58 @@ bool make_tma_2d_u16(void* map, const void* base, int rows, int cols, int box_co
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+void split3_rows(const float* A, int lda, int M, int K, __nv_bfloat16* out, long long plane, cudaStream_t s) {
+  const long total = (long)M * (K / 4);
+  if (total <= 0) return;
+  split3_kernel<<<(int)std::min<long>((total + 255) / 256, kSms * 16L), 256, 0, s>>>(A, lda, M, K, out, plane);
+}
+
 bool gemm_tc(const GemmArgs& a, cudaStream_t s) {
-  if (a.b_is_f32 || a.K % 16 != 0 || (a.ldb * 2) % 16 != 0) return false;
+  if (a.b_is_f32 || a.K % 16 != 0 || (a.ldb * 2) % 16 != 0 || a.epi == EPI_LOG10_MAX) return false;
+  if (!a.C && !a.c_split) return false;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 16) return false;
   TcScratch& sc = g_tc[dev];
+  const int MT = ceil_div(a.M, BM), NT = ceil_div(a.N, BN), nk = ceil_div(a.K, BK);
+  const int S = std::min(gemm_split_k(a.N, a.K, a.split_k), nk);
+  const __nv_bfloat16* planes = a.a_split;
+  int pld = a.a_split_ld;
+  long long pplane = a.a_split_plane;
   {
     std::lock_guard<std::mutex> lk(g_tc_mu);
-    size_t need = (size_t)a.M * a.K;
-    if (sc.cap < need) {
-      // Grow-only split buffers (the engine calls this outside any stream capture).
-      cudaStreamSynchronize(s);
-      if (sc.hi) cudaFree(sc.hi);
-      if (sc.lo) cudaFree(sc.lo);
-      size_t cap = std::max(need, (size_t)1 << 22);
-      if (cudaMalloc(&sc.hi, cap * 2) != cudaSuccess || cudaMalloc(&sc.lo, cap * 2) != cudaSuccess) {
-        sc.hi = sc.lo = nullptr;
-        sc.cap = 0;
-        return false;
-      }
-      sc.cap = cap;
-    }
-    if (!sc.err) {
+    if (!sc.init) {
       if (cudaMalloc(&sc.err, sizeof(int)) != cudaSuccess) return false;
       cudaMemset(sc.err, 0, sizeof(int));
       cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+      sc.init = true;
+    }
+    if (!planes) {
+      if (!grow(sc.planes, sc.planes_cap, (size_t)3 * a.M * a.K, s, false)) return false;
+    }
+    if (S > 1) {
+      if (!grow(sc.ws, sc.ws_cap, (size_t)MT * NT * S * BM * BN, s, false) ||
+          !grow(sc.tickets, sc.tickets_cap, (size_t)MT * NT, s, true))
+        return false;
     }
   }
-  const long total = (long)a.M * (a.K / 4);
-  split_bf16_kernel<<<(int)std::min<long>((total + 255) / 256, 148L * 16), 256, 0, s>>>(a.A, a.lda, a.M, a.K, sc.hi,
-                                                                                       sc.lo);
-  CUtensorMap mh, ml, mb;
-  if (!make_map(&mh, sc.hi, a.M, a.K, a.K, BM) || !make_map(&ml, sc.lo, a.M, a.K, a.K, BM) ||
-      !make_map(&mb, a.B, a.N, a.K, a.ldb, BN))
+  if (!planes) {
+    pplane = (long long)a.M * a.K;
+    pld = a.K;
+    split3_rows(a.A, a.lda, a.M, a.K, sc.planes, pplane, s);
+    planes = sc.planes;
+  }
+  if ((pld * 2) % 16 != 0 || (pplane * 2) % 16 != 0) return false;
+  CUtensorMap ma, mb;
+  if (!operand_map(&ma, planes, a.M, a.K, pld, NPART, pplane) || !operand_map(&mb, a.B, a.N, a.K, a.ldb, 1, 0))
     return false;
-  dim3 grid(ceil_div(a.N, BN), ceil_div(a.M, BM));
-  gemm_tc_kernel<<<grid, 128, kSmem, s>>>(mh, ml, mb, a, sc.err);
+  TcParams p;
+  p.M = a.M; p.N = a.N; p.K = a.K; p.MT = MT; p.NT = NT; p.S = S; p.nk = nk; p.units = MT * NT * S;
+  p.epi = a.epi; p.C = a.C; p.ldc = a.ldc; p.bias = a.bias; p.resid = a.resid; p.ldr = a.ldr;
+  p.cs = a.c_split; p.cs_ld = a.c_split_ld; p.cs_plane = a.c_split_plane;
+  p.ws = sc.ws; p.tickets = sc.tickets; p.err = sc.err;
+  const int grid = std::min(p.units, kSms);
+  gemm_tc_kernel<<<grid, kThreads, kSmem, s>>>(ma, mb, p);
   return true;
 }
 

@@ -33,14 +33,38 @@ struct GemmArgs {
   const float* resid = nullptr;  // [M][ldr] for EPI_RESID
   int ldr = 0;
   int* gmax = nullptr;           // EPI_LOG10_MAX
+  // Tensor-core path only. a_split: A already as bf16 planes hi/mid/lo [3][a_split_plane]
+  // of rows [M][a_split_ld] (written by the producing kernel; A is then only read by the
+  // SIMT path). c_split: also write the result as planes (input of the next GEMM).
+  const __nv_bfloat16* a_split = nullptr;
+  int a_split_ld = 0;
+  long long a_split_plane = 0;
+  __nv_bfloat16* c_split = nullptr;
+  int c_split_ld = 0;
+  long long c_split_plane = 0;
+  // K split policy: 0 = automatic from (N, K), -1 = never split, > 0 = that many splits.
+  // Never depends on M, so per-row results do not depend on the row count.
+  int split_k = 0;
 };
-void gemm(const GemmArgs& a, cudaStream_t s);
+// Bytes of a plane buffer for `rows` x `cols` (three bf16 planes).
+inline size_t split_planes_elems(size_t rows, size_t cols) { return 3 * rows * cols; }
+// Returns false (and records the error) when a bf16-weight GEMM could not run on the
+// tensor cores; the result is then computed by the SIMT kernel from the f32 A, and
+// gemm_tc_fallbacks() counts it.
+bool gemm(const GemmArgs& a, cudaStream_t s);
 // Plain SIMT FP32 reference GEMM (kept for parity tests of the tensor-core path).
 void gemm_simt(const GemmArgs& a, cudaStream_t s);
-// tcgen05/TMEM tensor-core GEMM (bf16 B, f32 A split into bf16 hi + lo). Returns false
-// when the shape is unsupported (the caller then uses the SIMT kernel).
+// tcgen05/TMEM tensor-core GEMM (bf16 B, f32 A as three bf16 planes). Returns false
+// when the shape is unsupported.
 bool gemm_tc(const GemmArgs& a, cudaStream_t s);
 bool gemm_tc_available();
+// Bf16-weight GEMMs that had to leave the tensor cores since the library loaded.
+long gemm_tc_fallbacks();
+void gemm_tc_note_fallback();
+// K splits the tensor-core GEMM uses for an (N, K) call under `policy` (GemmArgs::split_k).
+int gemm_split_k(int N, int K, int policy);
+// f32 rows [M][lda] -> bf16 planes hi/mid/lo at out, out + plane, out + 2 * plane (rows of K).
+void split3_rows(const float* A, int lda, int M, int K, __nv_bfloat16* out, long long plane, cudaStream_t s);
 // Nonzero when a bounded wait inside the tensor-core GEMM gave up (clears the flag).
 int gemm_tc_error();
 // 2-D TMA map over a row-major matrix of 16-bit elements [rows][cols], box = box_cols x
@@ -68,14 +92,28 @@ void conv1_gelu(const float* mel, int n_frames, int f0, int cw, int n_chunks, in
 void im2col_s2(const float* in, int n_chunks, int H, int W, float* cols, bool col_major_rows,
                cudaStream_t s);
 void add_pe_rows(float* x, int rows, int d, int period, const float* pe, cudaStream_t s);
+// planes (optional): the normalised rows also as bf16 planes [3][plane] of rows [rows][d].
 void layer_norm_rows(const float* x, float* y, int rows, int d, const float* w, const float* b, float eps,
-                     cudaStream_t s);
+                     cudaStream_t s, __nv_bfloat16* planes = nullptr, long long plane = 0);
 // Windowed bidirectional attention; qkv [T][3d] (q | k | v), out [T][d].
 void window_attention(const float* qkv, float* out, int T, int d, int n_heads, const int* win_starts,
                       int n_windows, int max_win, float scale, cudaStream_t s);
 
+// Tensor-core (tcgen05) attention, f32-level accuracy (attn_tc.cu). Optional `planes`: the
+// output also as bf16 planes [3][plane] (the o-projection GEMM's A). Return false when the
+// shape is outside the kernel (head_dim != 64 or a window above 128 rows for the encoder).
+bool window_attention_tc(const float* qkv, float* out, __nv_bfloat16* planes, long long plane, int d, int n_heads,
+                         int head_dim, const int* win_starts, int n_windows, int max_win, float scale,
+                         cudaStream_t s);
+bool prefill_attention_tc(const float* qkv, int S, int start, int n_heads, int n_kv, const float* kc,
+                          const float* vc, int max_seq, float scale, float* out, __nv_bfloat16* planes,
+                          long long plane, cudaStream_t s);
+// Nonzero when a bounded wait inside the attention kernels gave up (clears the flag).
+int attn_tc_error();
+
 // ---------------------------------------------------------------- decoder
-void rms_norm_rows(const float* x, float* y, int rows, int d, const float* w, float eps, cudaStream_t s);
+void rms_norm_rows(const float* x, float* y, int rows, int d, const float* w, float eps, cudaStream_t s,
+                   __nv_bfloat16* planes = nullptr, long long plane = 0);
 // Prefill: per-head RMSNorm + NeoX RoPE of q/k rows in qkv [S][q_dim + 2*kv_dim] at
 // positions start..start+S-1, then writes k/v into the f32 cache
 // [kv_heads][max_seq][128] of this layer.

@@ -11,7 +11,8 @@ constexpr int kHd = 128;  // decoder head_dim
 
 // ------------------------------------------------------------------ RMSNorm rows
 __global__ void rms_norm_kernel(const float* __restrict__ x, float* __restrict__ y, int d,
-                                const float* __restrict__ w, float eps) {
+                                const float* __restrict__ w, float eps, __nv_bfloat16* __restrict__ planes,
+                                long long plane) {
   __shared__ float red[32];
   const float* xr = x + (size_t)blockIdx.x * d;
   float* yr = y + (size_t)blockIdx.x * d;
@@ -19,11 +20,17 @@ __global__ void rms_norm_kernel(const float* __restrict__ x, float* __restrict__
   for (int i = threadIdx.x; i < d; i += blockDim.x) s = fmaf(xr[i], xr[i], s);
   float ss = block_sum(s, red);
   float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)d), eps)));
-  for (int i = threadIdx.x; i < d; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+  __nv_bfloat16* pr = planes ? planes + (size_t)blockIdx.x * d : nullptr;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const float v = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+    yr[i] = v;
+    if (pr) split3_bf16(v, pr[i], pr[i + plane], pr[i + 2 * plane]);
+  }
 }
 
-void rms_norm_rows(const float* x, float* y, int rows, int d, const float* w, float eps, cudaStream_t s) {
-  if (rows > 0) rms_norm_kernel<<<rows, 256, 0, s>>>(x, y, d, w, eps);
+void rms_norm_rows(const float* x, float* y, int rows, int d, const float* w, float eps, cudaStream_t s,
+                   __nv_bfloat16* planes, long long plane) {
+  if (rows > 0) rms_norm_kernel<<<rows, 256, 0, s>>>(x, y, d, w, eps, planes, plane);
 }
 
 // Per-head RMSNorm (kernels/mod.rs:1214-1240) + NeoX RoPE (generic path :1780-1788) of a

@@ -157,7 +157,8 @@ void add_pe_rows(float* x, int rows, int d, int period, const float* pe, cudaStr
 // ------------------------------------------------------------------ LayerNorm
 // kernels/mod.rs:1160-1189: population variance, eps inside the sqrt.
 __global__ void layer_norm_kernel(const float* __restrict__ x, float* __restrict__ y, int d,
-                                  const float* __restrict__ w, const float* __restrict__ b, float eps) {
+                                  const float* __restrict__ w, const float* __restrict__ b, float eps,
+                                  __nv_bfloat16* __restrict__ planes, long long plane) {
   __shared__ float red[32];
   const float* xr = x + (size_t)blockIdx.x * d;
   float* yr = y + (size_t)blockIdx.x * d;
@@ -171,13 +172,17 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, float* __restrict
   }
   float var = __fdiv_rn(block_sum(v, red), (float)d);
   float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(var, eps)));
-  for (int i = threadIdx.x; i < d; i += blockDim.x)
-    yr[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[i], mean), inv), w[i]), b[i]);
+  __nv_bfloat16* pr = planes ? planes + (size_t)blockIdx.x * d : nullptr;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const float v = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[i], mean), inv), w[i]), b[i]);
+    yr[i] = v;
+    if (pr) split3_bf16(v, pr[i], pr[i + plane], pr[i + 2 * plane]);
+  }
 }
 
 void layer_norm_rows(const float* x, float* y, int rows, int d, const float* w, const float* b, float eps,
-                     cudaStream_t s) {
-  if (rows > 0) layer_norm_kernel<<<rows, 256, 0, s>>>(x, y, d, w, b, eps);
+                     cudaStream_t s, __nv_bfloat16* planes, long long plane) {
+  if (rows > 0) layer_norm_kernel<<<rows, 256, 0, s>>>(x, y, d, w, b, eps, planes, plane);
 }
 
 // ------------------------------------------------------------------ windowed attention

@@ -29,7 +29,10 @@ std::mutex g_setup_mu;
 float* g_scratch_addr[64] = {nullptr};  // device address of g_mel_scratch, per device
 
 // Resolves the array's device address on the current device (once per device). In host
-// code `g_mel_scratch` names a host-side stand-in, so kernels must get this address.
+// code `g_mel_scratch` names a host-side stand-in, so kernels must get this address. The
+// cached address belongs to the device's primary context; a cudaDeviceReset destroys that
+// context together with every engine's allocations, so engines (and this entry point) are
+// only usable again in a process that reloads them - the cache is not refreshed.
 float* scratch_for_current_device() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
@@ -74,6 +77,15 @@ extern "C" int32_t qwen_asr_mel_noalloc(QwenAsrEngine* e, const float* d_samples
     return -1;
   }
   Engine& eng = e->ctx.eng;
+  // Runs on the engine's device and gives the caller back its current device on return.
+  int prev = -1;
+  cudaGetDevice(&prev);
+  struct Restore {
+    int dev;
+    ~Restore() {
+      if (dev >= 0) cudaSetDevice(dev);
+    }
+  } restore{prev};
   if (cudaSetDevice(eng.device()) != cudaSuccess) {
     set_error("mel_noalloc: cudaSetDevice failed");
     return -1;

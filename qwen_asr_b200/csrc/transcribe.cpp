@@ -36,7 +36,7 @@ void StreamState::reset() {
 }
 
 int Ctx::stream_slot(StreamState& st, bool& owned) {
-  const int first = kDecodeMaxBatch, n = std::max(1, std::min(max_stream_slots, kMaxSlots - first));
+  const int first = kDecodeMaxBatch, n = stream_slot_count();
   if ((int)slot_uid.size() < first + n) {
     slot_uid.resize(first + n, 0);
     slot_used.resize(first + n, 0);
@@ -685,8 +685,29 @@ bool Ctx::stream_push_audio(const std::vector<float>& samples, StreamState& st, 
 // its prepare step, the chunks whose KV slots are contiguous decode as one batch (weights
 // read once per step for all of them), then each finishes its delta. A stream's deltas
 // are the ones stream_push_audio gives it alone (same prompts, same per-sequence decode).
+int Ctx::stream_slot_count() const { return std::max(1, std::min(max_stream_slots, kMaxSlots - kDecodeMaxBatch)); }
+
+// Streams beyond the number of KV slots are pushed in groups of at most that many: within a
+// group every stream holds its own slot for the whole round (a slot is only ever reassigned
+// to a stream of a later group), so no stream's prefill can overwrite another's rows.
 bool Ctx::stream_push_many(const std::vector<const std::vector<float>*>& samples, const std::vector<StreamState*>& sts,
                            bool finalize, std::vector<std::string>& deltas) {
+  const size_t n = sts.size(), g = (size_t)stream_slot_count();
+  if (n <= g) return stream_push_group(samples, sts, finalize, deltas);
+  deltas.assign(n, std::string());
+  for (size_t i0 = 0; i0 < n; i0 += g) {
+    const size_t i1 = std::min(n, i0 + g);
+    std::vector<const std::vector<float>*> gs(samples.begin() + i0, samples.begin() + i1);
+    std::vector<StreamState*> gt(sts.begin() + i0, sts.begin() + i1);
+    std::vector<std::string> gd;
+    if (!stream_push_group(gs, gt, finalize, gd)) return false;
+    for (size_t i = i0; i < i1; ++i) deltas[i] = gd[i - i0];
+  }
+  return true;
+}
+
+bool Ctx::stream_push_group(const std::vector<const std::vector<float>*>& samples, const std::vector<StreamState*>& sts,
+                            bool finalize, std::vector<std::string>& deltas) {
   const size_t n = sts.size();
   deltas.assign(n, std::string());
   const int max_new = stream_max_new_tokens > 0 ? stream_max_new_tokens : 32;

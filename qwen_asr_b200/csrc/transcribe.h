@@ -118,6 +118,10 @@ class Ctx {
   bool stream_push_audio(const std::vector<float>& samples, StreamState& st, bool finalize, std::string& delta);
   bool stream_push_many(const std::vector<const std::vector<float>*>& samples, const std::vector<StreamState*>& sts,
                         bool finalize, std::vector<std::string>& deltas);
+  // Streams whose KV slots can be held at once (slots kDecodeMaxBatch.. of the engine).
+  int stream_slot_count() const;
+  bool stream_push_group(const std::vector<const std::vector<float>*>& samples, const std::vector<StreamState*>& sts,
+                         bool finalize, std::vector<std::string>& deltas);
   bool stream_chunk_prepare(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w,
                             bool defer_prefill = false);
   bool stream_chunk_begin(const std::vector<float>& samples, StreamState& st, bool finalize, StreamChunk& w);

@@ -29,6 +29,9 @@ PRESETS = {
     # name: (enc_d, enc_layers, enc_ffn, dec_hidden, dec_layers, dec_inter, q_heads, kv_heads)
     "0.6b": (896, 18, 3584, 1024, 28, 3072, 16, 8),
     "1.7b": (1024, 24, 4096, 2048, 28, 6144, 16, 8),
+    # 1.7B widths with 4 encoder and 4 decoder layers: long streaming parity runs at C5's
+    # shapes while the CPU oracle keeps up.
+    "1.7b-l4": (1024, 4, 4096, 2048, 4, 6144, 16, 8),
     # Small shapes for CPU tests (loaded through the shape-inferring config path).
     "tiny": (128, 2, 256, 256, 2, 512, 4, 2),
     # Forced aligner: the large (1.7B) encoder with the 0.6B decoder (config.rs:109-110) and

@@ -38,3 +38,13 @@ def tiny_dir():
 @pytest.fixture(scope="session")
 def m06_dir():
     return model_dir("0.6b", 0)
+
+
+@pytest.fixture(scope="session")
+def m17_dir():
+    return model_dir("1.7b", 1)
+
+
+@pytest.fixture(scope="session")
+def m17l4_dir():
+    return model_dir("1.7b-l4", 1)

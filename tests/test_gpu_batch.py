@@ -87,9 +87,9 @@ def test_persistent_decode_teacher_forced(Q, tiny_dir, m06_dir, preset, seconds,
     eng = Q.Engine(d)
     eng.set_persistent_decode(True)
     model = O.Model(d, decode_mode=mode)
-    ids, lg, ref_ids, ref_lg = _teacher_forced_case(eng, model, O, seconds, steps, mode, seed)
+    ids, lg, ref_ids, ref_lg, alt = _teacher_forced_case(eng, model, O, seconds, steps, mode, seed)
     assert eng.persistent_decode_active()
-    _check_agreement(ids, lg, ref_ids, ref_lg, mode)
+    _check_agreement(ids, lg, ref_ids, ref_lg, mode, alt)
 
 
 def test_persistent_decode_transcript_matches_chain(Q, tiny_dir):

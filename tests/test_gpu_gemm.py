@@ -61,7 +61,21 @@ def test_gemm_matches_f64(M, N, K, epi):
     resid = rng.standard_normal((M, N)).astype(np.float32) if epi == 3 else None
     want = ref(A, Bf, epi, bias, resid)
     scale = max(1e-12, float(np.max(np.abs(want))))
-    for impl, tol in ((0, 1e-5), (1, 5e-5)):
+    # both kernels at f32-level accuracy: the tensor-core GEMM takes A as three bf16 planes
+    for impl, tol in ((0, 1e-5), (1, 1e-5)):
         got = run(impl, A, Bbits, epi, bias, resid, M, N, K)
         err = float(np.max(np.abs(got - want))) / scale
         assert err < tol, (impl, err)
+
+
+@pytest.mark.parametrize("N,K", [(896, 3584), (1024, 2048), (2688, 896), (200, 48)])
+def test_gemm_rows_independent_of_row_count(N, K):
+    """A row's result must not depend on how many rows share the call (split-K is chosen
+    from N and K only): batched segments and streams rely on it to equal single ones."""
+    rng = np.random.default_rng(N + K)
+    A = rng.standard_normal((381, K)).astype(np.float32)
+    Bbits = bf16_bits(rng.standard_normal((N, K)).astype(np.float32) * 0.02)
+    full = run(1, A, Bbits, 0, None, None, 381, N, K)
+    for m in (1, 5, 130):
+        part = run(1, np.ascontiguousarray(A[:m]), Bbits, 0, None, None, m, N, K)
+        assert np.array_equal(part.view(np.uint32), full[:m].view(np.uint32)), m

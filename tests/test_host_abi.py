@@ -65,6 +65,26 @@ def test_null_arguments_return_null_or_minus_one():
     L.qwen_asr_stream_free(s)
 
 
+def test_non_utf8_arguments_are_rejected(tmp_path):
+    """c_api.rs:28-31, 59-62, 141-144: CStr::to_str failures give NULL / -1."""
+    L = Q.lib()
+    assert not L.qwen_asr_load_model(b"/tmp/\xff\xfe-model", 0, 0)
+    assert "UTF-8" in Q.last_error()
+    assert not L.qwen_asr_load_model(b"/tmp/\xed\xa0\x80", 0, 0)  # encoded surrogate
+    assert "UTF-8" in Q.last_error()
+    rng = np.random.default_rng(5)
+    cases = [b"plain", "真棒🦀".encode(), b"\xc0\xaf", b"\xe0\x80\xaf", b"\xf4\x90\x80\x80", b"\xf0\x9f\xa6",
+             b"\xc3", b"\x80", "\U0010ffff".encode(), b"\xef\xbf\xbf"]
+    cases += [bytes(rng.integers(1, 256, int(rng.integers(1, 8))).astype(np.uint8)) for _ in range(2000)]
+    for b in cases:
+        try:
+            b.decode("utf-8")
+            want = 1
+        except UnicodeDecodeError:
+            want = 0
+        assert L.qwen_asr_debug_valid_utf8(b) == want, b
+
+
 def test_missing_and_corrupt_model_fail_cleanly(tmp_path):
     L = Q.lib()
     assert not L.qwen_asr_load_model(str(tmp_path).encode(), 0, 0)
