@@ -122,6 +122,14 @@ int32_t qwen_asr_debug_decode(QwenAsrEngine* engine, const float* rows, int32_t 
  * Host buffers. Returns 0, or < 0 on error. (Parity hook for the contraction kernels.) */
 int32_t qwen_asr_debug_gemm(int32_t M, int32_t N, int32_t K, const float* A, const uint16_t* B, const float* bias,
                             const float* resid, int32_t epi, int32_t impl, float* C);
+/* Mean CUDA-event time in ms of `reps` back-to-back tensor-core GEMMs of the given shape and
+ * epilogue on the current device (zero operands); timeline (optional, 148 x 8 u64) receives
+ * per-CTA %globaltimer stamps of the last launch. Returns 0 or < 0. */
+int32_t qwen_asr_debug_gemm_timed(int32_t M, int32_t N, int32_t K, int32_t epi, int32_t reps, float* ms,
+                                  uint64_t* timeline);
+/* Debug: while dev_buf (device memory, 64 u64) is set, the tensor-core attention kernels write
+ * %globaltimer stamps of their phases (one CTA) into it; NULL turns it off. Returns 0. */
+int32_t qwen_asr_debug_attn_timeline(uint64_t* dev_buf);
 /* Bf16-weight GEMMs that could not run on the tensor cores since the library loaded (each
  * one also failed its stage with an error); 0 in a healthy process. */
 int64_t qwen_asr_gemm_fallbacks(void);

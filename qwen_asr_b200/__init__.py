@@ -69,6 +69,9 @@ SIGNATURES = {
     "qwen_asr_debug_gemm": (C.c_int32, [C.c_int32, C.c_int32, C.c_int32, _F32P, C.POINTER(C.c_uint16), _F32P,
                                          _F32P, C.c_int32, C.c_int32, _F32P]),
     "qwen_asr_gemm_fallbacks": (C.c_int64, []),
+    "qwen_asr_debug_attn_timeline": (C.c_int32, [C.c_void_p]),
+    "qwen_asr_debug_gemm_timed": (C.c_int32, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                              C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
     "qwen_asr_debug_valid_utf8": (C.c_int32, [C.c_char_p]),
     "qwen_asr_debug_kv": (C.c_int32, [_VP, C.c_int32, C.c_int32, C.c_int32, _F32P, _F32P]),
     "qwen_asr_debug_kv_capacity": (C.c_int32, [_VP]),

@@ -3,8 +3,10 @@
 // encoder.rs:292-298) and the decoder prefill's causal GQA attention over the f32 KV cache
 // (kernels/mod.rs:1480-1701 with a start offset, decoder.rs:455-547).
 //
-// One CTA (128 threads) owns up to 128 queries of one head; thread t owns query row t, which
-// is TMEM lane t, so the softmax of a row never leaves its thread. Keys go in blocks of BK:
+// One CTA (256 threads) owns up to 128 queries of one head. Query row r is TMEM lane r; the
+// two warps of lane quarter r / 32 each take half of the row's score columns and half of its
+// output dims, and combine row maxima and sums through shared memory (sums in a fixed order).
+// Keys go in blocks of BK:
 //   S = Q K^T  (tcgen05, M = 128, N = BK, K = D)  -> TMEM columns [0, BK)
 //   p = exp(S * scale - m), running max m and sum l per row (online softmax, as the
 //       reference's single-pass loop; masked keys get p = 0)
@@ -26,7 +28,7 @@
 namespace qasr {
 namespace {
 
-constexpr int kThreads = 128, BQ = 128;
+constexpr int kThreads = 256, BQ = 128;
 
 // K-major SW128 operand of R rows x C columns (bf16), three planes: plane p, 64-column chunk c
 // is an R x 128-byte block at (p * C / 64 + c) * R * 128; 16-byte unit u of row r sits at
@@ -87,18 +89,27 @@ __constant__ int kPairB[6] = {0, 1, 2, 0, 1, 0};
 // zero) as three K-major planes; four consecutive columns per thread-iteration, coalesced.
 template <int R, int D>
 __device__ __forceinline__ void stage_rows(unsigned char* dst, const float* src, long ld, int valid) {
-  constexpr int G = D / 4;
-  for (int idx = threadIdx.x; idx < R * G; idx += kThreads) {
-    const int r = idx / G, col = (idx % G) * 4;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (r < valid) v = *reinterpret_cast<const float4*>(src + (long)r * ld + col);
-    const float f[4] = {v.x, v.y, v.z, v.w};
-    __nv_bfloat16 h[4], m[4], l[4];
+  constexpr int G = D / 4, N = R * G / kThreads, U = N < 8 ? N : 8;  // float4s per thread, batch
+  static_assert(N % U == 0, "staging batch");
+#pragma unroll 1
+  for (int b = 0; b < N; b += U) {
+    float4 v[U];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) split3_bf16(f[j], h[j], m[j], l[j]);
-    *reinterpret_cast<uint2*>(dst + sw_off(R, D, 0, r, col)) = *reinterpret_cast<uint2*>(h);
-    *reinterpret_cast<uint2*>(dst + sw_off(R, D, 1, r, col)) = *reinterpret_cast<uint2*>(m);
-    *reinterpret_cast<uint2*>(dst + sw_off(R, D, 2, r, col)) = *reinterpret_cast<uint2*>(l);
+    for (int u = 0; u < U; ++u) {  // every load of the batch in flight before the first use
+      const int idx = threadIdx.x + (b + u) * kThreads, r = idx / G, col = (idx % G) * 4;
+      v[u] = r < valid ? *reinterpret_cast<const float4*>(src + (long)r * ld + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int idx = threadIdx.x + (b + u) * kThreads, r = idx / G, col = (idx % G) * 4;
+      const float f[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      __nv_bfloat16 h[4], m[4], l[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) split3_bf16(f[j], h[j], m[j], l[j]);
+      *reinterpret_cast<uint2*>(dst + sw_off(R, D, 0, r, col)) = *reinterpret_cast<uint2*>(h);
+      *reinterpret_cast<uint2*>(dst + sw_off(R, D, 1, r, col)) = *reinterpret_cast<uint2*>(m);
+      *reinterpret_cast<uint2*>(dst + sw_off(R, D, 2, r, col)) = *reinterpret_cast<uint2*>(l);
+    }
   }
 }
 
@@ -107,17 +118,26 @@ __device__ __forceinline__ void stage_rows(unsigned char* dst, const float* src,
 // of 8 consecutive keys (a warp reads 32 consecutive dims: coalesced) and writes 16 bytes.
 template <int BK, int D>
 __device__ __forceinline__ void stage_vt(unsigned char* dst, const float* src, long ld, int valid) {
-  for (int idx = threadIdx.x; idx < D * (BK / 8); idx += kThreads) {
-    const int d = idx % D, j0 = (idx / D) * 8;
-    __align__(16) __nv_bfloat16 h[8], m[8], l[8];
+  constexpr int N = D * (BK / 8) / kThreads;  // (dim, 8 keys) items per thread
+#pragma unroll 1
+  for (int b = 0; b < N; b += 2) {
+    float v[2][8];
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      const float v = (j0 + t < valid) ? src[(long)(j0 + t) * ld + d] : 0.f;
-      split3_bf16(v, h[t], m[t], l[t]);
+    for (int u = 0; u < 2; ++u) {  // 16 loads in flight
+      const int idx = threadIdx.x + (b + u) * kThreads, d = idx % D, j0 = (idx / D) * 8;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[u][t] = (j0 + t < valid) ? src[(long)(j0 + t) * ld + d] : 0.f;
     }
-    *reinterpret_cast<uint4*>(dst + sw_off(D, BK, 0, d, j0)) = *reinterpret_cast<uint4*>(h);
-    *reinterpret_cast<uint4*>(dst + sw_off(D, BK, 1, d, j0)) = *reinterpret_cast<uint4*>(m);
-    *reinterpret_cast<uint4*>(dst + sw_off(D, BK, 2, d, j0)) = *reinterpret_cast<uint4*>(l);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int idx = threadIdx.x + (b + u) * kThreads, d = idx % D, j0 = (idx / D) * 8;
+      __align__(16) __nv_bfloat16 h[8], m[8], l[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) split3_bf16(v[u][t], h[t], m[t], l[t]);
+      *reinterpret_cast<uint4*>(dst + sw_off(D, BK, 0, d, j0)) = *reinterpret_cast<uint4*>(h);
+      *reinterpret_cast<uint4*>(dst + sw_off(D, BK, 1, d, j0)) = *reinterpret_cast<uint4*>(m);
+      *reinterpret_cast<uint4*>(dst + sw_off(D, BK, 2, d, j0)) = *reinterpret_cast<uint4*>(l);
+    }
   }
 }
 
@@ -137,20 +157,26 @@ struct AttnArgs {
   const int* win;  // window starts [n_win + 1] (encoder)
   int n_q, start;  // prefill: query count and the KV position of query 0
   int* err;
+  unsigned long long* tl;  // optional timeline (debug): CTA (0, 0) thread 0 stamps phases
 };
 
 template <int D, int BK, bool CAUSAL>
 __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnArgs a) {
   constexpr int kQBytes = 3 * BQ * D * 2, kKVBytes = 3 * BK * D * 2, kPBytes = 3 * BQ * BK * 2;
   constexpr int kCols = BK + D <= 128 ? 128 : 256;
+  constexpr int SH = BK / 2, DH = D / 2;  // score columns and output dims of one warp
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* sQ = smem;
   unsigned char* sKV = sQ + kQBytes;
   unsigned char* sP = sKV + kKVBytes;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + kPBytes);
+  float* red_max = reinterpret_cast<float*>(sP + kPBytes);  // [2][BQ]: per column half
+  float* red_sum = red_max + 2 * BQ;                        // [2][BQ]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(red_sum + 2 * BQ);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
-  const int tid = threadIdx.x, warp = tid >> 5, h = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, h = blockIdx.y;
+  // warps w and w + 4 share TMEM lane quarter w % 4 (query rows); half = which column half
+  const int quarter = warp & 3, half = warp >> 2, row = quarter * 32 + lane;
   const int kvh = h / a.heads_per_kv;
 
   // this CTA's queries and keys
@@ -179,21 +205,24 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnArgs a) 
                  "r"(kCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  unsigned long long* tl = (a.tl && blockIdx.x == gridDim.x - 1 && blockIdx.y == 0 && tid == 0) ? a.tl : nullptr;
+  int ti = 0;
+  if (tl) tl[ti++] = global_timer_ns();
   const float* qsrc = a.q + (long)q0 * a.ldq + (long)h * D;
   stage_rows<BQ, D>(sQ, qsrc, a.ldq, nq);
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = *tmem_slot;
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
   const uint32_t uQ = smem_u32(sQ), uKV = smem_u32(sKV), uP = smem_u32(sP);
 
   const float* kbase = a.k + (long)kvh * a.kv_head_stride + (long)k0 * a.ldk;
   const float* vbase = a.v + (long)kvh * a.kv_head_stride + (long)k0 * a.ldk;
-  const int my_last = CAUSAL ? qpos0 + tid : nk - 1;  // last key this row may see
-  float o[D];
+  const int my_last = CAUSAL ? qpos0 + row : nk - 1;  // last key this row may see
+  float o[DH];
 #pragma unroll
-  for (int d = 0; d < D; ++d) o[d] = 0.f;
+  for (int d = 0; d < DH; ++d) o[d] = 0.f;
   float m_run = -1e30f, l_run = 0.f;
   uint32_t phase = 0;
   bool ok = true;
@@ -201,7 +230,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnArgs a) 
   for (int kb = 0; kb < nk && ok; kb += BK) {
     const int valid = min(BK, nk - kb);
     // ---- S = Q K^T
+    if (tl && ti < 60) tl[ti++] = global_timer_ns();
     stage_rows<BK, D>(sKV, kbase + (long)kb * a.ldk, a.ldk, valid);
+    if (tl && ti < 60) tl[ti++] = global_timer_ns();
     fence_async_smem();
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
@@ -219,48 +250,57 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnArgs a) 
     }
     ok = __syncthreads_and(mbar_wait(bar, phase, a.err, 21)) != 0;
     phase ^= 1u;
+    if (tl && ti < 60) tl[ti++] = global_timer_ns();
     asm volatile("tcgen05.fence::after_thread_sync;");
-    // ---- online softmax of this row's block
-    float s[BK];
+    // ---- online softmax: this warp's half of the row's scores
+    float s[SH];
 #pragma unroll
-    for (int c = 0; c < BK; c += 32) {
+    for (int c = 0; c < SH; c += 32) {
       uint32_t r[32];
-      TMEM_LD32(trow + (uint32_t)c, r);
+      TMEM_LD32(trow + (uint32_t)(half * SH + c), r);
       asm volatile("tcgen05.wait::ld.sync.aligned;");
 #pragma unroll
       for (int j = 0; j < 32; ++j) s[c + j] = __uint_as_float(r[j]);
     }
-    float m_blk = -1e30f;
+    const int kj0 = kb + half * SH;  // key index of s[0]
+    float m_part = -1e30f;
 #pragma unroll
-    for (int j = 0; j < BK; ++j) {
-      const bool vis = (kb + j < nk) && (kb + j <= my_last);
+    for (int j = 0; j < SH; ++j) {
+      const bool vis = (kj0 + j < nk) && (kj0 + j <= my_last);
       s[j] = vis ? __fmul_rn(s[j], a.scale) : -INFINITY;
-      m_blk = fmaxf(m_blk, s[j]);
+      m_part = fmaxf(m_part, s[j]);
     }
-    const float m_new = fmaxf(m_run, m_blk);
+    red_max[half * BQ + row] = m_part;
+    __syncthreads();
+    const float m_new = fmaxf(m_run, fmaxf(red_max[row], red_max[BQ + row]));
     const float corr = expf(__fsub_rn(m_run, m_new));
     float psum = 0.f;
 #pragma unroll
-    for (int j = 0; j < BK; ++j) {
+    for (int j = 0; j < SH; ++j) {
       s[j] = s[j] == -INFINITY ? 0.f : expf(__fsub_rn(s[j], m_new));
       psum = __fadd_rn(psum, s[j]);
     }
-    l_run = __fadd_rn(__fmul_rn(l_run, corr), psum);
+    red_sum[half * BQ + row] = psum;
     m_run = m_new;
-    // P planes (this row) and V^T planes (the K planes are no longer read: S is complete)
+    // P planes (this warp's columns of the row) and V^T planes (S is complete: K is free)
 #pragma unroll
-    for (int j0 = 0; j0 < BK; j0 += 8) {
+    for (int j0 = 0; j0 < SH; j0 += 8) {
       __align__(16) __nv_bfloat16 ph[8], pm[8], pl[8];
 #pragma unroll
       for (int t = 0; t < 8; ++t) split3_bf16(s[j0 + t], ph[t], pm[t], pl[t]);
-      *reinterpret_cast<uint4*>(sP + sw_off(BQ, BK, 0, tid, j0)) = *reinterpret_cast<uint4*>(ph);
-      *reinterpret_cast<uint4*>(sP + sw_off(BQ, BK, 1, tid, j0)) = *reinterpret_cast<uint4*>(pm);
-      *reinterpret_cast<uint4*>(sP + sw_off(BQ, BK, 2, tid, j0)) = *reinterpret_cast<uint4*>(pl);
+      const int col = half * SH + j0;
+      *reinterpret_cast<uint4*>(sP + sw_off(BQ, BK, 0, row, col)) = *reinterpret_cast<uint4*>(ph);
+      *reinterpret_cast<uint4*>(sP + sw_off(BQ, BK, 1, row, col)) = *reinterpret_cast<uint4*>(pm);
+      *reinterpret_cast<uint4*>(sP + sw_off(BQ, BK, 2, row, col)) = *reinterpret_cast<uint4*>(pl);
     }
+    if (tl && ti < 60) tl[ti++] = global_timer_ns();
     stage_vt<BK, D>(sKV, vbase + (long)kb * a.ldk, a.ldk, valid);
+    if (tl && ti < 60) tl[ti++] = global_timer_ns();
     fence_async_smem();
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
+    // row sum in a fixed order (half 0 + half 1): both warps of a row keep the same l
+    l_run = __fadd_rn(__fmul_rn(l_run, corr), __fadd_rn(red_sum[row], red_sum[BQ + row]));
     // ---- O_blk = P V
     if (tid == 0 && ok) {
       asm volatile("tcgen05.fence::after_thread_sync;");
@@ -276,11 +316,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnArgs a) 
     }
     if (ok) ok = __syncthreads_and(mbar_wait(bar, phase, a.err, 22)) != 0;
     phase ^= 1u;
+    if (tl && ti < 60) tl[ti++] = global_timer_ns();
     asm volatile("tcgen05.fence::after_thread_sync;");
 #pragma unroll
-    for (int c = 0; c < D; c += 32) {
+    for (int c = 0; c < DH; c += 32) {
       uint32_t r[32];
-      TMEM_LD32(trow + (uint32_t)(BK + c), r);
+      TMEM_LD32(trow + (uint32_t)(BK + half * DH + c), r);
       asm volatile("tcgen05.wait::ld.sync.aligned;");
 #pragma unroll
       for (int j = 0; j < 32; ++j) o[c + j] = __fadd_rn(__fmul_rn(o[c + j], corr), __uint_as_float(r[j]));
@@ -289,12 +330,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnArgs a) 
     __syncthreads();  // the next block's operands overwrite sKV / sP and its MMAs reuse TMEM
   }
 
-  if (ok && tid < nq) {
+  if (tl && ti < 63) tl[ti++] = global_timer_ns();
+  if (ok && row < nq) {
     const float inv = l_run > 0.f ? __fdiv_rn(1.0f, l_run) : 0.f;
-    float* orow = a.out + (long)(q0 + tid) * a.ldo + (long)h * D;
-    __nv_bfloat16* prow = a.planes ? a.planes + (long)(q0 + tid) * a.ldo + (long)h * D : nullptr;
+    float* orow = a.out + (long)(q0 + row) * a.ldo + (long)h * D + half * DH;
+    __nv_bfloat16* prow = a.planes ? a.planes + (long)(q0 + row) * a.ldo + (long)h * D + half * DH : nullptr;
 #pragma unroll
-    for (int d = 0; d < D; d += 4) {
+    for (int d = 0; d < DH; d += 4) {
       float4 v = make_float4(__fmul_rn(o[d], inv), __fmul_rn(o[d + 1], inv), __fmul_rn(o[d + 2], inv),
                              __fmul_rn(o[d + 3], inv));
       *reinterpret_cast<float4*>(orow + d) = v;
@@ -316,10 +358,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnArgs a) 
 
 template <int D, int BK, bool CAUSAL>
 constexpr int attn_smem() {
-  return 1024 + 3 * BQ * D * 2 + 3 * BK * D * 2 + 3 * BQ * BK * 2 + 64;
+  return 1024 + 3 * BQ * D * 2 + 3 * BK * D * 2 + 3 * BQ * BK * 2 + 4 * BQ * 4 + 64;
 }
 
 int* g_attn_err[16] = {};
+unsigned long long* g_attn_tl = nullptr;
 
 int* attn_err() {
   int dev = 0;
@@ -348,7 +391,7 @@ bool window_attention_tc(const float* qkv, float* out, __nv_bfloat16* planes, lo
   a.q = qkv; a.ldq = 3L * d;
   a.k = qkv + d; a.v = qkv + 2L * d; a.ldk = 3L * d; a.kv_head_stride = 64; a.heads_per_kv = 1;
   a.out = out; a.ldo = d; a.planes = planes; a.plane = plane; a.scale = scale;
-  a.win = win_starts; a.err = err;
+  a.win = win_starts; a.err = err; a.tl = g_attn_tl;
   attn_tc_kernel<64, 128, false><<<dim3(n_windows, n_heads), kThreads, attn_smem<64, 128, false>(), s>>>(a);
   return true;
 }
@@ -364,10 +407,12 @@ bool prefill_attention_tc(const float* qkv, int S, int start, int n_heads, int n
   a.q = qkv; a.ldq = qd + 2L * kvd;
   a.k = kc; a.v = vc; a.ldk = 128; a.kv_head_stride = (long)max_seq * 128; a.heads_per_kv = n_heads / n_kv;
   a.out = out; a.ldo = qd; a.planes = planes; a.plane = plane; a.scale = scale;
-  a.n_q = S; a.start = start; a.err = err;
+  a.n_q = S; a.start = start; a.err = err; a.tl = g_attn_tl;
   attn_tc_kernel<128, 64, true><<<dim3(ceil_div(S, BQ), n_heads), kThreads, attn_smem<128, 64, true>(), s>>>(a);
   return true;
 }
+
+void attn_tc_set_timeline(unsigned long long* dev_buf) { g_attn_tl = dev_buf; }
 
 int attn_tc_error() {
   int dev = 0;

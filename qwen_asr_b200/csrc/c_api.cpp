@@ -454,6 +454,52 @@ int64_t qwen_asr_debug_quant(QwenAsrEngine* e, int32_t layer, int32_t which, int
   return e->ctx.eng.copy_quant(layer, which, q, s, cap_rows);
 }
 
+int32_t qwen_asr_debug_gemm_timed(int32_t M, int32_t N, int32_t K, int32_t epi, int32_t reps, float* ms,
+                                  uint64_t* timeline) {
+  // Times `reps` back-to-back tensor-core GEMMs of random operands on the current device
+  // (CUDA events); timeline (optional, 148 x 8 stamps) records the last launch.
+  if (M <= 0 || N <= 0 || K <= 0 || reps <= 0 || !ms) return -1;
+  const int ncols = epi == qasr::EPI_SWIGLU ? N / 2 : N;
+  qasr::DevBuf<float> dA, dC, db;
+  qasr::DevBuf<uint16_t> dB;
+  qasr::DevBuf<unsigned long long> dtl;
+  if (!dA.alloc((size_t)M * K) || !dB.alloc((size_t)N * K) || !dC.alloc((size_t)M * ncols) || !db.alloc(N) ||
+      !dtl.alloc(148 * 8))
+    return -1;
+  cudaMemset(dA.p, 0, (size_t)M * K * 4);
+  cudaMemset(dB.p, 0, (size_t)N * K * 2);
+  cudaMemset(db.p, 0, (size_t)N * 4);
+  cudaMemset(dC.p, 0, (size_t)M * ncols * 4);
+  cudaMemset(dtl.p, 0, 148 * 8 * 8);
+  qasr::GemmArgs g;
+  g.M = M; g.N = N; g.K = K; g.A = dA.p; g.lda = K; g.B = dB.p; g.ldb = K; g.C = dC.p; g.ldc = ncols; g.epi = epi;
+  g.bias = db.p; g.resid = dC.p; g.ldr = ncols;
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  if (!qasr::gemm_tc(g, 0)) return -2;  // warm-up (tensor maps, scratch)
+  cudaEventRecord(e0, 0);
+  for (int i = 0; i < reps; ++i) {
+    if (timeline && i == reps - 1) qasr::gemm_tc_set_timeline(dtl.p);
+    qasr::gemm_tc(g, 0);
+  }
+  cudaEventRecord(e1, 0);
+  qasr::gemm_tc_set_timeline(nullptr);
+  if (cudaEventSynchronize(e1) != cudaSuccess) return -3;
+  cudaEventElapsedTime(ms, e0, e1);
+  *ms /= reps;
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (timeline) cudaMemcpy(timeline, dtl.p, 148 * 8 * 8, cudaMemcpyDeviceToHost);
+  return qasr::gemm_tc_error() ? -4 : 0;
+}
+
+int32_t qwen_asr_debug_attn_timeline(uint64_t* dev_buf) {
+  // Points the attention kernels' debug timeline at a device buffer of 64 u64 (NULL: off).
+  qasr::attn_tc_set_timeline((unsigned long long*)dev_buf);
+  return 0;
+}
+
 int32_t qwen_asr_debug_gemm(int32_t M, int32_t N, int32_t K, const float* A, const uint16_t* B, const float* bias,
                             const float* resid, int32_t epi, int32_t impl, float* C) {
   if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) return -1;

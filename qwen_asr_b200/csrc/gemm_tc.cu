@@ -11,11 +11,12 @@
 // the producing kernel (LayerNorm/RMSNorm, GEMM epilogues, attention) or from split3_kernel.
 //
 // Schedule. A persistent grid (one CTA per SM) walks work units (m tile, n tile, k split)
-// in a fixed order. Warp 0 issues TMA into a 3-stage ring (per stage the three A planes and
-// the B tile, 64 KB), warp 1 issues 12 MMAs (128x128x16) per stage into one of two TMEM
-// accumulators, and warps 2-5 drain the other accumulator: tcgen05.ld, a transpose through
-// shared memory, then the fused epilogue with coalesced row-wise stores. So the epilogue of
-// one unit overlaps the mainloop of the next.
+// in a fixed order. Tiles are 128 x BN, BN = 128 for wide outputs and 64 for narrow ones.
+// Warp 0 issues TMA into a 3-stage ring (per stage the three A planes and the B tile), warp 1
+// issues 12 MMAs (128 x BN x 16) per stage into one of two TMEM accumulators, and warps 2-9
+// drain the other accumulator (two warps per TMEM lane quarter, each half the columns):
+// tcgen05.ld, a transpose through shared memory, then the fused epilogue with coalesced
+// row-wise stores. So the epilogue of one unit overlaps the mainloop of the next.
 //
 // Split K. A GEMM with few output tiles splits K into S parts so that about 148 CTAs work.
 // S depends only on the call's (N, K) and its split policy, never on M, so a row's result
@@ -36,14 +37,23 @@
 namespace qasr {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3, NPART = 3;
-constexpr int kTile = BM * BK * 2;           // 16 KB: one bf16 operand tile (an A plane or B)
-constexpr int kStage = (NPART + 1) * kTile;  // 64 KB
-constexpr int kEpiPitch = 33;                // floats per staged row (bank-conflict padding)
-constexpr int kEpiBytes = 4 * 32 * kEpiPitch * 4;
-constexpr int kSmem = 1024 /*align*/ + STAGES * kStage + kEpiBytes + 256 /*barriers*/;
-constexpr int kThreads = 192;
+constexpr int BM = 128, BK = 64, STAGES = 3, NPART = 3;
+constexpr int kTile = BM * BK * 2;  // 16 KB: one bf16 A plane tile
+constexpr int kEpiWarps = 8;
+constexpr int kEpiPitch = 33;       // floats per staged row (bank-conflict padding)
+constexpr int kEpiBytes = kEpiWarps * 32 * kEpiPitch * 4;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+template <int BN>
+struct Tile {
+  static constexpr int kB = BN * BK * 2;              // B tile bytes
+  static constexpr int kStage = NPART * kTile + kB;   // 56 or 64 KB
+  static constexpr int kSmem = 1024 + STAGES * kStage + kEpiBytes + 256;
+  // kind::f16 instruction descriptor: f32 accumulator, bf16 A and B, both K-major, M = 128
+  static constexpr uint32_t kIdesc =
+      (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+};
 constexpr int kSms = 148;
+constexpr int kMaxSplit = 16;
 
 struct TcParams {
   int M, N, K, MT, NT, S, nk, units;
@@ -59,6 +69,10 @@ struct TcParams {
   float* ws;     // split-K partial tiles [tile][S][BM][BN]
   int* tickets;  // [tile], zero at rest
   int* err;
+  // Optional timeline (debug): per CTA 8 %globaltimer stamps: entry, set-up done, first stage
+  // landed, first unit's MMAs committed, first unit's accumulator ready, first unit stored,
+  // (unused), exit.
+  unsigned long long* tl;
 };
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row groups
@@ -72,10 +86,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   d |= (uint64_t)2 << 61;            // SWIZZLE_128B
   return d;
 }
-
-// Instruction descriptor, kind::f16: f32 accumulator, bf16 A and B, both K-major, M=128, N=128.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(BM >> 4) << 24);
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -92,11 +102,12 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accum) {
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accum) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accum));
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum));
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -104,7 +115,7 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 #define TMEM_LD32(taddr, r)                                                                                       \
   asm volatile(                                                                                                   \
@@ -139,24 +150,9 @@ __device__ __forceinline__ void store_out(const TcParams& p, int m, int n, float
     q[2 * p.cs_plane] = l;
   }
 }
-__device__ __forceinline__ float epi_value(const TcParams& p, int m, int n, float v) {
-  switch (p.epi) {
-    case EPI_BIAS:
-      return __fadd_rn(v, p.bias[n]);
-    case EPI_BIAS_GELU:
-      return gelu_tanh(__fadd_rn(v, p.bias[n]));
-    case EPI_RESID: {
-      float r = p.resid[(size_t)m * p.ldr + n];
-      if (p.bias) r = __fadd_rn(r, p.bias[n]);
-      return __fadd_rn(v, r);
-    }
-    default:
-      return v;
-  }
-}
-
 // One 32x32 block (rows m0.., columns n0..) staged in st[32][kEpiPitch]: epilogue + stores,
-// lane = column, so every store instruction writes consecutive addresses of one row.
+// lane = column, so every store instruction writes consecutive addresses of one row. All
+// global loads of the block (bias, residual rows) are issued before the first use.
 __device__ __forceinline__ void epilogue_block(const TcParams& p, const float* st, int m0, int n0, int lane) {
   if (p.epi == EPI_SWIGLU) {
     // columns (2j, 2j+1) = (gate, up) -> output column n/2 + j; two rows per pass
@@ -168,20 +164,39 @@ __device__ __forceinline__ void epilogue_block(const TcParams& p, const float* s
     return;
   }
   const int n = n0 + lane;
-#pragma unroll 4
+  const bool n_ok = n < p.N;
+  const float bias = (p.bias && n_ok && p.epi != EPI_STORE) ? p.bias[n] : 0.f;
+  float res[32];
+  if (p.epi == EPI_RESID) {
+#pragma unroll
+    for (int r = 0; r < 32; ++r) res[r] = (n_ok && m0 + r < p.M) ? p.resid[(size_t)(m0 + r) * p.ldr + n] : 0.f;
+  }
+#pragma unroll
   for (int r = 0; r < 32; ++r) {
     const int m = m0 + r;
-    if (m < p.M && n < p.N) store_out(p, m, n, epi_value(p, m, n, st[r * kEpiPitch + lane]));
+    if (m >= p.M || !n_ok) continue;
+    const float acc = st[r * kEpiPitch + lane];
+    float v;
+    switch (p.epi) {
+      case EPI_BIAS: v = __fadd_rn(acc, bias); break;
+      case EPI_BIAS_GELU: v = gelu_tanh(__fadd_rn(acc, bias)); break;
+      case EPI_RESID: v = __fadd_rn(acc, p.bias ? __fadd_rn(res[r], bias) : res[r]); break;
+      default: v = acc;
+    }
+    store_out(p, m, n, v);
   }
 }
 
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
                                                               const __grid_constant__ CUtensorMap map_b,
                                                               const TcParams p) {
+  using T = Tile<BN>;
+  constexpr int kChunks = BN / 64;  // 32-column chunks per epilogue warp (each warp: half the columns)
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  float* epi_st = reinterpret_cast<float*>(smem + STAGES * kStage);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStage + kEpiBytes);
+  float* epi_st = reinterpret_cast<float*>(smem + STAGES * T::kStage);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * T::kStage + kEpiBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -189,6 +204,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
   volatile int* abort_flag = last_flag + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  unsigned long long* tl = (p.tl && blockIdx.x < kSms) ? p.tl + blockIdx.x * 8 : nullptr;
+  if (tl && tid == 0) tl[0] = global_timer_ns();
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -197,12 +214,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], kEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0) {  // TMEM: two 128 x 128 f32 accumulators = 256 columns
+  if (warp == 0) {  // TMEM: two 128 x BN f32 accumulators
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(2 * BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -211,6 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem = *tmem_slot;
+  if (tl && tid == 0) tl[1] = global_timer_ns();
 
   if (warp == 0) {
     // ---- TMA producer
@@ -226,8 +244,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             *abort_flag = 1;
             break;
           }
-          unsigned char* sp = smem + st * kStage;
-          mbar_expect_tx(&full[st], kStage);
+          unsigned char* sp = smem + st * T::kStage;
+          mbar_expect_tx(&full[st], T::kStage);
 #pragma unroll
           for (int q = 0; q < NPART; ++q) tma_load_3d(sp + q * kTile, &map_a, kt * BK, mt * BM, q, &full[st]);
           tma_load_2d(sp + NPART * kTile, &map_b, kt * BK, nt * BN, &full[st]);
@@ -256,14 +274,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             ok = false;
             break;
           }
+          if (tl && it == 0) tl[2] = global_timer_ns();
           asm volatile("tcgen05.fence::after_thread_sync;");
-          const uint32_t sa = smem_u32(smem + st * kStage), sb = sa + NPART * kTile;
+          const uint32_t sa = smem_u32(smem + st * T::kStage), sb = sa + NPART * kTile;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {  // K = 16 per instruction = 32 bytes along the row
             const uint64_t bd = sw128_desc(sb + kk * 32);
 #pragma unroll
             for (int q = 0; q < NPART; ++q)
-              mma_bf16(acc, sw128_desc(sa + q * kTile + kk * 32), bd, (kt > k0 || kk > 0 || q > 0) ? 1u : 0u);
+              mma_bf16(acc, sw128_desc(sa + q * kTile + kk * 32), bd, T::kIdesc,
+                       (kt > k0 || kk > 0 || q > 0) ? 1u : 0u);
           }
           mma_commit(&empty[st]);  // stage reusable once these MMAs have read it
         }
@@ -272,11 +292,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           break;
         }
         mma_commit(&acc_full[ab]);
+        if (tl && lt == 0) tl[3] = global_timer_ns();
       }
     }
   } else {
-    // ---- epilogue warps 2..5: TMEM lane quarter q = warp % 4 -> tile rows 32q..32q+31
-    const int q = warp & 3;
+    // ---- epilogue warps 2..9: TMEM lane quarter q = warp % 4 -> tile rows 32q..32q+31;
+    // column half h = (warp - 2) / 4 -> columns [h * BN / 2, (h + 1) * BN / 2)
+    const int q = warp & 3, half = (warp - 2) >> 2;
     float* st = epi_st + (warp - 2) * 32 * kEpiPitch;
     int lt = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++lt) {
@@ -287,25 +309,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         *abort_flag = 1;
         break;
       }
+      if (tl && tid == 64 && lt == 0) tl[4] = global_timer_ns();
       asm volatile("tcgen05.fence::after_thread_sync;");
-      const int m0 = mt * BM + q * 32, nb = nt * BN;
-      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
+      const int m0 = mt * BM + q * 32, nb = nt * BN + half * (BN / 2);
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN + half * (BN / 2));
       const int tile = nt * p.MT + mt;
       float* wsp = p.S > 1 ? p.ws + ((size_t)tile * p.S + s) * (BM * BN) : nullptr;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c = 0; c < kChunks; ++c) {
         uint32_t r[32];
-        TMEM_LD32(trow + c0, r);
+        TMEM_LD32(trow + c * 32, r);
         asm volatile("tcgen05.wait::ld.sync.aligned;");
 #pragma unroll
         for (int j = 0; j < 32; ++j) st[lane * kEpiPitch + j] = __uint_as_float(r[j]);
         __syncwarp();
         if (wsp) {
-          // raw partial, rows 32q.. of the tile, columns c0..c0+31
-#pragma unroll 4
-          for (int rr = 0; rr < 32; ++rr) wsp[(size_t)(q * 32 + rr) * BN + c0 + lane] = st[rr * kEpiPitch + lane];
+          // raw partial: rows 32q.. of the tile, this warp's 32 columns
+          float* w = wsp + (size_t)(q * 32) * BN + half * (BN / 2) + c * 32 + lane;
+#pragma unroll 8
+          for (int rr = 0; rr < 32; ++rr) w[(size_t)rr * BN] = st[rr * kEpiPitch + lane];
         } else {
-          epilogue_block(p, st, m0, nb + c0, lane);
+          epilogue_block(p, st, m0, nb + c * 32, lane);
         }
         __syncwarp();
       }
@@ -321,18 +345,32 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         epi_bar();
         if (*last_flag) {
           __threadfence();
-          const float* w0 = p.ws + (size_t)tile * p.S * (BM * BN);
+          const float* w0 = p.ws + (size_t)tile * p.S * (BM * BN) + (size_t)(q * 32) * BN + half * (BN / 2) + lane;
 #pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 32) {
-#pragma unroll 2
-            for (int rr = 0; rr < 32; ++rr) {
-              const size_t off = (size_t)(q * 32 + rr) * BN + c0 + lane;
-              float v = __ldcg(w0 + off);
-              for (int k = 1; k < p.S; ++k) v = __fadd_rn(v, __ldcg(w0 + (size_t)k * (BM * BN) + off));
-              st[rr * kEpiPitch + lane] = v;
+          for (int c = 0; c < kChunks; ++c) {
+            // partials summed in split order; two splits' 32 rows in flight per round
+            float v[32];
+#pragma unroll
+            for (int rr = 0; rr < 32; ++rr) v[rr] = __ldcg(w0 + (size_t)rr * BN + c * 32);
+#pragma unroll 1
+            for (int k = 1; k < p.S; k += 2) {
+              const bool two = k + 1 < p.S;
+              float t0[32], t1[32];
+#pragma unroll
+              for (int rr = 0; rr < 32; ++rr) {
+                t0[rr] = __ldcg(w0 + (size_t)k * (BM * BN) + (size_t)rr * BN + c * 32);
+                t1[rr] = two ? __ldcg(w0 + (size_t)(k + 1) * (BM * BN) + (size_t)rr * BN + c * 32) : 0.f;
+              }
+#pragma unroll
+              for (int rr = 0; rr < 32; ++rr) {
+                v[rr] = __fadd_rn(v[rr], t0[rr]);
+                if (two) v[rr] = __fadd_rn(v[rr], t1[rr]);
+              }
             }
+#pragma unroll
+            for (int rr = 0; rr < 32; ++rr) st[rr * kEpiPitch + lane] = v[rr];
             __syncwarp();
-            epilogue_block(p, st, m0, nb + c0, lane);
+            epilogue_block(p, st, m0, nb + c * 32, lane);
             __syncwarp();
           }
           epi_bar();
@@ -340,11 +378,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         }
         epi_bar();
       }
+      if (tl && tid == 64 && lt == 0) tl[5] = global_timer_ns();
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+  if (tl && tid == 0) tl[7] = global_timer_ns();
 }
 
 // f32 rows [M][lda] -> bf16 planes hi/mid/lo [3][plane] of rows [M][K] (ld = K).
@@ -387,15 +427,17 @@ EncodeTiledFn get_encode() {
 // engine's activation buffers only change address when they grow.
 struct MapKey {
   const void* base;
-  long long rows, cols, ld, planes, plane;
+  long long rows, cols, ld, planes, plane, box_rows;
   bool operator==(const MapKey& o) const {
-    return base == o.base && rows == o.rows && cols == o.cols && ld == o.ld && planes == o.planes && plane == o.plane;
+    return base == o.base && rows == o.rows && cols == o.cols && ld == o.ld && planes == o.planes &&
+           plane == o.plane && box_rows == o.box_rows;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     size_t h = std::hash<const void*>()(k.base);
-    for (long long v : {k.rows, k.cols, k.ld, k.planes, k.plane}) h = h * 1000003u ^ std::hash<long long>()(v);
+    for (long long v : {k.rows, k.cols, k.ld, k.planes, k.plane, k.box_rows})
+      h = h * 1000003u ^ std::hash<long long>()(v);
     return h;
   }
 };
@@ -403,9 +445,10 @@ std::mutex g_map_mu;
 std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
 // bf16 operand [planes][rows][cols] (row pitch ld, plane pitch `plane` elements), box =
-// 64 columns x 128 rows x 1 plane, 128-byte swizzle; out-of-range boxes read zeros.
-bool operand_map(CUtensorMap* out, const void* base, int rows, int cols, int ld, int planes, long long plane) {
-  MapKey key{base, rows, cols, ld, planes, plane};
+// 64 columns x box_rows rows x 1 plane, 128-byte swizzle; out-of-range boxes read zeros.
+bool operand_map(CUtensorMap* out, const void* base, int rows, int cols, int ld, int planes, long long plane,
+                 int box_rows) {
+  MapKey key{base, rows, cols, ld, planes, plane, box_rows};
   std::lock_guard<std::mutex> lk(g_map_mu);
   auto itm = g_maps.find(key);
   if (itm != g_maps.end()) {
@@ -416,7 +459,7 @@ bool operand_map(CUtensorMap* out, const void* base, int rows, int cols, int ld,
   if (!enc) return false;
   cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)planes};
   cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)plane * 2};
-  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)BM, 1};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUtensorMap m;
   if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, planes > 1 ? 3 : 2, const_cast<void*>(base), dims, strides, box, estr,
@@ -442,6 +485,7 @@ struct TcScratch {
 TcScratch g_tc[16];
 std::mutex g_tc_mu;
 long g_fallbacks = 0;
+unsigned long long* g_gemm_tl = nullptr;  // debug timeline target (qwen_asr_debug_gemm_timeline)
 
 // Grow-only device buffer (the engine calls gemm outside stream capture).
 template <typename T>
@@ -465,6 +509,8 @@ bool grow(T*& p, size_t& cap, size_t need, cudaStream_t s, bool zero) {
 
 bool gemm_tc_available() { return get_encode() != nullptr; }
 
+void gemm_tc_set_timeline(unsigned long long* dev_buf) { g_gemm_tl = dev_buf; }
+
 long gemm_tc_fallbacks() {
   std::lock_guard<std::mutex> lk(g_tc_mu);
   return g_fallbacks;
@@ -474,14 +520,17 @@ void gemm_tc_note_fallback() {
   ++g_fallbacks;
 }
 
+// Output tile width: 128 columns when that already gives about half a wave of 128 x 128
+// tiles for a ~384-row call, else 64 (twice the tiles for narrow outputs).
+int gemm_tile_n(int N) { return 3 * ceil_div(N, 128) >= 74 ? 128 : 64; }
+
 int gemm_split_k(int N, int K, int policy) {
-  if (policy > 0) return policy;
-  const int nk = (K + BK - 1) / BK, nt = (N + BN - 1) / BN;
+  if (policy > 0) return std::min(policy, kMaxSplit);
   if (policy < 0) return 1;
-  // about one wave of 148 CTAs for a ~384-row call (3 row tiles), >= 4 k-steps per split
-  int s = (kSms + 3 * nt - 1) / (3 * nt);
-  s = std::min(s, std::max(1, nk / 4));
-  return std::max(1, std::min(s, 16));
+  const int nk = ceil_div(K, BK), nt = ceil_div(N, gemm_tile_n(N));
+  // fill about one wave of 148 CTAs for a ~384-row call (3 row tiles), >= 8 k-steps per split
+  const int s = std::min(kSms / (3 * nt), nk / 8);
+  return std::max(1, std::min(s, kMaxSplit));
 }
 
 bool make_tma_2d_u16(void* map, const void* base, int rows, int cols, int box_cols, int box_rows, bool swizzle128) {
@@ -509,6 +558,7 @@ bool gemm_tc(const GemmArgs& a, cudaStream_t s) {
   cudaGetDevice(&dev);
   if (dev >= 16) return false;
   TcScratch& sc = g_tc[dev];
+  const int BN = gemm_tile_n(a.N);
   const int MT = ceil_div(a.M, BM), NT = ceil_div(a.N, BN), nk = ceil_div(a.K, BK);
   const int S = std::min(gemm_split_k(a.N, a.K, a.split_k), nk);
   const __nv_bfloat16* planes = a.a_split;
@@ -519,7 +569,8 @@ bool gemm_tc(const GemmArgs& a, cudaStream_t s) {
     if (!sc.init) {
       if (cudaMalloc(&sc.err, sizeof(int)) != cudaSuccess) return false;
       cudaMemset(sc.err, 0, sizeof(int));
-      cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+      cudaFuncSetAttribute(gemm_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Tile<64>::kSmem);
+      cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, Tile<128>::kSmem);
       sc.init = true;
     }
     if (!planes) {
@@ -539,15 +590,19 @@ bool gemm_tc(const GemmArgs& a, cudaStream_t s) {
   }
   if ((pld * 2) % 16 != 0 || (pplane * 2) % 16 != 0) return false;
   CUtensorMap ma, mb;
-  if (!operand_map(&ma, planes, a.M, a.K, pld, NPART, pplane) || !operand_map(&mb, a.B, a.N, a.K, a.ldb, 1, 0))
+  if (!operand_map(&ma, planes, a.M, a.K, pld, NPART, pplane, BM) ||
+      !operand_map(&mb, a.B, a.N, a.K, a.ldb, 1, 0, BN))
     return false;
   TcParams p;
   p.M = a.M; p.N = a.N; p.K = a.K; p.MT = MT; p.NT = NT; p.S = S; p.nk = nk; p.units = MT * NT * S;
   p.epi = a.epi; p.C = a.C; p.ldc = a.ldc; p.bias = a.bias; p.resid = a.resid; p.ldr = a.ldr;
   p.cs = a.c_split; p.cs_ld = a.c_split_ld; p.cs_plane = a.c_split_plane;
-  p.ws = sc.ws; p.tickets = sc.tickets; p.err = sc.err;
+  p.ws = sc.ws; p.tickets = sc.tickets; p.err = sc.err; p.tl = g_gemm_tl;
   const int grid = std::min(p.units, kSms);
-  gemm_tc_kernel<<<grid, kThreads, kSmem, s>>>(ma, mb, p);
+  if (BN == 128)
+    gemm_tc_kernel<128><<<grid, kThreads, Tile<128>::kSmem, s>>>(ma, mb, p);
+  else
+    gemm_tc_kernel<64><<<grid, kThreads, Tile<64>::kSmem, s>>>(ma, mb, p);
   return true;
 }
 

@@ -60,6 +60,8 @@ bool gemm_tc(const GemmArgs& a, cudaStream_t s);
 bool gemm_tc_available();
 // Bf16-weight GEMMs that had to leave the tensor cores since the library loaded.
 long gemm_tc_fallbacks();
+// Debug: the next tensor-core GEMM launches write 8 %globaltimer stamps per CTA (148 x 8) here.
+void gemm_tc_set_timeline(unsigned long long* dev_buf);
 void gemm_tc_note_fallback();
 // K splits the tensor-core GEMM uses for an (N, K) call under `policy` (GemmArgs::split_k).
 int gemm_split_k(int N, int K, int policy);
@@ -110,6 +112,8 @@ bool prefill_attention_tc(const float* qkv, int S, int start, int n_heads, int n
                           long long plane, cudaStream_t s);
 // Nonzero when a bounded wait inside the attention kernels gave up (clears the flag).
 int attn_tc_error();
+// Debug: attention launches stamp phase times (64 u64) of one CTA here while set.
+void attn_tc_set_timeline(unsigned long long* dev_buf);
 
 // ---------------------------------------------------------------- decoder
 void rms_norm_rows(const float* x, float* y, int rows, int d, const float* w, float eps, cudaStream_t s,
