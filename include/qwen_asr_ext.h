@@ -36,12 +36,6 @@ void qwen_asr_set_force_n_tokens(QwenAsrEngine* engine, int32_t n);
 int32_t qwen_asr_stream_push_many(QwenAsrEngine* engine, QwenAsrStreamState* const* states,
                                   const float* const* samples, const int32_t* n_samples, int32_t count,
                                   int32_t finalize, char** deltas_out);
-/* 1 (default): a single sequence decodes through the persistent one-launch-per-step kernel
- * (one CTA per SM, a TMA producer warp streaming the step's weights, grid barriers between
- * the phases of a layer) when the device supports it; 0: the multi-kernel chain. */
-void qwen_asr_set_persistent_decode(QwenAsrEngine* engine, int32_t on);
-/* 1 when the last single-sequence decode ran on the persistent kernel. */
-int32_t qwen_asr_persistent_decode_active(QwenAsrEngine* engine);
 /* Transcribes `count` independent segments [starts[i], ends[i]) of one buffer (each padded
  * to 0.5 s like the -S loop, transcribe.rs:374-384), decoding them in batches. texts_out[i]
  * receives segment i's text (free with qwen_asr_free_string). Returns 0, or -1 on error
@@ -186,6 +180,34 @@ int32_t qwen_asr_debug_lossy_trim(const char* bytes, int32_t n, char* out, int32
  * qwen_asr_load_model, qwen_asr_transcribe_file and qwen_asr_set_language apply), else 0. */
 int32_t qwen_asr_debug_valid_utf8(const char* s);
 int32_t qwen_asr_debug_normalize_language(const char* lang, char* out, int32_t cap);
+
+/* ---- multi-GPU pool (no counterpart in c_api.rs; the reference runs one context) ----
+ * One engine per GPU, each on its own worker thread. Segmented transcription shards the
+ * `-S` segments (transcribe.rs:328-423) over the GPUs longest-first and joins the texts in
+ * segment order (transcribe.rs:401-422); with past-text conditioning on, or one segment, the
+ * first GPU transcribes alone. n_devices = 0 uses every visible GPU; a device may be listed
+ * more than once (several engines on one GPU). */
+typedef struct QwenAsrPool QwenAsrPool;
+QwenAsrPool* qwen_asr_pool_new(const char* model_dir, const int32_t* devices, int32_t n_devices, int32_t verbosity);
+void qwen_asr_pool_free(QwenAsrPool* pool);
+int32_t qwen_asr_pool_size(const QwenAsrPool* pool);
+/* The engine of worker i (for per-engine settings and statistics); owned by the pool. */
+QwenAsrEngine* qwen_asr_pool_engine(QwenAsrPool* pool, int32_t i);
+void qwen_asr_pool_set_segment_sec(QwenAsrPool* pool, float sec);
+int32_t qwen_asr_pool_set_language(QwenAsrPool* pool, const char* language);
+void qwen_asr_pool_set_decode_mode(QwenAsrPool* pool, int32_t mode); /* 0 int8, 1 bf16 */
+void qwen_asr_pool_set_force_n_tokens(QwenAsrPool* pool, int32_t n);
+void qwen_asr_pool_stream_set_max_new_tokens(QwenAsrPool* pool, int32_t n);
+/* Like qwen_asr_transcribe_pcm, the segments spread over the pool's GPUs. */
+char* qwen_asr_pool_transcribe_pcm(QwenAsrPool* pool, const float* samples, int32_t n_samples);
+/* Like qwen_asr_stream_push_many; stream i runs on worker i % size, so a stream must keep
+ * its position in the list from call to call. */
+int32_t qwen_asr_pool_stream_push_many(QwenAsrPool* pool, QwenAsrStreamState* const* states,
+                                       const float* const* samples, const int32_t* n_samples, int32_t count,
+                                       int32_t finalize, char** deltas_out);
+/* The pool's segment assignment (host only): worker_of[i] for segment lengths[i] over
+ * `workers` workers, longest first to the least-loaded worker. Returns 0 or -1. */
+int32_t qwen_asr_debug_assign_longest_first(const int64_t* lengths, int32_t n, int32_t workers, int32_t* worker_of);
 
 #ifdef __cplusplus
 }

@@ -52,10 +52,8 @@ SIGNATURES = {
     "qwen_asr_set_force_n_tokens": (None, [_VP, C.c_int32]),
     "qwen_asr_set_use_graph": (None, [_VP, C.c_int32]),
     "qwen_asr_set_decode_batch": (C.c_int32, [_VP, C.c_int32]),
-    "qwen_asr_set_persistent_decode": (None, [_VP, C.c_int32]),
     "qwen_asr_stream_push_many": (C.c_int32, [_VP, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), _I32P, C.c_int32,
                                               C.c_int32, C.POINTER(C.c_void_p)]),
-    "qwen_asr_persistent_decode_active": (C.c_int32, [_VP]),
     "qwen_asr_transcribe_segments": (C.c_int32, [_VP, _F32P, C.c_int64, C.POINTER(C.c_int64), C.POINTER(C.c_int64),
                                                  C.c_int32, C.POINTER(C.c_void_p)]),
     "qwen_asr_last_tokens": (C.c_int32, [_VP, C.c_int32, _I32P, C.c_int32]),
@@ -69,6 +67,19 @@ SIGNATURES = {
     "qwen_asr_debug_gemm": (C.c_int32, [C.c_int32, C.c_int32, C.c_int32, _F32P, C.POINTER(C.c_uint16), _F32P,
                                          _F32P, C.c_int32, C.c_int32, _F32P]),
     "qwen_asr_gemm_fallbacks": (C.c_int64, []),
+    "qwen_asr_pool_new": (_VP, [C.c_char_p, _I32P, C.c_int32, C.c_int32]),
+    "qwen_asr_pool_free": (None, [_VP]),
+    "qwen_asr_pool_size": (C.c_int32, [_VP]),
+    "qwen_asr_pool_engine": (_VP, [_VP, C.c_int32]),
+    "qwen_asr_pool_set_segment_sec": (None, [_VP, C.c_float]),
+    "qwen_asr_pool_set_language": (C.c_int32, [_VP, C.c_char_p]),
+    "qwen_asr_pool_set_decode_mode": (None, [_VP, C.c_int32]),
+    "qwen_asr_pool_set_force_n_tokens": (None, [_VP, C.c_int32]),
+    "qwen_asr_pool_stream_set_max_new_tokens": (None, [_VP, C.c_int32]),
+    "qwen_asr_pool_transcribe_pcm": (_VP, [_VP, _F32P, C.c_int32]),
+    "qwen_asr_pool_stream_push_many": (C.c_int32, [_VP, C.POINTER(C.c_void_p), C.POINTER(_F32P), _I32P, C.c_int32,
+                                                   C.c_int32, C.POINTER(C.c_void_p)]),
+    "qwen_asr_debug_assign_longest_first": (C.c_int32, [_I64P, C.c_int32, C.c_int32, _I32P]),
     "qwen_asr_debug_attn_timeline": (C.c_int32, [C.c_void_p]),
     "qwen_asr_debug_gemm_timed": (C.c_int32, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                               C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
@@ -213,12 +224,6 @@ class Engine:
             raise RuntimeError(last_error())
         return [_take_string(out[i]) for i in range(k)]
 
-    def set_persistent_decode(self, on: bool):
-        lib().qwen_asr_set_persistent_decode(self._h, int(on))
-
-    def persistent_decode_active(self) -> bool:
-        return bool(lib().qwen_asr_persistent_decode_active(self._h))
-
     def set_decode_batch(self, n: int) -> int:
         return lib().qwen_asr_set_decode_batch(self._h, n)
 
@@ -362,6 +367,73 @@ class Engine:
         if n < 0:
             raise RuntimeError(last_error())
         return ids[:n_steps], lg, hd
+
+
+class Pool:
+    """One engine per GPU behind the C ABI (qwen_asr_pool_*): segmented transcription and
+    concurrent streams sharded over the GPUs by the library's own worker threads."""
+
+    def __init__(self, model_dir: str, devices=(), verbosity: int = 0):
+        d = np.ascontiguousarray(list(devices), dtype=np.int32)
+        self._h = lib().qwen_asr_pool_new(model_dir.encode(), d.ctypes.data_as(_I32P) if len(d) else None, len(d),
+                                          verbosity)
+        if not self._h:
+            raise RuntimeError(f"pool load failed: {last_error()}")
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().qwen_asr_pool_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def size(self) -> int:
+        return lib().qwen_asr_pool_size(self._h)
+
+    def set_segment_sec(self, sec: float):
+        lib().qwen_asr_pool_set_segment_sec(self._h, sec)
+
+    def set_language(self, lang: str) -> int:
+        return lib().qwen_asr_pool_set_language(self._h, lang.encode())
+
+    def set_decode_mode(self, mode: str):
+        lib().qwen_asr_pool_set_decode_mode(self._h, 1 if mode == "bf16" else 0)
+
+    def set_force_n_tokens(self, n: int):
+        lib().qwen_asr_pool_set_force_n_tokens(self._h, n)
+
+    def stream_set_max_new_tokens(self, n: int):
+        lib().qwen_asr_pool_stream_set_max_new_tokens(self._h, n)
+
+    def transcribe_pcm(self, samples) -> str | None:
+        x, p = _f32(samples)
+        return _take_string(lib().qwen_asr_pool_transcribe_pcm(self._h, p, len(x)))
+
+    def stream_push_many(self, streams, chunks, finalize: bool = False) -> list:
+        n = len(streams)
+        arrs = [np.ascontiguousarray(c, dtype=np.float32) for c in chunks]
+        st = (C.c_void_p * n)(*[s._h for s in streams])
+        ptrs = (_F32P * n)(*[a.ctypes.data_as(_F32P) for a in arrs])
+        lens = np.array([len(a) for a in arrs], dtype=np.int32)
+        out = (C.c_void_p * n)()
+        if lib().qwen_asr_pool_stream_push_many(self._h, st, ptrs, lens.ctypes.data_as(_I32P), n, int(finalize),
+                                                out) != 0:
+            raise RuntimeError(last_error())
+        return [_take_string(out[i]) for i in range(n)]
+
+
+def assign_longest_first(lengths, workers: int) -> list[int]:
+    """The pool's segment-to-GPU assignment (host only)."""
+    l = np.ascontiguousarray(lengths, dtype=np.int64)
+    out = np.zeros(len(l), dtype=np.int32)
+    if lib().qwen_asr_debug_assign_longest_first(l.ctypes.data_as(_I64P), len(l), workers,
+                                                 out.ctypes.data_as(_I32P)) != 0:
+        raise RuntimeError("assign failed")
+    return out.tolist()
 
 
 def gemm_fallbacks() -> int:

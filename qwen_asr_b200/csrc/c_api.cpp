@@ -281,13 +281,6 @@ int32_t qwen_asr_transcribe_segments(QwenAsrEngine* e, const float* samples, int
   return 0;
 }
 
-void qwen_asr_set_persistent_decode(QwenAsrEngine* e, int32_t on) {
-  if (e) e->ctx.eng.set_persistent_decode(on != 0);
-}
-int32_t qwen_asr_persistent_decode_active(QwenAsrEngine* e) {
-  return e && e->ctx.eng.persistent_decode_active() ? 1 : 0;
-}
-
 int32_t qwen_asr_set_decode_batch(QwenAsrEngine* e, int32_t n) {
   if (!e) return 0;
   e->ctx.decode_batch = n > 0 ? n : 0;

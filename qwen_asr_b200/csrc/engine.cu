@@ -15,7 +15,6 @@ Engine::~Engine() {
     if (g) cudaGraphExecDestroy(g);
   for (auto& kv : run_graphs_)
     if (kv.second.first) cudaGraphExecDestroy(kv.second.first);
-  if (mega_) mega_destroy(mega_);
   for (void* p : allocs_) cudaFree(p);
   if (hstate_) cudaFreeHost(hstate_);
   if (htokens_) cudaFreeHost(htokens_);
@@ -85,7 +84,6 @@ bool Engine::load(const std::string& dir, int device, bool trunc_quant) {
   if (!detect_config(st, cfg_)) return false;
   CUDA_OK(cudaSetDevice(device), false);
   decode_kernels_init();
-  if (const char* pm = getenv("QASR_DECODE_MEGA")) persistent_ = strcmp(pm, "0") != 0;
 
   enc_kernels_init();
   CUDA_OK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), false);
@@ -920,22 +918,7 @@ DecodeArgs Engine::dargs(const int* forced, float* logits, int slot) {
   return a;
 }
 
-bool Engine::mega_usable() {
-  if (!persistent_) return false;
-  if (!mega_ && !mega_tried_) {
-    mega_tried_ = true;
-    mega_ = mega_create(dargs(nullptr, nullptr));
-    cudaGetLastError();
-  }
-  return mega_ != nullptr;
-}
-
-bool Engine::persistent_decode_active() { return persistent_ && !profile && mega_ != nullptr; }
-
-void Engine::enqueue_step(const DecodeArgs& a) {
-  if (persistent_ && a.on_launch == nullptr && mega_ && mega_step(mega_, a, stream_)) return;
-  decode_step(a, stream_);
-}
+void Engine::enqueue_step(const DecodeArgs& a) { decode_step(a, stream_); }
 
 // qkv+attention, o, gate/up, down per layer, then lm_head (batched steps add a q/k/v matvec)
 int Engine::decode_step_launches_1() const {
@@ -979,7 +962,6 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
                               stream_),
               false);
     }
-    const bool mega = !profile && mega_usable();
     DecodeArgs a = dargs(forced ? dforced_.p : nullptr, logits ? dlogits_.p : nullptr, slot);
     if (profile) {
       a.on_launch = [](void* ctx, int kind) {
@@ -995,8 +977,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     if (logits) logits->resize((size_t)max_steps * V);
     for (int i = 0; i < max_steps; ++i) {
       if (profile) a.on_launch(this, -1);
-      if (mega) enqueue_step(a);
-      else decode_step(a, stream_);
+      decode_step(a, stream_);
       if (logits)
         CUDA_OK(cudaMemcpyAsync(logits->data() + (size_t)i * V, dlogits_.p, (size_t)V * 4, cudaMemcpyDeviceToHost,
                                 stream_),
@@ -1009,7 +990,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     CUDA_OK(cudaGetLastError(), false);
     out.assign(htokens_, htokens_ + max_steps);
     if (record_logits) recorded_logits.insert(recorded_logits.end(), logits->end() - V, logits->end());
-    launches += (long)max_steps * (mega ? 1 : decode_step_launches_1());
+    launches += (long)max_steps * decode_step_launches_1();
     for (size_t i = 1; i < prof_ev_.size(); ++i) {
       int k = prof_ev_[i].first;
       if (k < 0) continue;
@@ -1060,7 +1041,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
       if (checked >= max_steps) stop = true;
     }
     CUDA_OK(cudaStreamSynchronize(stream_), false);
-    launches += (long)launched * (persistent_decode_active() ? 1 : decode_step_launches_1());
+    launches += (long)launched * decode_step_launches_1();
     for (auto e : evs) cudaEventDestroy(e);
     CUDA_OK(cudaGetLastError(), false);
   }
@@ -1069,7 +1050,6 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     CUDA_OK(cudaMemcpy(&herr, derr_.p, sizeof(int), cudaMemcpyDeviceToHost), false);
     if (herr) {
       cudaMemset(derr_.p, 0, sizeof(int));
-      if (mega_) mega_reset(mega_, stream_);
       set_error("decode: a device-side wait timed out (code " + std::to_string(herr) + ")");
       return false;
     }
@@ -1115,27 +1095,21 @@ bool Engine::graph_for(int B) {
   if (built_gen_[B] == graph_gen_ && graph_exec_[B]) return true;
   if (graph_exec_[B]) cudaGraphExecDestroy(graph_exec_[B]);
   graph_exec_[B] = nullptr;
-  if (B == 0) mega_usable();  // state creation allocates: not inside the capture
-  for (int attempt = 0; attempt < 2; ++attempt) {
-    DecodeArgs a = dargs(nullptr, nullptr);
-    a.batch = std::max(B, 1);
-    cudaGraph_t g = nullptr;
-    CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);
-    if (B == 0) enqueue_step(a);
-    else decode_step(a, stream_);
-    const cudaError_t e1 = cudaStreamEndCapture(stream_, &g);
-    cudaError_t e2 = cudaErrorUnknown;
-    if (e1 == cudaSuccess) e2 = cudaGraphInstantiate(&graph_exec_[B], g, 0);
-    if (g) cudaGraphDestroy(g);
-    if (e1 == cudaSuccess && e2 == cudaSuccess) {
-      built_gen_[B] = graph_gen_;
-      return true;
-    }
-    cudaGetLastError();
-    graph_exec_[B] = nullptr;
-    if (B != 0 || !persistent_decode_active()) break;
-    persistent_ = false;  // the persistent step could not be captured: use the kernel chain
+  DecodeArgs a = dargs(nullptr, nullptr);
+  a.batch = std::max(B, 1);
+  cudaGraph_t g = nullptr;
+  CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);
+  decode_step(a, stream_);
+  const cudaError_t e1 = cudaStreamEndCapture(stream_, &g);
+  cudaError_t e2 = cudaErrorUnknown;
+  if (e1 == cudaSuccess) e2 = cudaGraphInstantiate(&graph_exec_[B], g, 0);
+  if (g) cudaGraphDestroy(g);
+  if (e1 == cudaSuccess && e2 == cudaSuccess) {
+    built_gen_[B] = graph_gen_;
+    return true;
   }
+  cudaGetLastError();
+  graph_exec_[B] = nullptr;
   set_error("decode: CUDA graph capture of the decode step failed");
   return false;
 }
@@ -1148,7 +1122,6 @@ bool Engine::graph_for_slot(int slot) {
   if (slot_graph_gen_[slot] == graph_gen_ && slot_graph_[slot]) return true;
   if (slot_graph_[slot]) cudaGraphExecDestroy(slot_graph_[slot]);
   slot_graph_[slot] = nullptr;
-  mega_usable();
   DecodeArgs a = dargs(nullptr, nullptr, slot);
   cudaGraph_t g = nullptr;
   CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);

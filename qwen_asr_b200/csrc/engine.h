@@ -107,18 +107,7 @@ class Engine {
   bool decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<std::vector<int>>& out, int first_slot = 0);
   // Largest B decode_batch accepts for this model (shared-memory bound, <= kDecodeMaxBatch).
   int max_decode_batch();
-  // Single-sequence decode through the persistent one-launch kernel (decode_mega.cu) when the
-  // device and model allow it; otherwise (and for batches, profiling, timelines) the
-  // multi-kernel chain.
-  void set_persistent_decode(bool on) {
-    persistent_ = on;
-    ++graph_gen_;
-  }
-  bool persistent_decode_active();
   void set_decode_mode(DecodeMode m) {
-    if (mega_) mega_destroy(mega_);
-    mega_ = nullptr;
-    mega_tried_ = false;
     mode_ = m;
     max_batch_ = 0;
     ++graph_gen_;
@@ -214,10 +203,6 @@ class Engine {
   int tokens_rows_ = 0;
   bool ensure_tokens(int max_steps, int B);
   int max_batch_ = 0;
-  bool persistent_ = false;  // QASR_DECODE_MEGA=1 or qwen_asr_set_persistent_decode enables
-  MegaState* mega_ = nullptr;
-  bool mega_tried_ = false;
-  bool mega_usable();  // creates the persistent-kernel state on first use
   void enqueue_step(const DecodeArgs& a);  // one single-sequence decode step
   int decode_step_launches_1() const;
   // decode graphs, one per batch size; valid while built_gen_[B] == graph_gen_

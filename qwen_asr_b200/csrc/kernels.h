@@ -174,7 +174,7 @@ struct DecodeArgs {
   int layers;
   // scratch
   float* x;        // [hidden] residual stream
-  float* qkv;      // [batch][q_dim + 2 kv_dim] projected q/k/v (batched steps, persistent kernel)
+  float* qkv;      // [batch][q_dim + 2 kv_dim] projected q/k/v (split q/k/v path)
   float* attn;     // [q_dim]
   float* ffn;      // [inter]
   float* part;     // attention split partials
@@ -208,15 +208,6 @@ constexpr int kMaxSlots = 64;  // KV slots / decode states an engine can hold
 int decode_max_batch(int hidden, int inter, int q_heads, int kv_heads, bool int8);
 // Whether a single-sequence step projects q/k/v with a separate matvec (5 kernels per layer).
 bool decode_split_qkv(int hidden, int q_heads, int kv_heads, bool int8);
-// Persistent one-launch decode step for a single sequence (decode_mega.cu). mega_create
-// returns nullptr when the device or the model shape is not supported; the state holds the
-// weight tensor maps of the decode mode of `a` (int8 or bf16).
-struct MegaState;
-MegaState* mega_create(const DecodeArgs& a);
-void mega_destroy(MegaState* m);
-bool mega_step(MegaState* m, const DecodeArgs& a, cudaStream_t s);
-// Clears the grid-barrier and ticket words after a step that reported an error.
-bool mega_reset(MegaState* m, cudaStream_t s);
 // Per-device kernel attributes (dynamic shared memory limits); call once per device.
 void decode_kernels_init();
 void enc_kernels_init();

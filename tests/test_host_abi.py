@@ -227,3 +227,31 @@ def test_boundary_space_rule():
     assert not O.should_insert_boundary_space(ord("a"), ord(","))
     assert not O.should_insert_boundary_space(ord(" "), ord("b"))
     assert not O.should_insert_boundary_space(0xA0, ord("b"))
+
+
+# ----------------------------------------------------------------- multi-GPU pool (host logic)
+def test_pool_assignment_matches_shard_assign():
+    """The C++ pool's longest-first assignment equals the Python sharding helper's, so the
+    torch.distributed driver (qwen_asr_b200.shard) and the library pool split work alike."""
+    from qwen_asr_b200 import shard
+    rng = np.random.default_rng(3)
+    for n, w in [(41, 8), (41, 1), (5, 8), (0, 3), (17, 4), (100, 7)]:
+        lens = rng.integers(8000, 480000, n)
+        lens[: n // 4] = 480000  # ties
+        segs = []
+        a = 0
+        for L in lens:
+            segs.append((a, a + int(L)))
+            a += int(L)
+        want = shard.assign(segs, w)
+        got = Q.assign_longest_first(lens, w)
+        assert [[i for i in range(n) if got[i] == r] for r in range(w)] == want
+
+
+def test_pool_rejects_bad_arguments():
+    L = Q.lib()
+    assert not L.qwen_asr_pool_new(None, None, 0, 0)
+    assert not L.qwen_asr_pool_new(b"/nonexistent", None, -1, 0)
+    assert L.qwen_asr_pool_size(None) == 0
+    assert not L.qwen_asr_pool_transcribe_pcm(None, None, 0)
+    L.qwen_asr_pool_free(None)
