@@ -81,6 +81,15 @@ struct Timeline {
   __device__ __forceinline__ void mark(int i) {
     if (slot) slot[i] = global_timer_ns();
   }
+  // A sub-phase record {kind, t, 0, 0} after this kernel's record (CTA 0 only).
+  __device__ __forceinline__ void sub(unsigned long long* tl, int* cnt, int kind) {
+    if (slot && threadIdx.x == 0) {
+      unsigned long long* r = tl + 4 * (size_t)atomicAdd(cnt, 1);
+      r[0] = (unsigned long long)kind;
+      r[1] = global_timer_ns();
+      r[2] = r[3] = 0;
+    }
+  }
 };
 
 constexpr int kChunk = 512;  // bytes of a weight row per stage (32 lanes x 16 bytes)
@@ -184,45 +193,86 @@ __device__ float stage_x(const MvArgs& a, int b, float* xs_b, int8_t* xq_b, cons
     if (tok >= 0) erow = reinterpret_cast<const uint16_t*>(a.embed) + (size_t)tok * K;
   }
   const float* xsrc = a.x + (size_t)b * a.ldx;
+  // Thread t holds elements 4t.., 4(t + kThreads).. in registers (at most kMaxV float4s):
+  // the sum of squares accumulates in that order, every reduction has its own shared
+  // buffer (one barrier each), and the vector is normalised and quantised in registers.
+  constexpr int kMaxV = 3;  // K <= 3 * 4 * kThreads = 6144
+  __shared__ float red_ss[kWarps], red_mx[kWarps];
+  float4 v[kMaxV];
   float ss = 0.f;
-  for (int i = tid * 4; i < K; i += kThreads * 4) {
-    float4 v;
-    if (erow) {
-      uint2 u = *reinterpret_cast<const uint2*>(erow + i);
-      v = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
-                      __uint_as_float(u.y & 0xFFFF0000u));
-      if (blockIdx.x == 0) *reinterpret_cast<float4*>(a.x_out + (size_t)b * a.ldx + i) = v;
-    } else {
-      v = *reinterpret_cast<const float4*>(xsrc + i);
+#pragma unroll
+  for (int j = 0; j < kMaxV; ++j) {
+    const int i = (tid + j * kThreads) * 4;
+    v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < K) {
+      if (erow) {
+        uint2 u = *reinterpret_cast<const uint2*>(erow + i);
+        v[j] = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                           __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+        if (blockIdx.x == 0) *reinterpret_cast<float4*>(a.x_out + (size_t)b * a.ldx + i) = v[j];
+      } else {
+        v[j] = *reinterpret_cast<const float4*>(xsrc + i);
+      }
+      ss = fmaf(v[j].x, v[j].x, ss);
+      ss = fmaf(v[j].y, v[j].y, ss);
+      ss = fmaf(v[j].z, v[j].z, ss);
+      ss = fmaf(v[j].w, v[j].w, ss);
     }
-    *reinterpret_cast<float4*>(xs_b + i) = v;
-    ss = fmaf(v.x, v.x, ss);
-    ss = fmaf(v.y, v.y, ss);
-    ss = fmaf(v.z, v.z, ss);
-    ss = fmaf(v.w, v.w, ss);
+  }
+  const int warp = tid >> 5, lane = tid & 31;
+  if (a.norm_w) {
+    ss = warp_sum(ss);
+    if (lane == 0) red_ss[warp] = ss;
+    __syncthreads();
+    const float tot = warp_sum(lane < kWarps ? red_ss[lane] : 0.f);
+    const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+#pragma unroll
+    for (int j = 0; j < kMaxV; ++j) {
+      const int i = (tid + j * kThreads) * 4;
+      if (i < K) {
+        v[j].x = __fmul_rn(__fmul_rn(v[j].x, inv), snw[i]);
+        v[j].y = __fmul_rn(__fmul_rn(v[j].y, inv), snw[i + 1]);
+        v[j].z = __fmul_rn(__fmul_rn(v[j].z, inv), snw[i + 2]);
+        v[j].w = __fmul_rn(__fmul_rn(v[j].w, inv), snw[i + 3]);
+      }
+    }
   }
   for (int i = K + tid; i < kpad; i += kThreads) {  // padding past K multiplies zero weights
     xs_b[i] = 0.f;
     if (INT8) xq_b[i] = 0;
   }
-  __syncthreads();
-  if (a.norm_w) {
-    float tot = block_sum(ss, red);
-    float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
-    for (int i = tid; i < K; i += kThreads) xs_b[i] = __fmul_rn(__fmul_rn(xs_b[i], inv), snw[i]);
-  }
   float xscale = 1.0f;
   if (INT8) {
     float mx = 0.f;
-    for (int i = tid; i < K; i += kThreads) mx = fmaxf(mx, fabsf(xs_b[i]));
-    mx = block_max(mx, red);
+#pragma unroll
+    for (int j = 0; j < kMaxV; ++j)
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+    mx = warp_max(mx);
+    if (lane == 0) red_mx[warp] = mx;
+    __syncthreads();
+    mx = warp_max(lane < kWarps ? red_mx[lane] : 0.f);
     xscale = mx > 0.f ? __fdiv_rn(mx, 127.0f) : 1.0f;
-    float inv = __fdiv_rn(127.0f, fmaxf(mx, 1e-10f));
-    for (int i = tid; i < K; i += kThreads) {
-      float r = roundf(__fmul_rn(xs_b[i], inv));
-      xq_b[i] = (int8_t)fminf(fmaxf(r, -127.f), 127.f);
+    const float inv = __fdiv_rn(127.0f, fmaxf(mx, 1e-10f));
+#pragma unroll
+    for (int j = 0; j < kMaxV; ++j) {
+      const int i = (tid + j * kThreads) * 4;
+      if (i < K) {
+        const float f[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+        char4 q;
+        int8_t* qp = reinterpret_cast<int8_t*>(&q);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) qp[e] = (int8_t)fminf(fmaxf(roundf(__fmul_rn(f[e], inv)), -127.f), 127.f);
+        *reinterpret_cast<char4*>(xq_b + i) = q;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kMaxV; ++j) {
+      const int i = (tid + j * kThreads) * 4;
+      if (i < K) *reinterpret_cast<float4*>(xs_b + i) = v[j];
     }
   }
+  (void)red;
   __syncthreads();
   return xscale;
 }
@@ -663,7 +713,9 @@ __device__ __forceinline__ void mv_small_body(const CUtensorMap& wmap, const MvA
   } else {
     stage_all<INT8>(a, xs, xq, snw, red, sinv, xscale, kpad);
   }
+  tline.sub(a.tl, a.tl_count, 20);
   mbar_wait(&bar, 0, a.err, 5);
+  tline.sub(a.tl, a.tl_count, 21);
   if (BATCH) {
     // items of kRG rows x one 512-byte chunk: each sequence's input chunk is read once and
     // dotted with the kRG rows (rows past R repeat row R - 1 and are dropped; sequences past
@@ -788,6 +840,7 @@ __device__ __forceinline__ void mv_small_body(const CUtensorMap& wmap, const MvA
     }
   }
   __syncthreads();
+  tline.sub(a.tl, a.tl_count, 22);
   auto row_value = [&](int b, int r) -> float {
     const float* p = part + ((size_t)b * R + r) * nkc;
     if (INT8) {
@@ -1079,6 +1132,7 @@ qkv_attn_kernel(QkvAttnArgs a) {
     }
   }
   __syncthreads();
+  tline.sub(a.tl, a.tl_count, 29);
   cluster_wait();  // every CTA of the cluster has started
   for (int t = d; t < rpc * kSplits; t += kQA) {  // this CTA's rows into every CTA's allv
     const int q = t / rpc, rr = t - q * rpc;
@@ -1086,6 +1140,7 @@ qkv_attn_kernel(QkvAttnArgs a) {
   }
   cluster_arrive();
   cluster_wait();  // every CTA's rows have arrived
+  tline.sub(a.tl, a.tl_count, 30);
   }
 
   // ---- phase 2: gather this head group's raw q/k/v from the cluster
@@ -1228,6 +1283,7 @@ qkv_attn_kernel(QkvAttnArgs a) {
   }
   // Push this split's partial of the dims each CTA finalises (CTA q: dims [q*8, q*8 + 8) of
   // every head of the group), then one cluster barrier; nothing reads a peer afterwards.
+  tline.sub(a.tl, a.tl_count, 31);
   __syncthreads();
   if (!PROJ) cluster_wait();  // every CTA of the cluster has started
   for (int i = d; i < G * kHd; i += kQA) {
