@@ -1,4 +1,4 @@
-// Bulk-async copy (TMA 1-D, no multicast), mbarrier and programmatic-dependent-launch
+// Bulk-async copy (TMA 1-D, one CTA per copy), mbarrier and programmatic-dependent-launch
 // helpers for sm_100a, written as inline PTX.
 #pragma once
 #include <cstdint>

@@ -1037,39 +1037,72 @@ qkv_attn_kernel(QkvAttnArgs a) {
     int tok = a.st->cur_token;
     if (tok >= 0) erow = reinterpret_cast<const uint16_t*>(a.embed) + (size_t)tok * K;
   }
+  // x, RMSNorm and the quantiser in registers: thread d holds elements 4d.., 4(d + kQA)..
+  // (the sum of squares accumulates in that order), one barrier per block reduction
+  constexpr int kMaxV = 4;  // K <= 4 * 4 * kQA
+  __shared__ float red_ss[kQAW], red_mx[kQAW];
+  float4 xv4[kMaxV];
   float ss = 0.f;
-  for (int i = d * 4; i < K; i += kQA * 4) {
-    float4 v;
-    if (erow) {
-      uint2 b = *reinterpret_cast<const uint2*>(erow + i);
-      v = make_float4(__uint_as_float(b.x << 16), __uint_as_float(b.x & 0xFFFF0000u), __uint_as_float(b.y << 16),
-                      __uint_as_float(b.y & 0xFFFF0000u));
-      if (kvh == 0 && rank == 0) *reinterpret_cast<float4*>(a.x_out + i) = v;
-    } else {
-      v = *reinterpret_cast<const float4*>(a.x + i);
+#pragma unroll
+  for (int j = 0; j < kMaxV; ++j) {
+    const int i = (d + j * kQA) * 4;
+    xv4[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < K) {
+      if (erow) {
+        uint2 b = *reinterpret_cast<const uint2*>(erow + i);
+        xv4[j] = make_float4(__uint_as_float(b.x << 16), __uint_as_float(b.x & 0xFFFF0000u),
+                             __uint_as_float(b.y << 16), __uint_as_float(b.y & 0xFFFF0000u));
+        if (kvh == 0 && rank == 0) *reinterpret_cast<float4*>(a.x_out + i) = xv4[j];
+      } else {
+        xv4[j] = *reinterpret_cast<const float4*>(a.x + i);
+      }
+      ss = fmaf(xv4[j].x, xv4[j].x, ss);
+      ss = fmaf(xv4[j].y, xv4[j].y, ss);
+      ss = fmaf(xv4[j].z, xv4[j].z, ss);
+      ss = fmaf(xv4[j].w, xv4[j].w, ss);
     }
-    *reinterpret_cast<float4*>(xs + i) = v;
-    ss = fmaf(v.x, v.x, ss);
-    ss = fmaf(v.y, v.y, ss);
-    ss = fmaf(v.z, v.z, ss);
-    ss = fmaf(v.w, v.w, ss);
   }
-  __syncthreads();
   {
-    float tot = block_sum(ss, red32);
-    float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
-    for (int i = d; i < K; i += kQA) xs[i] = __fmul_rn(__fmul_rn(xs[i], inv), snw[i]);
+    ss = warp_sum(ss);
+    if (lane == 0) red_ss[warp] = ss;
+    __syncthreads();
+    const float tot = warp_sum(lane < kQAW ? red_ss[lane] : 0.f);
+    const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+#pragma unroll
+    for (int j = 0; j < kMaxV; ++j) {
+      const int i = (d + j * kQA) * 4;
+      if (i < K) {
+        xv4[j].x = __fmul_rn(__fmul_rn(xv4[j].x, inv), snw[i]);
+        xv4[j].y = __fmul_rn(__fmul_rn(xv4[j].y, inv), snw[i + 1]);
+        xv4[j].z = __fmul_rn(__fmul_rn(xv4[j].z, inv), snw[i + 2]);
+        xv4[j].w = __fmul_rn(__fmul_rn(xv4[j].w, inv), snw[i + 3]);
+        *reinterpret_cast<float4*>(xs + i) = xv4[j];
+      }
+    }
   }
   float xscale = 1.0f;
   if (INT8) {
     float mx = 0.f;
-    for (int i = d; i < K; i += kQA) mx = fmaxf(mx, fabsf(xs[i]));
-    mx = block_max(mx, red32);
+#pragma unroll
+    for (int j = 0; j < kMaxV; ++j)
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(xv4[j].x), fabsf(xv4[j].y)), fmaxf(fabsf(xv4[j].z), fabsf(xv4[j].w))));
+    mx = warp_max(mx);
+    if (lane == 0) red_mx[warp] = mx;
+    __syncthreads();
+    mx = warp_max(lane < kQAW ? red_mx[lane] : 0.f);
     xscale = mx > 0.f ? __fdiv_rn(mx, 127.0f) : 1.0f;
-    float inv = __fdiv_rn(127.0f, fmaxf(mx, 1e-10f));
-    for (int i = d; i < K; i += kQA) {
-      float r = roundf(__fmul_rn(xs[i], inv));
-      xq[i] = (int8_t)fminf(fmaxf(r, -127.f), 127.f);
+    const float inv = __fdiv_rn(127.0f, fmaxf(mx, 1e-10f));
+#pragma unroll
+    for (int j = 0; j < kMaxV; ++j) {
+      const int i = (d + j * kQA) * 4;
+      if (i < K) {
+        const float f[4] = {xv4[j].x, xv4[j].y, xv4[j].z, xv4[j].w};
+        char4 q;
+        int8_t* qp = reinterpret_cast<int8_t*>(&q);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) qp[e] = (int8_t)fminf(fmaxf(roundf(__fmul_rn(f[e], inv)), -127.f), 127.f);
+        *reinterpret_cast<char4*>(xq + i) = q;
+      }
     }
   }
   __syncthreads();

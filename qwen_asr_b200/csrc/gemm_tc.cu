@@ -1,5 +1,5 @@
 // Tensor-core GEMM for sm_100a: C = epi(A[M][K] * B[N][K]^T) on tcgen05 with the
-// accumulators in TMEM and every operand moved by TMA (cp.async.bulk.tensor, no multicast).
+// accumulators in TMEM and every operand moved by TMA (cp.async.bulk.tensor; each CTA loads its own tiles).
 //
 // Precision. B holds bf16 weights, exact (the reference upcasts the same bf16 values to
 // f32 before its sgemm). A holds f32 activations and enters as three bf16 planes,
