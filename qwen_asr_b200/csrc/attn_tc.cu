@@ -20,6 +20,10 @@
 // 128-byte-swizzle layout tcgen05 reads (the layout TMA's SWIZZLE_128B writes); the
 // generic-proxy writes are made visible to the tensor core with fence.proxy.async. Every wait
 // on the MMA-completion barrier is bounded (an error code, never a hang).
+#include <algorithm>
+#include <cstdlib>
+#include <vector>
+
 #include "bulk.cuh"
 #include "common.h"
 #include "dev_util.cuh"
@@ -29,6 +33,9 @@ namespace qasr {
 namespace {
 
 constexpr int kThreads = 256, BQ = 128;
+// floats per query row of a split partial: 128 output dims, the row max and the row sum,
+// padded to a multiple of 4 (float4 stores)
+constexpr int kPartRow = 132;
 
 // K-major SW128 operand of R rows x C columns (bf16), three planes: plane p, 64-column chunk c
 // is an R x 128-byte block at (p * C / 64 + c) * R * 128; 16-byte unit u of row r sits at
@@ -141,6 +148,16 @@ __device__ __forceinline__ void stage_vt(unsigned char* dst, const float* src, l
   }
 }
 
+// A prefill work item: queries [q0, q0 + nq) of the packed rows (KV positions qpos0..) of one
+// sequence against its keys [kb0, kb1). A query tile whose keys span several chunks is split
+// over several items (split / nsplit of one group); the last item of the group to finish
+// merges the partials in split order.
+struct AttnItem {
+  int q0, nq, qpos0, kb0, kb1, split, nsplit, group;
+  long long kv_off;   // floats from the layer's slot-0 K/V base to this sequence's slot
+  long long ws_off;   // floats into the partial workspace of this group (head 0, split 0)
+};
+
 struct AttnArgs {
   const float* q;  // query row i of head h: q + i * ldq + h * D
   long ldq;
@@ -156,6 +173,10 @@ struct AttnArgs {
   // encoder: windows (blockIdx.x = window); prefill: query tiles of BQ rows, causal
   const int* win;  // window starts [n_win + 1] (encoder)
   int n_q, start;  // prefill: query count and the KV position of query 0
+  const AttnItem* items;  // prefill: blockIdx.x -> work item (all jobs of a layer in one launch)
+  long long kv_layer_off; // floats from a.k / a.v to this layer of slot 0
+  float* ws;              // split partials: [BQ rows][D + 2] (O, m, l) per (group, head, split)
+  int* tickets;           // [group][head], zero at rest
   int* err;
   unsigned long long* tl;  // optional timeline (debug): CTA (0, 0) thread 0 stamps phases
 };
@@ -181,12 +202,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnArgs a) 
 
   // this CTA's queries and keys
   int q0, nq, k0, nk, qpos0;
+  AttnItem item{};
+  long long kv_off = 0;
   if (CAUSAL) {
-    q0 = blockIdx.x * BQ;
-    nq = min(BQ, a.n_q - q0);
-    k0 = 0;
-    qpos0 = a.start + q0;  // KV position of query row 0 of the tile
-    nk = qpos0 + nq;       // keys 0 .. last query's position
+    item = a.items[blockIdx.x];
+    q0 = item.q0;
+    nq = item.nq;
+    qpos0 = item.qpos0;  // KV position of query row 0 of the tile
+    k0 = item.kb0;       // this item's keys [kb0, kb1) of the sequence's 0 .. last query position
+    nk = item.kb1 - item.kb0;
+    kv_off = a.kv_layer_off + item.kv_off;
   } else {
     q0 = a.win[blockIdx.x];
     nq = a.win[blockIdx.x + 1] - q0;
@@ -217,9 +242,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnArgs a) 
   const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
   const uint32_t uQ = smem_u32(sQ), uKV = smem_u32(sKV), uP = smem_u32(sP);
 
-  const float* kbase = a.k + (long)kvh * a.kv_head_stride + (long)k0 * a.ldk;
-  const float* vbase = a.v + (long)kvh * a.kv_head_stride + (long)k0 * a.ldk;
-  const int my_last = CAUSAL ? qpos0 + row : nk - 1;  // last key this row may see
+  const float* kbase = a.k + kv_off + (long)kvh * a.kv_head_stride + (long)k0 * a.ldk;
+  const float* vbase = a.v + kv_off + (long)kvh * a.kv_head_stride + (long)k0 * a.ldk;
+  const int my_last = CAUSAL ? qpos0 + row - k0 : nk - 1;  // last key (relative to k0) this row may see
   float o[DH];
 #pragma unroll
   for (int d = 0; d < DH; ++d) o[d] = 0.f;
@@ -331,6 +356,52 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const AttnArgs a) 
   }
 
   if (tl && ti < 63) tl[ti++] = global_timer_ns();
+  __shared__ int s_last;
+  bool merged = false;
+  if (CAUSAL && item.nsplit > 1) {
+    // partial (O unnormalised, m, l) of this split; the last split of the group merges
+    constexpr int kRow = kPartRow;  // D dims + m + l, padded so every row starts 16-byte aligned
+    static_assert(D + 2 <= kPartRow, "partial row");
+    float* wp = a.ws + item.ws_off + ((long long)h * item.nsplit + item.split) * (BQ * kRow) + (long)row * kRow;
+    if (ok && row < nq) {
+#pragma unroll
+      for (int d = 0; d < DH; d += 4)
+        *reinterpret_cast<float4*>(wp + half * DH + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+      if (half == 0) {
+        wp[D] = m_run;
+        wp[D + 1] = l_run;
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(a.tickets + item.group * gridDim.y + h, 1) == item.nsplit - 1;
+    __syncthreads();
+    if (!s_last) {
+      ok = false;  // another split of the group writes the output
+    } else {
+      __threadfence();
+      if (row < nq) {
+        const float* w0 = a.ws + item.ws_off + (long long)h * item.nsplit * (BQ * kRow) + (long)row * kRow;
+        float mx = -1e30f;
+        for (int sp = 0; sp < item.nsplit; ++sp) mx = fmaxf(mx, __ldcg(w0 + (long long)sp * BQ * kRow + D));
+        float l = 0.f;
+#pragma unroll
+        for (int d = 0; d < DH; ++d) o[d] = 0.f;
+        for (int sp = 0; sp < item.nsplit; ++sp) {
+          const float* ws = w0 + (long long)sp * BQ * kRow;
+          const float c = expf(__fsub_rn(__ldcg(ws + D), mx));
+          l = __fadd_rn(l, __fmul_rn(__ldcg(ws + D + 1), c));
+#pragma unroll
+          for (int d = 0; d < DH; ++d) o[d] = __fadd_rn(o[d], __fmul_rn(__ldcg(ws + half * DH + d), c));
+        }
+        l_run = l;
+      }
+      __syncthreads();
+      if (tid == 0) a.tickets[item.group * gridDim.y + h] = 0;  // ready for the next launch
+      merged = true;
+    }
+  }
+  (void)merged;
   if (ok && row < nq) {
     const float inv = l_run > 0.f ? __fdiv_rn(1.0f, l_run) : 0.f;
     float* orow = a.out + (long)(q0 + row) * a.ldo + (long)h * D + half * DH;
@@ -396,10 +467,96 @@ bool window_attention_tc(const float* qkv, float* out, __nv_bfloat16* planes, lo
   return true;
 }
 
-bool prefill_attention_tc(const float* qkv, int S, int start, int n_heads, int n_kv, const float* kc,
-                          const float* vc, int max_seq, float scale, float* out, __nv_bfloat16* planes,
-                          long long plane, cudaStream_t s) {
-  if (S <= 0) return true;
+namespace {
+struct PlanBufs {
+  AttnItem* items = nullptr;
+  size_t items_cap = 0;
+  float* ws = nullptr;
+  size_t ws_cap = 0;
+  int* tickets = nullptr;
+  size_t tickets_cap = 0;
+};
+PlanBufs g_plan[16];
+
+template <typename T>
+bool grow_buf(T*& p, size_t& cap, size_t need, bool zero) {
+  if (p && cap >= need) return true;
+  if (p) cudaFree(p);
+  p = nullptr;
+  cap = 0;
+  need = std::max<size_t>(need, 1024);
+  if (cudaMalloc(&p, need * sizeof(T)) != cudaSuccess) {
+    p = nullptr;
+    return false;
+  }
+  if (zero && cudaMemset(p, 0, need * sizeof(T)) != cudaSuccess) return false;
+  cap = need;
+  return true;
+}
+}  // namespace
+
+// Keys per split of a query tile (QASR_ATTN_KEY_CHUNK overrides, a multiple of 64).
+static int attn_key_chunk() {
+  static const int v = [] {
+    const char* e = getenv("QASR_ATTN_KEY_CHUNK");
+    const int c = e ? atoi(e) : kAttnKeyChunk;
+    return c >= 64 ? c / 64 * 64 : kAttnKeyChunk;
+  }();
+  return v;
+}
+
+bool prefill_attention_plan(const std::vector<AttnBlock>& blocks, int n_heads, size_t kv_slot_stride,
+                            cudaStream_t s, AttnPlan& plan) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 16 || !attn_err()) return false;
+  std::vector<AttnItem> items;
+  long long ws = 0;
+  int groups = 0;
+  for (const AttnBlock& b : blocks) {
+    for (int t0 = 0; t0 < b.S; t0 += BQ) {
+      const int nq = std::min(BQ, b.S - t0), qpos0 = b.start + t0, kend = qpos0 + nq;
+      const int chunk = attn_key_chunk();
+      const int nsplit = (kend + chunk - 1) / chunk;
+      for (int sp = 0; sp < nsplit; ++sp) {
+        AttnItem it{};
+        it.q0 = b.off + t0;
+        it.nq = nq;
+        it.qpos0 = qpos0;
+        it.kb0 = sp * chunk;
+        it.kb1 = std::min(kend, it.kb0 + chunk);
+        it.split = sp;
+        it.nsplit = nsplit;
+        it.group = groups;
+        it.kv_off = (long long)b.slot * (long long)kv_slot_stride;
+        it.ws_off = ws;
+        items.push_back(it);
+      }
+      if (nsplit > 1) ws += (long long)n_heads * nsplit * BQ * kPartRow;
+      ++groups;
+    }
+  }
+  PlanBufs& pb = g_plan[dev];
+  // growing frees buffers a previous launch may still read: wait for the stream first
+  if (pb.items_cap < items.size() || pb.ws_cap < (size_t)ws + 1 || pb.tickets_cap < (size_t)groups * n_heads)
+    cudaStreamSynchronize(s);
+  if (!grow_buf(pb.items, pb.items_cap, items.size(), false) || !grow_buf(pb.ws, pb.ws_cap, (size_t)ws + 1, false) ||
+      !grow_buf(pb.tickets, pb.tickets_cap, (size_t)groups * n_heads, true))
+    return false;
+  if (!items.empty() &&
+      cudaMemcpyAsync(pb.items, items.data(), items.size() * sizeof(AttnItem), cudaMemcpyHostToDevice, s) != cudaSuccess)
+    return false;
+  plan.items = pb.items;
+  plan.n_items = (int)items.size();
+  plan.ws = pb.ws;
+  plan.tickets = pb.tickets;
+  return true;
+}
+
+bool prefill_attention_tc(const AttnPlan& plan, const float* qkv, int n_heads, int n_kv, const float* kc,
+                          const float* vc, long long kv_layer_off, int max_seq, float scale, float* out,
+                          __nv_bfloat16* planes, long long plane, cudaStream_t s) {
+  if (plan.n_items <= 0) return true;
   int* err = attn_err();
   if (!err) return false;
   const int qd = n_heads * 128, kvd = n_kv * 128;
@@ -407,8 +564,9 @@ bool prefill_attention_tc(const float* qkv, int S, int start, int n_heads, int n
   a.q = qkv; a.ldq = qd + 2L * kvd;
   a.k = kc; a.v = vc; a.ldk = 128; a.kv_head_stride = (long)max_seq * 128; a.heads_per_kv = n_heads / n_kv;
   a.out = out; a.ldo = qd; a.planes = planes; a.plane = plane; a.scale = scale;
-  a.n_q = S; a.start = start; a.err = err; a.tl = g_attn_tl;
-  attn_tc_kernel<128, 64, true><<<dim3(ceil_div(S, BQ), n_heads), kThreads, attn_smem<128, 64, true>(), s>>>(a);
+  a.items = (const AttnItem*)plan.items; a.kv_layer_off = kv_layer_off; a.ws = plan.ws; a.tickets = plan.tickets;
+  a.err = err; a.tl = g_attn_tl;
+  attn_tc_kernel<128, 64, true><<<dim3(plan.n_items, n_heads), kThreads, attn_smem<128, 64, true>(), s>>>(a);
   return true;
 }
 

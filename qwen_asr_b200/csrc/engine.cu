@@ -602,6 +602,16 @@ bool Engine::prefill_layers(float* x, int R, const std::vector<RowBlock>& blocks
     return false;
   const long long plH = (long long)R * h, plI = (long long)R * inter, plQ = (long long)R * qd;
   const bool simt_att = simt_attention();
+  AttnPlan plan;
+  if (!simt_att) {
+    std::vector<AttnBlock> ab;
+    for (const RowBlock& bk : blocks)
+      if (bk.S > 0) ab.push_back({bk.off, bk.S, bk.start, bk.slot});
+    if (!prefill_attention_plan(ab, c.dec_heads, kv_slot_stride(), stream_, plan)) {
+      set_error("prefill: could not set up the attention work items");
+      return false;
+    }
+  }
   for (int l = 0; l < c.dec_layers; ++l) {
     const DecLayerW& L = dec_layers_[l];
     rms_norm_rows(x, pxn_.p, R, h, L.n1, c.dec_rms_norm_eps, stream_, pl_a_.p, plH);
@@ -610,32 +620,28 @@ bool Engine::prefill_layers(float* x, int R, const std::vector<RowBlock>& blocks
     a.C = pqkv_.p; a.ldc = ldq;
     a.a_split = pl_a_.p; a.a_split_ld = h; a.a_split_plane = plH;
     gemm(a, stream_);
-    bool tc_att = !simt_att;
     for (const RowBlock& bk : blocks) {
       if (bk.S == 0) continue;
+      const size_t so = (size_t)bk.slot * kv_slot_stride() + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
+      float* qk = pqkv_.p + (size_t)bk.off * ldq;
+      prefill_qk_rope_kv(qk, bk.S, bk.start, c.dec_heads, c.dec_kv_heads, L.qn, L.kn, c.dec_rms_norm_eps,
+                         rope_cos_, rope_sin_, kc_.p + so, vc_.p + so, max_seq_, stream_);
+      launches += 1;
       if (simt_att) {
-        const size_t so = (size_t)bk.slot * kv_slot_stride() + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
-        float* qk = pqkv_.p + (size_t)bk.off * ldq;
-        prefill_qk_rope_kv(qk, bk.S, bk.start, c.dec_heads, c.dec_kv_heads, L.qn, L.kn, c.dec_rms_norm_eps,
-                           rope_cos_, rope_sin_, kc_.p + so, vc_.p + so, max_seq_, stream_);
         prefill_attention(qk, bk.S, bk.start, c.dec_heads, c.dec_kv_heads, kc_.p + so, vc_.p + so, max_seq_, scale,
                           patt_.p + (size_t)bk.off * qd, stream_);
-        launches += 2;
-        continue;
+        launches += 1;
       }
-      const size_t slot_off = (size_t)bk.slot * kv_slot_stride() + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
-      float* qkv = pqkv_.p + (size_t)bk.off * ldq;
-      prefill_qk_rope_kv(qkv, bk.S, bk.start, c.dec_heads, c.dec_kv_heads, L.qn, L.kn, c.dec_rms_norm_eps,
-                         rope_cos_, rope_sin_, kc_.p + slot_off, vc_.p + slot_off, max_seq_, stream_);
-      if (tc_att)
-        tc_att = prefill_attention_tc(qkv, bk.S, bk.start, c.dec_heads, c.dec_kv_heads, kc_.p + slot_off,
-                                      vc_.p + slot_off, max_seq_, scale, patt_.p + (size_t)bk.off * qd,
-                                      pl_c_.p + (size_t)bk.off * qd, plQ, stream_);
-      if (!tc_att) {
+    }
+    // every sequence's attention of this layer in one tensor-core launch
+    if (!simt_att) {
+      if (!prefill_attention_tc(plan, pqkv_.p, c.dec_heads, c.dec_kv_heads, kc_.p, vc_.p,
+                                (long long)l * c.dec_kv_heads * max_seq_ * 128, max_seq_, scale, patt_.p, pl_c_.p,
+                                plQ, stream_)) {
         set_error("prefill: the tensor-core attention kernel could not run");
         return false;
       }
-      launches += 2;
+      launches += 1;
     }
     GemmArgs o;
     o.M = R; o.N = h; o.K = qd; o.A = patt_.p; o.lda = qd; o.B = L.wo; o.ldb = qd;

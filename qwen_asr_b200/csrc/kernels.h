@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cstdint>
+#include <vector>
 
 namespace qasr {
 
@@ -107,9 +108,29 @@ void window_attention(const float* qkv, float* out, int T, int d, int n_heads, c
 bool window_attention_tc(const float* qkv, float* out, __nv_bfloat16* planes, long long plane, int d, int n_heads,
                          int head_dim, const int* win_starts, int n_windows, int max_win, float scale,
                          cudaStream_t s);
-bool prefill_attention_tc(const float* qkv, int S, int start, int n_heads, int n_kv, const float* kc,
-                          const float* vc, int max_seq, float scale, float* out, __nv_bfloat16* planes,
-                          long long plane, cudaStream_t s);
+// Prefill attention of several sequences in one launch: block b is packed rows
+// [off, off + S) at KV positions start.. in KV slot `slot`. A query tile whose keys exceed
+// the key chunk is split over several CTAs and merged in split order (deterministic: the
+// split depends only on the sequence's own positions). Measured on C2, C3 and C5 the split
+// never paid for its partial round trip (e.g. C3 prefill 14.9 ms unsplit, 16.1 ms at 256-key
+// chunks), so by default tiles are not split; QASR_ATTN_KEY_CHUNK=<keys> enables it.
+constexpr int kAttnKeyChunk = 1 << 30;
+struct AttnBlock {
+  int off, S, start, slot;
+};
+struct AttnPlan {
+  const void* items = nullptr;  // device work items
+  int n_items = 0;
+  float* ws = nullptr;
+  int* tickets = nullptr;
+};
+// Builds and uploads the work items of `blocks` (the same for every layer of one prefill).
+bool prefill_attention_plan(const std::vector<AttnBlock>& blocks, int n_heads, size_t kv_slot_stride,
+                            cudaStream_t s, AttnPlan& plan);
+// kc / vc: slot 0's cache base; kv_layer_off: floats to the layer within a slot.
+bool prefill_attention_tc(const AttnPlan& plan, const float* qkv, int n_heads, int n_kv, const float* kc,
+                          const float* vc, long long kv_layer_off, int max_seq, float scale, float* out,
+                          __nv_bfloat16* planes, long long plane, cudaStream_t s);
 // Nonzero when a bounded wait inside the attention kernels gave up (clears the flag).
 int attn_tc_error();
 // Debug: attention launches stamp phase times (64 u64) of one CTA here while set.

@@ -229,3 +229,25 @@ def test_graph_and_direct_decode_agree(Q, tiny_dir):
     b = eng.transcribe_pcm(x)
     tb = eng.last_tokens()
     assert a == b and ta == tb
+
+
+def test_prefill_attention_key_split_matches_oracle(m06_dir):
+    """The prefill attention's optional key split (QASR_ATTN_KEY_CHUNK, 64-key chunks here:
+    every query tile of the 28.2 s clip splits, partials merged in split order) keeps the
+    bf16 teacher-forced tolerances. Runs in a child process (the setting is read once)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = (
+        "import sys; sys.path.insert(0, %r); sys.path.insert(0, %r)\n"
+        "import qwen_asr_b200 as Q\n"
+        "from oracle import qwen_oracle as O\n"
+        "from test_gpu_parity import _teacher_forced_case, _check_agreement\n"
+        "eng = Q.Engine(%r)\n"
+        "model = O.Model(%r, decode_mode='bf16')\n"
+        "r = _teacher_forced_case(eng, model, O, 28.2, 16, 'bf16', 1)\n"
+        "print('agree', _check_agreement(*r[:4], 'bf16'))\n" % (root, os.path.join(root, "tests"), m06_dir, m06_dir))
+    env = dict(os.environ, QASR_ATTN_KEY_CHUNK="64")
+    p = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, cwd=root)
+    assert p.returncode == 0 and "agree" in p.stdout, p.stdout + p.stderr
