@@ -611,6 +611,17 @@ bool Engine::prefill_layers(float* x, int R, const std::vector<RowBlock>& blocks
       set_error("prefill: could not set up the attention work items");
       return false;
     }
+    // per packed row: KV position and slot offset
+    std::vector<int> rp(R, 0);
+    std::vector<long long> rk(R, 0);
+    for (const RowBlock& bk : blocks)
+      for (int i = 0; i < bk.S; ++i) {
+        rp[bk.off + i] = bk.start + i;
+        rk[bk.off + i] = (long long)bk.slot * (long long)kv_slot_stride();
+      }
+    if (!prow_pos_.alloc(R) || !prow_kv_.alloc(R)) return false;
+    CUDA_OK(cudaMemcpyAsync(prow_pos_.p, rp.data(), R * sizeof(int), cudaMemcpyHostToDevice, stream_), false);
+    CUDA_OK(cudaMemcpyAsync(prow_kv_.p, rk.data(), R * sizeof(long long), cudaMemcpyHostToDevice, stream_), false);
   }
   for (int l = 0; l < c.dec_layers; ++l) {
     const DecLayerW& L = dec_layers_[l];
@@ -620,18 +631,23 @@ bool Engine::prefill_layers(float* x, int R, const std::vector<RowBlock>& blocks
     a.C = pqkv_.p; a.ldc = ldq;
     a.a_split = pl_a_.p; a.a_split_ld = h; a.a_split_plane = plH;
     gemm(a, stream_);
-    for (const RowBlock& bk : blocks) {
-      if (bk.S == 0) continue;
-      const size_t so = (size_t)bk.slot * kv_slot_stride() + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
-      float* qk = pqkv_.p + (size_t)bk.off * ldq;
-      prefill_qk_rope_kv(qk, bk.S, bk.start, c.dec_heads, c.dec_kv_heads, L.qn, L.kn, c.dec_rms_norm_eps,
-                         rope_cos_, rope_sin_, kc_.p + so, vc_.p + so, max_seq_, stream_);
-      launches += 1;
-      if (simt_att) {
+    if (simt_att) {
+      for (const RowBlock& bk : blocks) {
+        if (bk.S == 0) continue;
+        const size_t so = (size_t)bk.slot * kv_slot_stride() + (size_t)l * c.dec_kv_heads * max_seq_ * 128;
+        float* qk = pqkv_.p + (size_t)bk.off * ldq;
+        prefill_qk_rope_kv(qk, bk.S, bk.start, c.dec_heads, c.dec_kv_heads, L.qn, L.kn, c.dec_rms_norm_eps,
+                           rope_cos_, rope_sin_, kc_.p + so, vc_.p + so, max_seq_, stream_);
         prefill_attention(qk, bk.S, bk.start, c.dec_heads, c.dec_kv_heads, kc_.p + so, vc_.p + so, max_seq_, scale,
                           patt_.p + (size_t)bk.off * qd, stream_);
-        launches += 1;
+        launches += 2;
       }
+    } else {
+      // q/k norm + RoPE + KV append of every sequence's rows in one launch
+      const size_t lo = (size_t)l * c.dec_kv_heads * max_seq_ * 128;
+      prefill_qk_rope_kv_packed(pqkv_.p, R, prow_pos_.p, prow_kv_.p, c.dec_heads, c.dec_kv_heads, L.qn, L.kn,
+                                c.dec_rms_norm_eps, rope_cos_, rope_sin_, kc_.p + lo, vc_.p + lo, max_seq_, stream_);
+      launches += 1;
     }
     // every sequence's attention of this layer in one tensor-core launch
     if (!simt_att) {

@@ -145,6 +145,11 @@ void rms_norm_rows(const float* x, float* y, int rows, int d, const float* w, fl
 void prefill_qk_rope_kv(float* qkv, int S, int start, int n_heads, int n_kv, const float* qn, const float* kn,
                         float eps, const float* rope_cos, const float* rope_sin, float* kc, float* vc,
                         int max_seq, cudaStream_t s);
+// Same over R packed rows of several sequences: row r at KV position row_pos[r], its K/V
+// written at kc / vc + row_kv[r] (the row's slot offset; kc / vc: slot 0 of the layer).
+void prefill_qk_rope_kv_packed(float* qkv, int R, const int* row_pos, const long long* row_kv, int n_heads, int n_kv,
+                               const float* qn, const float* kn, float eps, const float* rope_cos,
+                               const float* rope_sin, float* kc, float* vc, int max_seq, cudaStream_t s);
 // Causal GQA attention of S queries at positions start.. over the cache; out [S][n_heads*128].
 void prefill_attention(const float* qkv, int S, int start, int n_heads, int n_kv, const float* kc,
                        const float* vc, int max_seq, float scale, float* out, cudaStream_t s);

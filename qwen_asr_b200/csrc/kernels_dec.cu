@@ -66,12 +66,19 @@ __global__ void __launch_bounds__(128) prefill_qk_rope_kv_kernel(float* __restri
                                                                  const float* __restrict__ kn, float eps,
                                                                  const float* __restrict__ rc,
                                                                  const float* __restrict__ rs, float* __restrict__ kc,
-                                                                 float* __restrict__ vc, int max_seq) {
+                                                                 float* __restrict__ vc, int max_seq,
+                                                                 const int* __restrict__ row_pos,
+                                                                 const long long* __restrict__ row_kv) {
   __shared__ float sh[kHd];
   __shared__ float red[4];
   const int row = blockIdx.x, hh = blockIdx.y, d = threadIdx.x;
   const int ld = (n_heads + 2 * n_kv) * kHd;
-  const int pos = start + row;
+  // packed rows of several sequences: each row's own position and KV slot offset
+  const int pos = row_pos ? row_pos[row] : start + row;
+  if (row_kv) {
+    kc += row_kv[row];
+    vc += row_kv[row];
+  }
   float c = rc[(size_t)pos * (kHd / 2) + (d & 63)], sn = rs[(size_t)pos * (kHd / 2) + (d & 63)];
   float* base = qkv + (size_t)row * ld;
   if (hh < n_heads) {
@@ -93,7 +100,16 @@ void prefill_qk_rope_kv(float* qkv, int S, int start, int n_heads, int n_kv, con
   if (S <= 0) return;
   dim3 grid(S, n_heads + n_kv);
   prefill_qk_rope_kv_kernel<<<grid, 128, 0, s>>>(qkv, start, n_heads, n_kv, qn, kn, eps, rope_cos, rope_sin, kc, vc,
-                                                 max_seq);
+                                                 max_seq, nullptr, nullptr);
+}
+
+void prefill_qk_rope_kv_packed(float* qkv, int R, const int* row_pos, const long long* row_kv, int n_heads, int n_kv,
+                               const float* qn, const float* kn, float eps, const float* rope_cos,
+                               const float* rope_sin, float* kc, float* vc, int max_seq, cudaStream_t s) {
+  if (R <= 0) return;
+  dim3 grid(R, n_heads + n_kv);
+  prefill_qk_rope_kv_kernel<<<grid, 128, 0, s>>>(qkv, 0, n_heads, n_kv, qn, kn, eps, rope_cos, rope_sin, kc, vc,
+                                                 max_seq, row_pos, row_kv);
 }
 
 // ------------------------------------------------------------------ prefill attention
