@@ -459,7 +459,9 @@ int Engine::encode_many(const std::vector<EncInput>& in, std::vector<int>& seq) 
     set_error("encode: no input frames");
     return 0;
   }
-  if (!act1_.alloc(max_a1) || !act2_.alloc(max_a2) || !act3_.alloc(max_a3) || !cols_.alloc(max_cols) ||
+  const bool conv_planes = !gemm_simt_forced();
+  if (!act1_.alloc(max_a1) || !act2_.alloc(max_a2) || !act3_.alloc(max_a3) ||
+      !cols_.alloc(conv_planes ? 1 : max_cols) || (conv_planes && !pl_conv_.alloc(3 * max_cols)) ||
       !x_enc_.alloc((size_t)T * d) || !xn_enc_.alloc((size_t)T * d) || !qkv_enc_.alloc((size_t)T * 3 * d) ||
       !att_enc_.alloc((size_t)T * d) || !mid_enc_.alloc((size_t)T * std::max(c.enc_ffn_dim, d)) ||
       !enc_.alloc((size_t)T * c.enc_output_dim) || !pl_a_.alloc(split_planes_elems(T, d)) ||
@@ -472,14 +474,23 @@ int Engine::encode_many(const std::vector<EncInput>& in, std::vector<int>& seq) 
   for (auto& g : groups) {
     int w1 = cw(g.w), w2 = cw(w1), w3 = cw(w2);
     conv1_gelu(in[g.input].mel, in[g.input].F, g.c0 * cs, cs, g.nc, g.w, conv1_w, conv1_b, act1_.p, stream_);
-    im2col_s2(act1_.p, g.nc, 64, w1, cols_.p, false, stream_);
+    // im2col straight into the tensor-core GEMM's bf16 planes (f32 columns under QASR_GEMM=simt)
+    const bool planes = !gemm_simt_forced();
     GemmArgs a;
     a.M = g.nc * 32 * w2; a.N = H; a.K = 9 * H;
+    long long pl = (long long)a.M * a.K;
+    im2col_s2(act1_.p, g.nc, 64, w1, cols_.p, false, stream_, planes ? pl_conv_.p : nullptr, pl);
     a.A = cols_.p; a.lda = 9 * H; a.B = conv2_w; a.ldb = 9 * H;
     a.C = act2_.p; a.ldc = H; a.epi = EPI_BIAS_GELU; a.bias = conv2_b; a.split_k = -1;
+    if (planes) {
+      a.a_split = pl_conv_.p; a.a_split_ld = a.K; a.a_split_plane = pl;
+    }
     gemm(a, stream_);
-    im2col_s2(act2_.p, g.nc, 32, w2, cols_.p, true, stream_);
-    a.M = g.nc * w3 * 16; a.A = cols_.p; a.B = conv3_w; a.C = act3_.p; a.bias = conv3_b;
+    a.M = g.nc * w3 * 16;
+    pl = (long long)a.M * a.K;
+    im2col_s2(act2_.p, g.nc, 32, w2, cols_.p, true, stream_, planes ? pl_conv_.p : nullptr, pl);
+    a.A = cols_.p; a.B = conv3_w; a.C = act3_.p; a.bias = conv3_b;
+    if (planes) a.a_split_plane = pl;
     gemm(a, stream_);
     GemmArgs o;
     o.M = g.nc * w3; o.N = d; o.K = 16 * H;

@@ -224,7 +224,7 @@ class Engine {
   bool gemm_stage_ok(long fallbacks_before);
   static bool simt_attention();  // QASR_ATTN=simt: the SIMT attention kernels (A/B checks)
   // bf16 planes (hi/mid/lo) of GEMM inputs written by their producers
-  DevBuf<__nv_bfloat16> pl_a_, pl_b_, pl_c_;
+  DevBuf<__nv_bfloat16> pl_a_, pl_b_, pl_c_, pl_conv_;
   DevBuf<int> prow_pos_;        // packed prefill rows: KV position
   DevBuf<long long> prow_kv_;   // packed prefill rows: KV slot offset (floats)
   cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;

@@ -21,6 +21,8 @@ static bool force_simt() {
   return v == 1;
 }
 
+bool gemm_simt_forced() { return force_simt(); }
+
 bool gemm(const GemmArgs& a, cudaStream_t s) {
   if (a.M <= 0 || a.N <= 0) return true;
   if (a.b_is_f32 || force_simt()) {

@@ -521,13 +521,15 @@ void gemm_tc_note_fallback() {
 }
 
 // Output tile width: 128 columns when that already gives about half a wave of 128 x 128
-// tiles for a ~384-row call, else 64 (twice the tiles for narrow outputs).
-int gemm_tile_n(int N) { return 3 * ceil_div(N, 128) >= 74 ? 128 : 64; }
+// tiles for a ~384-row call, or when M alone fills the GPU (the conv stem: fewer column tiles
+// mean fewer re-reads of the three A planes), else 64. The width never changes a result
+// (each output element accumulates its own K sequence).
+int gemm_tile_n(int N, int M) { return (M >= 2048 || 3 * ceil_div(N, 128) >= 74) ? 128 : 64; }
 
 int gemm_split_k(int N, int K, int policy) {
   if (policy > 0) return std::min(policy, kMaxSplit);
   if (policy < 0) return 1;
-  const int nk = ceil_div(K, BK), nt = ceil_div(N, gemm_tile_n(N));
+  const int nk = ceil_div(K, BK), nt = ceil_div(N, gemm_tile_n(N, 384));
   // fill about one wave of 148 CTAs for a ~384-row call (3 row tiles), >= 8 k-steps per split
   const int s = std::min(kSms / (3 * nt), nk / 8);
   return std::max(1, std::min(s, kMaxSplit));
@@ -558,7 +560,7 @@ bool gemm_tc(const GemmArgs& a, cudaStream_t s) {
   cudaGetDevice(&dev);
   if (dev >= 16) return false;
   TcScratch& sc = g_tc[dev];
-  const int BN = gemm_tile_n(a.N);
+  const int BN = gemm_tile_n(a.N, a.M);
   const int MT = ceil_div(a.M, BM), NT = ceil_div(a.N, BN), nk = ceil_div(a.K, BK);
   const int S = std::min(gemm_split_k(a.N, a.K, a.split_k), nk);
   const __nv_bfloat16* planes = a.a_split;

@@ -53,6 +53,8 @@ inline size_t split_planes_elems(size_t rows, size_t cols) { return 3 * rows * c
 // tensor cores; the result is then computed by the SIMT kernel from the f32 A, and
 // gemm_tc_fallbacks() counts it.
 bool gemm(const GemmArgs& a, cudaStream_t s);
+// QASR_GEMM=simt: every GEMM runs on the SIMT f32 kernel (producers must then write f32 A).
+bool gemm_simt_forced();
 // Plain SIMT FP32 reference GEMM (kept for parity tests of the tensor-core path).
 void gemm_simt(const GemmArgs& a, cudaStream_t s);
 // tcgen05/TMEM tensor-core GEMM (bf16 B, f32 A as three bf16 planes). Returns false
@@ -92,8 +94,10 @@ void conv1_gelu(const float* mel, int n_frames, int f0, int cw, int n_chunks, in
                 const float* w1, const float* b1, float* out, cudaStream_t s);
 // im2col for a 3x3 s2 p1 conv over channels-last input [c][H][W][480]; rows ordered
 // (c, oh, ow) or, with col_major_rows, (c, ow, oh); columns k = (ki*3+kj)*480 + ic.
+// planes (optional): write the columns as the tensor-core GEMM's bf16 planes [3][plane]
+// instead of f32 `cols`.
 void im2col_s2(const float* in, int n_chunks, int H, int W, float* cols, bool col_major_rows,
-               cudaStream_t s);
+               cudaStream_t s, __nv_bfloat16* planes = nullptr, long long plane = 0);
 void add_pe_rows(float* x, int rows, int d, int period, const float* pe, cudaStream_t s);
 // planes (optional): the normalised rows also as bf16 planes [3][plane] of rows [rows][d].
 void layer_norm_rows(const float* x, float* y, int rows, int d, const float* w, const float* b, float eps,

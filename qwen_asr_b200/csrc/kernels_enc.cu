@@ -106,9 +106,11 @@ void conv1_gelu(const float* mel, int n_frames, int f0, int cw, int n_chunks, in
   conv1_gelu_kernel<<<grid, 256, 0, s>>>(mel, n_frames, f0, cw, w, w1, w1p, b1, out, total);
 }
 
-// im2col over channels-last input; each thread moves 4 consecutive input channels.
+// im2col over channels-last input; each thread moves 4 consecutive input channels. With
+// `planes` the columns go straight to the tensor-core GEMM's three bf16 planes (no f32 copy).
 __global__ void im2col_s2_kernel(const float* __restrict__ in, int H, int W, int Ho, int Wo, float* __restrict__ cols,
-                                 bool col_major_rows, long total4) {
+                                 bool col_major_rows, long total4, __nv_bfloat16* __restrict__ planes,
+                                 long long plane) {
   const int K = 9 * kConvHidden;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total4; i += (long)gridDim.x * blockDim.x) {
     int k4 = (int)(i % (K / 4));
@@ -129,15 +131,27 @@ __global__ void im2col_s2_kernel(const float* __restrict__ in, int H, int W, int
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (ih >= 0 && ih < H && iw >= 0 && iw < W)
       v = *reinterpret_cast<const float4*>(in + (((size_t)c * H + ih) * W + iw) * kConvHidden + ic);
-    *reinterpret_cast<float4*>(cols + (size_t)row * K + kk * kConvHidden + ic) = v;
+    const size_t o = (size_t)row * K + kk * kConvHidden + ic;
+    if (planes) {
+      const float f[4] = {v.x, v.y, v.z, v.w};
+      __nv_bfloat16 h[4], m[4], l[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) split3_bf16(f[j], h[j], m[j], l[j]);
+      *reinterpret_cast<uint2*>(planes + o) = *reinterpret_cast<uint2*>(h);
+      *reinterpret_cast<uint2*>(planes + plane + o) = *reinterpret_cast<uint2*>(m);
+      *reinterpret_cast<uint2*>(planes + 2 * plane + o) = *reinterpret_cast<uint2*>(l);
+    } else {
+      *reinterpret_cast<float4*>(cols + o) = v;
+    }
   }
 }
 
-void im2col_s2(const float* in, int n_chunks, int H, int W, float* cols, bool col_major_rows, cudaStream_t s) {
+void im2col_s2(const float* in, int n_chunks, int H, int W, float* cols, bool col_major_rows, cudaStream_t s,
+               __nv_bfloat16* planes, long long plane) {
   int Ho = (H + 2 - 3) / 2 + 1, Wo = (W + 2 - 3) / 2 + 1;
   long total4 = (long)n_chunks * Ho * Wo * (9 * kConvHidden / 4);
   int grid = (int)std::min<long>((total4 + 255) / 256, 148L * 32);
-  im2col_s2_kernel<<<grid, 256, 0, s>>>(in, H, W, Ho, Wo, cols, col_major_rows, total4);
+  im2col_s2_kernel<<<grid, 256, 0, s>>>(in, H, W, Ho, Wo, cols, col_major_rows, total4, planes, plane);
 }
 
 __global__ void add_pe_kernel(float* x, long total, int d, int period, const float* pe) {
