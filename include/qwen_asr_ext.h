@@ -176,6 +176,12 @@ int64_t qwen_asr_debug_compact_silence(const float* samples, int64_t n, float* o
 /* String::from_utf8_lossy + str::trim as used on transcripts (transcribe.rs:237-238). */
 int32_t qwen_asr_debug_lossy_trim(const char* bytes, int32_t n, char* out, int32_t cap);
 /* normalize_language (config.rs:167-182); "" when unsupported. */
+/* GPU Kaiser-sinc resampling (audio.rs:133-196) of n host samples at from_rate to 16 kHz, the
+ * step qwen_asr_transcribe_file / _wav_buffer run on the engine's GPU for non-16 kHz files.
+ * out (host, optional) receives the samples when cap is large enough. Returns the output
+ * length or -1. */
+int64_t qwen_asr_debug_resample(QwenAsrEngine* engine, const float* in, int64_t n, int32_t from_rate, float* out,
+                                int64_t cap);
 /* 1 when the NUL-terminated bytes are strict UTF-8 as CStr::to_str accepts them (the check
  * qwen_asr_load_model, qwen_asr_transcribe_file and qwen_asr_set_language apply), else 0. */
 int32_t qwen_asr_debug_valid_utf8(const char* s);

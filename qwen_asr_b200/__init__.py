@@ -67,6 +67,7 @@ SIGNATURES = {
     "qwen_asr_debug_gemm": (C.c_int32, [C.c_int32, C.c_int32, C.c_int32, _F32P, C.POINTER(C.c_uint16), _F32P,
                                          _F32P, C.c_int32, C.c_int32, _F32P]),
     "qwen_asr_gemm_fallbacks": (C.c_int64, []),
+    "qwen_asr_debug_resample": (C.c_int64, [_VP, _F32P, C.c_int64, C.c_int32, _F32P, C.c_int64]),
     "qwen_asr_pool_new": (_VP, [C.c_char_p, _I32P, C.c_int32, C.c_int32]),
     "qwen_asr_pool_free": (None, [_VP]),
     "qwen_asr_pool_size": (C.c_int32, [_VP]),
@@ -316,6 +317,17 @@ class Engine:
         if T <= 0:
             raise RuntimeError(last_error())
         return out[:T * hid].reshape(T, hid).copy()
+
+    def debug_resample(self, samples, from_rate: int) -> np.ndarray:
+        """GPU resampling to 16 kHz (the transcribe_file path for non-16 kHz WAV files)."""
+        x, p = _f32(samples)
+        n = lib().qwen_asr_debug_resample(self._h, p, len(x), from_rate, None, 0)
+        if n < 0:
+            raise RuntimeError(last_error())
+        out = np.zeros(n, dtype=np.float32)
+        if lib().qwen_asr_debug_resample(self._h, p, len(x), from_rate, out.ctypes.data_as(_F32P), n) != n:
+            raise RuntimeError(last_error())
+        return out
 
     def debug_kv(self, layer: int, n_pos: int, slot: int = 0):
         """(k, v) f32 [kv_heads][n_pos][128] of one layer of a KV slot."""

@@ -80,6 +80,34 @@ char* run_transcribe(QwenAsrEngine* e, const std::vector<float>& samples) {
   }
   return to_c_string(out);
 }
+// A parsed WAV file: 16 kHz input goes straight to the transcriber; any other rate is
+// resampled on the GPU (audio.rs:133-196) and, when neither segmentation nor silence
+// compaction needs the samples on the host, transcribed from device memory.
+char* run_transcribe_native(QwenAsrEngine* e, const std::vector<float>& samples, int rate) {
+  if (rate == qasr::kSampleRate) return run_transcribe(e, samples);
+  std::string out;
+  try {
+    long n = 0;
+    const float* d = e->ctx.eng.resample_to_device(samples.data(), (long)samples.size(), rate, &n);
+    if (!d) return nullptr;
+    if (e->ctx.segment_sec <= 0.0f && !e->ctx.skip_silence) {
+      if (!e->ctx.transcribe_device(d, (size_t)n, out)) return nullptr;
+    } else {
+      std::vector<float> h(n);
+      if (cudaMemcpyAsync(h.data(), d, (size_t)n * 4, cudaMemcpyDeviceToHost, e->ctx.eng.stream()) != cudaSuccess ||
+          cudaStreamSynchronize(e->ctx.eng.stream()) != cudaSuccess) {
+        qasr::set_error("resample: device-to-host copy failed");
+        return nullptr;
+      }
+      if (!e->ctx.transcribe_audio(h, out)) return nullptr;
+    }
+  } catch (const std::exception& ex) {
+    qasr::set_error(std::string("transcribe: ") + ex.what());
+    return nullptr;
+  }
+  return to_c_string(out);
+}
+
 }  // namespace
 
 extern "C" {
@@ -118,8 +146,9 @@ char* qwen_asr_transcribe_file(QwenAsrEngine* e, const char* wav_path) {
   ss << f.rdbuf();
   std::string data = ss.str();
   std::vector<float> samples;
-  if (!qasr::parse_wav_buffer((const uint8_t*)data.data(), data.size(), samples)) return nullptr;
-  return run_transcribe(e, samples);
+  int rate = 0;
+  if (!qasr::parse_wav_native((const uint8_t*)data.data(), data.size(), samples, rate)) return nullptr;
+  return run_transcribe_native(e, samples, rate);
 }
 
 char* qwen_asr_transcribe_pcm(QwenAsrEngine* e, const float* samples, int32_t n_samples) {
@@ -130,8 +159,9 @@ char* qwen_asr_transcribe_pcm(QwenAsrEngine* e, const float* samples, int32_t n_
 char* qwen_asr_transcribe_wav_buffer(QwenAsrEngine* e, const uint8_t* wav_data, int32_t wav_len) {
   if (!e || !wav_data || wav_len <= 0) return nullptr;
   std::vector<float> samples;
-  if (!qasr::parse_wav_buffer(wav_data, (size_t)wav_len, samples)) return nullptr;
-  return run_transcribe(e, samples);
+  int rate = 0;
+  if (!qasr::parse_wav_native(wav_data, (size_t)wav_len, samples, rate)) return nullptr;
+  return run_transcribe_native(e, samples, rate);
 }
 
 void qwen_asr_set_segment_sec(QwenAsrEngine* e, float sec) {
@@ -424,6 +454,18 @@ int32_t qwen_asr_debug_decode(QwenAsrEngine* e, const float* rows, int32_t n_row
     for (int i = 0; i < (int)ids.size(); ++i) out_ids[i] = ids[i];
   if (out_logits) memcpy(out_logits, lg.data(), lg.size() * 4);
   return (int32_t)ids.size();
+}
+
+int64_t qwen_asr_debug_resample(QwenAsrEngine* e, const float* in, int64_t n, int32_t from_rate, float* out,
+                                int64_t cap) {
+  if (!e || !in || n <= 0 || from_rate <= 0) return -1;
+  long m = 0;
+  const float* d = e->ctx.eng.resample_to_device(in, (long)n, from_rate, &m);
+  if (!d) return -1;
+  if (out && m <= cap) {
+    if (cudaMemcpy(out, d, (size_t)m * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  }
+  return m;
 }
 
 int32_t qwen_asr_debug_valid_utf8(const char* s) { return s && valid_utf8(s) ? 1 : 0; }

@@ -855,6 +855,21 @@ bool Engine::run_prefill(int n, int start_pos, int slot) {
   return true;
 }
 
+const float* Engine::resample_to_device(const float* h_in, long n, int rate, long* n_out) {
+  cudaSetDevice(device_);
+  const long m = resampled_length(n, rate, kSampleRate);
+  if (n <= 0 || rate <= 0 || m <= 0) {
+    set_error("resample: empty input or bad rate");
+    return nullptr;
+  }
+  if (!rs_in_.alloc(n) || !rs_out_.alloc(m)) return nullptr;
+  CUDA_OK(cudaMemcpyAsync(rs_in_.p, h_in, (size_t)n * 4, cudaMemcpyHostToDevice, stream_), nullptr);
+  resample_device(rs_in_.p, n, rate, kSampleRate, rs_out_.p, stream_);
+  CUDA_OK(cudaGetLastError(), nullptr);
+  *n_out = m;
+  return rs_out_.p;
+}
+
 bool Engine::copy_kv(int slot, int layer, int n_pos, float* k, float* v) {
   cudaSetDevice(device_);
   const Config& c = cfg_;

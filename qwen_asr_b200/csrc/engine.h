@@ -131,6 +131,9 @@ class Engine {
 
   // Debug: final hidden of prefill rows (after the last layer, before final norm).
   bool copy_prefill_hidden(std::vector<float>& out, int rows);
+  // Resamples host samples at `rate` to 16 kHz on the GPU (audio.rs:133-196); returns the
+  // device buffer (valid until the next call) and its length in *n_out, or nullptr.
+  const float* resample_to_device(const float* h_in, long n, int rate, long* n_out);
   // Debug: K and V rows [kv_heads][n_pos][128] of positions 0..n_pos-1 of one slot and layer.
   bool copy_kv(int slot, int layer, int n_pos, float* k, float* v);
   int kv_capacity() const { return max_seq_; }
@@ -225,6 +228,7 @@ class Engine {
   static bool simt_attention();  // QASR_ATTN=simt: the SIMT attention kernels (A/B checks)
   // bf16 planes (hi/mid/lo) of GEMM inputs written by their producers
   DevBuf<__nv_bfloat16> pl_a_, pl_b_, pl_c_, pl_conv_;
+  DevBuf<float> rs_in_, rs_out_;  // resampler input / output
   DevBuf<int> prow_pos_;        // packed prefill rows: KV position
   DevBuf<long long> prow_kv_;   // packed prefill rows: KV slot offset (floats)
   cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;

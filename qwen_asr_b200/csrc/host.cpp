@@ -498,6 +498,13 @@ bool Tokenizer::encode(const std::string& text, std::vector<int>& ids) const {
 // Audio (audio.rs)
 // =====================================================================================
 bool parse_wav_buffer(const uint8_t* d, size_t len, std::vector<float>& out) {
+  int rate = 0;
+  if (!parse_wav_native(d, len, out, rate)) return false;
+  if (rate != kSampleRate) out = resample(out, rate, kSampleRate);
+  return true;
+}
+
+bool parse_wav_native(const uint8_t* d, size_t len, std::vector<float>& out, int& rate_out) {
   if (len < 44 || memcmp(d, "RIFF", 4) != 0 || memcmp(d + 8, "WAVE", 4) != 0) {
     set_error("parse_wav_buffer: not a valid WAV file");
     return false;
@@ -546,7 +553,7 @@ bool parse_wav_buffer(const uint8_t* d, size_t len, std::vector<float>& out) {
       out[i] = (sum / (float)channels) / 32768.0f;
     }
   }
-  if (rate != kSampleRate) out = resample(out, rate, kSampleRate);
+  rate_out = rate;
   return true;
 }
 

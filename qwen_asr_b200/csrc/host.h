@@ -79,6 +79,8 @@ class Tokenizer {
 
 // ---------------------------------------------------------------- audio
 bool parse_wav_buffer(const uint8_t* data, size_t len, std::vector<float>& out);
+// The same parse without the resampling step: mono samples at the file's own rate.
+bool parse_wav_native(const uint8_t* data, size_t len, std::vector<float>& out, int& rate);
 std::vector<float> resample(const std::vector<float>& in, int from_rate, int to_rate);
 std::vector<float> compact_silence(const std::vector<float>& in);
 // Segment start offsets of transcribe_audio (transcribe.rs:328-346); {0} when unsplit.

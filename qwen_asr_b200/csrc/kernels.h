@@ -87,6 +87,11 @@ void mel_reset_max(int* gmax, cudaStream_t s);
 // logmel [F][128] in place: (max(v, gmax - 8) + 4) / 4
 void mel_normalize(float* logmel, int n_frames, const int* gmax, cudaStream_t s);
 
+// Kaiser-sinc resampling (audio.rs:133-196) of n samples at from_rate into
+// resampled_length(n, from_rate, to_rate) samples at to_rate; device buffers.
+long resampled_length(long n, int from_rate, int to_rate);
+void resample_device(const float* in, long n, int from_rate, int to_rate, float* out, cudaStream_t s);
+
 // ---------------------------------------------------------------- encoder
 // conv2d1 (1 -> 480, 3x3 s2 p1) + bias + GELU on `n_chunks` chunks of width w taken from
 // mel [F][128] starting at frame f0 + c*cw; output channels-last [c][64][w1][480].
