@@ -463,7 +463,11 @@ int64_t qwen_asr_debug_resample(QwenAsrEngine* e, const float* in, int64_t n, in
   const float* d = e->ctx.eng.resample_to_device(in, (long)n, from_rate, &m);
   if (!d) return -1;
   if (out && m <= cap) {
-    if (cudaMemcpy(out, d, (size_t)m * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    // the engine's stream does not synchronise with the default stream: copy on it
+    cudaStream_t s = e->ctx.eng.stream();
+    if (cudaMemcpyAsync(out, d, (size_t)m * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+      return -1;
   }
   return m;
 }
