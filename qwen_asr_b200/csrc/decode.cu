@@ -50,6 +50,7 @@ struct MvArgs {
   int block_rows;              // R: 16, 32 or 64 weight rows per stage (R / 16 per warp)
   int nkc;                     // 512-byte column chunks per row
   int stages;
+  int cps;                     // 512-byte chunks per ring stage (streaming kernel; divides nkc)
   unsigned long long* am_part; // [B][gridDim.x]
   int* am_ticket;
   StepState* st;               // [B]
@@ -518,8 +519,9 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__
   unsigned char* sm = (unsigned char*)(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = a.K, R = a.block_rows, nkc = a.nkc, B = BATCH ? a.B : 1;
+  const int cps = a.cps, nsc = nkc / cps;  // chunks per stage, stages per row block
   const int kpad = nkc * kChunk / (INT8 ? 1 : 2);  // padded vector length in elements
-  const int stage_bytes = R * kChunk;
+  const int stage_bytes = R * kChunk * cps;  // [chunk][R rows][512 B]
   unsigned char* wst = sm;
   float* xs = reinterpret_cast<float*>(sm + (size_t)a.stages * stage_bytes);  // int8: [kpad] (B = 1 staging); bf16: [B][kpad]
   int8_t* xq = reinterpret_cast<int8_t*>(xs + (INT8 ? kpad : B * kpad));    // int8: [B][kpad]
@@ -531,11 +533,12 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__
   const int r0 = blockIdx.x * a.rows_per_cta;
   const int nrows = max(0, min(a.N, r0 + a.rows_per_cta) - r0);
   const int nblocks = (nrows + R - 1) / R;
-  const int nt = nblocks * nkc;
+  const int nt = nblocks * nsc;
   auto issue = [&](int t) {
-    const int s = t % a.stages;
+    const int s = t % a.stages, kc0 = (t % nsc) * cps, row = r0 + (t / nsc) * R;
     mbar_expect_tx(&full[s], (uint32_t)stage_bytes);
-    tma_box(wst + (size_t)s * stage_bytes, &wmap, (t % nkc) * (kChunk / 2), r0 + (t / nkc) * R, &full[s]);
+    for (int c = 0; c < cps; ++c)
+      tma_box(wst + (size_t)s * stage_bytes + (size_t)c * R * kChunk, &wmap, (kc0 + c) * (kChunk / 2), row, &full[s]);
   };
   if (tid == 0) {
     for (int s = 0; s < a.stages; ++s) {
@@ -573,9 +576,12 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__
     }
   }
   for (int t = 0; t < nt; ++t) {
-    const int s = t % a.stages, blk = t / nkc, kc = t % nkc;
+    const int s = t % a.stages, blk = t / nsc;
     mbar_wait(&full[s], (uint32_t)(t / a.stages) & 1u, a.err, 1);
-    const unsigned char* tw = wst + (size_t)s * stage_bytes + (size_t)(warp * RPW) * kChunk + lane * 16;
+    // chunks in column order, so every lane accumulates a row exactly as with one chunk per stage
+    for (int c = 0; c < cps; ++c) {
+    const int kc = (t % nsc) * cps + c;
+    const unsigned char* tw = wst + (size_t)s * stage_bytes + (size_t)c * R * kChunk + (size_t)(warp * RPW) * kChunk + lane * 16;
     if (INT8) {
       int4 w[RPW];
 #pragma unroll
@@ -613,13 +619,14 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__
         }
       }
     }
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     if (tid == 0 && t + a.stages < nt) {
       mbar_wait(&empty[s], (uint32_t)(t / a.stages) & 1u, a.err, 2);  // every warp is done with it
       issue(t + a.stages);
     }
-    if (kc == nkc - 1) {
+    if (t % nsc == nsc - 1) {
       // row block finished: reduce, scale, epilogue for every sequence
       const int lr = blk * R + warp * RPW + lane_row<RPW>(lane);
       const int row = r0 + lr;
@@ -1359,38 +1366,69 @@ qkv_attn_kernel(QkvAttnArgs a) {
 
 // ------------------------------------------------------------------ host side
 namespace {
-constexpr int kSmemBudget = 112 * 1024;  // two decode kernels co-reside on one SM
+// Shared memory of a streaming matvec inside the step: 160 KB of weight stages in flight per
+// SM keep HBM busy (the 1.7B bf16 gate/up and down projections ran at 1.7-2.7 TB/s with the
+// earlier 112 KB), at the cost of the successor's early CTAs sharing the SM only when small.
+constexpr int kSmemBudget = 160 * 1024;
 constexpr size_t kSmallSmemMax = 200 * 1024;
 constexpr int kAttnKvRows = 16;  // K/V rows per CTA staged before the wait (attention-only kernel)
 constexpr size_t kSplitSlabBytes = 64 * 1024;  // single-sequence split above this slab (1.7B bf16)
 
 struct MvPlan {
-  int grid, rows_per_cta, block_rows, nkc, stages;
+  int grid, rows_per_cta, block_rows, nkc, stages, cps;
   size_t smem;
 };
 
-MvPlan plan_mv(int N, int K, bool int8, int B, int num_sms, bool swiglu, bool last_kernel) {
+int env_int(const char* name, int dflt) {
+  const char* e = getenv(name);
+  return e ? atoi(e) : dflt;
+}
+
+// Streaming-matvec tuning (read once): block rows of a stage for the inner kernels (0: by
+// rows per CTA), their ring-depth cap and their shared-memory budget in KB.
+struct MvTune {
+  int block, max_stages, budget, stage_kb;
+};
+const MvTune& mv_tune() {
+  static const MvTune t{env_int("QASR_MV_BLOCK", 0), env_int("QASR_MV_STAGES", 12),
+                        env_int("QASR_MV_BUDGET_KB", kSmemBudget / 1024),
+                        env_int("QASR_MV_STAGE_KB", 64)};
+  return t;
+}
+
+// norm: the kernel stages RMSNorm weights (K floats of shared memory).
+MvPlan plan_mv(int N, int K, bool int8, int B, int num_sms, bool swiglu, bool last_kernel, bool norm = true) {
   MvPlan p{};
+  const MvTune& tune = mv_tune();
   const int row_bytes = K * (int8 ? 1 : 2);
   const int raw = (N + num_sms - 1) / num_sms;
   p.block_rows = raw >= 48 ? 64 : (raw >= 24 || swiglu) ? 32 : 16;
+  if (!last_kernel && tune.block > 0) p.block_rows = std::max(tune.block, swiglu ? 32 : 16);
   p.rows_per_cta = (raw + p.block_rows - 1) / p.block_rows * p.block_rows;
   p.grid = (N + p.rows_per_cta - 1) / p.rows_per_cta;
   p.nkc = (row_bytes + kChunk - 1) / kChunk;
   const int kpad = p.nkc * kChunk / (int8 ? 1 : 2);
   const size_t xbytes = int8 ? (size_t)kpad * 4 + (((size_t)B * kpad + 15) & ~(size_t)15) : (size_t)B * kpad * 4;
-  const size_t fixed = 1024 + xbytes + 16 * 8 + (size_t)p.rows_per_cta * 4 + (size_t)K * 4;
+  const size_t fixed = 1024 + xbytes + 16 * 8 + (size_t)p.rows_per_cta * 4 + (norm ? (size_t)K * 4 : 0);
   // The step's last kernel (lm_head) has no successor to share the SM with: deeper ring.
   // Batched steps read each weight stage for several sequences, so they take the larger
   // budget as well (fewer resident successors matter less than the longer compute).
-  const size_t budget = (last_kernel || B > 1) ? kSmallSmemMax : kSmemBudget;
-  const size_t stage = (size_t)p.block_rows * kChunk;
-  const int total = (p.rows_per_cta / p.block_rows) * p.nkc;
+  const size_t budget = (last_kernel || B > 1) ? kSmallSmemMax : (size_t)tune.budget * 1024;
+  // Chunks per stage: the largest divisor of nkc keeping a stage within tune.stage_kb and two
+  // stages within the budget. Fewer, larger stages cut the per-stage barrier round trips that
+  // bound short row blocks (the 16-row down projection: 24 stages of 8 KB otherwise).
+  p.cps = 1;
+  for (int c = 2; c <= p.nkc; ++c) {
+    const size_t st = (size_t)p.block_rows * kChunk * c;
+    if (p.nkc % c == 0 && st <= (size_t)tune.stage_kb * 1024 && fixed + 2 * st <= budget) p.cps = c;
+  }
+  const size_t stage = (size_t)p.block_rows * kChunk * p.cps;
+  const int total = (p.rows_per_cta / p.block_rows) * (p.nkc / p.cps);
   if (fixed + 2 * stage > budget) {
     p.stages = 0;
     return p;
   }
-  p.stages = (int)std::max<size_t>(2, std::min<size_t>((budget - fixed) / stage, last_kernel ? 8 : 6));
+  p.stages = (int)std::max<size_t>(2, std::min<size_t>((budget - fixed) / stage, last_kernel ? 8 : B > 1 ? 6 : tune.max_stages));
   p.stages = std::min(p.stages, std::max(total, 1));
   p.smem = (size_t)p.stages * stage + fixed;
   return p;
@@ -1398,8 +1436,8 @@ MvPlan plan_mv(int N, int K, bool int8, int B, int num_sms, bool swiglu, bool la
 
 // Launch with programmatic stream serialisation (PDL) and an optional cluster shape.
 template <typename... KArgs, typename... Args>
-void launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
-               int cluster_y, Args... args) {
+cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                      int cluster_y, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -1421,22 +1459,28 @@ void launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  cudaLaunchKernelEx(&cfg, kernel, args...);
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 template <bool INT8, int EPI>
-void mv_launch(const CUtensorMap& map, const MvArgs& m, const MvPlan& p, cudaStream_t s, bool pdl, bool batch) {
+cudaError_t mv_launch(const CUtensorMap& map, const MvArgs& m, const MvPlan& p, cudaStream_t s, bool pdl, bool batch) {
   const int rpw = p.block_rows / kWarps;
   const dim3 g(p.grid), t(kThreads);
   if (batch) {
-    if (rpw == 4) launch_ex(mv_kernel<INT8, EPI, 4, true>, g, t, p.smem, s, pdl, 1, map, m);
-    else if (rpw == 2) launch_ex(mv_kernel<INT8, EPI, 2, true>, g, t, p.smem, s, pdl, 1, map, m);
-    else launch_ex(mv_kernel<INT8, EPI, 1, true>, g, t, p.smem, s, pdl, 1, map, m);
+    if (rpw == 4) return launch_ex(mv_kernel<INT8, EPI, 4, true>, g, t, p.smem, s, pdl, 1, map, m);
+    else if (rpw == 2) return launch_ex(mv_kernel<INT8, EPI, 2, true>, g, t, p.smem, s, pdl, 1, map, m);
+    else return launch_ex(mv_kernel<INT8, EPI, 1, true>, g, t, p.smem, s, pdl, 1, map, m);
   } else {
-    if (rpw == 4) launch_ex(mv_kernel<INT8, EPI, 4, false>, g, t, p.smem, s, pdl, 1, map, m);
-    else if (rpw == 2) launch_ex(mv_kernel<INT8, EPI, 2, false>, g, t, p.smem, s, pdl, 1, map, m);
-    else launch_ex(mv_kernel<INT8, EPI, 1, false>, g, t, p.smem, s, pdl, 1, map, m);
+    if (rpw == 4) return launch_ex(mv_kernel<INT8, EPI, 4, false>, g, t, p.smem, s, pdl, 1, map, m);
+    else if (rpw == 2) return launch_ex(mv_kernel<INT8, EPI, 2, false>, g, t, p.smem, s, pdl, 1, map, m);
+    else return launch_ex(mv_kernel<INT8, EPI, 1, false>, g, t, p.smem, s, pdl, 1, map, m);
   }
+}
+
+bool launched_ok(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return true;
+  set_error(std::string("decode: ") + what + " launch failed: " + cudaGetErrorString(e));
+  return false;
 }
 
 // Shared memory of the single-stage small matvec for B sequences (0 when it does not apply).
@@ -1467,7 +1511,7 @@ bool small_ok(int N, int K, bool int8, int B, int num_sms) {
 template <int EPI>
 // batch_kernels selects the batched instantiations also for B = 1 (their staging order is
 // the one sum_threads names).
-void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pdl = true, bool allow_small = true,
+bool mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pdl = true, bool allow_small = true,
         bool batch_kernels = false) {
   const bool batch = m.B > 1 || batch_kernels;
   const int row_bytes = m.K * (int8 ? 1 : 2);
@@ -1480,35 +1524,37 @@ void mv(bool int8, const void* W, MvArgs m, int num_sms, cudaStream_t s, bool pd
     CUtensorMap map;
     if (!make_tma_2d_u16(&map, W, m.N, row_bytes / 2, kChunk / 2, rpc)) {
       set_error("decode: cannot encode the weight tensor map");
-      return;
+      return false;
     }
     dim3 grid((m.N + rpc - 1) / rpc);
     const dim3 t(kThreads);
+    cudaError_t e;
     if (batch) {
-      if (int8) launch_ex(mv_small_batch_kernel<true, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
-      else launch_ex(mv_small_batch_kernel<false, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
+      if (int8) e = launch_ex(mv_small_batch_kernel<true, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
+      else e = launch_ex(mv_small_batch_kernel<false, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
     } else {
-      if (int8) launch_ex(mv_small_kernel<true, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
-      else launch_ex(mv_small_kernel<false, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
+      if (int8) e = launch_ex(mv_small_kernel<true, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
+      else e = launch_ex(mv_small_kernel<false, EPI>, grid, t, smem_small, s, pdl, 1, map, m);
     }
-    return;
+    return launched_ok(e, "small matvec");
   }
-  MvPlan p = plan_mv(m.N, m.K, int8, m.B, num_sms, EPI == MV_SWIGLU, EPI == MV_ARGMAX);
+  MvPlan p = plan_mv(m.N, m.K, int8, m.B, num_sms, EPI == MV_SWIGLU, EPI == MV_ARGMAX, m.norm_w != nullptr);
   if (p.stages == 0) {
-    set_error("decode: batch too large for the matvec shared memory");
-    return;
+    set_error("decode: no ring of two stages fits the matvec shared memory");
+    return false;
   }
   m.rows_per_cta = p.rows_per_cta;
   m.block_rows = p.block_rows;
   m.nkc = p.nkc;
   m.stages = p.stages;
+  m.cps = p.cps;
   CUtensorMap map;
   if (!make_tma_2d_u16(&map, W, m.N, row_bytes / 2, kChunk / 2, p.block_rows)) {
     set_error("decode: cannot encode the weight tensor map");
-    return;
+    return false;
   }
-  if (int8) mv_launch<true, EPI>(map, m, p, s, pdl, batch);
-  else mv_launch<false, EPI>(map, m, p, s, pdl, batch);
+  return launched_ok(int8 ? mv_launch<true, EPI>(map, m, p, s, pdl, batch) : mv_launch<false, EPI>(map, m, p, s, pdl, batch),
+                     "streaming matvec");
 }
 
 template <bool INT8, int EPI>
@@ -1596,7 +1642,7 @@ int decode_max_batch(int hidden, int inter, int q_heads, int kv_heads, bool int8
   return best;
 }
 
-void decode_step(const DecodeArgs& a, cudaStream_t s) {
+bool decode_step(const DecodeArgs& a, cudaStream_t s) {
   static thread_local int cached_dev = -1, cached_sms = 148;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1613,9 +1659,11 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
     const cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) fprintf(stderr, "decode_step: %s (layer %d, batch %d): %s\n", what, layer, B, cudaGetErrorString(e));
   };
+  bool ok = true;  // every launch of the step was planned and accepted
+  auto launched = [&](cudaError_t e) { ok = launched_ok(e, "attention") && ok; };
   auto run = [&](auto epi_tag, const void* W, const MvArgs& m) {
     constexpr int EPI = decltype(epi_tag)::value;
-    mv<EPI>(a.int8, W, m, nsm, s);
+    ok = mv<EPI>(a.int8, W, m, nsm, s) && ok;
   };
   using Resid = std::integral_constant<int, MV_RESID>;
   using Swiglu = std::integral_constant<int, MV_SWIGLU>;
@@ -1645,7 +1693,7 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
       }
       m.norm_w = a.n1[l]; m.K = a.hidden; m.N = nqkv; m.ws = a.s_qkv[l]; m.out = a.qkv; m.ldo = nqkv;
       m.sum_threads = a.int8 ? qa_threads<true>() : qa_threads<false>();
-      mv<MV_STORE>(a.int8, a.w_qkv[l], m, nsm, s, l != 0, a.int8, true);
+      ok = mv<MV_STORE>(a.int8, a.w_qkv[l], m, nsm, s, l != 0, a.int8, true) && ok;
       if (a.on_launch) a.on_launch(a.hook_ctx, 0);
       check("qkv_proj", l);
     }
@@ -1677,11 +1725,11 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
         const size_t smem = (size_t)q.kv_rows * kHd * 8;
         const dim3 t(128);
         if (g2) {
-          if (a.int8) launch_ex(qkv_attn_kernel<true, false, 2>, grid, t, smem, s, true, kSplits, q);
-          else launch_ex(qkv_attn_kernel<false, false, 2>, grid, t, smem, s, true, kSplits, q);
+          if (a.int8) launched(launch_ex(qkv_attn_kernel<true, false, 2>, grid, t, smem, s, true, kSplits, q));
+          else launched(launch_ex(qkv_attn_kernel<false, false, 2>, grid, t, smem, s, true, kSplits, q));
         } else {
-          if (a.int8) launch_ex(qkv_attn_kernel<true, false, kMaxG>, grid, t, smem, s, true, kSplits, q);
-          else launch_ex(qkv_attn_kernel<false, false, kMaxG>, grid, t, smem, s, true, kSplits, q);
+          if (a.int8) launched(launch_ex(qkv_attn_kernel<true, false, kMaxG>, grid, t, smem, s, true, kSplits, q));
+          else launched(launch_ex(qkv_attn_kernel<false, false, kMaxG>, grid, t, smem, s, true, kSplits, q));
         }
       } else {
         const size_t wbytes = ((size_t)q.rows_per_cta * a.hidden * (a.int8 ? 1 : 2) + 127) & ~(size_t)127;
@@ -1691,11 +1739,11 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
         const size_t smem = wbytes + (size_t)q.kv_rows * kHd * 8 + tail;
         const bool p = l != 0;
         if (g2) {
-          if (a.int8) launch_ex(qkv_attn_kernel<true, true, 2>, grid, dim3(qa_threads<true>()), smem, s, p, kSplits, q);
-          else launch_ex(qkv_attn_kernel<false, true, 2>, grid, dim3(qa_threads<false>()), smem, s, p, kSplits, q);
+          if (a.int8) launched(launch_ex(qkv_attn_kernel<true, true, 2>, grid, dim3(qa_threads<true>()), smem, s, p, kSplits, q));
+          else launched(launch_ex(qkv_attn_kernel<false, true, 2>, grid, dim3(qa_threads<false>()), smem, s, p, kSplits, q));
         } else {
-          if (a.int8) launch_ex(qkv_attn_kernel<true, true, kMaxG>, grid, dim3(qa_threads<true>()), smem, s, p, kSplits, q);
-          else launch_ex(qkv_attn_kernel<false, true, kMaxG>, grid, dim3(qa_threads<false>()), smem, s, p, kSplits, q);
+          if (a.int8) launched(launch_ex(qkv_attn_kernel<true, true, kMaxG>, grid, dim3(qa_threads<true>()), smem, s, p, kSplits, q));
+          else launched(launch_ex(qkv_attn_kernel<false, true, kMaxG>, grid, dim3(qa_threads<false>()), smem, s, p, kSplits, q));
         }
       }
       if (a.on_launch) a.on_launch(a.hook_ctx, 1);
@@ -1732,6 +1780,7 @@ void decode_step(const DecodeArgs& a, cudaStream_t s) {
   run(Argmax{}, a.lm_w, m);
   if (a.on_launch) a.on_launch(a.hook_ctx, 5);
   check("lm_head", -1);
+  return ok;
 }
 
 }  // namespace qasr

@@ -966,7 +966,7 @@ DecodeArgs Engine::dargs(const int* forced, float* logits, int slot) {
   return a;
 }
 
-void Engine::enqueue_step(const DecodeArgs& a) { decode_step(a, stream_); }
+bool Engine::enqueue_step(const DecodeArgs& a) { return decode_step(a, stream_); }
 
 // qkv+attention, o, gate/up, down per layer, then lm_head (batched steps add a q/k/v matvec)
 int Engine::decode_step_launches_1() const {
@@ -1025,7 +1025,10 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
     if (logits) logits->resize((size_t)max_steps * V);
     for (int i = 0; i < max_steps; ++i) {
       if (profile) a.on_launch(this, -1);
-      decode_step(a, stream_);
+      if (!decode_step(a, stream_)) {
+        cudaStreamSynchronize(stream_);
+        return false;
+      }
       if (logits)
         CUDA_OK(cudaMemcpyAsync(logits->data() + (size_t)i * V, dlogits_.p, (size_t)V * 4, cudaMemcpyDeviceToHost,
                                 stream_),
@@ -1147,18 +1150,18 @@ bool Engine::graph_for(int B) {
   a.batch = std::max(B, 1);
   cudaGraph_t g = nullptr;
   CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);
-  decode_step(a, stream_);
+  const bool planned = decode_step(a, stream_);
   const cudaError_t e1 = cudaStreamEndCapture(stream_, &g);
   cudaError_t e2 = cudaErrorUnknown;
-  if (e1 == cudaSuccess) e2 = cudaGraphInstantiate(&graph_exec_[B], g, 0);
+  if (planned && e1 == cudaSuccess) e2 = cudaGraphInstantiate(&graph_exec_[B], g, 0);
   if (g) cudaGraphDestroy(g);
-  if (e1 == cudaSuccess && e2 == cudaSuccess) {
+  if (planned && e1 == cudaSuccess && e2 == cudaSuccess) {
     built_gen_[B] = graph_gen_;
     return true;
   }
   cudaGetLastError();
   graph_exec_[B] = nullptr;
-  set_error("decode: CUDA graph capture of the decode step failed");
+  if (planned) set_error("decode: CUDA graph capture of the decode step failed");
   return false;
 }
 
@@ -1173,8 +1176,12 @@ bool Engine::graph_for_slot(int slot) {
   DecodeArgs a = dargs(nullptr, nullptr, slot);
   cudaGraph_t g = nullptr;
   CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);
-  enqueue_step(a);
+  const bool planned = enqueue_step(a);
   CUDA_OK(cudaStreamEndCapture(stream_, &g), false);
+  if (!planned) {
+    cudaGraphDestroy(g);
+    return false;
+  }
   const cudaError_t e = cudaGraphInstantiate(&slot_graph_[slot], g, 0);
   cudaGraphDestroy(g);
   CUDA_OK(e, false);
@@ -1228,8 +1235,12 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
       ga.batch = B;
       cudaGraph_t g = nullptr;
       CUDA_OK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), false);
-      decode_step(ga, stream_);
+      const bool planned = decode_step(ga, stream_);
       CUDA_OK(cudaStreamEndCapture(stream_, &g), false);
+      if (!planned) {
+        cudaGraphDestroy(g);
+        return false;
+      }
       const cudaError_t e = cudaGraphInstantiate(&entry.first, g, 0);
       cudaGraphDestroy(g);
       CUDA_OK(e, false);
@@ -1251,7 +1262,7 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
     int c = std::min(chunk, max_steps - launched);
     for (int i = 0; i < c; ++i) {
       if (run_graph) CUDA_OK(cudaGraphLaunch(run_graph, stream_), false);
-      else decode_step(direct_args, stream_);
+      else if (!decode_step(direct_args, stream_)) return false;
     }
     CUDA_OK(cudaMemcpy2DAsync(htokens_ + launched, (size_t)ld * 4, dtokens_.p + (size_t)first_slot * ld + launched,
                               (size_t)ld * 4, (size_t)c * 4, B, cudaMemcpyDeviceToHost, stream_),

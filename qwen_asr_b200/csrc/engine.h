@@ -206,7 +206,7 @@ class Engine {
   int tokens_rows_ = 0;
   bool ensure_tokens(int max_steps, int B);
   int max_batch_ = 0;
-  void enqueue_step(const DecodeArgs& a);  // one single-sequence decode step
+  bool enqueue_step(const DecodeArgs& a);  // one single-sequence decode step (false: not planned)
   int decode_step_launches_1() const;
   // decode graphs, one per batch size; valid while built_gen_[B] == graph_gen_
   cudaGraphExec_t graph_exec_[kDecodeMaxBatch + 1] = {};

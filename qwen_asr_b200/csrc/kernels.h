@@ -247,6 +247,8 @@ bool decode_split_qkv(int hidden, int q_heads, int kv_heads, bool int8);
 void decode_kernels_init();
 void enc_kernels_init();
 // Enqueues one full decode step (embedding -> layers -> lm_head argmax).
-void decode_step(const DecodeArgs& a, cudaStream_t s);
+// false (with the reason in last_error) when a launch of the step could not be planned or
+// was refused; the caller must not use the step's results.
+bool decode_step(const DecodeArgs& a, cudaStream_t s);
 
 }  // namespace qasr

@@ -66,3 +66,49 @@ def test_stream_17b_widths_46_chunks(m17l4_dir):
         assert got == (None if want is None or "\x00" in want else want), i // step
     ref = O.lossy(st.result_bytes) or None
     assert s.result() == (None if ref is None or "\x00" in ref else ref)
+
+
+def _child(env_extra, code, model_dir):
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    prog = ("import sys, hashlib; sys.path.insert(0, %r)\n"
+            "import numpy as np\n"
+            "import qwen_asr_b200 as Q\n"
+            "eng = Q.Engine(%r)\n"
+            "h = eng.model_info()['dec_hidden']\n"
+            "rows = (np.random.default_rng(1).standard_normal((300, h)) * 0.02).astype(np.float32)\n"
+            "forced = np.random.default_rng(2).integers(0, 151643, 6).astype(np.int32)\n" % (root, model_dir)) + code
+    return subprocess.run([sys.executable, "-c", prog], env=dict(os.environ, **env_extra), capture_output=True,
+                          text=True, cwd=root)
+
+
+def test_streaming_matvec_stage_size_keeps_bits(m17l4_dir):
+    """The streaming decode matvec (1.7B gate/up at one sequence) may put several 512-byte
+    column chunks in one ring stage; every lane still adds its chunks in column order, so the
+    logits are bit-identical for 8 KB and 64 KB stages, in both weight modes."""
+    code = ("for mode in ('bf16', 'int8'):\n"
+            "    eng.set_decode_mode(mode)\n"
+            "    _, lg, _ = eng.debug_decode(rows, 6, forced=forced, want_logits=True)\n"
+            "    print(mode, hashlib.sha1(lg.tobytes()).hexdigest())\n")
+    outs = []
+    for kb in ("8", "64"):
+        p = _child({"QASR_MV_STAGE_KB": kb}, code, m17l4_dir)
+        assert p.returncode == 0, p.stdout + p.stderr
+        outs.append([ln for ln in p.stdout.splitlines() if ln.startswith(("bf16", "int8"))])
+    assert len(outs[0]) == 2 and outs[0] == outs[1], outs
+
+
+def test_unplannable_matvec_fails_loudly(m17l4_dir):
+    """A decode matvec whose ring of two stages does not fit its shared-memory budget is not
+    launched, and the decode reports that instead of returning tokens from a partial step."""
+    code = ("eng.set_decode_mode('bf16')\n"
+            "try:\n"
+            "    eng.debug_decode(rows, 4, forced=forced)\n"
+            "    print('decoded')\n"
+            "except RuntimeError as e:\n"
+            "    print('raised:', e)\n")
+    p = _child({"QASR_MV_BUDGET_KB": "16"}, code, m17l4_dir)
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert "raised:" in p.stdout and "two stages" in p.stdout, p.stdout + p.stderr
