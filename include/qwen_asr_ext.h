@@ -171,8 +171,12 @@ int64_t qwen_asr_debug_parse_wav(const uint8_t* data, int64_t len, float* out, i
 /* Segment start offsets of transcribe_audio (transcribe.rs:253-346); returns the count. */
 int32_t qwen_asr_debug_split_points(const float* samples, int64_t n, float segment_sec, float search_sec,
                                     int64_t* out, int32_t cap);
-/* compact_silence (audio.rs:375-479); returns the kept sample count. */
+/* compact_silence (audio.rs:375-479) as the host restatement (the oracle's check of the
+ * algorithm); returns the kept sample count. */
 int64_t qwen_asr_debug_compact_silence(const float* samples, int64_t n, float* out, int64_t cap);
+/* The same on the engine's GPU (the path skip_silence takes); NULL out queries the count. */
+int64_t qwen_asr_debug_compact_silence_gpu(QwenAsrEngine* e, const float* samples, int64_t n, float* out,
+                                           int64_t cap);
 /* String::from_utf8_lossy + str::trim as used on transcripts (transcribe.rs:237-238). */
 int32_t qwen_asr_debug_lossy_trim(const char* bytes, int32_t n, char* out, int32_t cap);
 /* normalize_language (config.rs:167-182); "" when unsupported. */

@@ -103,6 +103,7 @@ SIGNATURES = {
     "qwen_asr_debug_parse_wav": (C.c_int64, [_U8P, C.c_int64, _F32P, C.c_int64]),
     "qwen_asr_debug_split_points": (C.c_int32, [_F32P, C.c_int64, C.c_float, C.c_float, _I64P, C.c_int32]),
     "qwen_asr_debug_compact_silence": (C.c_int64, [_F32P, C.c_int64, _F32P, C.c_int64]),
+    "qwen_asr_debug_compact_silence_gpu": (C.c_int64, [_VP, _F32P, C.c_int64, _F32P, C.c_int64]),
     "qwen_asr_debug_lossy_trim": (C.c_int32, [C.c_char_p, C.c_int32, C.c_char_p, C.c_int32]),
     "qwen_asr_debug_normalize_language": (C.c_int32, [C.c_char_p, C.c_char_p, C.c_int32]),
     "qwen_asr_forced_align": (_VP, [_VP, _F32P, C.c_int64, C.c_char_p, C.c_char_p]),
@@ -328,6 +329,15 @@ class Engine:
         if lib().qwen_asr_debug_resample(self._h, p, len(x), from_rate, out.ctypes.data_as(_F32P), n) != n:
             raise RuntimeError(last_error())
         return out
+
+    def debug_compact_silence(self, samples) -> np.ndarray:
+        """GPU silence compaction (the skip_silence path); at most len(samples) samples."""
+        x, p = _f32(samples)
+        out = np.zeros(max(len(x), 1), dtype=np.float32)
+        n = lib().qwen_asr_debug_compact_silence_gpu(self._h, p, len(x), out.ctypes.data_as(_F32P), len(x))
+        if n < 0:
+            raise RuntimeError(last_error())
+        return out[:n]
 
     def debug_kv(self, layer: int, n_pos: int, slot: int = 0):
         """(k, v) f32 [kv_heads][n_pos][128] of one layer of a KV slot."""

@@ -614,6 +614,18 @@ int32_t qwen_asr_debug_split_points(const float* samples, int64_t n, float segme
   return (int32_t)sp.size();
 }
 
+int64_t qwen_asr_debug_compact_silence_gpu(QwenAsrEngine* e, const float* samples, int64_t n, float* out,
+                                           int64_t cap) {
+  if (!e || !samples || n < 0) return -1;
+  std::vector<float> r;
+  if (!e->ctx.eng.compact_silence(samples, (long)n, r)) return -1;
+  if (out) {
+    if ((int64_t)r.size() > cap) return -1;
+    memcpy(out, r.data(), r.size() * 4);
+  }
+  return (int64_t)r.size();
+}
+
 int64_t qwen_asr_debug_compact_silence(const float* samples, int64_t n, float* out, int64_t cap) {
   if (!samples || n < 0) return -1;
   auto r = qasr::compact_silence(std::vector<float>(samples, samples + n));

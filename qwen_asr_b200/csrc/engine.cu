@@ -870,6 +870,30 @@ const float* Engine::resample_to_device(const float* h_in, long n, int rate, lon
   return rs_out_.p;
 }
 
+bool Engine::compact_silence(const float* h_in, long n, std::vector<float>& out) {
+  cudaSetDevice(device_);
+  out.clear();
+  if (n <= 0) return true;
+  if (!cs_in_.alloc(n) || !cs_out_.alloc(n) || !cs_scratch_.alloc(compact_silence_scratch(n)) || !cs_count_.alloc(2))
+    return false;
+  CUDA_OK(cudaMemcpyAsync(cs_in_.p, h_in, (size_t)n * 4, cudaMemcpyHostToDevice, stream_), false);
+  compact_silence_device(cs_in_.p, n, cs_out_.p, cs_scratch_.p, cs_count_.p, stream_);
+  CUDA_OK(cudaGetLastError(), false);
+  long long cnt[2] = {0, 0};
+  CUDA_OK(cudaMemcpyAsync(cnt, cs_count_.p, sizeof(cnt), cudaMemcpyDeviceToHost, stream_), false);
+  CUDA_OK(cudaStreamSynchronize(stream_), false);
+  if (cnt[0] < 0 || cnt[0] > n) {
+    set_error("compact_silence: kept count out of range");
+    return false;
+  }
+  out.resize((size_t)cnt[0]);
+  if (cnt[0] > 0) {
+    CUDA_OK(cudaMemcpyAsync(out.data(), cs_out_.p, (size_t)cnt[0] * 4, cudaMemcpyDeviceToHost, stream_), false);
+    CUDA_OK(cudaStreamSynchronize(stream_), false);
+  }
+  return true;
+}
+
 bool Engine::copy_kv(int slot, int layer, int n_pos, float* k, float* v) {
   cudaSetDevice(device_);
   const Config& c = cfg_;

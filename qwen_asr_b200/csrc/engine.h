@@ -134,6 +134,9 @@ class Engine {
   // Resamples host samples at `rate` to 16 kHz on the GPU (audio.rs:133-196); returns the
   // device buffer (valid until the next call) and its length in *n_out, or nullptr.
   const float* resample_to_device(const float* h_in, long n, int rate, long* n_out);
+  // Silence compaction of host samples on the GPU (audio.rs:375-479, skip_silence): out gets
+  // the kept samples, equal to the reference's compact_silence.
+  bool compact_silence(const float* h_in, long n, std::vector<float>& out);
   // Debug: K and V rows [kv_heads][n_pos][128] of positions 0..n_pos-1 of one slot and layer.
   bool copy_kv(int slot, int layer, int n_pos, float* k, float* v);
   int kv_capacity() const { return max_seq_; }
@@ -229,6 +232,9 @@ class Engine {
   // bf16 planes (hi/mid/lo) of GEMM inputs written by their producers
   DevBuf<__nv_bfloat16> pl_a_, pl_b_, pl_c_, pl_conv_;
   DevBuf<float> rs_in_, rs_out_;  // resampler input / output
+  DevBuf<float> cs_in_, cs_out_;  // silence compaction input / output
+  DevBuf<unsigned char> cs_scratch_;
+  DevBuf<long long> cs_count_;
   DevBuf<int> prow_pos_;        // packed prefill rows: KV position
   DevBuf<long long> prow_kv_;   // packed prefill rows: KV slot offset (floats)
   cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;

@@ -92,6 +92,12 @@ void mel_normalize(float* logmel, int n_frames, const int* gmax, cudaStream_t s)
 long resampled_length(long n, int from_rate, int to_rate);
 void resample_device(const float* in, long n, int from_rate, int to_rate, float* out, cudaStream_t s);
 
+// Silence compaction (audio.rs:375-479) of in[n] into out (capacity n) on the GPU; d_count[2]
+// receives {kept samples, 1 if nothing was kept and the first 0.5 s was copied}. scratch holds
+// compact_silence_scratch(n) bytes.
+size_t compact_silence_scratch(long n);
+void compact_silence_device(const float* in, long n, float* out, void* scratch, long long* d_count, cudaStream_t s);
+
 // ---------------------------------------------------------------- encoder
 // conv2d1 (1 -> 480, 3x3 s2 p1) + bias + GELU on `n_chunks` chunks of width w taken from
 // mel [F][128] starting at frame f0 + c*cw; output channels-last [c][64][w1][480].

@@ -218,7 +218,9 @@ char* qwen_asr_pool_transcribe_pcm(QwenAsrPool* p, const float* samples, int32_t
   std::vector<float> in(samples, samples + n_samples);
   std::string result;
   // one segment, or segments that depend on each other (past-text conditioning): worker 0
-  std::vector<float> audio = c0.skip_silence ? qasr::compact_silence(in) : in;
+  std::vector<float> audio;
+  if (!c0.skip_silence) audio = in;
+  else if (!c0.eng.compact_silence(in.data(), (long)in.size(), audio)) return nullptr;
   std::vector<size_t> splits = qasr::split_points(audio, c0.segment_sec, c0.search_sec);
   if (splits.size() <= 1 || c0.past_text_conditioning || p->workers.size() == 1) {
     const std::vector<int> first{0};

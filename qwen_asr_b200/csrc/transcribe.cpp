@@ -234,7 +234,9 @@ bool Ctx::transcribe_audio(const std::vector<float>& in, std::string& result) {
   reset_perf();
   last_tokens.clear();
   perf_audio_ms = 1000.0 * (double)in.size() / kSampleRate;
-  std::vector<float> audio = skip_silence ? compact_silence(in) : in;
+  std::vector<float> audio;
+  if (!skip_silence) audio = in;
+  else if (!eng.compact_silence(in.data(), (long)in.size(), audio)) return false;
   if (!prepare_prompt_tokens()) return false;
   std::vector<size_t> splits = split_points(audio, segment_sec, search_sec);
   result.clear();
