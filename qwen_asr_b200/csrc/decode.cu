@@ -71,24 +71,32 @@ __device__ __forceinline__ unsigned long long am_key(float v, int idx) {
 }
 
 struct Timeline {
+  // Each kernel's CTA 0 reserves kRecords records at entry (one atomic, before its dependency
+  // wait): {kind, t_entry, t_after_wait, t_exit}, then kRecords - 1 sub-phase records
+  // {code, t, 0, 0} written with plain stores, so a stamp does not stall the CTA on a
+  // returning atomic. code = 100 + 10 * kind + phase; unused records keep code kUnused.
+  static constexpr int kRecords = 8;
+  static constexpr unsigned long long kUnused = 0xFFFFFFFFull;
   unsigned long long* slot = nullptr;
+  int nsub = 0;
   __device__ __forceinline__ void begin(unsigned long long* tl, int* cnt, int kind) {
     if (tl && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0) {
-      slot = tl + 4 * (size_t)atomicAdd(cnt, 1);
+      slot = tl + 4 * (size_t)atomicAdd(cnt, kRecords);
       slot[0] = (unsigned long long)kind;
       slot[1] = global_timer_ns();
+      slot[2] = slot[3] = 0;
+      for (int i = 1; i < kRecords; ++i) slot[4 * i] = kUnused;
     }
   }
   __device__ __forceinline__ void mark(int i) {
     if (slot) slot[i] = global_timer_ns();
   }
-  // A sub-phase record {kind, t, 0, 0} after this kernel's record (CTA 0 only).
-  __device__ __forceinline__ void sub(unsigned long long* tl, int* cnt, int kind) {
-    if (slot && threadIdx.x == 0) {
-      unsigned long long* r = tl + 4 * (size_t)atomicAdd(cnt, 1);
-      r[0] = (unsigned long long)kind;
+  __device__ __forceinline__ void sub(unsigned long long*, int*, int code) {
+    if (slot && threadIdx.x == 0 && nsub < kRecords - 1) {
+      unsigned long long* r = slot + 4 * (1 + nsub++);
       r[1] = global_timer_ns();
       r[2] = r[3] = 0;
+      r[0] = (unsigned long long)code;
     }
   }
 };
@@ -339,11 +347,14 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
   const int c0 = has0 ? tid : 0;
   float4 hold[kMaxB];
   float acc[kMaxB];  // sum of squares (norm) or max |x| (int8 without norm)
+  // Sequences b >= B are skipped (break) in every per-sequence loop: a B = 1 launch does the
+  // work of one sequence, with each sequence's summation order unchanged.
 #pragma unroll
-  for (int b = 0; b < kMaxB; ++b) hold[b] = ldx(b, c0);
+  for (int b = 0; b < kMaxB; ++b) hold[b] = b < B ? ldx(b, c0) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int b = 0; b < kMaxB; ++b) {
     acc[b] = 0.f;
+    if (b >= B) break;
     if (!has0) continue;
     if (!INT8 && b < B) *reinterpret_cast<float4*>(xs + (size_t)b * kpad + xperm4(c0)) = hold[b];
     if (a.embed && blockIdx.x == 0 && b < B && stok[b] >= 0)
@@ -353,6 +364,7 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
   for (int c = tid + P; c < nc && tid < P; c += P) {  // chunks j >= 1
 #pragma unroll
     for (int h = 0; h < kMaxB; h += 4) {  // four sequences' loads in flight (registers)
+      if (h >= B) break;
       float4 t[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) t[i] = ldx(h + i, c);
@@ -370,6 +382,7 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
   auto reduce = [&](bool is_sum) {
 #pragma unroll
     for (int b = 0; b < kMaxB; ++b) {
+      if (b >= B) break;
       const float v = is_sum ? warp_sum(acc[b]) : warp_max(acc[b]);
       if (lane == 0 && b < B) red[b * kWarps + warp] = v;
     }
@@ -394,12 +407,14 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
     if (INT8) {
 #pragma unroll
       for (int b = 0; b < kMaxB; ++b) {
+        if (b >= B) break;
         hold[b] = normed(hold[b], sinv[min(b, B - 1)], c0);
         acc[b] = has0 ? absmax(0.f, hold[b]) : 0.f;
       }
       for (int c = tid + P; c < nc && tid < P; c += P) {
 #pragma unroll
         for (int h = 0; h < kMaxB; h += 4) {
+          if (h >= B) break;
           float4 t[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) t[i] = ldx(h + i, c);
@@ -431,6 +446,7 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
     for (int c = tid + P; c < nc && tid < P; c += P) {
 #pragma unroll
       for (int h = 0; h < kMaxB; h += 4) {
+        if (h >= B) break;
         float4 t[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) t[i] = ldx(h + i, c);
@@ -562,6 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__
   } else {
     stage_all<INT8>(a, xs, xq, snw, red, sinv, xscale, kpad);
   }
+  tline.sub(a.tl, a.tl_count, 103 + 10 * a.kind);
 
   unsigned long long best[kMaxB];
   int iacc[4][kMaxB];
@@ -578,6 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__
   for (int t = 0; t < nt; ++t) {
     const int s = t % a.stages, blk = t / nsc;
     mbar_wait(&full[s], (uint32_t)(t / a.stages) & 1u, a.err, 1);
+    if (t == a.stages - 1) tline.sub(a.tl, a.tl_count, 104 + 10 * a.kind);  // prefetched stages consumed
     // chunks in column order, so every lane accumulates a row exactly as with one chunk per stage
     for (int c = 0; c < cps; ++c) {
     const int kc = (t % nsc) * cps + c;
@@ -720,9 +738,9 @@ __device__ __forceinline__ void mv_small_body(const CUtensorMap& wmap, const MvA
   } else {
     stage_all<INT8>(a, xs, xq, snw, red, sinv, xscale, kpad);
   }
-  tline.sub(a.tl, a.tl_count, 20);
+  tline.sub(a.tl, a.tl_count, 100 + 10 * a.kind);
   mbar_wait(&bar, 0, a.err, 5);
-  tline.sub(a.tl, a.tl_count, 21);
+  tline.sub(a.tl, a.tl_count, 101 + 10 * a.kind);
   if (BATCH) {
     // items of kRG rows x one 512-byte chunk: each sequence's input chunk is read once and
     // dotted with the kRG rows (rows past R repeat row R - 1 and are dropped; sequences past
@@ -820,34 +838,62 @@ __device__ __forceinline__ void mv_small_body(const CUtensorMap& wmap, const MvA
   }
     }
   const int items = BATCH ? 0 : B * R * nkc;
-  for (int it = warp; it < items; it += kWarps) {
-    const int b = it / (R * nkc), r = (it / nkc) % R, kc = it % nkc;
-    const unsigned char* w = wst + ((size_t)kc * R + r) * kChunk + lane * 16;
+  // bf16: four (sequence, row, chunk) items of a warp at a time, independent load / dot /
+  // shuffle chains that overlap, each item computed exactly as on its own (int8 launches have
+  // 2-6 items per warp, where the grouping measured slower).
+  constexpr int kIlp = INT8 ? 1 : 4;
+  for (int it0 = warp; it0 < items; it0 += kIlp * kWarps) {
+    int its[kIlp];
+#pragma unroll
+    for (int u = 0; u < kIlp; ++u) its[u] = min(it0 + u * kWarps, items - 1);  // tail repeats the last item
     if (INT8) {
-      const int4 xv = *reinterpret_cast<const int4*>(xq + (size_t)b * kpad + kc * kChunk + lane * 16);
-      const int4 wv = *reinterpret_cast<const int4*>(w);
-      int acc = __dp4a(wv.x, xv.x, 0);
-      acc = __dp4a(wv.y, xv.y, acc);
-      acc = __dp4a(wv.z, xv.z, acc);
-      acc = __dp4a(wv.w, xv.w, acc);
-      acc = warp_sum_i(acc);
-      if (lane == 0) part[it] = __int_as_float(acc);
+      int acc[kIlp];
+#pragma unroll
+      for (int u = 0; u < kIlp; ++u) {
+        const int it = its[u], b = it / (R * nkc), r = (it / nkc) % R, kc = it % nkc;
+        const int4 xv = *reinterpret_cast<const int4*>(xq + (size_t)b * kpad + kc * kChunk + lane * 16);
+        const int4 wv = *reinterpret_cast<const int4*>(wst + ((size_t)kc * R + r) * kChunk + lane * 16);
+        acc[u] = __dp4a(wv.x, xv.x, 0);
+        acc[u] = __dp4a(wv.y, xv.y, acc[u]);
+        acc[u] = __dp4a(wv.z, xv.z, acc[u]);
+        acc[u] = __dp4a(wv.w, xv.w, acc[u]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int u = 0; u < kIlp; ++u) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);  // warp_sum_i
+      if (lane == 0)
+#pragma unroll
+        for (int u = 0; u < kIlp; ++u)
+          if (it0 + u * kWarps < items) part[its[u]] = __int_as_float(acc[u]);
     } else {
-      const float* xb = xs + (size_t)b * kpad + kc * (kChunk / 2) + lane * 8;
-      const float4 x0 = *reinterpret_cast<const float4*>(xb);
-      const float4 x1 = *reinterpret_cast<const float4*>(xb + 4);
-      float f[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(w), f);
-      float acc = f[0] * x0.x;
-      acc = fmaf(f[1], x0.y, acc); acc = fmaf(f[2], x0.z, acc); acc = fmaf(f[3], x0.w, acc);
-      acc = fmaf(f[4], x1.x, acc); acc = fmaf(f[5], x1.y, acc); acc = fmaf(f[6], x1.z, acc);
-      acc = fmaf(f[7], x1.w, acc);
-      acc = warp_sum(acc);
-      if (lane == 0) part[it] = acc;
+      float acc[kIlp];
+#pragma unroll
+      for (int u = 0; u < kIlp; ++u) {
+        const int it = its[u], b = it / (R * nkc), r = (it / nkc) % R, kc = it % nkc;
+        const float* xb = xs + (size_t)b * kpad + kc * (kChunk / 2) + lane * 8;
+        const float4 x0 = *reinterpret_cast<const float4*>(xb);
+        const float4 x1 = *reinterpret_cast<const float4*>(xb + 4);
+        float f[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4*>(wst + ((size_t)kc * R + r) * kChunk + lane * 16), f);
+        float v = f[0] * x0.x;
+        v = fmaf(f[1], x0.y, v); v = fmaf(f[2], x0.z, v); v = fmaf(f[3], x0.w, v);
+        v = fmaf(f[4], x1.x, v); v = fmaf(f[5], x1.y, v); v = fmaf(f[6], x1.z, v);
+        v = fmaf(f[7], x1.w, v);
+        acc[u] = v;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int u = 0; u < kIlp; ++u) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);  // warp_sum
+      if (lane == 0)
+#pragma unroll
+        for (int u = 0; u < kIlp; ++u)
+          if (it0 + u * kWarps < items) part[its[u]] = acc[u];
     }
   }
   __syncthreads();
-  tline.sub(a.tl, a.tl_count, 22);
+  tline.sub(a.tl, a.tl_count, 102 + 10 * a.kind);
   auto row_value = [&](int b, int r) -> float {
     const float* p = part + ((size_t)b * R + r) * nkc;
     if (INT8) {
@@ -1172,7 +1218,7 @@ qkv_attn_kernel(QkvAttnArgs a) {
     }
   }
   __syncthreads();
-  tline.sub(a.tl, a.tl_count, 29);
+  tline.sub(a.tl, a.tl_count, 110);
   cluster_wait();  // every CTA of the cluster has started
   for (int t = d; t < rpc * kSplits; t += kQA) {  // this CTA's rows into every CTA's allv
     const int q = t / rpc, rr = t - q * rpc;
@@ -1180,7 +1226,7 @@ qkv_attn_kernel(QkvAttnArgs a) {
   }
   cluster_arrive();
   cluster_wait();  // every CTA's rows have arrived
-  tline.sub(a.tl, a.tl_count, 30);
+  tline.sub(a.tl, a.tl_count, 111);
   }
 
   // ---- phase 2: gather this head group's raw q/k/v from the cluster
@@ -1323,7 +1369,7 @@ qkv_attn_kernel(QkvAttnArgs a) {
   }
   // Push this split's partial of the dims each CTA finalises (CTA q: dims [q*8, q*8 + 8) of
   // every head of the group), then one cluster barrier; nothing reads a peer afterwards.
-  tline.sub(a.tl, a.tl_count, 31);
+  tline.sub(a.tl, a.tl_count, 112);
   __syncthreads();
   if (!PROJ) cluster_wait();  // every CTA of the cluster has started
   for (int i = d; i < G * kHd; i += kQA) {

@@ -1012,7 +1012,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
   if (!ensure_kv(start_pos + max_steps + 1)) return false;
   if (!ensure_tokens(max_steps, slot + 1)) return false;
   if (timeline_) {
-    size_t need = (size_t)max_steps * (cfg_.dec_layers * 10 + 4) * 4 + 64;
+    size_t need = (size_t)max_steps * (cfg_.dec_layers * 5 + 1) * 8 * 4 + 64;  // 8 records a kernel
     if (dtl_.n < need) {
       if (!dtl_.alloc(need)) return false;
       ++graph_gen_;
@@ -1235,7 +1235,7 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
   for (int b = 0; b < B; ++b) maxpos = std::max(maxpos, hstate_[first_slot + b].pos);
   if (!ensure_kv(maxpos + max_steps + 1) || !ensure_tokens(max_steps, first_slot + B)) return false;
   if (timeline_) {
-    size_t need = (size_t)max_steps * (cfg_.dec_layers * 10 + 4) * 4 + 64;
+    size_t need = (size_t)max_steps * (cfg_.dec_layers * 5 + 1) * 8 * 4 + 64;  // 8 records a kernel
     if (dtl_.n < need) {
       if (!dtl_.alloc(need)) return false;
       ++graph_gen_;
