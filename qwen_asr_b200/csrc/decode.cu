@@ -63,7 +63,11 @@ struct MvArgs {
   int* tl_count;
   int kind;
   int sum_threads;             // batched staging: threads owning sum-of-squares chunks (0: all)
+  const void* staged;          // batched steps: the inputs as stage_kernel left them, or null
 };
+
+// Byte offset of the f32 per-sequence scales in an int8 staged buffer ([B][kpad] int8 first).
+__host__ __device__ inline size_t staged_scale_off(int B, int kpad) { return ((size_t)B * kpad + 15) & ~(size_t)15; }
 
 __device__ __forceinline__ unsigned long long am_key(float v, int idx) {
   unsigned int hv = (unsigned int)float_to_ordered(v) ^ 0x80000000u;
@@ -459,6 +463,73 @@ __device__ void stage_all(const MvArgs& a, float* xs, int8_t* xq, const float* s
   __syncthreads();
 }
 
+// The batched matvecs' inputs as stage_kernel computed them once for the whole grid: int8
+// vectors [B][kpad] and their scales, or normalised f32 vectors [B][kpad] in the permuted
+// layout the dot loops read. Copied verbatim, so the kernel sees the bits stage_all gives.
+template <bool INT8>
+__device__ void load_staged(const MvArgs& a, float* xs, int8_t* xq, float* xscale, int kpad) {
+  const int tid = threadIdx.x, B = a.B;
+  if (INT8) {
+    const int4* src = reinterpret_cast<const int4*>(a.staged);
+    int4* dst = reinterpret_cast<int4*>(xq);
+    for (int i = tid; i < B * kpad / 16; i += kThreads) dst[i] = __ldcg(src + i);
+    const float* sc = reinterpret_cast<const float*>(reinterpret_cast<const unsigned char*>(a.staged) +
+                                                     staged_scale_off(B, kpad));
+    if (tid < B) xscale[tid] = __ldcg(sc + tid);
+  } else {
+    const float4* src = reinterpret_cast<const float4*>(a.staged);
+    float4* dst = reinterpret_cast<float4*>(xs);
+    for (int i = tid; i < B * kpad / 4; i += kThreads) dst[i] = __ldcg(src + i);
+    if (tid < B) xscale[tid] = 1.0f;
+  }
+  __syncthreads();
+}
+
+// Batched steps: the input staging (RMSNorm, int8 quantisation, embedding gather) of the
+// next matvec, done once by one CTA with stage_all's threads and order and written to
+// a.staged, instead of by every CTA of the matvec (each of which would otherwise read all B
+// input vectors from L2, two or three times).
+template <bool INT8>
+__global__ void __launch_bounds__(kThreads, 1) stage_kernel(MvArgs a) {
+  // one CTA per sequence (blockIdx.y): each sequence's staging is independent (its own block
+  // reductions), so a one-sequence stage_all gives the bits the all-sequence one does
+  Timeline tline;
+  tline.begin(a.tl, a.tl_count, a.kind);
+  extern __shared__ unsigned char sm_raw[];
+  __shared__ float red[kMaxB * kWarps];
+  __shared__ float sinv[2 * kMaxB];
+  __shared__ float xscale[kMaxB];
+  unsigned char* sm = (unsigned char*)(((uintptr_t)sm_raw + 15) & ~(uintptr_t)15);
+  const int tid = threadIdx.x, b = blockIdx.y, K = a.K;
+  const int kpad = a.nkc * kChunk / (INT8 ? 1 : 2);
+  MvArgs s1 = a;
+  s1.B = 1;
+  s1.x = a.x + (size_t)b * a.ldx;
+  if (a.x_out) s1.x_out = a.x_out + (size_t)b * a.ldx;
+  s1.st = a.st + b;
+  float* xs = reinterpret_cast<float*>(sm);                      // bf16: [kpad]
+  int8_t* xq = reinterpret_cast<int8_t*>(xs + (INT8 ? 0 : kpad));  // int8: [kpad]
+  float* snw = reinterpret_cast<float*>(xq + (INT8 ? kpad : 0));
+  if (a.norm_w)
+    for (int i = tid; i < K; i += kThreads) snw[i] = a.norm_w[i];
+  pdl_launch_dependents();
+  pdl_wait();
+  tline.mark(2);
+  stage_all<INT8>(s1, xs, xq, snw, red, sinv, xscale, kpad);
+  unsigned char* out = reinterpret_cast<unsigned char*>(const_cast<void*>(a.staged));
+  if (INT8) {
+    const int4* src = reinterpret_cast<const int4*>(xq);
+    int4* dst = reinterpret_cast<int4*>(out + (size_t)b * kpad);
+    for (int i = tid; i < kpad / 16; i += kThreads) dst[i] = src[i];
+    if (tid == 0) reinterpret_cast<float*>(out + staged_scale_off(a.B, kpad))[b] = xscale[0];
+  } else {
+    const float4* src = reinterpret_cast<const float4*>(xs);
+    float4* dst = reinterpret_cast<float4*>(out) + (size_t)b * kpad / 4;
+    for (int i = tid; i < kpad / 4; i += kThreads) dst[i] = src[i];
+  }
+  tline.mark(3);
+}
+
 // Greedy-token bookkeeping of sequence b after its argmax (decoder.rs:550-645 returns the
 // token; transcribe.rs feeds it back as the next input).
 __device__ __forceinline__ void commit_token(const MvArgs& a, int b, unsigned long long key) {
@@ -575,6 +646,8 @@ __global__ void __launch_bounds__(kThreads, 1) mv_kernel(const __grid_constant__
     const float sc = stage_x<INT8>(a, 0, xs, xq, snw, red, kpad);
     if (tid == 0) xscale[0] = sc;
     __syncthreads();
+  } else if (a.staged) {
+    load_staged<INT8>(a, xs, xq, xscale, kpad);
   } else {
     stage_all<INT8>(a, xs, xq, snw, red, sinv, xscale, kpad);
   }
@@ -735,6 +808,8 @@ __device__ __forceinline__ void mv_small_body(const CUtensorMap& wmap, const MvA
       const float sc = stage_x<INT8>(a, b, INT8 ? xs : xs + (size_t)b * kpad, xq + (size_t)b * kpad, snw, red, kpad);
       if (tid == 0) xscale[b] = sc;
     }
+  } else if (a.staged) {
+    load_staged<INT8>(a, xs, xq, xscale, kpad);
   } else {
     stage_all<INT8>(a, xs, xq, snw, red, sinv, xscale, kpad);
   }
@@ -1618,8 +1693,28 @@ int sm_count() {
 }
 }  // namespace
 
+size_t decode_staged_bytes(int hidden, int q_dim, int inter) {
+  const int k = std::max(hidden, std::max(q_dim, inter));
+  const size_t kpad = ((size_t)k + kChunk - 1) / kChunk * kChunk;  // >= either mode's padding
+  return (size_t)kDecodeMaxBatch * kpad * 4 + 1024;
+}
+
+bool decode_stage_once() {
+  static const bool on = [] {
+    const char* e = getenv("QASR_STAGE_ONCE");
+    return !e || atoi(e) != 0;
+  }();
+  return on;
+}
+
+int decode_batched_step_launches(int layers, bool int8) {
+  return int8 && decode_stage_once() ? 9 * layers + 2 : 5 * layers + 1;
+}
+
 void decode_kernels_init() {
   const int kMax = 210 * 1024;
+  for (auto k : {stage_kernel<true>, stage_kernel<false>})
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   for (auto k : {mv_small_kernel<true, MV_RESID>, mv_small_kernel<false, MV_RESID>, mv_small_kernel<true, MV_STORE>,
                  mv_small_kernel<false, MV_STORE>, mv_small_kernel<true, MV_SWIGLU>,
                  mv_small_kernel<false, MV_SWIGLU>, mv_small_batch_kernel<true, MV_RESID>,
@@ -1706,7 +1801,23 @@ bool decode_step(const DecodeArgs& a, cudaStream_t s) {
     if (e != cudaSuccess) fprintf(stderr, "decode_step: %s (layer %d, batch %d): %s\n", what, layer, B, cudaGetErrorString(e));
   };
   bool ok = true;  // every launch of the step was planned and accepted
-  auto launched = [&](cudaError_t e) { ok = launched_ok(e, "attention") && ok; };
+  auto launched = [&](cudaError_t e) { ok = launched_ok(e, "kernel") && ok; };
+  // Batched int8 steps: each matvec's inputs staged once by stage_kernel (one CTA a
+  // sequence) before it. int8 staging reads the inputs three times (norm, absmax, quantise),
+  // 4-9 us per CTA-redundant pass at B = 8 (1.7B); bf16 staging is cheaper than the extra
+  // kernel hand-over, so bf16 batched steps keep staging in every CTA.
+  const bool pre_stage = B > 1 && a.int8 && a.staged && decode_stage_once();
+  auto stage = [&](MvArgs& m, bool pdl) {
+    if (!pre_stage) return;
+    MvArgs sa = m;
+    sa.nkc = (m.K * (a.int8 ? 1 : 2) + kChunk - 1) / kChunk;
+    sa.staged = a.staged;
+    sa.kind = 6;
+    const int kpad = sa.nkc * kChunk / (a.int8 ? 1 : 2);
+    const size_t smem = 16 + (size_t)kpad * (a.int8 ? 1 : 4) + (m.norm_w ? (size_t)m.K * 4 : 0);
+    launched(launch_ex(a.int8 ? stage_kernel<true> : stage_kernel<false>, dim3(1, B), dim3(kThreads), smem, s, pdl, 1, sa));
+    m.staged = a.staged;
+  };
   auto run = [&](auto epi_tag, const void* W, const MvArgs& m) {
     constexpr int EPI = decltype(epi_tag)::value;
     ok = mv<EPI>(a.int8, W, m, nsm, s) && ok;
@@ -1739,7 +1850,8 @@ bool decode_step(const DecodeArgs& a, cudaStream_t s) {
       }
       m.norm_w = a.n1[l]; m.K = a.hidden; m.N = nqkv; m.ws = a.s_qkv[l]; m.out = a.qkv; m.ldo = nqkv;
       m.sum_threads = a.int8 ? qa_threads<true>() : qa_threads<false>();
-      ok = mv<MV_STORE>(a.int8, a.w_qkv[l], m, nsm, s, l != 0, a.int8, true) && ok;
+      stage(m, l != 0);  // the step's first kernel is a plain launch
+      ok = mv<MV_STORE>(a.int8, a.w_qkv[l], m, nsm, s, l != 0 || pre_stage, a.int8, true) && ok;
       if (a.on_launch) a.on_launch(a.hook_ctx, 0);
       check("qkv_proj", l);
     }
@@ -1799,6 +1911,7 @@ bool decode_step(const DecodeArgs& a, cudaStream_t s) {
     MvArgs m = base(2);
     m.x = a.attn; m.ldx = qd; m.K = qd; m.N = a.hidden;
     m.ws = a.s_o[l]; m.out = a.x; m.resid = a.x; m.ldo = a.hidden;
+    stage(m, true);
     run(Resid{}, a.w_o[l], m);
     if (a.on_launch) a.on_launch(a.hook_ctx, 2);
     check("o_proj", l);
@@ -1806,6 +1919,7 @@ bool decode_step(const DecodeArgs& a, cudaStream_t s) {
     m = base(3);
     m.x = a.x; m.ldx = a.hidden; m.norm_w = a.n2[l]; m.K = a.hidden; m.N = 2 * a.inter;
     m.ws = a.s_gu[l]; m.out = a.ffn; m.ldo = a.inter;
+    stage(m, true);
     run(Swiglu{}, a.w_gu[l], m);
     if (a.on_launch) a.on_launch(a.hook_ctx, 3);
     check("gate_up", l);
@@ -1813,6 +1927,7 @@ bool decode_step(const DecodeArgs& a, cudaStream_t s) {
     m = base(4);
     m.x = a.ffn; m.ldx = a.inter; m.K = a.inter; m.N = a.hidden;
     m.ws = a.s_down[l]; m.out = a.x; m.resid = a.x; m.ldo = a.hidden;
+    stage(m, true);
     run(Resid{}, a.w_down[l], m);
     if (a.on_launch) a.on_launch(a.hook_ctx, 4);
     check("down", l);
@@ -1823,6 +1938,7 @@ bool decode_step(const DecodeArgs& a, cudaStream_t s) {
   m.am_part = a.am_part; m.am_ticket = a.am_ticket; m.st = a.st; m.tokens = a.tokens; m.forced = a.forced;
   m.tokens_ld = a.tokens_ld;
   m.logits = a.logits;
+  stage(m, true);
   run(Argmax{}, a.lm_w, m);
   if (a.on_launch) a.on_launch(a.hook_ctx, 5);
   check("lm_head", -1);

@@ -288,7 +288,8 @@ bool Engine::load(const std::string& dir, int device, bool trunc_quant) {
   if (!dx_.alloc((size_t)kMaxSlots * h) || !dqkv_.alloc((size_t)mb * (qd + 2 * kvd)) || !dattn_.alloc((size_t)mb * qd) ||
       !dffn_.alloc((size_t)mb * inter) || !dpart_.alloc((size_t)c.dec_heads * 16 * 130) ||
       !dticket_.alloc(c.dec_kv_heads) || !dam_ticket_.alloc(1) || !dam_part_.alloc((size_t)mb * 1024) ||
-      !dstate_.alloc(kMaxSlots) || !dlogits_.alloc(c.vocab_size) || !derr_.alloc(1))
+      !dstate_.alloc(kMaxSlots) || !dlogits_.alloc(c.vocab_size) || !derr_.alloc(1) ||
+      !dstaged_.alloc(decode_staged_bytes(h, qd, inter)))
     return false;
   CUDA_OK(cudaMemset(dticket_.p, 0, c.dec_kv_heads * sizeof(int)), false);
   CUDA_OK(cudaMemset(dam_ticket_.p, 0, sizeof(int)), false);
@@ -974,6 +975,7 @@ DecodeArgs Engine::dargs(const int* forced, float* logits, int slot) {
   a.k_cache = kc_.p; a.v_cache = vc_.p; a.layers = c.dec_layers;
   a.x = dx_.p; a.qkv = dqkv_.p; a.attn = dattn_.p; a.ffn = dffn_.p; a.part = dpart_.p; a.ticket = dticket_.p;
   a.am_ticket = dam_ticket_.p; a.am_part = dam_part_.p; a.st = dstate_.p; a.tokens = dtokens_.p;
+  a.staged = dstaged_.p;
   a.kv_slot_stride = kv_slot_stride(); a.tokens_ld = tokens_ld_; a.batch = 1;
   if (slot > 0) {  // one sequence in its own slot: offset the per-sequence buffers
     a.k_cache += (size_t)slot * kv_slot_stride();
@@ -1012,7 +1014,7 @@ bool Engine::decode(int max_steps, bool stop_on_eos, std::vector<int>& out, cons
   if (!ensure_kv(start_pos + max_steps + 1)) return false;
   if (!ensure_tokens(max_steps, slot + 1)) return false;
   if (timeline_) {
-    size_t need = (size_t)max_steps * (cfg_.dec_layers * 5 + 1) * 8 * 4 + 64;  // 8 records a kernel
+    size_t need = (size_t)max_steps * (cfg_.dec_layers * 9 + 2) * 8 * 4 + 64;  // 8 records a kernel
     if (dtl_.n < need) {
       if (!dtl_.alloc(need)) return false;
       ++graph_gen_;
@@ -1235,7 +1237,7 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
   for (int b = 0; b < B; ++b) maxpos = std::max(maxpos, hstate_[first_slot + b].pos);
   if (!ensure_kv(maxpos + max_steps + 1) || !ensure_tokens(max_steps, first_slot + B)) return false;
   if (timeline_) {
-    size_t need = (size_t)max_steps * (cfg_.dec_layers * 5 + 1) * 8 * 4 + 64;  // 8 records a kernel
+    size_t need = (size_t)max_steps * (cfg_.dec_layers * 9 + 2) * 8 * 4 + 64;  // 8 records a kernel
     if (dtl_.n < need) {
       if (!dtl_.alloc(need)) return false;
       ++graph_gen_;
@@ -1332,7 +1334,7 @@ bool Engine::decode_batch(int B, int max_steps, bool stop_on_eos, std::vector<st
     return false;
   }
   CUDA_OK(cudaGetLastError(), false);
-  launches += (long)launched * (B > 1 ? 5 * cfg_.dec_layers + 1 : decode_step_launches_1());
+  launches += (long)launched * (B > 1 ? decode_batched_step_launches(cfg_.dec_layers, mode_ == DECODE_INT8) : decode_step_launches_1());
   int herr = 0;
   CUDA_OK(cudaMemcpy(&herr, derr_.p, sizeof(int), cudaMemcpyDeviceToHost), false);
   if (herr) {

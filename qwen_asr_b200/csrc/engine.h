@@ -199,6 +199,7 @@ class Engine {
   DevBuf<float> dx_, dqkv_, dattn_, dffn_, dpart_, dlogits_, drec_;
   DevBuf<int> dticket_, dam_ticket_, dtokens_, dforced_, derr_;
   DevBuf<unsigned long long> dam_part_;
+  DevBuf<unsigned char> dstaged_;  // batched steps: each matvec's inputs, staged once
   DevBuf<StepState> dstate_;
   bool timeline_ = false;
   DevBuf<unsigned long long> dtl_;

@@ -242,11 +242,19 @@ struct DecodeArgs {
   int batch = 1;
   size_t kv_slot_stride = 0;
   int tokens_ld = 0;
+  // Batched steps: device buffer of decode_staged_bytes() where each matvec's inputs are
+  // staged once (stage_kernel) instead of by every CTA; null stages in every CTA.
+  void* staged = nullptr;
 };
 constexpr int kDecodeMaxBatch = 8;
 constexpr int kMaxSlots = 64;  // KV slots / decode states an engine can hold
 // Largest batch the decode kernels' shared memory admits for this model shape.
 int decode_max_batch(int hidden, int inter, int q_heads, int kv_heads, bool int8);
+// Bytes of DecodeArgs::staged for these widths, and whether batched steps use it
+// (QASR_STAGE_ONCE=0 turns it off); kernels a batched step launches.
+size_t decode_staged_bytes(int hidden, int q_dim, int inter);
+bool decode_stage_once();
+int decode_batched_step_launches(int layers, bool int8);
 // Whether a single-sequence step projects q/k/v with a separate matvec (5 kernels per layer).
 bool decode_split_qkv(int hidden, int q_heads, int kv_heads, bool int8);
 // Per-device kernel attributes (dynamic shared memory limits); call once per device.
