@@ -862,51 +862,29 @@ __device__ __forceinline__ void mv_small_body(const CUtensorMap& wmap, const MvA
       for (int j = 0; j < kRG; ++j)
         wv[j] = *reinterpret_cast<const uint4*>(wst + ((size_t)kc * R + min(rb + j, R - 1)) * kChunk + lane * 16);
       for (int bh = 0; bh < kMaxB / 4 && bh * 4 < B; ++bh) {  // sequences in groups of four
-        if (false) {
-          int acc[kRG][4];
+        float acc[kRG][4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int b = min(bh * 4 + i, B - 1);
-            const int4 xv = *reinterpret_cast<const int4*>(xq + (size_t)b * kpad + kc * kChunk + lane * 16);
-#pragma unroll
-            for (int j = 0; j < kRG; ++j) {
-              acc[j][i] = __dp4a((int)wv[j].x, xv.x, 0);
-              acc[j][i] = __dp4a((int)wv[j].y, xv.y, acc[j][i]);
-              acc[j][i] = __dp4a((int)wv[j].z, xv.z, acc[j][i]);
-              acc[j][i] = __dp4a((int)wv[j].w, xv.w, acc[j][i]);
-            }
-          }
+        for (int i = 0; i < 4; ++i) {
+          const int b = min(bh * 4 + i, B - 1);
+          const float* xb = xs + (size_t)b * kpad + kc * (kChunk / 2) + lane * 4;
+          const float4 x0 = *reinterpret_cast<const float4*>(xb);
+          const float4 x1 = *reinterpret_cast<const float4*>(xb + 128);
 #pragma unroll
           for (int j = 0; j < kRG; ++j) {
-            const int u = warp_reduce4(acc[j], lane);
-            const int b = bh * 4 + sel;
-            if ((lane & 7) == 0 && b < B && rb + j < R) part[((size_t)b * R + rb + j) * nkc + kc] = __int_as_float(u);
+            float f[8];
+            bf16x8_to_f32(wv[j], f);
+            float s = f[0] * x0.x;
+            s = fmaf(f[1], x0.y, s); s = fmaf(f[2], x0.z, s); s = fmaf(f[3], x0.w, s);
+            s = fmaf(f[4], x1.x, s); s = fmaf(f[5], x1.y, s); s = fmaf(f[6], x1.z, s);
+            s = fmaf(f[7], x1.w, s);
+            acc[j][i] = s;
           }
-        } else {
-          float acc[kRG][4];
+        }
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int b = min(bh * 4 + i, B - 1);
-            const float* xb = xs + (size_t)b * kpad + kc * (kChunk / 2) + lane * 4;
-            const float4 x0 = *reinterpret_cast<const float4*>(xb);
-            const float4 x1 = *reinterpret_cast<const float4*>(xb + 128);
-#pragma unroll
-            for (int j = 0; j < kRG; ++j) {
-              float f[8];
-              bf16x8_to_f32(wv[j], f);
-              float s = f[0] * x0.x;
-              s = fmaf(f[1], x0.y, s); s = fmaf(f[2], x0.z, s); s = fmaf(f[3], x0.w, s);
-              s = fmaf(f[4], x1.x, s); s = fmaf(f[5], x1.y, s); s = fmaf(f[6], x1.z, s);
-              s = fmaf(f[7], x1.w, s);
-              acc[j][i] = s;
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < kRG; ++j) {
-            const float u = warp_reduce4(acc[j], lane);
-            const int b = bh * 4 + sel;
-            if ((lane & 7) == 0 && b < B && rb + j < R) part[((size_t)b * R + rb + j) * nkc + kc] = u;
-          }
+        for (int j = 0; j < kRG; ++j) {
+          const float u = warp_reduce4(acc[j], lane);
+          const int b = bh * 4 + sel;
+          if ((lane & 7) == 0 && b < B && rb + j < R) part[((size_t)b * R + rb + j) * nkc + kc] = u;
         }
       }
     }
@@ -1081,7 +1059,6 @@ qkv_attn_kernel(QkvAttnArgs a) {
   tline.begin(a.tl, a.tl_count, 1);
   extern __shared__ __align__(128) unsigned char dsm[];
   __shared__ __align__(8) uint64_t wbar, kvbar;
-  __shared__ float red32[32];
   __shared__ float vals[64];                          // this CTA's projected rows
   __shared__ __align__(16) float hv[MG + 2][kHd];  // normalised q heads, k, v of `pos`
   __shared__ float red[4][MG + 1];
