@@ -126,3 +126,35 @@ def test_decoder_logits_match_transformers(pin_model):
     for step, (a, b) in enumerate(zip(lg, out)):
         assert float(np.max(np.abs(a - b))) <= 1e-5 * float(np.max(np.abs(a))), step
         assert int(np.argmax(a)) == int(np.argmax(b)), step
+
+
+def test_tokenizer_matches_hf_tokenizers(tiny_dir):
+    """The oracle's whole-string byte-level BPE (tokenizer.rs:227-279: no pre-tokenizer split,
+    lowest-rank merge first) and its id -> bytes table equal the `tokenizers` library's BPE
+    model on the same vocab.json / merges.txt with a byte-level pre-tokenizer that does not
+    split (the host C++ tokenizer is checked against the oracle in test_host_abi.py)."""
+    import json
+    import os
+    import random
+    tokenizers = pytest.importorskip("tokenizers")
+    from oracle import qwen_oracle as O
+    T = O.Tokenizer(tiny_dir)
+    with open(os.path.join(tiny_dir, "vocab.json"), encoding="utf-8") as f:
+        vocab = json.load(f)
+    merges = []
+    with open(os.path.join(tiny_dir, "merges.txt"), encoding="utf-8") as f:
+        for line in f.read().splitlines():
+            if line and not line.startswith("#"):
+                a, b = line.split(" ", 1)
+                merges.append((a, b))
+    tk = tokenizers.Tokenizer(tokenizers.models.BPE(vocab=vocab, merges=merges))
+    tk.pre_tokenizer = tokenizers.pre_tokenizers.ByteLevel(add_prefix_space=False, use_regex=False)
+    rng = random.Random(1)
+    words = ["the", " and", " speech", " model", "ing", " 你好", "é", "\n", " 123", "!?", " 😀", "  "]
+    texts = ["hello world", " The quick brown fox.", "Zürich — 東京 😀", "a" * 50, "language English<asr_text>"]
+    texts += ["".join(rng.choice(words) for _ in range(rng.randint(1, 12))) for _ in range(200)]
+    for t in texts:
+        assert T.encode(t) == tk.encode(t).ids, t
+    for tid in range(0, len(vocab), 7):
+        tok = tk.id_to_token(tid)
+        assert bytes(T.b2u.index(ord(c)) for c in tok) == T.decode_bytes(tid), tid
