@@ -1,6 +1,7 @@
-"""Pins the CPU oracle against an independent implementation of the same architecture:
-transformers' Qwen3-Omni audio encoder (Qwen3OmniMoeAudioEncoder) for the audio tower and
-Qwen3ForCausalLM for the text decoder, loaded with the synthetic checkpoint's weights in f32.
+"""Pins the CPU oracle against independent implementations of the same network and
+tokeniser: transformers' Qwen3-Omni audio encoder (Qwen3OmniMoeAudioEncoder) for the audio
+tower and Qwen3ForCausalLM for the text decoder, loaded with the synthetic checkpoint's
+weights in f32, and the `tokenizers` library's byte-level BPE for the tokeniser.
 
 The reference's encoder (crates/qwen-asr/src/encoder.rs:186-358) and decoder
 (crates/qwen-asr/src/decoder.rs:455-645) are the same network as those classes, with three
